@@ -1,0 +1,201 @@
+/*
+ * titania_b200.h — C ABI of the B200 (sm_100a) backend for Titania's model.
+ *
+ * Two layers of entry points:
+ *
+ *  1. The `Device` trait, one function per method (reference:
+ *     model/device.rs:9-89). A Rust `model/b200.rs` implementing `Device`
+ *     binds these one to one, exactly as model/titania.rs:99-220 binds a
+ *     Titania GPU. Buffers hold f32 activations, weights hold bf16 bits.
+ *     Operations are enqueued in order on the device's stream; `tb200_read`
+ *     waits for them, so results are observed exactly as the synchronous
+ *     reference devices give them.
+ *
+ *  2. A fused model path with no trait counterpart: the Qwen3 forward pass of
+ *     model/model.rs:83-149 run as a handful of fused kernels per layer,
+ *     replayed from a CUDA graph, with a bf16 key/value cache and an
+ *     on-device greedy sampler. A caller builds it from weights it already
+ *     uploaded through (1), naming them as model/model.rs:48-72 does.
+ *
+ * Errors: the reference panics on a violated assertion (model/cpu.rs:22,40,
+ * 52-53; model/titania.rs:125,140,147,156-157,186-188,204-205). Every
+ * function here instead returns a nonzero TB200_ERR_* code and keeps a
+ * message for tb200_last_error(); a Rust wrapper panics on it.
+ *
+ * Threading: as in the reference (the trait needs neither Send nor Sync),
+ * one thread drives a device at a time.
+ */
+#ifndef TITANIA_B200_H
+#define TITANIA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TB200_API __attribute__((visibility("default")))
+#else
+#define TB200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TB200_OK = 0,
+  TB200_ERR_ARG = 1,     /* an argument violates the op's contract (a reference panic) */
+  TB200_ERR_CUDA = 2,    /* a CUDA runtime error */
+  TB200_ERR_TIMEOUT = 3, /* a bounded wait inside a kernel gave up */
+};
+
+typedef struct tb200_device tb200_device; /* a Device on one GPU */
+typedef struct tb200_buffer tb200_buffer; /* Device::Buffer, f32 (model/device.rs:13) */
+typedef struct tb200_weight tb200_weight; /* Device::Weight, bf16 (model/device.rs:15) */
+typedef struct tb200_model tb200_model;   /* fused-path model (no trait counterpart) */
+typedef struct tb200_state tb200_state;   /* fused-path State (model/model.rs:156-172) */
+
+/* Message for the last nonzero return on this thread. */
+TB200_API const char* tb200_last_error(void);
+
+/* Opens the device with CUDA ordinal `ordinal`; replaces `Titania::new`
+ * (model/titania.rs:58-68) / the `Cpu` unit value (model/cpu.rs:9). */
+TB200_API int tb200_device_open(int ordinal, tb200_device** out);
+TB200_API int tb200_device_close(tb200_device* dev);
+/* Waits for every enqueued operation; reports a kernel-side timeout. */
+TB200_API int tb200_sync(tb200_device* dev);
+/* The cudaStream_t all operations run on (for callers that time them). */
+TB200_API void* tb200_device_stream(tb200_device* dev);
+/* Number of SMs; kernels size their grids to it. */
+TB200_API int tb200_device_sms(tb200_device* dev);
+
+/* The RoPE table State::new uploads (model/model.rs:239-250): for each
+ * position < max_len and pair i < head_dim/2, (cos, sin) of
+ * pos / theta^(2i/head_dim), in f32 with the platform libm as the reference
+ * computes it. `out` holds max_len * head_dim floats. */
+TB200_API int tb200_rope_table(size_t max_len, size_t head_dim, float theta, float* out);
+
+/* ---- Device trait (model/device.rs) ------------------------------------ */
+
+/* device.rs:18 `upload(&self, tensor: Tensor) -> Weight`; `data` holds the
+ * product of `shape` bf16 values, row-major (model/weights.rs:14-17). */
+TB200_API int tb200_upload(tb200_device* dev, const uint16_t* data, const size_t* shape, size_t ndim, tb200_weight** out);
+/* device.rs:21 `alloc(&self, len) -> Buffer`: a zeroed buffer. */
+TB200_API int tb200_alloc(tb200_device* dev, size_t len, tb200_buffer** out);
+/* device.rs:26 `resize(&self, &mut Buffer, len)`: len <= allocated length. */
+TB200_API int tb200_resize(tb200_device* dev, tb200_buffer* buf, size_t len);
+/* The buffer's current length (Vec::len of `read`'s result). */
+TB200_API size_t tb200_buffer_len(const tb200_buffer* buf);
+/* device.rs:29 `read(&self, &Buffer) -> Vec<f32>`; `len` must equal the
+ * buffer's length. Waits for the device. */
+TB200_API int tb200_read(tb200_device* dev, const tb200_buffer* buf, float* out, size_t len);
+/* device.rs:32 `write(&self, &mut Buffer, &[f32])`; `len` must equal the
+ * buffer's length. */
+TB200_API int tb200_write(tb200_device* dev, tb200_buffer* buf, const float* data, size_t len);
+/* device.rs:35-42 `copy`: dst[dst_offset..][..len] = src[src_offset..][..len]. */
+TB200_API int tb200_copy(tb200_device* dev, tb200_buffer* dst, size_t dst_offset, const tb200_buffer* src, size_t src_offset,
+               size_t len);
+/* device.rs:46 `embed(&self, out, table, tokens)`. */
+TB200_API int tb200_embed(tb200_device* dev, tb200_buffer* out, const tb200_weight* table, const uint32_t* tokens, size_t n);
+/* device.rs:51 `matmul(&self, out, w, x)`: out[t] = w · x[t]. */
+TB200_API int tb200_matmul(tb200_device* dev, tb200_buffer* out, const tb200_weight* w, const tb200_buffer* x);
+/* device.rs:54 `add(&self, x, y)`: x += y. */
+TB200_API int tb200_add(tb200_device* dev, tb200_buffer* x, const tb200_buffer* y);
+/* device.rs:58 `rmsnorm(&self, x, weight, eps)`: rows of weight's length. */
+TB200_API int tb200_rmsnorm(tb200_device* dev, tb200_buffer* x, const tb200_weight* weight, float eps);
+/* device.rs:66 `rope(&self, x, table, pos, n_heads, head_dim)`. */
+TB200_API int tb200_rope(tb200_device* dev, tb200_buffer* x, const tb200_buffer* table, size_t pos, size_t n_heads,
+               size_t head_dim);
+/* device.rs:75-85 `attention(&self, out, q, k_cache, v_cache, pos, n_heads,
+ * head_dim, n_kv_heads)`; caches laid out [position][kv head][head_dim]. */
+TB200_API int tb200_attention(tb200_device* dev, tb200_buffer* out, const tb200_buffer* q, const tb200_buffer* k_cache,
+                    const tb200_buffer* v_cache, size_t pos, size_t n_heads, size_t head_dim, size_t n_kv_heads);
+/* device.rs:88 `silu_mul(&self, gate, up)`. */
+TB200_API int tb200_silu_mul(tb200_device* dev, tb200_buffer* gate, const tb200_buffer* up);
+
+/* The trait has no free (handles live as long as the process, as with
+ * Titania, model/titania.rs:43-55); these let a caller give memory back. */
+TB200_API int tb200_free_buffer(tb200_device* dev, tb200_buffer* buf);
+TB200_API int tb200_free_weight(tb200_device* dev, tb200_weight* w);
+
+/* Greedy sampling (model/sampler.rs:21-33 at temperature 0) on the device:
+ * the index of the largest element under IEEE total order, ties to the
+ * lowest index. */
+TB200_API int tb200_argmax(tb200_device* dev, const tb200_buffer* logits, uint32_t* out);
+
+/* ---- Fused model path --------------------------------------------------- */
+
+/* The config.json fields the model reads (model/config.rs:10-35); head_dim
+ * resolved by the caller as Config::head_dim does. */
+typedef struct tb200_config {
+  size_t hidden_size;
+  size_t intermediate_size;
+  size_t num_hidden_layers;
+  size_t num_attention_heads;
+  size_t num_key_value_heads;
+  size_t head_dim;
+  float rms_norm_eps;
+  float rope_theta;
+  size_t vocab_size;
+  int tie_word_embeddings;
+} tb200_config;
+
+/* Starts a fused model for `config` on `dev` (Model::load,
+ * model/model.rs:40-77, after its uploads). */
+TB200_API int tb200_model_create(tb200_device* dev, const tb200_config* config, tb200_model** out);
+/* Names an uploaded weight with its checkpoint tensor name
+ * (model/model.rs:48-72, e.g. "model.layers.3.self_attn.q_proj.weight"). */
+TB200_API int tb200_model_bind(tb200_model* model, const char* name, const tb200_weight* w);
+/* Checks that every tensor is bound with the right shape and packs the fused
+ * layouts (q|k|v rows, gate/up rows interleaved). */
+TB200_API int tb200_model_finalize(tb200_model* model);
+TB200_API int tb200_model_free(tb200_model* model);
+
+/* State::new (model/model.rs:176-211) for the fused path: bf16 K/V cache for
+ * `max_len` positions and the RoPE table (model/model.rs:239-250). */
+TB200_API int tb200_state_new(tb200_model* model, size_t max_len, tb200_state** out);
+TB200_API int tb200_state_free(tb200_state* state);
+
+/* Model::forward (model/model.rs:83-91): runs `tokens`, the first at `pos`,
+ * adding their keys and values to the cache, and writes the logits for the
+ * token after the last one to `logits` (vocab_size floats, host memory; may
+ * be NULL) and the greedy choice to `next_token` (may be NULL). */
+TB200_API int tb200_forward(tb200_model* model, tb200_state* state, const uint32_t* tokens, size_t n, size_t pos,
+                  float* logits, uint32_t* next_token);
+
+/* Greedy decoding entirely on the device (model/chat.rs:149-196 with
+ * temperature 0): feeds `token` at `pos`, then each chosen token, `steps`
+ * times; writes the `steps` chosen tokens to `out` (host memory). */
+TB200_API int tb200_generate(tb200_model* model, tb200_state* state, uint32_t token, size_t pos, size_t steps,
+                   uint32_t* out);
+
+/* Enqueues greedy decode steps on the device's stream without waiting or
+ * copying anything back: feeds `token` at `pos`, then each chosen token,
+ * `steps` times (what tb200_generate runs, minus its copies and wait). For
+ * callers that time the device or overlap it with host work. */
+TB200_API int tb200_decode_enqueue(tb200_model* model, tb200_state* state, uint32_t token, size_t pos, size_t steps);
+
+/* The fused kernels of one decode step, for tb200_enqueue_op. */
+enum {
+  TB200_OP_EMBED = 0,     /* x = embed[token]                               */
+  TB200_OP_QKV = 1,       /* q|k|v = W_qkv . rmsnorm(x)                     */
+  TB200_OP_ATTENTION = 2, /* QK-norm, RoPE, K/V append, attention           */
+  TB200_OP_O = 3,         /* x += W_o . att                                 */
+  TB200_OP_GATE_UP = 4,   /* h = silu(W_g . rmsnorm(x)) * (W_u . rmsnorm(x)) */
+  TB200_OP_DOWN = 5,      /* x += W_d . h                                   */
+  TB200_OP_LM_HEAD = 6,   /* logits = W_lm . rmsnorm(x); greedy token; pos++ */
+};
+
+/* Enqueues one fused kernel of the decode step (of layer `layer` for ops
+ * 1-5) on the device's stream, exactly as the step's graph runs it, without
+ * waiting: for timing and testing kernels one at a time. */
+TB200_API int tb200_enqueue_op(tb200_model* model, tb200_state* state, int op, size_t layer);
+
+/* Reads position `pos` of layer `layer`'s key (which=0) or value (which=1)
+ * cache as f32, Hkv*head_dim values, for tests. Waits for the device. */
+TB200_API int tb200_state_read_kv(tb200_state* state, size_t layer, int which, size_t pos, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TITANIA_B200_H */

@@ -319,11 +319,13 @@ Json parse_json(const std::string& s) {
 std::string read_file(const std::string& path) {
   FILE* f = std::fopen(path.c_str(), "rb");
   if (!f) panic("can't open " + path);
-  std::string s;
-  char buf[1 << 16];
-  size_t k;
-  while ((k = std::fread(buf, 1, sizeof buf, f)) > 0) s.append(buf, k);
+  std::fseek(f, 0, SEEK_END);
+  long size = std::ftell(f);
+  std::fseek(f, 0, SEEK_SET);
+  std::string s(size_t(size > 0 ? size : 0), '\0');
+  size_t got = size > 0 ? std::fread(&s[0], 1, s.size(), f) : 0;
   std::fclose(f);
+  if (got != s.size()) panic("short read of " + path);
   return s;
 }
 

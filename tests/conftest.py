@@ -35,3 +35,26 @@ def tiny_model_dir():
         sha = synth.write_model(d, synth.TINY, seed=meta["seed"])
         assert sha == meta["sha256"], "the seeded generator no longer reproduces the golden checkpoint"
     return d
+
+
+def close(actual, expected, rel, abs_):
+    """Asserts |actual - expected| <= abs_ + rel * |expected| elementwise."""
+    import numpy as np
+
+    actual = np.asarray(actual, dtype=np.float64)
+    expected = np.asarray(expected, dtype=np.float64)
+    assert actual.shape == expected.shape, (actual.shape, expected.shape)
+    err = np.abs(actual - expected)
+    tol = abs_ + rel * np.abs(expected)
+    bad = np.flatnonzero(err > tol)
+    assert bad.size == 0, (f"{bad.size}/{actual.size} elements out of tolerance; first at {bad[0]}: "
+                           f"got {actual.flat[bad[0]]}, expected {expected.flat[bad[0]]}; "
+                           f"max err {err.max():.3g}")
+
+
+@pytest.fixture(scope="session")
+def b200():
+    """The B200 device; the CUDA library must be built (no fallback)."""
+    import titania_b200 as tb
+
+    return tb.B200(0)

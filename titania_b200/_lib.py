@@ -1,0 +1,112 @@
+"""Loads libtitania_b200.so and declares the C ABI of include/titania_b200.h.
+
+There is no fallback: if the library is missing or cannot be loaded, every
+use raises. Build it with `python -m titania_b200.build`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtitania_b200.so")
+
+TB200_OK, TB200_ERR_ARG, TB200_ERR_CUDA, TB200_ERR_TIMEOUT = 0, 1, 2, 3
+
+
+class DeviceError(RuntimeError):
+    """A nonzero status from the library: the reference would have panicked
+    (TB200_ERR_ARG), or CUDA / a kernel-side wait failed."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("hidden_size", ctypes.c_size_t),
+        ("intermediate_size", ctypes.c_size_t),
+        ("num_hidden_layers", ctypes.c_size_t),
+        ("num_attention_heads", ctypes.c_size_t),
+        ("num_key_value_heads", ctypes.c_size_t),
+        ("head_dim", ctypes.c_size_t),
+        ("rms_norm_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+        ("vocab_size", ctypes.c_size_t),
+        ("tie_word_embeddings", ctypes.c_int),
+    ]
+
+
+P = ctypes.c_void_p
+SZ = ctypes.c_size_t
+PP = ctypes.POINTER(ctypes.c_void_p)
+F32P = ctypes.POINTER(ctypes.c_float)
+U16P = ctypes.POINTER(ctypes.c_uint16)
+U32P = ctypes.POINTER(ctypes.c_uint32)
+SZP = ctypes.POINTER(ctypes.c_size_t)
+
+# name: (restype, argtypes); every int-returning function is a status.
+SIGNATURES = {
+    "tb200_last_error": (ctypes.c_char_p, []),
+    "tb200_device_open": (ctypes.c_int, [ctypes.c_int, PP]),
+    "tb200_device_close": (ctypes.c_int, [P]),
+    "tb200_sync": (ctypes.c_int, [P]),
+    "tb200_device_stream": (ctypes.c_void_p, [P]),
+    "tb200_device_sms": (ctypes.c_int, [P]),
+    "tb200_rope_table": (ctypes.c_int, [SZ, SZ, ctypes.c_float, F32P]),
+    "tb200_upload": (ctypes.c_int, [P, U16P, SZP, SZ, PP]),
+    "tb200_alloc": (ctypes.c_int, [P, SZ, PP]),
+    "tb200_resize": (ctypes.c_int, [P, P, SZ]),
+    "tb200_buffer_len": (ctypes.c_size_t, [P]),
+    "tb200_read": (ctypes.c_int, [P, P, F32P, SZ]),
+    "tb200_write": (ctypes.c_int, [P, P, F32P, SZ]),
+    "tb200_copy": (ctypes.c_int, [P, P, SZ, P, SZ, SZ]),
+    "tb200_embed": (ctypes.c_int, [P, P, P, U32P, SZ]),
+    "tb200_matmul": (ctypes.c_int, [P, P, P, P]),
+    "tb200_add": (ctypes.c_int, [P, P, P]),
+    "tb200_rmsnorm": (ctypes.c_int, [P, P, P, ctypes.c_float]),
+    "tb200_rope": (ctypes.c_int, [P, P, P, SZ, SZ, SZ]),
+    "tb200_attention": (ctypes.c_int, [P, P, P, P, P, SZ, SZ, SZ, SZ]),
+    "tb200_silu_mul": (ctypes.c_int, [P, P, P]),
+    "tb200_free_buffer": (ctypes.c_int, [P, P]),
+    "tb200_free_weight": (ctypes.c_int, [P, P]),
+    "tb200_argmax": (ctypes.c_int, [P, P, U32P]),
+    "tb200_model_create": (ctypes.c_int, [P, ctypes.POINTER(Config), PP]),
+    "tb200_model_bind": (ctypes.c_int, [P, ctypes.c_char_p, P]),
+    "tb200_model_finalize": (ctypes.c_int, [P]),
+    "tb200_model_free": (ctypes.c_int, [P]),
+    "tb200_state_new": (ctypes.c_int, [P, SZ, PP]),
+    "tb200_state_free": (ctypes.c_int, [P]),
+    "tb200_forward": (ctypes.c_int, [P, P, U32P, SZ, SZ, F32P, U32P]),
+    "tb200_generate": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P]),
+    "tb200_decode_enqueue": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ]),
+    "tb200_enqueue_op": (ctypes.c_int, [P, P, ctypes.c_int, SZ]),
+    "tb200_state_read_kv": (ctypes.c_int, [P, SZ, ctypes.c_int, SZ, F32P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library, with every entry point declared."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m titania_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != TB200_OK:
+        raise DeviceError(rc, lib().tb200_last_error().decode(errors="replace"))
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args))

@@ -1,0 +1,159 @@
+// common.cuh — device helpers shared by the kernels: bf16 unpacking, warp
+// reductions, and thin wrappers over sm_90+/sm_100a PTX (mbarrier,
+// cp.async.bulk, programmatic dependent launch). Every wait on an mbarrier
+// is bounded in wall time; on expiry it records TB200_ERR_TIMEOUT in the
+// device's error word and the kernel returns.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/titania_b200.h"
+
+namespace tb {
+
+// One second: the longest any in-kernel wait may take before it gives up.
+constexpr unsigned long long kWaitNs = 1000000000ull;
+
+__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+// The two bf16 values packed in a 32-bit word, low half first.
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// f32 -> bf16 bits, round to nearest even.
+__device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_umax64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
+  }
+  return v;
+}
+
+// IEEE total order (Rust's f32::total_cmp) as an unsigned key, with ties
+// broken toward the lower index: larger key = preferred.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  int32_t b = __float_as_int(v);
+  b ^= int32_t(uint32_t(b >> 31) >> 1);
+  uint32_t k = uint32_t(b) ^ 0x80000000u;
+  return (static_cast<unsigned long long>(k) << 32) | (0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t argmax_index(unsigned long long key) {
+  return 0xFFFFFFFFu - uint32_t(key & 0xFFFFFFFFu);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void set_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start while the previous kernel in the stream still runs. Each kernel calls
+// pdl_launch_dependents() first (so the next kernel can start staging its own
+// weights) and pdl_wait() before touching anything the previous kernel
+// writes. Every CTA must reach pdl_wait() before it exits: completion of a
+// kernel then implies completion of every kernel before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- mbarrier / bulk copy ---------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with `parity` to complete, at most kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitNs) {
+      set_error(err, TB200_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// An L2 policy that lets streamed-once data (weights) be evicted first, so
+// that activations and the key/value cache stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst and src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32), id 1..15.
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// 8 bf16 weights (one 16-byte word) dotted with 8 f32 activations, in the
+// order w0*x0 + ... accumulated into acc.
+__device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
+  acc = fmaf(bf_lo(w.x), a.x, acc);
+  acc = fmaf(bf_hi(w.x), a.y, acc);
+  acc = fmaf(bf_lo(w.y), a.z, acc);
+  acc = fmaf(bf_hi(w.y), a.w, acc);
+  acc = fmaf(bf_lo(w.z), b.x, acc);
+  acc = fmaf(bf_hi(w.z), b.y, acc);
+  acc = fmaf(bf_lo(w.w), b.z, acc);
+  acc = fmaf(bf_hi(w.w), b.w, acc);
+  return acc;
+}
+
+}  // namespace tb

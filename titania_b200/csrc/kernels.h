@@ -1,0 +1,96 @@
+// kernels.h — host-side launchers for the CUDA kernels (ops.cu: one kernel
+// per Device-trait op; fused.cu: the fused decode path).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace tb {
+
+// ---- Device-trait ops (model/cpu.rs:34-155 semantics) ----------------------
+void launch_copy(cudaStream_t s, float* dst, const float* src, size_t n);
+void launch_embed(cudaStream_t s, float* out, const uint16_t* table, size_t dim, const uint32_t* tokens, size_t n);
+void launch_matmul(cudaStream_t s, float* out, const uint16_t* w, size_t rows, size_t cols, const float* x, size_t n);
+void launch_add(cudaStream_t s, float* x, const float* y, size_t n);
+void launch_rmsnorm(cudaStream_t s, float* x, size_t rows, const uint16_t* w, size_t dim, float eps);
+void launch_rope(cudaStream_t s, float* x, size_t n_tokens, const float* table, size_t pos, size_t n_heads,
+                 size_t head_dim);
+void launch_attention(cudaStream_t s, float* out, const float* q, size_t n_tokens, const float* k_cache,
+                      const float* v_cache, size_t pos, size_t n_heads, size_t head_dim, size_t n_kv_heads);
+void launch_silu_mul(cudaStream_t s, float* g, const float* u, size_t n);
+// Writes the argmax key (see argmax_key) of x[0..n) into *best, which the
+// caller zeroes first.
+void launch_argmax(cudaStream_t s, const float* x, size_t n, unsigned long long* best, int sms);
+
+// ---- fused decode path ------------------------------------------------------
+
+// Epilogues of the fused matrix-vector kernel.
+enum MvEpilogue {
+  kMvStore = 0,   // out[r] = w_r · x
+  kMvResidual,    // out[r] += w_r · x            (residual stream update)
+  kMvSiluPair,    // rows interleaved (gate, up): out[r/2] = silu(g) * u
+  kMvArgmax,      // out[r] = w_r · x, plus the greedy choice over all rows
+};
+
+struct MvArgs {
+  const uint16_t* w;       // [rows][cols] bf16
+  int rows, cols;
+  int row_align;           // CTA row ranges start at multiples of this
+  const float* x;          // [cols] input
+  const uint16_t* norm_w;  // RMSNorm weight applied to x first, or null
+  float eps;
+  float* out;
+  // kMvArgmax only:
+  unsigned long long* partial;  // [grid] per-CTA best key
+  unsigned* ticket;             // zero between launches
+  int* token;                   // next input token (written)
+  int* pos;                     // position (incremented)
+  int* step;                    // generated-token counter (incremented)
+  int* tokens_out;              // [tokens_cap] generated tokens
+  int tokens_cap;
+  int* err;
+};
+
+struct MvPlan {
+  int grid, chunk_rows, slots;
+  size_t smem;
+};
+MvPlan plan_mv(int rows, int cols, int row_align, int sms, size_t smem_budget);
+// Raises the shared-memory limit of every matrix-vector kernel; call once per
+// device before capturing or launching them.
+void init_fused_kernels();
+void launch_mv(cudaStream_t s, const MvPlan& plan, int epilogue, const MvArgs& a, bool pdl);
+
+struct AttnArgs {
+  const float* qkv;         // [q_dim | kv_dim | kv_dim] raw projections
+  const uint16_t* q_norm;   // [head_dim] bf16 or null
+  const uint16_t* k_norm;   // [head_dim] bf16 or null
+  float eps;
+  const float* rope;        // [max_len][head_dim] (cos, sin) pairs
+  uint16_t* k_cache;        // [Hkv][max_len][head_dim] bf16
+  uint16_t* v_cache;
+  int max_len, n_heads, n_kv_heads;
+  const int* pos;           // position of the token (device)
+  float* out;               // [n_heads][head_dim]
+  float* part;              // [Hkv][max_split][group][head_dim + 2]
+  unsigned* ticket;         // [Hkv], zero between launches
+  int max_split;
+  int* err;
+};
+void launch_attn_decode(cudaStream_t s, const AttnArgs& a, bool pdl);
+
+// io[0] = token, io[1] = pos, io[2] = 0 (the step's input and counters).
+void launch_set_io(cudaStream_t s, int* io, int token, int pos);
+
+// out = table[*token] as f32; a token outside [0, vocab) records TB200_ERR_ARG.
+void launch_embed_token(cudaStream_t s, float* out, const uint16_t* table, int dim, const int* token, int vocab,
+                        int* err, bool pdl);
+
+// Packs gate [F][H] and up [F][H] into rows interleaved g0,u0,g1,u1,...
+void launch_interleave_rows(cudaStream_t s, uint16_t* dst, const uint16_t* a, const uint16_t* b, size_t rows,
+                            size_t cols);
+// bf16 [rows][cols] -> f32, for reading the cache in tests.
+void launch_bf16_to_f32(cudaStream_t s, float* dst, const uint16_t* src, size_t n);
+
+}  // namespace tb

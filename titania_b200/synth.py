@@ -74,19 +74,27 @@ def tensor_list(c: dict) -> list[tuple[str, tuple[int, ...], str]]:
     return out
 
 
-def _gen(shape, init, seed, index, std):
+def _chunks(shape, init, seed, index, std, buf, bits):
+    """Yields the tensor's bf16 bytes in chunks, reusing the scratch arrays."""
     n = int(np.prod(shape))
     if init == "ones":
-        return np.full(n, 0x3F80, dtype=np.uint16)
+        yield np.full(n, 0x3F80, dtype=np.uint16).tobytes()
+        return
     rng = np.random.Generator(np.random.PCG64([seed, index]))
-    out = np.empty(n, dtype=np.uint16)
-    step = 1 << 24
+    step = buf.size
     for s in range(0, n, step):
         k = min(step, n - s)
-        v = rng.standard_normal(k, dtype=np.float32)
+        v = buf[:k]
+        rng.standard_normal(out=v, dtype=np.float32)
         v *= np.float32(std)
-        out[s:s + k] = f32_to_bf16_bits(v)
-    return out
+        u = v.view(np.uint32)
+        b = bits[:k]
+        np.right_shift(u, 16, out=b)
+        np.bitwise_and(b, 1, out=b)
+        b += np.uint32(0x7FFF)
+        b += u
+        b >>= 16
+        yield b.astype(np.uint16).tobytes()
 
 
 def write_model(dirpath: str, config: dict, seed: int = 0, std: float = 0.02) -> str:
@@ -108,10 +116,12 @@ def write_model(dirpath: str, config: dict, seed: int = 0, std: float = 0.02) ->
         pre = struct.pack("<Q", len(hbytes)) + hbytes
         fh.write(pre)
         h.update(pre)
+        buf = np.empty(1 << 22, dtype=np.float32)
+        bits = np.empty(1 << 22, dtype=np.uint32)
         for index, (name, shape, init) in enumerate(tensors):
-            data = _gen(shape, init, seed, index, std).tobytes()
-            fh.write(data)
-            h.update(data)
+            for data in _chunks(shape, init, seed, index, std, buf, bits):
+                fh.write(data)
+                h.update(data)
     os.replace(tmp, os.path.join(dirpath, "model.safetensors"))
     cfg = dict(config)
     cfg["architectures"] = ["Qwen3ForCausalLM"]
