@@ -150,9 +150,15 @@ TB200_API int tb200_model_bind(tb200_model* model, const char* name, const tb200
 TB200_API int tb200_model_finalize(tb200_model* model);
 TB200_API int tb200_model_free(tb200_model* model);
 
-/* State::new (model/model.rs:176-211) for the fused path: bf16 K/V cache for
- * `max_len` positions and the RoPE table (model/model.rs:239-250). */
-TB200_API int tb200_state_new(tb200_model* model, size_t max_len, tb200_state** out);
+/* Element type of the fused path's key/value cache. The reference caches
+ * f32 (model/model.rs:206-207); bf16 halves the bytes attention reads. */
+enum { TB200_KV_BF16 = 0, TB200_KV_F32 = 1 };
+
+/* State::new (model/model.rs:176-211) for the fused path: a key/value cache
+ * of `kv_dtype` (TB200_KV_*) for `max_len` positions and the RoPE table
+ * (model/model.rs:239-250). A state keeps its model alive: tb200_model_free
+ * on a model with states defers the free to the last tb200_state_free. */
+TB200_API int tb200_state_new(tb200_model* model, size_t max_len, int kv_dtype, tb200_state** out);
 TB200_API int tb200_state_free(tb200_state* state);
 
 /* Model::forward (model/model.rs:83-91): runs `tokens`, the first at `pos`,
@@ -189,6 +195,52 @@ enum {
  * 1-5) on the device's stream, exactly as the step's graph runs it, without
  * waiting: for timing and testing kernels one at a time. */
 TB200_API int tb200_enqueue_op(tb200_model* model, tb200_state* state, int op, size_t layer);
+
+/* ---- tracing ------------------------------------------------------------ */
+
+/* Events a traced kernel records, one per CTA. */
+enum {
+  TB200_TRACE_START = 0,   /* the CTA began (it may still wait on the previous kernel) */
+  TB200_TRACE_WAITED = 1,  /* the previous kernel's results became visible */
+  TB200_TRACE_INPUT = 2,   /* the input vector is staged (and normalized) */
+  TB200_TRACE_WEIGHTS = 3, /* the CTA's first weight chunk is in shared memory */
+  TB200_TRACE_DONE = 4,         /* the CTA finished its rows */
+  TB200_TRACE_ISSUED = 5,       /* the CTA's last weight copy was issued */
+  TB200_TRACE_LAST_WEIGHTS = 6, /* the CTA's last weight chunk is in shared memory */
+};
+
+/* One trace record: tag = op << 16 | layer (TB200_OP_*), the CTA index, the
+ * event, the SM, and the GPU's global timer in nanoseconds. */
+typedef struct tb200_trace_record {
+  uint32_t tag, cta, event, sm;
+  uint64_t ns;
+} tb200_trace_record;
+
+/* Starts recording the state's decode step: every kernel of the step's graph
+ * owns fixed record slots (8 per CTA), so a replay overwrites the previous
+ * one and the buffer holds the last step. `capacity` records are allocated;
+ * the graph is rebuilt to carry the buffer. */
+TB200_API int tb200_trace_start(tb200_state* state, size_t capacity);
+/* Stops recording, copies up to `cap` record slots to `out` (slots with
+ * ns == 0 were not written) and the number of slots one step uses to `*n`. */
+TB200_API int tb200_trace_stop(tb200_state* state, tb200_trace_record* out, size_t cap, size_t* n);
+
+/* The fused path's activation buffers, for tb200_state_read/write. */
+enum {
+  TB200_BUF_X = 0,      /* residual stream, hidden_size */
+  TB200_BUF_QKV = 1,    /* raw q|k|v projections, (heads + 2 kv_heads) * head_dim */
+  TB200_BUF_ATT = 2,    /* attention output, heads * head_dim */
+  TB200_BUF_H = 3,      /* silu(gate) * up, intermediate_size */
+  TB200_BUF_LOGITS = 4, /* vocab_size */
+};
+
+/* Copies a state buffer to the host (`n` must be its length); waits for the
+ * device. For testing the fused kernels one at a time. */
+TB200_API int tb200_state_read(tb200_state* state, int which, float* out, size_t n);
+/* Overwrites a state buffer from the host (`n` must be its length). */
+TB200_API int tb200_state_write(tb200_state* state, int which, const float* data, size_t n);
+/* Sets the token and position the next step (or tb200_enqueue_op) reads. */
+TB200_API int tb200_state_set_position(tb200_state* state, uint32_t token, size_t pos);
 
 /* Reads position `pos` of layer `layer`'s key (which=0) or value (which=1)
  * cache as f32, Hkv*head_dim values, for tests. Waits for the device. */

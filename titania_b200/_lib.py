@@ -76,12 +76,17 @@ SIGNATURES = {
     "tb200_model_bind": (ctypes.c_int, [P, ctypes.c_char_p, P]),
     "tb200_model_finalize": (ctypes.c_int, [P]),
     "tb200_model_free": (ctypes.c_int, [P]),
-    "tb200_state_new": (ctypes.c_int, [P, SZ, PP]),
+    "tb200_state_new": (ctypes.c_int, [P, SZ, ctypes.c_int, PP]),
     "tb200_state_free": (ctypes.c_int, [P]),
     "tb200_forward": (ctypes.c_int, [P, P, U32P, SZ, SZ, F32P, U32P]),
     "tb200_generate": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P]),
     "tb200_decode_enqueue": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ]),
     "tb200_enqueue_op": (ctypes.c_int, [P, P, ctypes.c_int, SZ]),
+    "tb200_trace_start": (ctypes.c_int, [P, SZ]),
+    "tb200_trace_stop": (ctypes.c_int, [P, P, SZ, SZP]),
+    "tb200_state_read": (ctypes.c_int, [P, ctypes.c_int, F32P, SZ]),
+    "tb200_state_write": (ctypes.c_int, [P, ctypes.c_int, F32P, SZ]),
+    "tb200_state_set_position": (ctypes.c_int, [P, ctypes.c_uint32, SZ]),
     "tb200_state_read_kv": (ctypes.c_int, [P, SZ, ctypes.c_int, SZ, F32P]),
 }
 

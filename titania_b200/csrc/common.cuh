@@ -60,6 +60,28 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// ---- device-side trace -------------------------------------------------------
+// When a state is traced, its kernels append one record per (launch, CTA,
+// event) with the global timer, so a host tool can lay out the timeline.
+struct TraceRec {
+  uint32_t tag;    // op << 16 | layer
+  uint32_t cta;    // blockIdx.x + blockIdx.y * gridDim.x
+  uint32_t event;  // TB200_TRACE_* (include/titania_b200.h)
+  uint32_t sm;
+  uint64_t ns;
+};
+struct Trace {
+  TraceRec* rec;  // null: tracing off
+  unsigned cap;   // records
+};
+// Record slots per CTA of a traced launch (one per TB200_TRACE_* event).
+constexpr uint32_t kTraceEvents = 8;
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

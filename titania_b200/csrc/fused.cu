@@ -4,24 +4,26 @@
 //   embed_token                      x = table[token]
 //   per layer:
 //     mv<norm, store>      (q|k|v)   qkv = Wqkv · rmsnorm(x)
-//     attn_decode                    QK-norm, RoPE, bf16 K/V append, GQA
-//                                    attention (split over the context)
+//     attn_decode                    QK-norm, RoPE, K/V append, GQA attention
+//                                    (split over the context, 64 positions
+//                                    per CTA, merged by the last CTA)
 //     mv<residual>         (o)       x += Wo · att
 //     mv<norm, silu pair>  (gate|up) h = silu(Wg · rmsnorm(x)) * (Wu · ...)
 //     mv<residual>         (down)    x += Wd · h
 //   mv<norm, argmax>       (lm_head) logits, greedy token, position += 1
 //
-// The matrix-vector kernel is the HBM-bound core (1.19 GB of weights per
-// token for Qwen3-0.6B). Each CTA owns a contiguous slice of rows; a
-// producer warp streams the slice into a shared-memory ring with
-// cp.async.bulk (TMA bulk copies, L2 evict-first), and eight consumer warps
-// each take whole chunks of rows. Kernels are launched with programmatic
-// dependent launch: a kernel starts while its predecessor runs and stages
-// its weights (which no kernel writes) before griddepcontrol.wait, so the
-// weight stream does not stop at kernel boundaries.
+// At batch 1 every kernel is short and the step is a chain of 142 dependent
+// launches, so the design goal is the critical path of each link. Kernels
+// are launched with programmatic dependent launch: a kernel starts while its
+// predecessor runs, and everything that does not depend on the predecessor
+// — its weights (streamed by a producer warp into a shared-memory ring with
+// cp.async.bulk, L2 evict-first), norm weights, the RoPE row, the cached
+// keys and values of earlier positions — is staged before
+// griddepcontrol.wait. After the wait a kernel makes one round trip to L2
+// for its input vector, computes from shared memory, and writes.
 
 #include <algorithm>
-#include <mutex>
+#include <type_traits>
 #include <utility>
 
 #include "common.cuh"
@@ -31,39 +33,61 @@ namespace tb {
 
 namespace {
 
-constexpr int kMvWarps = 8;                     // consumer warps
+constexpr int kMvWarps = 8;                      // consumer warps
 constexpr int kMvThreads = (kMvWarps + 1) * 32;  // + one producer warp
+constexpr size_t kMvStageBytes = 64 * 1024;      // most bytes in one weight copy
 
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Trace slots are fixed per (launch, CTA, event): no atomics on the path.
+__device__ __forceinline__ void trace_at(const Trace& t, uint32_t base, uint32_t tag, uint32_t cta, uint32_t ev) {
+  if (t.rec) {
+    const uint32_t i = base + cta * kTraceEvents + ev;
+    if (i < t.cap) t.rec[i] = TraceRec{tag, cta, ev, sm_id(), global_ns()};
+  }
+}
+
+// Each CTA owns rows [r0, r1). The producer warp copies them in stages of
+// `stage_rows` rows (large bulk copies: a TMA copy's cost is mostly per copy,
+// so a few tens of KB per copy reach far higher per-SM bandwidth than rows
+// one at a time). Every consumer warp walks every stage in order and takes
+// its own chunk of CH rows in it (stage_rows <= kMvWarps * CH), so a warp
+// never waits on a slot's barrier more than one phase ahead of it.
+// With NORM, the input is stored pre-multiplied by the norm weight and the
+// RMS scale is applied to each dot product: scale * (w · (x ∘ g)), the
+// reference's w · (x ∘ (scale * g)) with the scale factored out.
 template <int CH, int EPI, bool NORM>
-__global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int slots) {
+__global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows, int slots) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float red[kMvWarps];
   __shared__ unsigned long long best_sm[kMvWarps];
+  __shared__ float resid[kMaxResidualRows];
   __shared__ int is_last;
 
   pdl_launch_dependents();
+  const int c = blockIdx.x, G = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_START);
 
   const int cols = a.cols;
   float* xs = reinterpret_cast<float*>(smem);
-  unsigned char* ring = smem + align_up(size_t(cols) * 4, 128);
-  const uint32_t slot_bytes = uint32_t(CH) * cols * 2;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(slots) * slot_bytes);
+  float* nw = reinterpret_cast<float*>(smem + align_up(size_t(cols) * 4, 128));
+  unsigned char* ring = smem + align_up(size_t(cols) * 4, 128) * (NORM ? 2 : 1);
+  const uint32_t row_bytes = uint32_t(cols) * 2;
+  const uint32_t stage_bytes = uint32_t(stage_rows) * row_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(slots) * stage_bytes);
   uint64_t* empty = full + slots;
 
-  const int G = gridDim.x, c = blockIdx.x;
   const int units = a.rows / a.row_align;
   const int r0 = int((long long)c * units / G) * a.row_align;
   const int r1 = int((long long)(c + 1) * units / G) * a.row_align;
   const int nrows = r1 - r0;
-  const int nchunks = (nrows + CH - 1) / CH;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nstages = (nrows + stage_rows - 1) / stage_rows;
 
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     for (int s = 0; s < slots; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kMvWarps);
     }
     fence_mbar_init();
   }
@@ -74,97 +98,129 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int slots) {
     // before (and while) the previous kernel finishes.
     if (lane == 0) {
       const uint64_t pol = l2_evict_first();
-      for (int i = 0; i < nchunks; i++) {
+      for (int i = 0; i < nstages; i++) {
         const int s = i % slots;
         if (i >= slots && !mbar_wait(&empty[s], ((i / slots) - 1) & 1, a.err)) break;
-        const int nr = min(CH, nrows - i * CH);
-        const uint32_t bytes = uint32_t(nr) * cols * 2;
+        const int nr = min(stage_rows, nrows - i * stage_rows);
+        const uint32_t bytes = uint32_t(nr) * row_bytes;
         mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(ring + size_t(s) * slot_bytes, a.w + size_t(r0 + i * CH) * cols, bytes, &full[s], pol);
+        bulk_g2s(ring + size_t(s) * stage_bytes, a.w + size_t(r0 + i * stage_rows) * cols, bytes, &full[s], pol);
       }
+      trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_ISSUED);
     }
     return;
   }
 
-  // Consumers. Everything below may read what the previous kernel wrote.
-  pdl_wait();
-  const int tid = threadIdx.x;  // 0 .. 255
+  // Consumers. Norm weights do not depend on the previous kernel either;
+  // each thread stages exactly the elements it multiplies below, so no
+  // barrier is needed between the two.
+  if (NORM)
+    for (int i = tid * 4; i < cols; i += kMvWarps * 32 * 4) {
+      const uint2 g = *reinterpret_cast<const uint2*>(a.norm_w + i);
+      *reinterpret_cast<float4*>(nw + i) = make_float4(bf_lo(g.x), bf_hi(g.x), bf_lo(g.y), bf_hi(g.y));
+    }
+
+  pdl_wait();  // everything below may read what the previous kernel wrote
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_WAITED);
+  if (EPI == kMvResidual && tid < nrows) resid[tid] = __ldcg(a.out + r0 + tid);
   float ss = 0.f;
   for (int i = tid * 4; i < cols; i += kMvWarps * 32 * 4) {
     float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + i));
+    if (NORM) {
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      const float4 g = *reinterpret_cast<const float4*>(nw + i);
+      v.x *= g.x;
+      v.y *= g.y;
+      v.z *= g.z;
+      v.w *= g.w;
+    }
     *reinterpret_cast<float4*>(xs + i) = v;
-    if (NORM) ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   if (NORM) {
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
-    named_sync(1, kMvWarps * 32);
+  }
+  named_sync(1, kMvWarps * 32);
+  float scale = 1.0f;
+  if (NORM) {
     float tot = 0.f;
 #pragma unroll
     for (int w = 0; w < kMvWarps; w++) tot += red[w];
-    const float scale = 1.0f / sqrtf(tot / float(cols) + a.eps);
-    for (int i = tid; i < cols; i += kMvWarps * 32) xs[i] = __fmul_rn(xs[i], __fmul_rn(scale, bf16f(a.norm_w[i])));
+    scale = 1.0f / sqrtf(tot / float(cols) + a.eps);
   }
-  named_sync(1, kMvWarps * 32);
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_INPUT);
 
   unsigned long long best = 0ull;
-  for (int i = warp; i < nchunks; i += kMvWarps) {
-    const int s = i % slots;
-    if (!mbar_wait(&full[s], (i / slots) & 1, a.err)) {
+  for (int st = 0; st < nstages; st++) {
+    const int s = st % slots;
+    if (!mbar_wait(&full[s], (st / slots) & 1, a.err)) {
       // Give an in-flight copy one more bounded wait to land, then skip the
       // rest; every consumer still reaches the barriers below.
-      mbar_wait(&full[s], (i / slots) & 1, nullptr);
+      mbar_wait(&full[s], (st / slots) & 1, nullptr);
       break;
     }
-    const int nr = min(CH, nrows - i * CH);
-    const unsigned char* base = ring + size_t(s) * slot_bytes;
-    float acc[CH];
+    if (tid == 0 && st == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_WEIGHTS);
+    if (tid == 0 && st == nstages - 1) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_LAST_WEIGHTS);
+    const int first = st * stage_rows + warp * CH;  // this warp's first row, relative to r0
+    const int nr = max(0, min(CH, min(nrows, (st + 1) * stage_rows) - first));
+    if (nr > 0) {
+      const unsigned char* base = ring + size_t(s) * stage_bytes + size_t(warp * CH) * row_bytes;
+      float acc[CH];
 #pragma unroll
-    for (int r = 0; r < CH; r++) acc[r] = 0.f;
-    for (int col = lane * 8; col < cols; col += 256) {
-      const float4 xa = *reinterpret_cast<const float4*>(xs + col);
-      const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+      for (int r = 0; r < CH; r++) acc[r] = 0.f;
+      for (int col = lane * 8; col < cols; col += 256) {
+        const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+        const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
 #pragma unroll
-      for (int r = 0; r < CH; r++) {
-        if (r < nr) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(base + (size_t(r) * cols + col) * 2);
-          acc[r] = dot8(wv, xa, xb, acc[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < CH; r++) acc[r] = warp_sum(acc[r]);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-
-    const int rb = r0 + i * CH;
-    if (EPI == kMvSiluPair) {
-      // rows rb + 2p (gate) and rb + 2p + 1 (up) -> out[rb/2 + p]
-#pragma unroll
-      for (int p = 0; p < CH / 2; p++) {
-        if (lane == p && 2 * p < nr) {
-          const float g = acc[2 * p], u = acc[2 * p + 1];
-          a.out[rb / 2 + p] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-        }
-      }
-    } else {
-      float v = acc[0];
-#pragma unroll
-      for (int r = 1; r < CH; r++)
-        if (lane == r) v = acc[r];
-      if (lane < nr) {
-        const int row = rb + lane;
-        if (EPI == kMvResidual) {
-          a.out[row] = __fadd_rn(__ldcg(a.out + row), v);
-        } else {
-          a.out[row] = v;
-          if (EPI == kMvArgmax) {
-            const unsigned long long k = argmax_key(v, uint32_t(row));
-            best = k > best ? k : best;
+        for (int r = 0; r < CH; r++) {
+          if (r < nr) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(base + size_t(r) * row_bytes + size_t(col) * 2);
+            acc[r] = dot8(wv, xa, xb, acc[r]);
           }
         }
       }
+#pragma unroll
+      for (int r = 0; r < CH; r++) acc[r] = warp_sum(acc[r]) * scale;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+
+      const int rb = r0 + first;
+      if (EPI == kMvSiluPair) {
+        // rows rb + 2p (gate) and rb + 2p + 1 (up) -> out[rb/2 + p]
+#pragma unroll
+        for (int p = 0; p < CH / 2; p++) {
+          if (lane == p && 2 * p < nr) {
+            const float g = acc[2 * p], u = acc[2 * p + 1];
+            a.out[rb / 2 + p] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+          }
+        }
+      } else {
+        float v = acc[0];
+#pragma unroll
+        for (int r = 1; r < CH; r++)
+          if (lane == r) v = acc[r];
+        if (lane < nr) {
+          const int row = rb + lane;
+          if (EPI == kMvResidual) {
+            a.out[row] = __fadd_rn(resid[row - r0], v);
+          } else {
+            a.out[row] = v;
+            if (EPI == kMvArgmax) {
+              const unsigned long long k = argmax_key(v, uint32_t(row));
+              best = k > best ? k : best;
+            }
+          }
+        }
+      }
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
+  }
+
+  if (a.trace.rec) {
+    named_sync(1, kMvWarps * 32);
+    if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_DONE);
   }
 
   if (EPI == kMvArgmax) {
@@ -191,9 +247,9 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int slots) {
       if (lane == 0) {
         const int tok = int(argmax_index(b));
         *a.token = tok;
-        const int st = *a.step;
-        if (st >= 0 && st < a.tokens_cap) a.tokens_out[st] = tok;
-        *a.step = st + 1;
+        const int stp = *a.step;
+        if (stp >= 0 && stp < a.tokens_cap) a.tokens_out[stp] = tok;
+        *a.step = stp + 1;
         *a.pos = *a.pos + 1;
         *a.ticket = 0u;
       }
@@ -201,7 +257,7 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int slots) {
   }
 }
 
-using MvFn = void (*)(MvArgs, int);
+using MvFn = void (*)(MvArgs, int, int);
 
 template <int CH>
 MvFn pick_epi(int epi, bool norm) {
@@ -227,59 +283,98 @@ MvFn pick_mv(int ch, int epi, bool norm) {
 
 // ---- attention -------------------------------------------------------------
 
-constexpr int kHd = 128;       // head_dim of the fused path (Qwen3)
-constexpr int kAttnMinChunk = 64;
+constexpr int kHd = 128;  // head_dim of the fused path (Qwen3)
 
-template <int GRP>
+// One CTA per (kv head, split of kAttnChunk positions). The key/value cache
+// holds bf16 (F32KV false) or f32 (F32KV true) values, laid out
+// [kv head][position][head_dim] per layer, so a split's earlier positions
+// are one contiguous run, staged by bulk copy before the dependency wait.
+template <int GRP, bool F32KV>
 __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
+  using KV = typename std::conditional<F32KV, float, uint16_t>::type;
+  extern __shared__ __align__(128) unsigned char smem[];
+  KV* ks = reinterpret_cast<KV*>(smem);   // [kAttnChunk][kHd]
+  KV* vs = ks + size_t(kAttnChunk) * kHd;  // [kAttnChunk][kHd]
   __shared__ __align__(16) float qs[GRP][kHd];
   __shared__ __align__(16) float kn[kHd];
   __shared__ __align__(16) float vn[kHd];
+  __shared__ __align__(16) float qnw[kHd], knw[kHd], rope_row[kHd];
   __shared__ float wm[4][GRP], wl[4][GRP];
   __shared__ __align__(16) float wacc[4][GRP][kHd];
+  __shared__ __align__(8) uint64_t kv_bar;
   __shared__ int is_last;
 
   pdl_launch_dependents();
   const int g = blockIdx.x, split = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // The position is written only at the end of the previous step.
+  const uint32_t cta = blockIdx.x + blockIdx.y * gridDim.x;
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_START);
+
+  // The position is written only at the end of the previous step, so it
+  // and everything derived from it can be read before the wait.
   const int pos = *a.pos;
+  const bool pos_ok = pos >= 0 && pos < a.max_len;
+  const int ctx = pos + 1;
+  const int nsplit = (ctx + kAttnChunk - 1) / kAttnChunk;
+  const int p0 = split * kAttnChunk, p1 = min(ctx, p0 + kAttnChunk);
+  const bool active = pos_ok && split < nsplit && nsplit <= a.max_split;
+  const int cached = active ? max(0, min(p1, pos) - p0) : 0;  // positions already in the cache
+
+  if (active) {
+    if (tid == 0) {
+      mbar_init(&kv_bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0 && cached > 0) {
+      const uint32_t bytes = uint32_t(cached) * kHd * sizeof(KV);
+      const size_t at = (size_t(g) * a.max_len + p0) * kHd;
+      const uint64_t pol = l2_evict_first();
+      mbar_arrive_expect_tx(&kv_bar, 2 * bytes);
+      bulk_g2s(ks, static_cast<const KV*>(a.k_cache) + at, bytes, &kv_bar, pol);
+      bulk_g2s(vs, static_cast<const KV*>(a.v_cache) + at, bytes, &kv_bar, pol);
+    }
+    qnw[tid] = a.q_norm ? bf16f(a.q_norm[tid]) : 1.0f;
+    knw[tid] = a.k_norm ? bf16f(a.k_norm[tid]) : 1.0f;
+    rope_row[tid] = a.rope[size_t(pos) * kHd + tid];
+  }
+
   pdl_wait();
-  if (pos < 0 || pos >= a.max_len) {
+  __syncthreads();  // the staged norm weights are read by other threads below
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_WAITED);
+  if (!pos_ok || nsplit > a.max_split) {
     if (g == 0 && split == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
     return;
   }
-  const int ctx = pos + 1;
-  const int nact = min(a.max_split, (ctx + kAttnMinChunk - 1) / kAttnMinChunk);
-  const int chunk = (ctx + nact - 1) / nact;
-  const int p0 = split * chunk, p1 = min(ctx, p0 + chunk);
-  if (split >= nact || p0 >= p1) return;
+  if (!active) return;
 
   // QK-norm (rmsnorm over each head, model.rs:111-116) on this group's query
   // heads and on the key head; lane l holds elements 4l .. 4l+3.
   const float* qraw = a.qkv + size_t(g) * GRP * kHd;
   const float* kraw = a.qkv + size_t(a.n_heads) * kHd + size_t(g) * kHd;
   const float* vraw = kraw + size_t(a.n_kv_heads) * kHd;
+  vn[tid] = __ldcg(vraw + tid);
   for (int h = warp; h < GRP + 1; h += 4) {
     const float* src = h < GRP ? qraw + h * kHd : kraw;
     float4 v = __ldcg(reinterpret_cast<const float4*>(src) + lane);
-    const uint16_t* nw = h < GRP ? a.q_norm : a.k_norm;
-    if (nw) {
-      float s = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+    const bool has_norm = h < GRP ? a.q_norm != nullptr : a.k_norm != nullptr;
+    if (has_norm) {
+      const float* w = h < GRP ? qnw : knw;
+      const float s = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
       const float scale = 1.0f / sqrtf(s / float(kHd) + a.eps);
-      v.x = __fmul_rn(v.x, __fmul_rn(scale, bf16f(nw[4 * lane + 0])));
-      v.y = __fmul_rn(v.y, __fmul_rn(scale, bf16f(nw[4 * lane + 1])));
-      v.z = __fmul_rn(v.z, __fmul_rn(scale, bf16f(nw[4 * lane + 2])));
-      v.w = __fmul_rn(v.w, __fmul_rn(scale, bf16f(nw[4 * lane + 3])));
+      v.x = __fmul_rn(v.x, __fmul_rn(scale, w[4 * lane + 0]));
+      v.y = __fmul_rn(v.y, __fmul_rn(scale, w[4 * lane + 1]));
+      v.z = __fmul_rn(v.z, __fmul_rn(scale, w[4 * lane + 2]));
+      v.w = __fmul_rn(v.w, __fmul_rn(scale, w[4 * lane + 3]));
     }
     float* dst = h < GRP ? qs[h] : kn;
     *reinterpret_cast<float4*>(dst + 4 * lane) = v;
   }
-  vn[tid] = __ldcg(vraw + tid);
   __syncthreads();
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_INPUT);
   // RoPE (cpu.rs:96-111) at `pos`: element i pairs with i + 64.
   if (tid < kHd / 2) {
-    const float c = a.rope[size_t(pos) * kHd + 2 * tid], s = a.rope[size_t(pos) * kHd + 2 * tid + 1];
+    const float c = rope_row[2 * tid], s = rope_row[2 * tid + 1];
 #pragma unroll
     for (int h = 0; h < GRP + 1; h++) {
       float* x = h < GRP ? qs[h] : kn;
@@ -289,18 +384,31 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
     }
   }
   __syncthreads();
-  // The cache holds bf16; this step uses the rounded key and value too, as
-  // every later step will.
+  // A bf16 cache holds the rounded key and value; this step uses the rounded
+  // values too, as every later step will.
   {
-    const uint16_t kb = f2bf(kn[tid]), vb = f2bf(vn[tid]);
-    kn[tid] = bf16f(kb);
-    vn[tid] = bf16f(vb);
-    if (p1 == ctx) {
-      a.k_cache[(size_t(g) * a.max_len + pos) * kHd + tid] = kb;
-      a.v_cache[(size_t(g) * a.max_len + pos) * kHd + tid] = vb;
+    const size_t at = (size_t(g) * a.max_len + pos) * kHd + tid;
+    if (F32KV) {
+      if (p1 == ctx) {
+        static_cast<float*>(a.k_cache)[at] = kn[tid];
+        static_cast<float*>(a.v_cache)[at] = vn[tid];
+      }
+    } else {
+      const uint16_t kb = f2bf(kn[tid]), vb = f2bf(vn[tid]);
+      kn[tid] = bf16f(kb);
+      vn[tid] = bf16f(vb);
+      if (p1 == ctx) {
+        static_cast<uint16_t*>(a.k_cache)[at] = kb;
+        static_cast<uint16_t*>(a.v_cache)[at] = vb;
+      }
     }
   }
   __syncthreads();
+  if (cached > 0 && !mbar_wait(&kv_bar, 0, a.err)) {
+    mbar_wait(&kv_bar, 0, nullptr);  // one more bounded wait for the copy in flight
+    return;
+  }
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_WEIGHTS);
 
   const float scale = 1.0f / sqrtf(float(kHd));
   float q[GRP][4], acc[GRP][4], m[GRP], l[GRP];
@@ -312,8 +420,6 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
     m[h] = -INFINITY;
     l[h] = 0.f;
   }
-  const uint16_t* kbase = a.k_cache + size_t(g) * a.max_len * kHd + 4 * lane;
-  const uint16_t* vbase = a.v_cache + size_t(g) * a.max_len * kHd + 4 * lane;
   for (int t = p0 + warp; t < p1; t += 4) {
     float k4[4], v4[4];
     if (t == pos) {
@@ -321,9 +427,18 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
       const float4 vv = *reinterpret_cast<const float4*>(&vn[4 * lane]);
       k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
       v4[0] = vv.x; v4[1] = vv.y; v4[2] = vv.z; v4[3] = vv.w;
+    } else if (F32KV) {
+      const float* kr = reinterpret_cast<const float*>(ks) + (t - p0) * kHd + 4 * lane;
+      const float* vr = reinterpret_cast<const float*>(vs) + (t - p0) * kHd + 4 * lane;
+      const float4 kk = *reinterpret_cast<const float4*>(kr);
+      const float4 vv = *reinterpret_cast<const float4*>(vr);
+      k4[0] = kk.x; k4[1] = kk.y; k4[2] = kk.z; k4[3] = kk.w;
+      v4[0] = vv.x; v4[1] = vv.y; v4[2] = vv.z; v4[3] = vv.w;
     } else {
-      const uint2 kw = __ldcg(reinterpret_cast<const uint2*>(kbase + size_t(t) * kHd));
-      const uint2 vw = __ldcg(reinterpret_cast<const uint2*>(vbase + size_t(t) * kHd));
+      const uint16_t* kr = reinterpret_cast<const uint16_t*>(ks) + (t - p0) * kHd + 4 * lane;
+      const uint16_t* vr = reinterpret_cast<const uint16_t*>(vs) + (t - p0) * kHd + 4 * lane;
+      const uint2 kw = *reinterpret_cast<const uint2*>(kr);
+      const uint2 vw = *reinterpret_cast<const uint2*>(vr);
       k4[0] = bf_lo(kw.x); k4[1] = bf_hi(kw.x); k4[2] = bf_lo(kw.y); k4[3] = bf_hi(kw.y);
       v4[0] = bf_lo(vw.x); v4[1] = bf_hi(vw.x); v4[2] = bf_lo(vw.y); v4[3] = bf_hi(vw.y);
     }
@@ -366,7 +481,7 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
       L += wl[w][h] * wt;
       o += wacc[w][h][tid] * wt;
     }
-    if (nact == 1) {
+    if (nsplit == 1) {
       a.out[size_t(g * GRP + h) * kHd + tid] = o / L;
     } else {
       float* pp = a.part + ((size_t(g) * a.max_split + split) * GRP + h) * stride;
@@ -377,21 +492,22 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
       }
     }
   }
-  if (nact == 1) return;
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_DONE);
+  if (nsplit == 1) return;
 
   // Split-context combine: the last CTA of this kv head merges the splits.
   __threadfence();
   __syncthreads();
-  if (tid == 0) is_last = (atomicAdd(a.ticket + g, 1u) == unsigned(nact - 1));
+  if (tid == 0) is_last = (atomicAdd(a.ticket + g, 1u) == unsigned(nsplit - 1));
   __syncthreads();
   if (!is_last) return;
   __threadfence();
   for (int h = 0; h < GRP; h++) {
     float M = -INFINITY;
-    for (int sp = 0; sp < nact; sp++)
+    for (int sp = 0; sp < nsplit; sp++)
       M = fmaxf(M, __ldcg(a.part + ((size_t(g) * a.max_split + sp) * GRP + h) * stride));
     float L = 0.f, o = 0.f;
-    for (int sp = 0; sp < nact; sp++) {
+    for (int sp = 0; sp < nsplit; sp++) {
       const float* pp = a.part + ((size_t(g) * a.max_split + sp) * GRP + h) * stride;
       const float mm = __ldcg(pp);
       const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
@@ -438,54 +554,103 @@ void launch_ex(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl, voi
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+template <int G, bool F>
+cudaError_t setup_attn() {
+  cudaError_t e = cudaFuncSetAttribute(attn_decode<G, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(attn_smem_bytes(F)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode<G, F>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  return e;
+}
+
 }  // namespace
 
-MvPlan plan_mv(int rows, int cols, int row_align, int sms, size_t smem_budget) {
+size_t attn_smem_bytes(bool kv_f32) { return size_t(2) * kAttnChunk * kHd * (kv_f32 ? 4 : 2); }
+
+MvPlan plan_mv(int rows, int cols, int row_align, bool norm, int sms, size_t smem_budget) {
   MvPlan p;
   p.grid = sms;
   const int units = rows / row_align;
   const int rpc = (units + p.grid - 1) / p.grid * row_align;  // most rows any CTA gets
-  int ch = rpc >= 16 ? 4 : (rpc >= 8 ? 2 : 1);
+  const size_t row = size_t(cols) * 2;
+  // A stage is one chunk of CH rows per consumer warp, at most kMvStageBytes
+  // (fewer rows, some warps idle, when rows are wide).
+  int ch = int(std::min<size_t>(4, std::max<size_t>(1, kMvStageBytes / (kMvWarps * row))));
+  if (rpc < kMvWarps * ch) ch = std::max(1, (rpc + kMvWarps - 1) / kMvWarps);
+  if (ch == 3) ch = 4;
   if (row_align == 2 && ch < 2) ch = 2;
   p.chunk_rows = ch;
-  const size_t slot = size_t(ch) * cols * 2;
-  const size_t xs = align_up(size_t(cols) * 4, 128);
-  const int nchunks = (rpc + ch - 1) / ch;
-  long long fit = (long long)((smem_budget - xs - 64) / (slot + 16));
-  int slots = int(std::min<long long>(nchunks, fit));
-  if (slots < 2) slots = 2;
+  int sr = std::min<int>(kMvWarps * ch, int(std::max<size_t>(size_t(ch), kMvStageBytes / row / ch * ch)));
+  if (row_align == 2 && sr % 2) sr -= 1;
+  p.stage_rows = sr;
+  const size_t stage = size_t(sr) * row;
+  const size_t xs = align_up(size_t(cols) * 4, 128) * (norm ? 2 : 1);
+  const int nstages = (rpc + sr - 1) / sr;
+  long long fit = (long long)((smem_budget - xs - 64) / (stage + 16));
+  int slots = int(std::min<long long>(nstages, fit));
+  if (slots < 2) slots = std::min(2, nstages);
+  if (slots < 1) slots = 1;
   p.slots = slots;
-  p.smem = xs + size_t(slots) * slot + size_t(slots) * 16;
+  p.smem = xs + size_t(slots) * stage + size_t(slots) * 16;
+  p.max_rows = rpc;
   return p;
 }
 
-void init_fused_kernels() {
-  // Every instantiation may use up to 227 KB of dynamic shared memory; set
-  // once, outside any stream capture.
-  static std::once_flag once;
-  std::call_once(once, [] {
-    for (int ch : {1, 2, 4})
-      for (int epi = kMvStore; epi <= kMvArgmax; epi++)
-        for (bool norm : {false, true})
-          if (MvFn fn = pick_mv(ch, epi, norm))
-            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  });
+cudaError_t init_fused_kernels(int max_smem_optin) {
+  // Every matrix-vector instantiation may use all the shared memory a block
+  // can opt into, less its static shared memory; and every fused kernel asks
+  // for the whole unified L1 as shared memory, so that a kernel and the next
+  // one (staging its weights) fit on an SM together. Set once per device,
+  // outside any stream capture.
+  for (int ch : {1, 2, 4})
+    for (int epi = kMvStore; epi <= kMvArgmax; epi++)
+      for (bool norm : {false, true})
+        if (MvFn fn = pick_mv(ch, epi, norm)) {
+          cudaFuncAttributes fa;
+          cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+          if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     max_smem_optin - int(fa.sharedSizeBytes));
+          if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
+          if (e != cudaSuccess) return e;
+        }
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {setup_attn<1, false>(), setup_attn<2, false>(), setup_attn<4, false>(),
+                        setup_attn<8, false>(), setup_attn<1, true>(), setup_attn<2, true>(),
+                        setup_attn<4, true>(), setup_attn<8, true>()})
+    if (r != cudaSuccess) e = r;
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_embed_token, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  return e;
 }
 
 void launch_mv(cudaStream_t s, const MvPlan& plan, int epilogue, const MvArgs& a, bool pdl) {
   MvFn fn = pick_mv(plan.chunk_rows, epilogue, a.norm_w != nullptr);
-  launch_ex(s, dim3(plan.grid), dim3(kMvThreads), plan.smem, pdl, fn, a, plan.slots);
+  launch_ex(s, dim3(plan.grid), dim3(kMvThreads), plan.smem, pdl, fn, a, plan.stage_rows, plan.slots);
 }
 
 void launch_attn_decode(cudaStream_t s, const AttnArgs& a, bool pdl) {
   const int group = a.n_heads / a.n_kv_heads;
-  dim3 grid(a.n_kv_heads, a.max_split);
+  const dim3 grid(a.n_kv_heads, a.max_split);
+  const size_t smem = attn_smem_bytes(a.kv_f32 != 0);
+#define TB_ATTN_CASE(G)                                                   \
+  case G:                                                                 \
+    if (a.kv_f32)                                                         \
+      launch_ex(s, grid, dim3(128), smem, pdl, attn_decode<G, true>, a);  \
+    else                                                                  \
+      launch_ex(s, grid, dim3(128), smem, pdl, attn_decode<G, false>, a); \
+    break;
   switch (group) {
-    case 1: launch_ex(s, grid, dim3(128), 0, pdl, attn_decode<1>, a); break;
-    case 2: launch_ex(s, grid, dim3(128), 0, pdl, attn_decode<2>, a); break;
-    case 4: launch_ex(s, grid, dim3(128), 0, pdl, attn_decode<4>, a); break;
-    case 8: launch_ex(s, grid, dim3(128), 0, pdl, attn_decode<8>, a); break;
+    TB_ATTN_CASE(1)
+    TB_ATTN_CASE(2)
+    TB_ATTN_CASE(4)
+    TB_ATTN_CASE(8)
   }
+#undef TB_ATTN_CASE
 }
 
 void launch_set_io(cudaStream_t s, int* io, int token, int pos) { k_set_io<<<1, 1, 0, s>>>(io, token, pos); }

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace tb {
 
 // ---- Device-trait ops (model/cpu.rs:34-155 semantics) ----------------------
@@ -50,16 +52,23 @@ struct MvArgs {
   int* tokens_out;              // [tokens_cap] generated tokens
   int tokens_cap;
   int* err;
+  Trace trace;
+  uint32_t trace_base;  // first record slot of this launch
+  uint32_t tag;
 };
 
+// Rows a CTA of a residual-epilogue launch may own (staged in shared memory).
+constexpr int kMaxResidualRows = 64;
+
 struct MvPlan {
-  int grid, chunk_rows, slots;
+  int grid, chunk_rows, stage_rows, slots;
   size_t smem;
+  int max_rows;  // most rows any CTA owns
 };
-MvPlan plan_mv(int rows, int cols, int row_align, int sms, size_t smem_budget);
-// Raises the shared-memory limit of every matrix-vector kernel; call once per
-// device before capturing or launching them.
-void init_fused_kernels();
+MvPlan plan_mv(int rows, int cols, int row_align, bool norm, int sms, size_t smem_budget);
+// Raises the shared-memory limit of every matrix-vector kernel to what a
+// block can opt into; call once per device before capturing or launching them.
+cudaError_t init_fused_kernels(int max_smem_optin);
 void launch_mv(cudaStream_t s, const MvPlan& plan, int epilogue, const MvArgs& a, bool pdl);
 
 struct AttnArgs {
@@ -68,8 +77,9 @@ struct AttnArgs {
   const uint16_t* k_norm;   // [head_dim] bf16 or null
   float eps;
   const float* rope;        // [max_len][head_dim] (cos, sin) pairs
-  uint16_t* k_cache;        // [Hkv][max_len][head_dim] bf16
-  uint16_t* v_cache;
+  void* k_cache;            // [Hkv][max_len][head_dim], bf16 or f32
+  void* v_cache;
+  int kv_f32;               // cache element: 0 bf16, 1 f32
   int max_len, n_heads, n_kv_heads;
   const int* pos;           // position of the token (device)
   float* out;               // [n_heads][head_dim]
@@ -77,7 +87,14 @@ struct AttnArgs {
   unsigned* ticket;         // [Hkv], zero between launches
   int max_split;
   int* err;
+  Trace trace;
+  uint32_t trace_base;
+  uint32_t tag;
 };
+// Context positions per attention CTA; a state's max_len / kAttnChunk
+// (rounded up) splits cover every position.
+constexpr int kAttnChunk = 64;
+size_t attn_smem_bytes(bool kv_f32);
 void launch_attn_decode(cudaStream_t s, const AttnArgs& a, bool pdl);
 
 // io[0] = token, io[1] = pos, io[2] = 0 (the step's input and counters).

@@ -8,6 +8,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -45,6 +46,8 @@ struct FusedLayer {
 
 struct tb200_model {
   tb200_device* dev = nullptr;
+  int live_states = 0;          // states built on this model
+  bool free_requested = false;  // tb200_model_free came while states lived
   tb200_config c{};
   std::map<std::string, const tb200_weight*> bound;
   bool finalized = false;
@@ -55,9 +58,11 @@ struct tb200_model {
 
 struct tb200_state {
   tb200_model* m = nullptr;
+  tb200_device* dev = nullptr;
   size_t max_len = 0;
+  int kv_f32 = 0;          // cache element: 0 bf16, 1 f32
   size_t host_pos = 0;     // the position the next step runs at, as the host knows it
-  uint16_t* kv = nullptr;  // [L][2][Hkv][max_len][head_dim] bf16
+  unsigned char* kv = nullptr;  // [L][2][Hkv][max_len][head_dim], bf16 or f32
   float* rope = nullptr;   // [max_len][head_dim]
   float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
   float* part = nullptr;
@@ -69,6 +74,8 @@ struct tb200_state {
   int* io_host = nullptr;     // pinned: [max_len][2] staged (token, pos) + [4] readback
   int max_split = 1;
   tb::MvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_lm{};
+  tb::Trace trace{};       // device trace buffer while tracing
+  uint32_t trace_next = 0;  // next free record slot while capturing
   cudaGraphExec_t graph = nullptr;
 };
 
@@ -142,7 +149,8 @@ int tb200_device_open(int ordinal, tb200_device** out) {
   if (prop.major != 10 || prop.minor != 0)
     return fail(TB200_ERR_CUDA, std::string("titania_b200 is built for sm_100a (B200); device is ") + prop.name +
                                     " sm_" + std::to_string(prop.major) + std::to_string(prop.minor));
-  tb::init_fused_kernels();
+  if (cudaError_t e = tb::init_fused_kernels(int(prop.sharedMemPerBlockOptin)); e != cudaSuccess)
+    return fail(TB200_ERR_CUDA, std::string("kernel setup: ") + cudaGetErrorString(e));
   auto* d = new tb200_device;
   d->ordinal = ordinal;
   d->sms = prop.multiProcessorCount;
@@ -505,15 +513,24 @@ int tb200_model_finalize(tb200_model* m) {
   return TB200_OK;
 }
 
-int tb200_model_free(tb200_model* m) {
-  if (!m) return TB200_OK;
-  if (int rc = use(m->dev)) return rc;
+static void delete_model(tb200_model* m) {
+  cudaSetDevice(m->dev->ordinal);
   cudaStreamSynchronize(m->dev->stream);
   for (auto& L : m->layers) {
     cudaFree(L.wqkv);
     cudaFree(L.wgu);
   }
   delete m;
+}
+
+int tb200_model_free(tb200_model* m) {
+  if (!m) return TB200_OK;
+  // States keep their model alive; the last one to go deletes it.
+  if (m->live_states > 0) {
+    m->free_requested = true;
+    return TB200_OK;
+  }
+  delete_model(m);
   return TB200_OK;
 }
 
@@ -533,8 +550,16 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
   const int H = int(c.hidden_size), F = int(c.intermediate_size);
   const size_t kv_layer = 2 * c.num_key_value_heads * st->max_len * c.head_dim;
   int* err = st->io + 3;
+  const uint32_t tag = (uint32_t(op) << 16) | uint32_t(l);
   tb::MvArgs a{};
   a.err = err;
+  a.trace = st->trace;
+  a.tag = tag;
+  auto slots_for = [&](uint32_t ctas) {
+    const uint32_t base = st->trace_next;
+    st->trace_next += ctas * tb::kTraceEvents;
+    return base;
+  };
   a.eps = c.rms_norm_eps;
   a.row_align = 1;
   switch (op) {
@@ -549,6 +574,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.x = st->x;
       a.norm_w = L.attn_norm;
       a.out = st->qkv;
+      a.trace_base = slots_for(st->p_qkv.grid);
       tb::launch_mv(s, st->p_qkv, tb::kMvStore, a, pdl);
       return;
     }
@@ -560,8 +586,10 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       t.k_norm = L.k_norm;
       t.eps = c.rms_norm_eps;
       t.rope = st->rope;
-      t.k_cache = st->kv + l * kv_layer;
-      t.v_cache = t.k_cache + kv_layer / 2;
+      const size_t eb = st->kv_f32 ? 4 : 2;
+      t.k_cache = st->kv + l * kv_layer * eb;
+      t.v_cache = st->kv + l * kv_layer * eb + kv_layer / 2 * eb;
+      t.kv_f32 = st->kv_f32;
       t.max_len = int(st->max_len);
       t.n_heads = int(c.num_attention_heads);
       t.n_kv_heads = int(c.num_key_value_heads);
@@ -571,6 +599,9 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       t.ticket = st->attn_ticket;
       t.max_split = st->max_split;
       t.err = err;
+      t.trace = st->trace;
+      t.tag = tag;
+      t.trace_base = slots_for(uint32_t(c.num_key_value_heads * st->max_split));
       tb::launch_attn_decode(s, t, pdl);
       return;
     }
@@ -580,6 +611,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.cols = int(m->q_dim);
       a.x = st->att;
       a.out = st->x;
+      a.trace_base = slots_for(st->p_o.grid);
       tb::launch_mv(s, st->p_o, tb::kMvResidual, a, pdl);
       return;
     }
@@ -591,6 +623,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.x = st->x;
       a.norm_w = m->layers[l].mlp_norm;
       a.out = st->h;
+      a.trace_base = slots_for(st->p_gu.grid);
       tb::launch_mv(s, st->p_gu, tb::kMvSiluPair, a, pdl);
       return;
     }
@@ -600,6 +633,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.cols = F;
       a.x = st->h;
       a.out = st->x;
+      a.trace_base = slots_for(st->p_down.grid);
       tb::launch_mv(s, st->p_down, tb::kMvResidual, a, pdl);
       return;
     }
@@ -617,6 +651,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.step = st->io + 2;
       a.tokens_out = st->tokens_out;
       a.tokens_cap = int(st->max_len);
+      a.trace_base = slots_for(st->p_lm.grid);
       tb::launch_mv(s, st->p_lm, tb::kMvArgmax, a, pdl);
       return;
     }
@@ -624,15 +659,25 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
 }
 
 int enqueue_step(tb200_state* st) {
-  enqueue_op(st, TB200_OP_EMBED, 0, true);
+  st->trace_next = 0;
+  // TB200_SERIAL=1 launches the step's kernels without programmatic
+  // dependent launch (each waits for the previous to finish): a diagnostic
+  // for ordering questions, slower but otherwise identical.
+  static const bool pdl = !(getenv("TB200_SERIAL") && getenv("TB200_SERIAL")[0] == '1');
+  enqueue_op(st, TB200_OP_EMBED, 0, pdl);
   for (size_t l = 0; l < st->m->c.num_hidden_layers; l++)
-    for (int op = TB200_OP_QKV; op <= TB200_OP_DOWN; op++) enqueue_op(st, op, l, true);
-  enqueue_op(st, TB200_OP_LM_HEAD, 0, true);
+    for (int op = TB200_OP_QKV; op <= TB200_OP_DOWN; op++) enqueue_op(st, op, l, pdl);
+  enqueue_op(st, TB200_OP_LM_HEAD, 0, pdl);
   return launched("decode step");
 }
 
 int build_graph(tb200_state* st) {
   cudaStream_t s = st->m->dev->stream;
+  if (st->graph) {
+    CUDA_TRY(cudaStreamSynchronize(s));
+    cudaGraphExecDestroy(st->graph);
+    st->graph = nullptr;
+  }
   CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   int rc = enqueue_step(st);
   cudaGraph_t g = nullptr;
@@ -661,28 +706,32 @@ int finish(tb200_state* st) {
 
 }  // namespace
 
-int tb200_state_new(tb200_model* m, size_t max_len, tb200_state** out) {
+int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** out) {
   ARG_CHECK(m && out, "null argument");
   ARG_CHECK(m->finalized, "model not finalized");
+  ARG_CHECK(!m->free_requested, "model already freed");
+  ARG_CHECK(kv_dtype == TB200_KV_BF16 || kv_dtype == TB200_KV_F32, "unknown key/value cache type");
   ARG_CHECK(max_len > 0 && max_len < (size_t(1) << 30), "state: bad max_len");
   if (int rc = use(m->dev)) return rc;
   const tb200_config& c = m->c;
   auto* st = new tb200_state;
   st->m = m;
+  st->dev = m->dev;
   st->max_len = max_len;
+  st->kv_f32 = kv_dtype == TB200_KV_F32;
+  m->live_states++;
   const int sms = m->dev->sms;
   const size_t Hkv = c.num_key_value_heads, D = c.head_dim, L = c.num_hidden_layers;
   const size_t group = c.num_attention_heads / Hkv;
-  // Splits over the context so that the attention grid fills the GPU at long
-  // contexts; each split covers at least 64 positions.
-  st->max_split = int(std::max<size_t>(1, std::min<size_t>((max_len + 63) / 64, size_t(2 * sms) / Hkv)));
+  // Attention splits of kAttnChunk positions cover the whole cache.
+  st->max_split = int((max_len + tb::kAttnChunk - 1) / tb::kAttnChunk);
   std::vector<float> table = rope_table(max_len, D, c.rope_theta);
   cudaError_t e = cudaSuccess;
   auto A = [&](void** p, size_t bytes) {
     if (e == cudaSuccess) e = cudaMalloc(p, bytes);
     if (e == cudaSuccess) e = cudaMemsetAsync(*p, 0, bytes, m->dev->stream);
   };
-  A((void**)&st->kv, L * 2 * Hkv * max_len * D * 2);
+  A((void**)&st->kv, L * 2 * Hkv * max_len * D * (st->kv_f32 ? 4 : 2));
   A((void**)&st->rope, table.size() * 4);
   A((void**)&st->x, c.hidden_size * 4);
   A((void**)&st->qkv, (m->q_dim + 2 * m->kv_dim) * 4);
@@ -704,11 +753,15 @@ int tb200_state_new(tb200_model* m, size_t max_len, tb200_state** out) {
     return fail(TB200_ERR_CUDA, std::string("state: ") + cudaGetErrorString(e));
   }
   const int H = int(c.hidden_size), F = int(c.intermediate_size);
-  st->p_qkv = tb::plan_mv(int(m->q_dim + 2 * m->kv_dim), H, 1, sms, kMvBudget);
-  st->p_o = tb::plan_mv(H, int(m->q_dim), 1, sms, kMvBudget);
-  st->p_gu = tb::plan_mv(2 * F, H, 2, sms, kMvBudget);
-  st->p_down = tb::plan_mv(H, F, 1, sms, kMvBudget);
-  st->p_lm = tb::plan_mv(int(c.vocab_size), H, 1, sms, kLmBudget);
+  st->p_qkv = tb::plan_mv(int(m->q_dim + 2 * m->kv_dim), H, 1, true, sms, kMvBudget);
+  st->p_o = tb::plan_mv(H, int(m->q_dim), 1, false, sms, kMvBudget);
+  st->p_gu = tb::plan_mv(2 * F, H, 2, true, sms, kMvBudget);
+  st->p_down = tb::plan_mv(H, F, 1, false, sms, kMvBudget);
+  st->p_lm = tb::plan_mv(int(c.vocab_size), H, 1, true, sms, kLmBudget);
+  if (st->p_o.max_rows > tb::kMaxResidualRows || st->p_down.max_rows > tb::kMaxResidualRows) {
+    tb200_state_free(st);
+    return fail(TB200_ERR_ARG, "hidden size too large for the residual kernels on this GPU");
+  }
   if (int rc = build_graph(st)) {
     tb200_state_free(st);
     return rc;
@@ -719,14 +772,16 @@ int tb200_state_new(tb200_model* m, size_t max_len, tb200_state** out) {
 
 int tb200_state_free(tb200_state* st) {
   if (!st) return TB200_OK;
-  cudaSetDevice(st->m->dev->ordinal);
-  cudaStreamSynchronize(st->m->dev->stream);
+  cudaSetDevice(st->dev->ordinal);
+  cudaStreamSynchronize(st->dev->stream);
   if (st->graph) cudaGraphExecDestroy(st->graph);
   void* ptrs[] = {st->kv, st->rope, st->x, st->qkv, st->att, st->h, st->logits, st->part, st->attn_ticket,
                   st->mv_partial, st->mv_ticket, st->io, st->tokens_out};
   for (void* p : ptrs) cudaFree(p);
   if (st->io_host) cudaFreeHost(st->io_host);
+  tb200_model* m = st->m;
   delete st;
+  if (--m->live_states == 0 && m->free_requested) delete_model(m);
   return TB200_OK;
 }
 
@@ -798,6 +853,76 @@ int tb200_enqueue_op(tb200_model* m, tb200_state* st, int op, size_t layer) {
   return launched("enqueue_op");
 }
 
+int tb200_trace_start(tb200_state* st, size_t capacity) {
+  ARG_CHECK(st && capacity > 0 && capacity < (size_t(1) << 31), "bad trace capacity");
+  ARG_CHECK(!st->trace.rec, "already tracing");
+  if (int rc = use(st->dev)) return rc;
+  CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
+  CUDA_TRY(cudaMalloc(&st->trace.rec, capacity * sizeof(tb::TraceRec)));
+  CUDA_TRY(cudaMemset(st->trace.rec, 0, capacity * sizeof(tb::TraceRec)));
+  st->trace.cap = unsigned(capacity);
+  return build_graph(st);
+}
+
+int tb200_trace_stop(tb200_state* st, tb200_trace_record* out, size_t cap, size_t* n) {
+  ARG_CHECK(st && n && (out || cap == 0), "null argument");
+  ARG_CHECK(st->trace.rec, "not tracing");
+  static_assert(sizeof(tb200_trace_record) == sizeof(tb::TraceRec), "trace record layout");
+  if (int rc = use(st->dev)) return rc;
+  CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
+  *n = st->trace_next;
+  const size_t k = std::min<size_t>(st->trace.cap, cap);
+  if (k) CUDA_TRY(cudaMemcpy(out, st->trace.rec, k * sizeof(tb::TraceRec), cudaMemcpyDeviceToHost));
+  cudaFree(st->trace.rec);
+  st->trace = tb::Trace{};
+  return build_graph(st);
+}
+
+static int state_buffer(tb200_state* st, int which, float** p, size_t* len) {
+  const tb200_config& c = st->m->c;
+  switch (which) {
+    case TB200_BUF_X: *p = st->x; *len = c.hidden_size; return TB200_OK;
+    case TB200_BUF_QKV: *p = st->qkv; *len = st->m->q_dim + 2 * st->m->kv_dim; return TB200_OK;
+    case TB200_BUF_ATT: *p = st->att; *len = st->m->q_dim; return TB200_OK;
+    case TB200_BUF_H: *p = st->h; *len = c.intermediate_size; return TB200_OK;
+    case TB200_BUF_LOGITS: *p = st->logits; *len = c.vocab_size; return TB200_OK;
+  }
+  return fail(TB200_ERR_ARG, "unknown state buffer");
+}
+
+int tb200_state_read(tb200_state* st, int which, float* out, size_t n) {
+  ARG_CHECK(st && out, "null argument");
+  if (int rc = use(st->dev)) return rc;
+  float* p;
+  size_t len;
+  if (int rc = state_buffer(st, which, &p, &len)) return rc;
+  ARG_CHECK(n == len, "state buffer holds " + std::to_string(len) + " values, not " + std::to_string(n));
+  CUDA_TRY(cudaMemcpyAsync(out, p, n * 4, cudaMemcpyDeviceToHost, st->dev->stream));
+  CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
+  return TB200_OK;
+}
+
+int tb200_state_write(tb200_state* st, int which, const float* data, size_t n) {
+  ARG_CHECK(st && data, "null argument");
+  if (int rc = use(st->dev)) return rc;
+  float* p;
+  size_t len;
+  if (int rc = state_buffer(st, which, &p, &len)) return rc;
+  ARG_CHECK(n == len, "state buffer holds " + std::to_string(len) + " values, not " + std::to_string(n));
+  CUDA_TRY(cudaMemcpyAsync(p, data, n * 4, cudaMemcpyHostToDevice, st->dev->stream));
+  CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
+  return TB200_OK;
+}
+
+int tb200_state_set_position(tb200_state* st, uint32_t token, size_t pos) {
+  ARG_CHECK(st, "null state");
+  ARG_CHECK(pos < st->max_len && token < st->m->c.vocab_size, "token or position out of range");
+  if (int rc = use(st->dev)) return rc;
+  tb::launch_set_io(st->dev->stream, st->io, int(token), int(pos));
+  st->host_pos = pos;
+  return launched("set_position");
+}
+
 int tb200_state_read_kv(tb200_state* st, size_t layer, int which, size_t pos, float* out) {
   ARG_CHECK(st && out, "null argument");
   const tb200_config& c = st->m->c;
@@ -806,14 +931,23 @@ int tb200_state_read_kv(tb200_state* st, size_t layer, int which, size_t pos, fl
   cudaStream_t s = st->m->dev->stream;
   const size_t Hkv = c.num_key_value_heads, D = c.head_dim;
   const size_t kv_layer = 2 * Hkv * st->max_len * D;
-  std::vector<uint16_t> tmp(Hkv * D);
+  const size_t eb = st->kv_f32 ? 4 : 2;
+  std::vector<unsigned char> tmp(Hkv * D * eb);
   for (size_t g = 0; g < Hkv; g++) {
-    const uint16_t* src = st->kv + layer * kv_layer + size_t(which) * (kv_layer / 2) + (g * st->max_len + pos) * D;
-    CUDA_TRY(cudaMemcpyAsync(tmp.data() + g * D, src, D * 2, cudaMemcpyDeviceToHost, s));
+    const unsigned char* src =
+        st->kv + (layer * kv_layer + size_t(which) * (kv_layer / 2) + (g * st->max_len + pos) * D) * eb;
+    CUDA_TRY(cudaMemcpyAsync(tmp.data() + g * D * eb, src, D * eb, cudaMemcpyDeviceToHost, s));
   }
   CUDA_TRY(cudaStreamSynchronize(s));
   for (size_t i = 0; i < Hkv * D; i++) {
-    uint32_t u = uint32_t(tmp[i]) << 16;
+    uint32_t u;
+    if (st->kv_f32) {
+      std::memcpy(&u, tmp.data() + 4 * i, 4);
+    } else {
+      uint16_t b;
+      std::memcpy(&b, tmp.data() + 2 * i, 2);
+      u = uint32_t(b) << 16;
+    }
     std::memcpy(out + i, &u, 4);
   }
   return TB200_OK;

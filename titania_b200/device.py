@@ -10,6 +10,7 @@ contract raises `DeviceError` where the reference panics.
 from __future__ import annotations
 
 import ctypes
+import sys
 
 import numpy as np
 
@@ -39,9 +40,9 @@ class Weight:
         self._h, self.shape, self._dev = handle, list(shape), dev
 
     def __del__(self):
-        if self._h and self._dev is not None and self._dev._h:
+        if self._h and self._dev is not None and self._dev._h and not sys.is_finalizing():
             lib().tb200_free_weight(self._dev._h, self._h)
-            self._h = None
+        self._h = None
 
 
 class Buffer:
@@ -56,9 +57,9 @@ class Buffer:
         return int(lib().tb200_buffer_len(self._h))
 
     def __del__(self):
-        if self._h and self._dev is not None and self._dev._h:
+        if self._h and self._dev is not None and self._dev._h and not sys.is_finalizing():
             lib().tb200_free_buffer(self._dev._h, self._h)
-            self._h = None
+        self._h = None
 
 
 def _f32(a):

@@ -16,6 +16,7 @@ from __future__ import annotations
 import ctypes
 import json
 import os
+import sys
 
 import numpy as np
 
@@ -244,12 +245,12 @@ class Model:
         return cls(c, device, load_weights(device, c, Weights.open(os.path.join(path, "model.safetensors"))))
 
     def __del__(self):
-        if getattr(self, "_h", None) and self.device._h:
+        if getattr(self, "_h", None) and not sys.is_finalizing():
             _lib.lib().tb200_model_free(self._h)
-            self._h = None
+        self._h = None
 
-    def state(self, max_len: int) -> "State":
-        return State(self, max_len)
+    def state(self, max_len: int, kv: str = "f32") -> "State":
+        return State(self, max_len, kv)
 
     def forward(self, state: "State", tokens, pos: int, logits: bool = True, out=None):
         """Model::forward (model/model.rs:83-91): the logits for the token after
@@ -283,20 +284,65 @@ class Model:
         call("tb200_enqueue_op", self._h, state._h, int(op), int(layer))
 
 
-class State:
-    """State (model/model.rs:156-211) of the fused path: bf16 K/V cache."""
+KV_TYPES = {"bf16": 0, "f32": 1}
 
-    def __init__(self, model: Model, max_len: int):
+
+class State:
+    """State (model/model.rs:156-211) of the fused path. The key/value cache
+    holds f32 like the reference (default) or bf16, which halves the bytes
+    attention reads at long contexts at the cost of rounding K and V."""
+
+    def __init__(self, model: Model, max_len: int, kv: str = "f32"):
+        if kv not in KV_TYPES:
+            raise ValueError(f"kv must be one of {sorted(KV_TYPES)}")
         h = ctypes.c_void_p()
-        call("tb200_state_new", model._h, int(max_len), ctypes.byref(h))
+        call("tb200_state_new", model._h, int(max_len), KV_TYPES[kv], ctypes.byref(h))
         self._h = h.value
         self.model = model
         self.max_len = max_len
+        self.kv = kv
 
     def __del__(self):
-        if getattr(self, "_h", None) and self.model.device._h:
+        if getattr(self, "_h", None) and not sys.is_finalizing():
             _lib.lib().tb200_state_free(self._h)
-            self._h = None
+        self._h = None
+
+    TRACE_DTYPE = np.dtype([("tag", "<u4"), ("cta", "<u4"), ("event", "<u4"), ("sm", "<u4"), ("ns", "<u8")])
+
+    def trace_start(self, capacity: int = 1 << 20) -> None:
+        """Starts recording the kernels' device-side trace events."""
+        call("tb200_trace_start", self._h, int(capacity))
+        self._trace_cap = int(capacity)
+
+    def trace_stop(self) -> np.ndarray:
+        """Stops tracing; returns the records (tag = op << 16 | layer, cta,
+        event, sm, ns) as a numpy structured array."""
+        out = np.zeros(self._trace_cap, dtype=self.TRACE_DTYPE)
+        n = ctypes.c_size_t()
+        call("tb200_trace_stop", self._h, out.ctypes.data_as(ctypes.c_void_p), out.size, ctypes.byref(n))
+        out = out[:min(n.value, out.size)]
+        return out[out["ns"] != 0]
+
+    BUFFERS = {"x": 0, "qkv": 1, "att": 2, "h": 3, "logits": 4}
+
+    def _buf_len(self, name):
+        c = self.model.config
+        d = c.head_dim()
+        return {"x": c.hidden_size, "qkv": (c.num_attention_heads + 2 * c.num_key_value_heads) * d,
+                "att": c.num_attention_heads * d, "h": c.intermediate_size, "logits": c.vocab_size}[name]
+
+    def read(self, name: str) -> np.ndarray:
+        """A copy of one of the fused path's activation buffers."""
+        out = np.empty(self._buf_len(name), dtype=np.float32)
+        call("tb200_state_read", self._h, self.BUFFERS[name], out.ctypes.data_as(_lib.F32P), out.size)
+        return out
+
+    def write(self, name: str, data) -> None:
+        a = np.ascontiguousarray(data, dtype=np.float32)
+        call("tb200_state_write", self._h, self.BUFFERS[name], a.ctypes.data_as(_lib.F32P), a.size)
+
+    def set_position(self, token: int, pos: int) -> None:
+        call("tb200_state_set_position", self._h, int(token), int(pos))
 
     def read_kv(self, layer: int, which: int, pos: int) -> np.ndarray:
         c = self.model.config
