@@ -122,6 +122,24 @@ TB200_API int tb200_free_weight(tb200_device* dev, tb200_weight* w);
  * lowest index. */
 TB200_API int tb200_argmax(tb200_device* dev, const tb200_buffer* logits, uint32_t* out);
 
+/* Greedy argmax like tb200_argmax, for callers that cannot allocate device
+ * memory: no counterpart in the reference. A caller whose GPU memory belongs
+ * to another allocator (say, a framework's caching allocator holding the
+ * device's memory), or that keeps cudaMalloc/cudaFree out of its per-token
+ * loop because they can synchronize the device, passes logits and an output
+ * word it already owns: `logits` is `n` f32 values in device memory, `out` a
+ * device uint32 that receives the index of the largest value (IEEE total
+ * order, ties to the lowest index). Runs on `stream` (a cudaStream_t; NULL
+ * is the default stream) and returns without waiting. It takes no device
+ * handle and allocates nothing: its scratch is a static array in the
+ * library (about 16 KB per GPU, held until the process exits), which limits
+ * `n` to 8,388,608; larger inputs return TB200_ERR_ARG. The first call on a
+ * GPU looks the array up on that GPU (set-up, once per device); make that
+ * first call before any stream capture. Calls share the array, so calls
+ * whose work overlaps on the GPU (other streams, other threads) race and
+ * must be ordered by the caller. */
+TB200_API int tb200_argmax_noalloc(const float* logits, size_t n, uint32_t* out, void* stream);
+
 /* ---- Fused model path --------------------------------------------------- */
 
 /* The config.json fields the model reads (model/config.rs:10-35); head_dim

@@ -72,6 +72,7 @@ SIGNATURES = {
     "tb200_free_buffer": (ctypes.c_int, [P, P]),
     "tb200_free_weight": (ctypes.c_int, [P, P]),
     "tb200_argmax": (ctypes.c_int, [P, P, U32P]),
+    "tb200_argmax_noalloc": (ctypes.c_int, [P, SZ, P, P]),
     "tb200_model_create": (ctypes.c_int, [P, ctypes.POINTER(Config), PP]),
     "tb200_model_bind": (ctypes.c_int, [P, ctypes.c_char_p, P]),
     "tb200_model_finalize": (ctypes.c_int, [P]),

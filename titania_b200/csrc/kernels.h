@@ -6,9 +6,14 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "common.cuh"
 
 namespace tb {
+
+// Records `msg` for tb200_last_error on this thread and returns `code`.
+int record_error(int code, const std::string& msg);
 
 // ---- Device-trait ops (model/cpu.rs:34-155 semantics) ----------------------
 void launch_copy(cudaStream_t s, float* dst, const float* src, size_t n);

@@ -134,6 +134,8 @@ std::vector<float> rope_table(size_t max_len, size_t head_dim, float theta) {
 
 }  // namespace
 
+int tb::record_error(int code, const std::string& msg) { return fail(code, msg); }
+
 extern "C" {
 
 const char* tb200_last_error(void) { return g_err.c_str(); }
