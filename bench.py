@@ -321,6 +321,24 @@ def run_reference(args):
     }
 
 
+def profile_op(args):
+    """A small case for ncu: loads the model and launches one fused kernel
+    `--launches` times (layers cycling), nothing else on the GPU besides set-up."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    from titania_b200.model import OP_ATTENTION, OP_DOWN, OP_GATE_UP, OP_LM_HEAD, OP_O, OP_QKV
+    ops = {"qkv": OP_QKV, "attention": OP_ATTENTION, "o": OP_O, "gate_up": OP_GATE_UP, "down": OP_DOWN,
+           "lm_head": OP_LM_HEAD}
+    dev = tb.B200(0)
+    m = tb.Model.load(synth.cached_model("qwen3-0.6b", seed=0), dev)
+    st = m.state(PROMPT + GEN + 1)
+    for i in range(args.launches):
+        st.set_position(1, PROMPT + (i % GEN))
+        m.enqueue_op(st, ops[args.profile_op], i % 28)
+    dev.sync()
+    print(json.dumps({"profile_op": args.profile_op, "launches": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -330,7 +348,13 @@ def main():
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timing")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--profile-op", choices=["qkv", "attention", "o", "gate_up", "down", "lm_head"],
+                    help="small case for ncu: launch one fused kernel only")
+    ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args()
+    if args.profile_op:
+        profile_op(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
