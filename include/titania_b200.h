@@ -198,7 +198,11 @@ TB200_API int tb200_generate(tb200_model* model, tb200_state* state, uint32_t to
  * callers that time the device or overlap it with host work. */
 TB200_API int tb200_decode_enqueue(tb200_model* model, tb200_state* state, uint32_t token, size_t pos, size_t steps);
 
-/* The fused kernels of one decode step, for tb200_enqueue_op. */
+/* The fused kernels of one decode step, for tb200_enqueue_op. A step runs
+ * EMBED, then per layer QKV, ATTENTION_O, GATE_UP_SUM, DOWN while the
+ * position is below 64, or QKV, ATTENTION, O, GATE_UP, DOWN beyond it, then
+ * LM_HEAD. GATE_UP(_SUM) also stores its input residual (x, or x plus the
+ * partials) to the X2 buffer, which DOWN adds back. */
 enum {
   TB200_OP_EMBED = 0,     /* x = embed[token]                               */
   TB200_OP_QKV = 1,       /* q|k|v = W_qkv . rmsnorm(x)                     */
@@ -207,6 +211,8 @@ enum {
   TB200_OP_GATE_UP = 4,   /* h = silu(W_g . rmsnorm(x)) * (W_u . rmsnorm(x)) */
   TB200_OP_DOWN = 5,      /* x += W_d . h                                   */
   TB200_OP_LM_HEAD = 6,   /* logits = W_lm . rmsnorm(x); greedy token; pos++ */
+  TB200_OP_ATTENTION_O = 7, /* short contexts: attention and o_proj per kv group -> partials */
+  TB200_OP_GATE_UP_SUM = 8, /* like GATE_UP on x + the summed o_proj partials */
 };
 
 /* Enqueues one fused kernel of the decode step (of layer `layer` for ops
@@ -250,6 +256,8 @@ enum {
   TB200_BUF_ATT = 2,    /* attention output, heads * head_dim */
   TB200_BUF_H = 3,      /* silu(gate) * up, intermediate_size */
   TB200_BUF_LOGITS = 4, /* vocab_size */
+  TB200_BUF_X2 = 5,     /* residual stream after attention, hidden_size */
+  TB200_BUF_PART = 6,   /* o_proj partials, kv_heads * hidden_size */
 };
 
 /* Copies a state buffer to the host (`n` must be its length); waits for the

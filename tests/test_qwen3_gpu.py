@@ -84,6 +84,31 @@ def test_tiny_op_path_against_golden(b200, tiny_model_dir, golden_tiny):
     close(logits, g["final_logits"], 1e-4, 1e-4)
 
 
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_tiny_crosses_from_short_to_long_context_graph(b200, tiny_model_dir, kv):
+    """Positions below 64 run the fused attention + o_proj graph, later ones
+    the split-attention graph: a 60-token prompt and 10 greedy steps cross
+    over, and prefill (graph by graph) and the on-device loop agree with the
+    oracle throughout."""
+    prompt = synth.prompt_tokens(60, 1024, seed=9)
+    ref = orc.Model(tiny_model_dir)
+    ref_tokens, ref_logits = orc.greedy_generate(ref, prompt, 10, max_len=80)
+    m = tb.Model.load(tiny_model_dir, b200)
+    st = m.state(80, kv=kv)
+    logits = m.forward(st, prompt, 0)
+    pos = len(prompt)
+    tol = (1e-3, 1e-3) if kv == "f32" else (REL, ABS)
+    for i in range(10):
+        close(logits, ref_logits[i], *tol)
+        t = int(np.argmax(logits))
+        assert t == ref_tokens[i]
+        logits = m.forward(st, [t], pos)
+        pos += 1
+    st2 = m.state(80, kv=kv)
+    first = m.forward(st2, prompt, 0, logits=False)
+    assert [first] + m.generate(st2, first, 60, 9) == ref_tokens
+
+
 def test_state_bounds(b200, tiny_model_dir):
     m = tb.Model.load(tiny_model_dir, b200)
     st = m.state(8)

@@ -36,6 +36,10 @@ namespace {
 constexpr int kMvWarps = 8;                      // consumer warps
 constexpr int kMvThreads = (kMvWarps + 1) * 32;  // + one producer warp
 constexpr size_t kMvStageBytes = 64 * 1024;      // most bytes in one weight copy
+constexpr int kMvKsplitRows = 8;                 // rows per stage of a K-split kernel
+
+// Shared-memory position of input element i (i a multiple of 4).
+__device__ __forceinline__ int xperm(int i) { return (i & ~255) + ((i >> 2) & 1) * 128 + ((i >> 3) & 31) * 4; }
 
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -56,12 +60,13 @@ __device__ __forceinline__ void trace_at(const Trace& t, uint32_t base, uint32_t
 // With NORM, the input is stored pre-multiplied by the norm weight and the
 // RMS scale is applied to each dot product: scale * (w · (x ∘ g)), the
 // reference's w · (x ∘ (scale * g)) with the scale factored out.
-template <int CH, int EPI, bool NORM>
+template <int CH, int EPI, bool NORM, bool KS>
 __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows, int slots) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ float red[kMvWarps];
   __shared__ unsigned long long best_sm[kMvWarps];
   __shared__ float resid[kMaxResidualRows];
+  __shared__ float ksum[kMvWarps][kMvKsplitRows];
   __shared__ int is_last;
 
   pdl_launch_dependents();
@@ -71,8 +76,8 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
 
   const int cols = a.cols;
   float* xs = reinterpret_cast<float*>(smem);
-  float* nw = reinterpret_cast<float*>(smem + align_up(size_t(cols) * 4, 128));
-  unsigned char* ring = smem + align_up(size_t(cols) * 4, 128) * (NORM ? 2 : 1);
+  float* nw = reinterpret_cast<float*>(smem + (align_up(size_t(cols), 256) * 4));
+  unsigned char* ring = smem + (align_up(size_t(cols), 256) * 4) * (NORM ? 2 : 1);
   const uint32_t row_bytes = uint32_t(cols) * 2;
   const uint32_t stage_bytes = uint32_t(stage_rows) * row_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(slots) * stage_bytes);
@@ -122,10 +127,35 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
 
   pdl_wait();  // everything below may read what the previous kernel wrote
   if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_WAITED);
-  if (EPI == kMvResidual && tid < nrows) resid[tid] = __ldcg(a.out + r0 + tid);
+  // The residual rows, the input and the partials are all requested before
+  // any is used, so staging costs one round trip to L2.
+  float rres = 0.f;
+  if (EPI == kMvResidual && tid < nrows) rres = __ldcg((a.resid_src ? a.resid_src : a.out) + r0 + tid);
   float ss = 0.f;
   for (int i = tid * 4; i < cols; i += kMvWarps * 32 * 4) {
     float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + i));
+    if (a.npartials > 0) {
+      // x + (p0 + p1 + ...): the o_proj output summed in group order, then
+      // added to the residual as the reference adds the whole product.
+      float4 pv[kMaxPartials];
+#pragma unroll
+      for (int p = 0; p < kMaxPartials; p++)
+        if (p < a.npartials) pv[p] = __ldcg(reinterpret_cast<const float4*>(a.partials + size_t(p) * cols + i));
+      float4 t = pv[0];
+#pragma unroll
+      for (int p = 1; p < kMaxPartials; p++)
+        if (p < a.npartials) {
+          t.x += pv[p].x;
+          t.y += pv[p].y;
+          t.z += pv[p].z;
+          t.w += pv[p].w;
+        }
+      v.x += t.x;
+      v.y += t.y;
+      v.z += t.z;
+      v.w += t.w;
+    }
+    if (a.x_out && c == 0) *reinterpret_cast<float4*>(a.x_out + i) = v;
     if (NORM) {
       ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
       const float4 g = *reinterpret_cast<const float4*>(nw + i);
@@ -134,8 +164,12 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
       v.z *= g.z;
       v.w *= g.w;
     }
-    *reinterpret_cast<float4*>(xs + i) = v;
+    // Permuted layout: the four values at column i = 256k + 8l + 4h go to
+    // 256k + 128h + 4l, so a warp reading a 256-column block (lane l: 8l ..
+    // 8l+7) reads two runs of 512 contiguous bytes, free of bank conflicts.
+    *reinterpret_cast<float4*>(xs + xperm(i)) = v;
   }
+  if (EPI == kMvResidual && tid < nrows) resid[tid] = rres;
   if (NORM) {
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
@@ -161,6 +195,62 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     }
     if (tid == 0 && st == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_WEIGHTS);
     if (tid == 0 && st == nstages - 1) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_LAST_WEIGHTS);
+    if (KS) {
+      // K-split: every warp takes every row of the stage over its share of
+      // the columns (8-column units tid, tid + 256, ...); warp sums meet in
+      // shared memory and warp 0 finishes the rows.
+      const int row0 = st * stage_rows;
+      const int nrs = min(stage_rows, nrows - row0);
+      const unsigned char* base = ring + size_t(s) * stage_bytes;
+      float acc[kMvKsplitRows];
+#pragma unroll
+      for (int r = 0; r < kMvKsplitRows; r++) acc[r] = 0.f;
+      for (int u = tid; u < cols / 8; u += kMvWarps * 32) {
+        const float* xb0 = xs + (u >> 5) * 256 + (u & 31) * 4;
+        const float4 xa = *reinterpret_cast<const float4*>(xb0);
+        const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
+#pragma unroll
+        for (int r = 0; r < kMvKsplitRows; r++)
+          if (r < nrs) acc[r] = dot8(*reinterpret_cast<const uint4*>(base + size_t(r) * row_bytes + size_t(u) * 16), xa, xb, acc[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < kMvKsplitRows; r++)
+        if (r < nrs) {
+          const float v = warp_sum(acc[r]);
+          if (lane == 0) ksum[warp][r] = v;
+        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      named_sync(1, kMvWarps * 32);
+      if (warp == 0) {
+        float v = 0.f;
+        if (lane < nrs) {
+#pragma unroll
+          for (int w = 0; w < kMvWarps; w++) v += ksum[w][lane];
+          v *= scale;
+        }
+        if (EPI == kMvSiluPair) {
+          const float u = __shfl_down_sync(0xffffffffu, v, 1);
+          if ((lane & 1) == 0 && lane < nrs) {
+            const int row = r0 + row0 + lane;
+            a.out[row / 2] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+          }
+        } else if (lane < nrs) {
+          const int row = r0 + row0 + lane;
+          if (EPI == kMvResidual) {
+            a.out[row] = __fadd_rn(resid[row - r0], v);
+          } else {
+            a.out[row] = v;
+            if (EPI == kMvArgmax) {
+              const unsigned long long k = argmax_key(v, uint32_t(row));
+              best = k > best ? k : best;
+            }
+          }
+        }
+      }
+      named_sync(1, kMvWarps * 32);  // ksum is reused by the next stage
+      continue;
+    }
     const int first = st * stage_rows + warp * CH;  // this warp's first row, relative to r0
     const int nr = max(0, min(CH, min(nrows, (st + 1) * stage_rows) - first));
     if (nr > 0) {
@@ -169,8 +259,9 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
 #pragma unroll
       for (int r = 0; r < CH; r++) acc[r] = 0.f;
       for (int col = lane * 8; col < cols; col += 256) {
-        const float4 xa = *reinterpret_cast<const float4*>(xs + col);
-        const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+        const float* xb0 = xs + (col - lane * 8) + lane * 4;
+        const float4 xa = *reinterpret_cast<const float4*>(xb0);
+        const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
 #pragma unroll
         for (int r = 0; r < CH; r++) {
           if (r < nr) {
@@ -259,24 +350,28 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
 
 using MvFn = void (*)(MvArgs, int, int);
 
-template <int CH>
+template <int CH, bool KS>
 MvFn pick_epi(int epi, bool norm) {
   switch (epi) {
-    case kMvStore: return norm ? mv_kernel<CH, kMvStore, true> : mv_kernel<CH, kMvStore, false>;
-    case kMvResidual: return norm ? mv_kernel<CH, kMvResidual, true> : mv_kernel<CH, kMvResidual, false>;
+    case kMvStore: return norm ? mv_kernel<CH, kMvStore, true, KS> : mv_kernel<CH, kMvStore, false, KS>;
+    case kMvResidual: return norm ? mv_kernel<CH, kMvResidual, true, KS> : mv_kernel<CH, kMvResidual, false, KS>;
     case kMvSiluPair:
-      if (CH < 2) return nullptr;
-      return norm ? mv_kernel<(CH < 2 ? 2 : CH), kMvSiluPair, true> : mv_kernel<(CH < 2 ? 2 : CH), kMvSiluPair, false>;
-    case kMvArgmax: return norm ? mv_kernel<CH, kMvArgmax, true> : mv_kernel<CH, kMvArgmax, false>;
+      if (CH < 2 && !KS) return nullptr;
+      return norm ? mv_kernel<CH, kMvSiluPair, true, KS> : mv_kernel<CH, kMvSiluPair, false, KS>;
+    case kMvArgmax: return norm ? mv_kernel<CH, kMvArgmax, true, KS> : mv_kernel<CH, kMvArgmax, false, KS>;
   }
   return nullptr;
 }
 
+// ch == 0: the K-split kernel (stages of up to kMvKsplitRows rows).
 MvFn pick_mv(int ch, int epi, bool norm) {
   switch (ch) {
-    case 1: return pick_epi<1>(epi, norm);
-    case 2: return pick_epi<2>(epi, norm);
-    case 4: return pick_epi<4>(epi, norm);
+    case 0: return pick_epi<1, true>(epi, norm);
+    case 1: return pick_epi<1, false>(epi, norm);
+    case 2: return pick_epi<2, false>(epi, norm);
+    case 4: return pick_epi<4, false>(epi, norm);
+    case 6: return pick_epi<6, false>(epi, norm);
+    case 8: return pick_epi<8, false>(epi, norm);
   }
   return nullptr;
 }
@@ -353,10 +448,20 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
   const float* qraw = a.qkv + size_t(g) * GRP * kHd;
   const float* kraw = a.qkv + size_t(a.n_heads) * kHd + size_t(g) * kHd;
   const float* vraw = kraw + size_t(a.n_kv_heads) * kHd;
-  vn[tid] = __ldcg(vraw + tid);
-  for (int h = warp; h < GRP + 1; h += 4) {
-    const float* src = h < GRP ? qraw + h * kHd : kraw;
-    float4 v = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+  // All loads in flight before any is used (GRP + 1 heads over 4 warps).
+  const float vval = __ldcg(vraw + tid);
+  float4 qkv4[(GRP + 4) / 4];
+#pragma unroll
+  for (int j = 0; j < (GRP + 4) / 4; j++) {
+    const int h = warp + 4 * j;
+    if (h < GRP + 1) qkv4[j] = __ldcg(reinterpret_cast<const float4*>(h < GRP ? qraw + h * kHd : kraw) + lane);
+  }
+  vn[tid] = vval;
+#pragma unroll
+  for (int j = 0; j < (GRP + 4) / 4; j++) {
+    const int h = warp + 4 * j;
+    if (h >= GRP + 1) break;
+    float4 v = qkv4[j];
     const bool has_norm = h < GRP ? a.q_norm != nullptr : a.k_norm != nullptr;
     if (has_norm) {
       const float* w = h < GRP ? qnw : knw;
@@ -519,6 +624,237 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
   if (tid == 0) a.ticket[g] = 0u;
 }
 
+// Fused attention + o_proj for short contexts. CTA (g, sl) stages, before
+// the dependency wait, its packed o_proj slice (rows of output slice sl,
+// columns of kv group g's query heads) and the group's cached keys and
+// values; after the wait it QK-norms and rotates the group's query heads and
+// key, appends the key and value (CTA sl == 0 writes the cache), and runs
+// the group's attention in three passes (scores, softmax as the reference:
+// exp(s - max) / sum, weighted values), then multiplies its o_proj slice by
+// the group's attention output into part[g][rows of sl].
+template <int GRP, bool F32KV>
+__global__ void __launch_bounds__(256) attn_o(AttnOArgs a) {
+  using KV = typename std::conditional<F32KV, float, uint16_t>::type;
+  constexpr int kCols = GRP * kHd;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint16_t* wo = reinterpret_cast<uint16_t*>(smem);  // [rows_per_slice][kCols]
+  KV* ks = reinterpret_cast<KV*>(smem + align_up(size_t(a.rows_per_slice) * kCols * 2, 128));
+  KV* vs = ks + size_t(kAttnOMaxCtx) * kHd;
+  __shared__ __align__(16) float qs[GRP][kHd];
+  __shared__ __align__(16) float kn[kHd];
+  __shared__ __align__(16) float vn[kHd];
+  __shared__ __align__(16) float qnw[kHd], knw[kHd], rope_row[kHd];
+  __shared__ float sc[GRP][kAttnOMaxCtx];
+  __shared__ __align__(16) float att[kCols];
+  __shared__ __align__(8) uint64_t bar;
+
+  pdl_launch_dependents();
+  const int g = blockIdx.x, sl = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t cta = blockIdx.x + blockIdx.y * gridDim.x;
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_START);
+
+  const int pos = *a.pos;  // written only at the end of the previous step
+  const bool ok = pos >= 0 && pos < a.max_len && pos < kAttnOMaxCtx;
+  const uint32_t wo_bytes = uint32_t(a.rows_per_slice) * kCols * 2;
+  const uint32_t kv_bytes = ok ? uint32_t(pos) * kHd * sizeof(KV) : 0u;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (ok) {
+    if (tid == 0) {
+      const uint64_t pol = l2_evict_first();
+      mbar_arrive_expect_tx(&bar, wo_bytes + 2 * kv_bytes);
+      bulk_g2s(wo, a.wo_packed + (size_t(g) * a.nslices + sl) * a.rows_per_slice * kCols, wo_bytes, &bar, pol);
+      if (kv_bytes) {
+        const size_t at = size_t(g) * a.max_len * kHd;
+        bulk_g2s(ks, static_cast<const KV*>(a.k_cache) + at, kv_bytes, &bar, pol);
+        bulk_g2s(vs, static_cast<const KV*>(a.v_cache) + at, kv_bytes, &bar, pol);
+      }
+    }
+    if (tid < kHd) {
+      qnw[tid] = a.q_norm ? bf16f(a.q_norm[tid]) : 1.0f;
+      knw[tid] = a.k_norm ? bf16f(a.k_norm[tid]) : 1.0f;
+      rope_row[tid] = a.rope[size_t(pos) * kHd + tid];
+    }
+  }
+
+  pdl_wait();
+  __syncthreads();
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_WAITED);
+  if (!ok) {
+    if (g == 0 && sl == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
+    return;
+  }
+
+  // QK-norm and RoPE, as in attn_decode.
+  const float* qraw = a.qkv + size_t(g) * GRP * kHd;
+  const float* kraw = a.qkv + size_t(a.n_heads) * kHd + size_t(g) * kHd;
+  const float* vraw = kraw + size_t(a.n_kv_heads) * kHd;
+  // Both loads in flight before either is used.
+  const float vval = tid < kHd ? __ldcg(vraw + tid) : 0.f;
+  float4 qkv4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp < GRP + 1) qkv4 = __ldcg(reinterpret_cast<const float4*>(warp < GRP ? qraw + warp * kHd : kraw) + lane);
+  if (tid < kHd) vn[tid] = vval;
+  for (int h = warp; h < GRP + 1; h += 8) {
+    float4 v = qkv4;
+    const bool has_norm = h < GRP ? a.q_norm != nullptr : a.k_norm != nullptr;
+    if (has_norm) {
+      const float* w = h < GRP ? qnw : knw;
+      const float s = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      const float scale = 1.0f / sqrtf(s / float(kHd) + a.eps);
+      v.x = __fmul_rn(v.x, __fmul_rn(scale, w[4 * lane + 0]));
+      v.y = __fmul_rn(v.y, __fmul_rn(scale, w[4 * lane + 1]));
+      v.z = __fmul_rn(v.z, __fmul_rn(scale, w[4 * lane + 2]));
+      v.w = __fmul_rn(v.w, __fmul_rn(scale, w[4 * lane + 3]));
+    }
+    float* dst = h < GRP ? qs[h] : kn;
+    *reinterpret_cast<float4*>(dst + 4 * lane) = v;
+  }
+  __syncthreads();
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_INPUT);
+  if (tid < kHd / 2) {
+    const float c = rope_row[2 * tid], s = rope_row[2 * tid + 1];
+#pragma unroll
+    for (int h = 0; h < GRP + 1; h++) {
+      float* x = h < GRP ? qs[h] : kn;
+      const float u = x[tid], w = x[tid + kHd / 2];
+      x[tid] = __fsub_rn(__fmul_rn(u, c), __fmul_rn(w, s));
+      x[tid + kHd / 2] = __fadd_rn(__fmul_rn(w, c), __fmul_rn(u, s));
+    }
+  }
+  __syncthreads();
+  if (tid < kHd) {
+    const size_t at = (size_t(g) * a.max_len + pos) * kHd + tid;
+    if (F32KV) {
+      if (sl == 0) {
+        static_cast<float*>(a.k_cache)[at] = kn[tid];
+        static_cast<float*>(a.v_cache)[at] = vn[tid];
+      }
+    } else {
+      const uint16_t kb = f2bf(kn[tid]), vb = f2bf(vn[tid]);
+      kn[tid] = bf16f(kb);
+      vn[tid] = bf16f(vb);
+      if (sl == 0) {
+        static_cast<uint16_t*>(a.k_cache)[at] = kb;
+        static_cast<uint16_t*>(a.v_cache)[at] = vb;
+      }
+    }
+  }
+  __syncthreads();
+  if (!mbar_wait(&bar, 0, a.err)) {
+    mbar_wait(&bar, 0, nullptr);  // one more bounded wait for the copies in flight
+    return;
+  }
+  if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_WEIGHTS);
+
+  // Scores: s = scale * (q_h . k_t), one thread per (position, head), each
+  // walking the head dimension from its own starting quad so that threads
+  // on different positions hit different shared-memory banks.
+  const float scale = 1.0f / sqrtf(float(kHd));
+  for (int idx = tid; idx < (pos + 1) * GRP; idx += 256) {
+    const int t = idx / GRP, h = idx % GRP;
+    const float4* qv = reinterpret_cast<const float4*>(qs[h]);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+    for (int j = 0; j < kHd / 4; j++) {
+      const int jj = (j + t) & (kHd / 4 - 1);
+      float4 kk;
+      if (t == pos) {
+        kk = reinterpret_cast<const float4*>(kn)[jj];
+      } else if (F32KV) {
+        kk = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(ks) + t * kHd)[jj];
+      } else {
+        const uint2 kw = reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(ks) + t * kHd)[jj];
+        kk = make_float4(bf_lo(kw.x), bf_hi(kw.x), bf_lo(kw.y), bf_hi(kw.y));
+      }
+      const float4 qq = qv[jj];
+      float& s = acc[j & 3];
+      s = fmaf(qq.x, kk.x, s);
+      s = fmaf(qq.y, kk.y, s);
+      s = fmaf(qq.z, kk.z, s);
+      s = fmaf(qq.w, kk.w, s);
+    }
+    sc[h][t] = scale * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
+  }
+  __syncthreads();
+  // Softmax per head (cpu.rs:183-193): exp(s - max), then divide by the sum.
+  for (int h = warp; h < GRP; h += 8) {
+    const float s0 = lane <= pos ? sc[h][lane] : -INFINITY;
+    const float s1 = lane + 32 <= pos ? sc[h][lane + 32] : -INFINITY;
+    const float mx = warp_max(fmaxf(s0, s1));
+    const float e0 = lane <= pos ? expf(s0 - mx) : 0.f;
+    const float e1 = lane + 32 <= pos ? expf(s1 - mx) : 0.f;
+    const float sum = warp_sum(e0 + e1);
+    if (lane <= pos) sc[h][lane] = e0 / sum;
+    if (lane + 32 <= pos) sc[h][lane + 32] = e1 / sum;
+  }
+  __syncthreads();
+  // Weighted values: att[h][d] = sum_t p[h][t] * v_t[d], four partial sums.
+  for (int o = tid; o < kCols; o += 256) {
+    const int h = o / kHd, d = o % kHd;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int t = 0; t < pos; t++) {
+      const float v = F32KV ? reinterpret_cast<const float*>(vs)[t * kHd + d]
+                            : bf16f(reinterpret_cast<const uint16_t*>(vs)[t * kHd + d]);
+      acc[t & 3] = fmaf(sc[h][t], v, acc[t & 3]);
+    }
+    acc[pos & 3] = fmaf(sc[h][pos], vn[d], acc[pos & 3]);
+    att[o] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  }
+  __syncthreads();
+  // This CTA's share of o_proj: rows sl * R .. + R of part[g].
+  // Eight rows per warp at a time: the attention output is read once per
+  // eight rows and the eight reductions overlap.
+  const int R = a.rows_per_slice;
+  float* outp = a.part + size_t(g) * a.hidden + size_t(sl) * R;
+  for (int base = warp * 8; base < R; base += 64) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
+#pragma unroll
+    for (int col = lane * 8; col < kCols; col += 256) {
+      const float4 xa = *reinterpret_cast<const float4*>(att + col);
+      const float4 xb = *reinterpret_cast<const float4*>(att + col + 4);
+#pragma unroll
+      for (int i = 0; i < 8; i++)
+        if (base + i < R) acc[i] = dot8(*reinterpret_cast<const uint4*>(wo + size_t(base + i) * kCols + col), xa, xb, acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = warp_sum(acc[i]);
+    if (lane < 8 && base + lane < R) {
+      float v = acc[0];
+#pragma unroll
+      for (int i = 1; i < 8; i++)
+        if (lane == i) v = acc[i];
+      outp[base + lane] = v;
+    }
+  }
+  if (a.trace.rec) {
+    __syncthreads();
+    if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, cta, TB200_TRACE_DONE);
+  }
+}
+
+// dst[g][s][r][c] = wo[s * R + r][g * cols + c], cols = group * head_dim.
+__global__ void k_pack_wo(uint16_t* __restrict__ dst, const uint16_t* __restrict__ wo, int hidden, int n_kv_heads,
+                          int cols, int nslices) {
+  const int R = hidden / nslices;
+  const size_t total = size_t(n_kv_heads) * hidden * cols;
+  const size_t q_dim = size_t(n_kv_heads) * cols;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+    const size_t c = i % cols;
+    const size_t rest = i / cols;  // (g * nslices + s) * R + r
+    const size_t r = rest % R;
+    const size_t gs = rest / R;
+    const size_t s = gs % nslices, g = gs / nslices;
+    dst[i] = wo[(s * R + r) * q_dim + g * cols + c];
+  }
+}
+
 __global__ void k_embed_token(float* __restrict__ out, const uint16_t* __restrict__ table, int dim,
                               const int* __restrict__ token, int vocab, int* err) {
   pdl_launch_dependents();
@@ -574,10 +910,36 @@ MvPlan plan_mv(int rows, int cols, int row_align, bool norm, int sms, size_t sme
   const int units = rows / row_align;
   const int rpc = (units + p.grid - 1) / p.grid * row_align;  // most rows any CTA gets
   const size_t row = size_t(cols) * 2;
-  // A stage is one chunk of CH rows per consumer warp, at most kMvStageBytes
-  // (fewer rows, some warps idle, when rows are wide).
+  const size_t xs = (align_up(size_t(cols), 256) * 4) * (norm ? 2 : 1);
+  p.max_rows = rpc;
+  // Few rows per CTA (o_proj, down): K-split, one stage, all warps per row.
+  if (rpc <= kMvKsplitRows && xs + size_t(kMvKsplitRows) * row + 64 <= smem_budget) {
+    p.chunk_rows = 0;
+    p.stage_rows = kMvKsplitRows;
+    p.slots = 1;
+    p.smem = xs + size_t(kMvKsplitRows) * row + 16;
+    return p;
+  }
+  // A CTA whose whole slice fits stages it in one copy: each warp takes up
+  // to 8 rows, and the kernel's shared memory stays small enough for the
+  // next kernel to stage its own weights on the same SM meanwhile.
+  for (int ch : {1, 2, 4, 6, 8}) {
+    if (row_align == 2 && ch % 2) continue;
+    if (kMvWarps * ch < rpc) continue;
+    const size_t stage = size_t(kMvWarps) * ch * row;
+    if (xs + stage + 64 <= smem_budget) {
+      p.chunk_rows = ch;
+      p.stage_rows = kMvWarps * ch;
+      p.slots = 1;
+      p.smem = xs + stage + 16;
+      return p;
+    }
+    break;
+  }
+  // Otherwise stream the slice through a ring: a stage is one chunk of CH
+  // rows per consumer warp, at most kMvStageBytes (fewer rows, some warps
+  // idle, when rows are wide).
   int ch = int(std::min<size_t>(4, std::max<size_t>(1, kMvStageBytes / (kMvWarps * row))));
-  if (rpc < kMvWarps * ch) ch = std::max(1, (rpc + kMvWarps - 1) / kMvWarps);
   if (ch == 3) ch = 4;
   if (row_align == 2 && ch < 2) ch = 2;
   p.chunk_rows = ch;
@@ -585,7 +947,6 @@ MvPlan plan_mv(int rows, int cols, int row_align, bool norm, int sms, size_t sme
   if (row_align == 2 && sr % 2) sr -= 1;
   p.stage_rows = sr;
   const size_t stage = size_t(sr) * row;
-  const size_t xs = align_up(size_t(cols) * 4, 128) * (norm ? 2 : 1);
   const int nstages = (rpc + sr - 1) / sr;
   long long fit = (long long)((smem_budget - xs - 64) / (stage + 16));
   int slots = int(std::min<long long>(nstages, fit));
@@ -593,7 +954,6 @@ MvPlan plan_mv(int rows, int cols, int row_align, bool norm, int sms, size_t sme
   if (slots < 1) slots = 1;
   p.slots = slots;
   p.smem = xs + size_t(slots) * stage + size_t(slots) * 16;
-  p.max_rows = rpc;
   return p;
 }
 
@@ -603,7 +963,7 @@ cudaError_t init_fused_kernels(int max_smem_optin) {
   // for the whole unified L1 as shared memory, so that a kernel and the next
   // one (staging its weights) fit on an SM together. Set once per device,
   // outside any stream capture.
-  for (int ch : {1, 2, 4})
+  for (int ch : {0, 1, 2, 4, 6, 8})
     for (int epi = kMvStore; epi <= kMvArgmax; epi++)
       for (bool norm : {false, true})
         if (MvFn fn = pick_mv(ch, epi, norm)) {
@@ -622,6 +982,18 @@ cudaError_t init_fused_kernels(int max_smem_optin) {
                         setup_attn<8, false>(), setup_attn<1, true>(), setup_attn<2, true>(),
                         setup_attn<4, true>(), setup_attn<8, true>()})
     if (r != cudaSuccess) e = r;
+  for (void* fn : {(void*)attn_o<1, false>, (void*)attn_o<2, false>, (void*)attn_o<4, false>,
+                   (void*)attn_o<8, false>, (void*)attn_o<1, true>, (void*)attn_o<2, true>, (void*)attn_o<4, true>,
+                   (void*)attn_o<8, true>}) {
+    cudaFuncAttributes fa;
+    cudaError_t r = cudaFuncGetAttributes(&fa, fn);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               max_smem_optin - int(fa.sharedSizeBytes));
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (r != cudaSuccess) e = r;
+  }
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_embed_token, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
@@ -651,6 +1023,44 @@ void launch_attn_decode(cudaStream_t s, const AttnArgs& a, bool pdl) {
     TB_ATTN_CASE(8)
   }
 #undef TB_ATTN_CASE
+}
+
+size_t attn_o_smem_bytes(int rows_per_slice, int group, bool kv_f32) {
+  return align_up(size_t(rows_per_slice) * group * kHd * 2, 128) + size_t(2) * kAttnOMaxCtx * kHd * (kv_f32 ? 4 : 2);
+}
+
+int attn_o_slices(int hidden, int group) {
+  const size_t row = size_t(group) * kHd * 2;
+  for (int ns = 1; ns <= hidden; ns++)
+    if (hidden % ns == 0 && size_t(hidden / ns) * row <= 48 * 1024) return ns;
+  return hidden;
+}
+
+void launch_pack_wo(cudaStream_t s, uint16_t* dst, const uint16_t* wo, int hidden, int n_kv_heads, int group,
+                    int nslices) {
+  const size_t total = size_t(n_kv_heads) * hidden * group * kHd;
+  const int grid = int(std::min<size_t>((total + 255) / 256, 148 * 16));
+  k_pack_wo<<<grid, 256, 0, s>>>(dst, wo, hidden, n_kv_heads, group * kHd, nslices);
+}
+
+void launch_attn_o(cudaStream_t s, const AttnOArgs& a, bool pdl) {
+  const int group = a.n_heads / a.n_kv_heads;
+  const dim3 grid(a.n_kv_heads, a.nslices);
+  const size_t smem = attn_o_smem_bytes(a.rows_per_slice, group, a.kv_f32 != 0);
+#define TB_ATTNO_CASE(G)                                                  \
+  case G:                                                                 \
+    if (a.kv_f32)                                                         \
+      launch_ex(s, grid, dim3(256), smem, pdl, attn_o<G, true>, a);       \
+    else                                                                  \
+      launch_ex(s, grid, dim3(256), smem, pdl, attn_o<G, false>, a);      \
+    break;
+  switch (group) {
+    TB_ATTNO_CASE(1)
+    TB_ATTNO_CASE(2)
+    TB_ATTNO_CASE(4)
+    TB_ATTNO_CASE(8)
+  }
+#undef TB_ATTNO_CASE
 }
 
 void launch_set_io(cudaStream_t s, int* io, int token, int pos) { k_set_io<<<1, 1, 0, s>>>(io, token, pos); }

@@ -45,9 +45,13 @@ struct MvArgs {
   int rows, cols;
   int row_align;           // CTA row ranges start at multiples of this
   const float* x;          // [cols] input
+  const float* partials;   // npartials vectors of [cols] added to x first (fixed order), or null
+  int npartials;
+  float* x_out;            // receives x + partials (written by CTA 0), or null
   const uint16_t* norm_w;  // RMSNorm weight applied to x first, or null
   float eps;
   float* out;
+  const float* resid_src;  // kMvResidual: the residual read (null: out itself)
   // kMvArgmax only:
   unsigned long long* partial;  // [grid] per-CTA best key
   unsigned* ticket;             // zero between launches
@@ -64,6 +68,8 @@ struct MvArgs {
 
 // Rows a CTA of a residual-epilogue launch may own (staged in shared memory).
 constexpr int kMaxResidualRows = 64;
+// Most partial vectors a matrix-vector kernel sums into its input.
+constexpr int kMaxPartials = 8;
 
 struct MvPlan {
   int grid, chunk_rows, stage_rows, slots;
@@ -96,6 +102,39 @@ struct AttnArgs {
   uint32_t trace_base;
   uint32_t tag;
 };
+// Fused attention + o_proj for short contexts (positions < kAttnOMaxCtx):
+// CTA (kv group g, output slice s) computes the group's attention and its
+// share of o_proj, writing part[g][rows of s]; the next kernel sums the
+// per-group partials in order.
+constexpr int kAttnOMaxCtx = 64;
+struct AttnOArgs {
+  const float* qkv;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  float eps;
+  const float* rope;
+  void* k_cache;
+  void* v_cache;
+  int kv_f32;
+  int max_len, n_heads, n_kv_heads;
+  const int* pos;
+  const uint16_t* wo_packed;  // [Hkv][nslices][rows_per_slice][group * head_dim]
+  int hidden, rows_per_slice, nslices;
+  float* part;                // [Hkv][hidden]
+  int* err;
+  Trace trace;
+  uint32_t trace_base;
+  uint32_t tag;
+};
+size_t attn_o_smem_bytes(int rows_per_slice, int group, bool kv_f32);
+void launch_attn_o(cudaStream_t s, const AttnOArgs& a, bool pdl);
+// Output slices per kv group for the fused attention + o_proj: the largest
+// slice of at most 48 KB of packed o_proj weights that divides `hidden`.
+int attn_o_slices(int hidden, int group);
+// Packs o_proj [hidden][n_heads * head_dim] into [Hkv][nslices][rows][group * head_dim].
+void launch_pack_wo(cudaStream_t s, uint16_t* dst, const uint16_t* wo, int hidden, int n_kv_heads, int group,
+                    int nslices);
+
 // Context positions per attention CTA; a state's max_len / kAttnChunk
 // (rounded up) splits cover every position.
 constexpr int kAttnChunk = 64;

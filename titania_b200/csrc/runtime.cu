@@ -42,6 +42,7 @@ struct FusedLayer {
   uint16_t* wqkv = nullptr;  // [q_dim + 2 kv_dim][H], owned
   uint16_t* wgu = nullptr;   // [2F][H] gate/up rows interleaved, owned
   const uint16_t *wo, *wd;
+  uint16_t* wo_packed = nullptr;  // o_proj packed per (kv group, output slice), owned
 };
 
 struct tb200_model {
@@ -54,6 +55,7 @@ struct tb200_model {
   std::vector<FusedLayer> layers;
   const uint16_t *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
   size_t q_dim = 0, kv_dim = 0;
+  int attn_o_slices = 0;  // output slices per kv group of the fused attention + o_proj
 };
 
 struct tb200_state {
@@ -65,6 +67,7 @@ struct tb200_state {
   unsigned char* kv = nullptr;  // [L][2][Hkv][max_len][head_dim], bf16 or f32
   float* rope = nullptr;   // [max_len][head_dim]
   float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+  float *x2 = nullptr, *part_o = nullptr;  // mid-layer residual; per-group o_proj partials
   float* part = nullptr;
   unsigned* attn_ticket = nullptr;
   unsigned long long* mv_partial = nullptr;
@@ -76,7 +79,8 @@ struct tb200_state {
   tb::MvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_lm{};
   tb::Trace trace{};       // device trace buffer while tracing
   uint32_t trace_next = 0;  // next free record slot while capturing
-  cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t graph = nullptr;        // positions >= kAttnOMaxCtx
+  cudaGraphExec_t graph_short = nullptr;  // positions < kAttnOMaxCtx (fused attention + o_proj)
 };
 
 namespace {
@@ -465,6 +469,7 @@ int tb200_model_finalize(tb200_model* m) {
   ARG_CHECK(c.num_attention_heads % c.num_key_value_heads == 0 && (group == 1 || group == 2 || group == 4 || group == 8),
             "the fused path needs 1, 2, 4 or 8 query heads per kv head");
   ARG_CHECK(H % 8 == 0 && F % 8 == 0, "the fused path needs hidden and FFN sizes divisible by 8");
+  ARG_CHECK(H <= 12288 && F <= 12288 && m->q_dim <= 12288, "the fused path supports widths up to 12288");
   cudaStream_t s = m->dev->stream;
   const tb200_weight* w = nullptr;
   if (int rc = get_bound(m, "model.embed_tokens.weight", {V, H}, false, &w)) return rc;
@@ -508,6 +513,10 @@ int tb200_model_finalize(tb200_model* m) {
     CUDA_TRY(cudaMalloc(&L.wgu, 2 * F * H * 2));
     tb::launch_interleave_rows(s, L.wgu, g->ptr, u->ptr, F, H);
     if (int rc2 = launched("interleave")) return rc2;
+    m->attn_o_slices = tb::attn_o_slices(int(H), int(group));
+    CUDA_TRY(cudaMalloc(&L.wo_packed, H * m->q_dim * 2));
+    tb::launch_pack_wo(s, L.wo_packed, o->ptr, int(H), int(c.num_key_value_heads), int(group), m->attn_o_slices);
+    if (int rc2 = launched("pack o_proj")) return rc2;
     m->layers.push_back(L);
   }
   CUDA_TRY(cudaStreamSynchronize(s));
@@ -521,6 +530,7 @@ static void delete_model(tb200_model* m) {
   for (auto& L : m->layers) {
     cudaFree(L.wqkv);
     cudaFree(L.wgu);
+    cudaFree(L.wo_packed);
   }
   delete m;
 }
@@ -538,9 +548,10 @@ int tb200_model_free(tb200_model* m) {
 
 namespace {
 
-// Budget of shared memory per matrix-vector CTA: two kernels fit on one SM
-// (228 KB), so a kernel can stage its weights while the previous one runs.
-constexpr size_t kMvBudget = 100 * 1024;
+// Budget of shared memory per matrix-vector CTA: two consecutive kernels fit
+// on one SM (228 KB), so a kernel can stage its weights while the previous
+// one runs.
+constexpr size_t kMvBudget = 110 * 1024;
 constexpr size_t kLmBudget = 160 * 1024;
 
 // Enqueues one fused kernel of the decode step: op 0 embed, 1 q|k|v,
@@ -607,6 +618,34 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       tb::launch_attn_decode(s, t, pdl);
       return;
     }
+    case TB200_OP_ATTENTION_O: {
+      const FusedLayer& L = m->layers[l];
+      tb::AttnOArgs t{};
+      t.qkv = st->qkv;
+      t.q_norm = L.q_norm;
+      t.k_norm = L.k_norm;
+      t.eps = c.rms_norm_eps;
+      t.rope = st->rope;
+      const size_t eb = st->kv_f32 ? 4 : 2;
+      t.k_cache = st->kv + l * kv_layer * eb;
+      t.v_cache = st->kv + l * kv_layer * eb + kv_layer / 2 * eb;
+      t.kv_f32 = st->kv_f32;
+      t.max_len = int(st->max_len);
+      t.n_heads = int(c.num_attention_heads);
+      t.n_kv_heads = int(c.num_key_value_heads);
+      t.pos = st->io + 1;
+      t.wo_packed = L.wo_packed;
+      t.hidden = H;
+      t.nslices = m->attn_o_slices;
+      t.rows_per_slice = H / m->attn_o_slices;
+      t.part = st->part_o;
+      t.err = err;
+      t.trace = st->trace;
+      t.tag = tag;
+      t.trace_base = slots_for(uint32_t(c.num_key_value_heads * m->attn_o_slices));
+      tb::launch_attn_o(s, t, pdl);
+      return;
+    }
     case TB200_OP_O: {
       a.w = m->layers[l].wo;
       a.rows = H;
@@ -617,12 +656,18 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       tb::launch_mv(s, st->p_o, tb::kMvResidual, a, pdl);
       return;
     }
-    case TB200_OP_GATE_UP: {
+    case TB200_OP_GATE_UP:
+    case TB200_OP_GATE_UP_SUM: {
       a.w = m->layers[l].wgu;
       a.rows = 2 * F;
       a.cols = H;
       a.row_align = 2;
       a.x = st->x;
+      a.x_out = st->x2;
+      if (op == TB200_OP_GATE_UP_SUM) {
+        a.partials = st->part_o;
+        a.npartials = int(c.num_key_value_heads);
+      }
       a.norm_w = m->layers[l].mlp_norm;
       a.out = st->h;
       a.trace_base = slots_for(st->p_gu.grid);
@@ -635,6 +680,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.cols = F;
       a.x = st->h;
       a.out = st->x;
+      a.resid_src = st->x2;
       a.trace_base = slots_for(st->p_down.grid);
       tb::launch_mv(s, st->p_down, tb::kMvResidual, a, pdl);
       return;
@@ -660,28 +706,35 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
   }
 }
 
-int enqueue_step(tb200_state* st) {
+// One decode step. `short_ctx`: the position is below kAttnOMaxCtx, so
+// attention and o_proj run fused, one kernel per layer less.
+int enqueue_step(tb200_state* st, bool short_ctx) {
   st->trace_next = 0;
   // TB200_SERIAL=1 launches the step's kernels without programmatic
   // dependent launch (each waits for the previous to finish): a diagnostic
   // for ordering questions, slower but otherwise identical.
   static const bool pdl = !(getenv("TB200_SERIAL") && getenv("TB200_SERIAL")[0] == '1');
   enqueue_op(st, TB200_OP_EMBED, 0, pdl);
-  for (size_t l = 0; l < st->m->c.num_hidden_layers; l++)
-    for (int op = TB200_OP_QKV; op <= TB200_OP_DOWN; op++) enqueue_op(st, op, l, pdl);
+  for (size_t l = 0; l < st->m->c.num_hidden_layers; l++) {
+    enqueue_op(st, TB200_OP_QKV, l, pdl);
+    if (short_ctx) {
+      enqueue_op(st, TB200_OP_ATTENTION_O, l, pdl);
+      enqueue_op(st, TB200_OP_GATE_UP_SUM, l, pdl);
+    } else {
+      enqueue_op(st, TB200_OP_ATTENTION, l, pdl);
+      enqueue_op(st, TB200_OP_O, l, pdl);
+      enqueue_op(st, TB200_OP_GATE_UP, l, pdl);
+    }
+    enqueue_op(st, TB200_OP_DOWN, l, pdl);
+  }
   enqueue_op(st, TB200_OP_LM_HEAD, 0, pdl);
   return launched("decode step");
 }
 
-int build_graph(tb200_state* st) {
+int capture(tb200_state* st, bool short_ctx, cudaGraphExec_t* out) {
   cudaStream_t s = st->m->dev->stream;
-  if (st->graph) {
-    CUDA_TRY(cudaStreamSynchronize(s));
-    cudaGraphExecDestroy(st->graph);
-    st->graph = nullptr;
-  }
   CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_step(st);
+  int rc = enqueue_step(st, short_ctx);
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (rc) {
@@ -689,10 +742,29 @@ int build_graph(tb200_state* st) {
     return rc;
   }
   if (e != cudaSuccess) return fail(TB200_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
-  e = cudaGraphInstantiate(&st->graph, g, 0);
+  e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return fail(TB200_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
   return TB200_OK;
+}
+
+int build_graph(tb200_state* st) {
+  cudaStream_t s = st->m->dev->stream;
+  CUDA_TRY(cudaStreamSynchronize(s));
+  for (cudaGraphExec_t* g : {&st->graph, &st->graph_short})
+    if (*g) {
+      cudaGraphExecDestroy(*g);
+      *g = nullptr;
+    }
+  if (int rc = capture(st, false, &st->graph)) return rc;
+  if (st->m->c.num_key_value_heads > size_t(tb::kMaxPartials)) return TB200_OK;
+  return capture(st, true, &st->graph_short);
+}
+
+// The graph for a step at `pos`: the fused attention + o_proj one for short
+// contexts when the model has at most kMaxPartials kv groups.
+cudaGraphExec_t step_graph(tb200_state* st, size_t pos) {
+  return pos < size_t(tb::kAttnOMaxCtx) && st->graph_short ? st->graph_short : st->graph;
 }
 
 // Copies back the io block and reports a kernel-side error.
@@ -739,6 +811,8 @@ int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** 
   A((void**)&st->qkv, (m->q_dim + 2 * m->kv_dim) * 4);
   A((void**)&st->att, m->q_dim * 4);
   A((void**)&st->h, c.intermediate_size * 4);
+  A((void**)&st->x2, c.hidden_size * 4);
+  A((void**)&st->part_o, Hkv * c.hidden_size * 4);
   A((void**)&st->logits, c.vocab_size * 4);
   A((void**)&st->part, Hkv * st->max_split * group * (D + 2) * 4);
   A((void**)&st->attn_ticket, Hkv * 4);
@@ -777,8 +851,9 @@ int tb200_state_free(tb200_state* st) {
   cudaSetDevice(st->dev->ordinal);
   cudaStreamSynchronize(st->dev->stream);
   if (st->graph) cudaGraphExecDestroy(st->graph);
+  if (st->graph_short) cudaGraphExecDestroy(st->graph_short);
   void* ptrs[] = {st->kv, st->rope, st->x, st->qkv, st->att, st->h, st->logits, st->part, st->attn_ticket,
-                  st->mv_partial, st->mv_ticket, st->io, st->tokens_out};
+                  st->mv_partial, st->mv_ticket, st->io, st->tokens_out, st->x2, st->part_o};
   for (void* p : ptrs) cudaFree(p);
   if (st->io_host) cudaFreeHost(st->io_host);
   tb200_model* m = st->m;
@@ -803,7 +878,7 @@ int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_
     stage[0] = int(tokens[i]);
     stage[1] = int(pos + i);
     CUDA_TRY(cudaMemcpyAsync(st->io, stage, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-    CUDA_TRY(cudaGraphLaunch(st->graph, s));
+    CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
   }
   if (logits) CUDA_TRY(cudaMemcpyAsync(logits, st->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
@@ -826,7 +901,7 @@ int tb200_generate(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, 
   stage[2] = 0;
   stage[3] = 0;
   CUDA_TRY(cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s));
-  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(st->graph, s));
+  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
   static_assert(sizeof(uint32_t) == sizeof(int), "token width");
   CUDA_TRY(cudaMemcpyAsync(out, st->tokens_out, steps * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
@@ -841,14 +916,14 @@ int tb200_decode_enqueue(tb200_model* m, tb200_state* st, uint32_t token, size_t
   if (int rc = use(m->dev)) return rc;
   tb::launch_set_io(m->dev->stream, st->io, int(token), int(pos));
   if (int rc = launched("set_io")) return rc;
-  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(st->graph, m->dev->stream));
+  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), m->dev->stream));
   st->host_pos = pos + steps;
   return TB200_OK;
 }
 
 int tb200_enqueue_op(tb200_model* m, tb200_state* st, int op, size_t layer) {
   ARG_CHECK(m && st && st->m == m, "bad model/state");
-  ARG_CHECK(op >= TB200_OP_EMBED && op <= TB200_OP_LM_HEAD, "unknown op");
+  ARG_CHECK(op >= TB200_OP_EMBED && op <= TB200_OP_GATE_UP_SUM, "unknown op");
   ARG_CHECK(layer < m->c.num_hidden_layers, "layer out of range");
   if (int rc = use(m->dev)) return rc;
   enqueue_op(st, op, layer, false);
@@ -888,6 +963,8 @@ static int state_buffer(tb200_state* st, int which, float** p, size_t* len) {
     case TB200_BUF_ATT: *p = st->att; *len = st->m->q_dim; return TB200_OK;
     case TB200_BUF_H: *p = st->h; *len = c.intermediate_size; return TB200_OK;
     case TB200_BUF_LOGITS: *p = st->logits; *len = c.vocab_size; return TB200_OK;
+    case TB200_BUF_X2: *p = st->x2; *len = c.hidden_size; return TB200_OK;
+    case TB200_BUF_PART: *p = st->part_o; *len = c.num_key_value_heads * c.hidden_size; return TB200_OK;
   }
   return fail(TB200_ERR_ARG, "unknown state buffer");
 }

@@ -27,7 +27,8 @@ from .device import B200, Tensor
 BATCH = 64  # model/model.rs:8
 
 # The fused kernels of a decode step (include/titania_b200.h TB200_OP_*).
-OP_EMBED, OP_QKV, OP_ATTENTION, OP_O, OP_GATE_UP, OP_DOWN, OP_LM_HEAD = range(7)
+OP_EMBED, OP_QKV, OP_ATTENTION, OP_O, OP_GATE_UP, OP_DOWN, OP_LM_HEAD, OP_ATTENTION_O, OP_GATE_UP_SUM = range(9)
+ATTN_O_MAX_CTX = 64  # positions below this run attention and o_proj fused
 
 
 class Config:
@@ -323,13 +324,14 @@ class State:
         out = out[:min(n.value, out.size)]
         return out[out["ns"] != 0]
 
-    BUFFERS = {"x": 0, "qkv": 1, "att": 2, "h": 3, "logits": 4}
+    BUFFERS = {"x": 0, "qkv": 1, "att": 2, "h": 3, "logits": 4, "x2": 5, "part": 6}
 
     def _buf_len(self, name):
         c = self.model.config
         d = c.head_dim()
         return {"x": c.hidden_size, "qkv": (c.num_attention_heads + 2 * c.num_key_value_heads) * d,
-                "att": c.num_attention_heads * d, "h": c.intermediate_size, "logits": c.vocab_size}[name]
+                "att": c.num_attention_heads * d, "h": c.intermediate_size, "logits": c.vocab_size,
+                "x2": c.hidden_size, "part": c.num_key_value_heads * c.hidden_size}[name]
 
     def read(self, name: str) -> np.ndarray:
         """A copy of one of the fused path's activation buffers."""
