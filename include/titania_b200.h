@@ -186,6 +186,47 @@ TB200_API int tb200_state_free(tb200_state* state);
 TB200_API int tb200_forward(tb200_model* model, tb200_state* state, const uint32_t* tokens, size_t n, size_t pos,
                   float* logits, uint32_t* next_token);
 
+/* ---- many sequences ------------------------------------------------------- */
+
+/* A state of `n_seqs` independent sequences, each with its own key/value
+ * cache of `max_len` positions: what `n_seqs` separate State::new
+ * (model/model.rs:176-211) would hold, in one allocation, so that one decode
+ * step runs every sequence at once. A one-sequence state from tb200_state_new
+ * is the case n_seqs = 1. The single-token entry points (tb200_generate,
+ * tb200_decode_enqueue, tb200_enqueue_op, tracing) take one-sequence states. */
+TB200_API int tb200_batch_state_new(tb200_model* model, size_t n_seqs, size_t max_len, int kv_dtype,
+                                    tb200_state** out);
+TB200_API size_t tb200_state_seqs(const tb200_state* state);
+
+/* Model::forward (model/model.rs:83-91) for sequence `seq` of the state: as
+ * tb200_forward. Prompts (n >= 2, here and in tb200_forward) run all their
+ * tokens at once through the tensor-core path. */
+TB200_API int tb200_forward_seq(tb200_model* model, tb200_state* state, size_t seq, const uint32_t* tokens,
+                                size_t n, size_t pos, float* logits, uint32_t* next_token);
+
+/* One decode step of every sequence: token tokens[i] of sequence i at
+ * positions[i] (n_seqs each). Writes the logits of every sequence to
+ * `logits` ([n_seqs][vocab_size] floats, host; may be NULL) and the greedy
+ * choices to `next_tokens` (n_seqs, host; may be NULL). */
+TB200_API int tb200_forward_batch(tb200_model* model, tb200_state* state, const uint32_t* tokens,
+                                  const size_t* positions, float* logits, uint32_t* next_tokens);
+
+/* Greedy decoding of every sequence on the device: feeds tokens[i] at
+ * positions[i], then each chosen token, `steps` times; writes the chosen
+ * tokens to `out` ([steps][n_seqs], host). */
+TB200_API int tb200_generate_batch(tb200_model* model, tb200_state* state, const uint32_t* tokens,
+                                   const size_t* positions, size_t steps, uint32_t* out);
+
+/* What tb200_generate_batch runs, without its copy back or final wait. */
+TB200_API int tb200_decode_batch_enqueue(tb200_model* model, tb200_state* state, const uint32_t* tokens,
+                                         const size_t* positions, size_t steps);
+
+/* Key (which = 0) or value (1) cache row of sequence `seq` at (layer, pos),
+ * kv_heads * head_dim values as f32. */
+TB200_API int tb200_batch_read_kv(tb200_state* state, size_t seq, size_t layer, int which, size_t pos, float* out);
+
+/* ---- single sequence, single token --------------------------------------- */
+
 /* Greedy decoding entirely on the device (model/chat.rs:149-196 with
  * temperature 0): feeds `token` at `pos`, then each chosen token, `steps`
  * times; writes the `steps` chosen tokens to `out` (host memory). */

@@ -15,7 +15,7 @@ CPU fallback.
 
 from ._lib import DeviceError
 from .device import B200, Buffer, Tensor, Weight
-from .model import BATCH, Config, Model, OpModel, OpState, Sampler, State, Weights
+from .model import BATCH, BatchState, Config, Model, OpModel, OpState, Sampler, State, Weights
 
-__all__ = ["B200", "Buffer", "Tensor", "Weight", "DeviceError", "BATCH", "Config", "Model", "OpModel", "OpState",
+__all__ = ["B200", "Buffer", "Tensor", "Weight", "DeviceError", "BATCH", "BatchState", "Config", "Model", "OpModel", "OpState",
            "Sampler", "State", "Weights"]

@@ -80,6 +80,13 @@ SIGNATURES = {
     "tb200_state_new": (ctypes.c_int, [P, SZ, ctypes.c_int, PP]),
     "tb200_state_free": (ctypes.c_int, [P]),
     "tb200_forward": (ctypes.c_int, [P, P, U32P, SZ, SZ, F32P, U32P]),
+    "tb200_batch_state_new": (ctypes.c_int, [P, SZ, SZ, ctypes.c_int, PP]),
+    "tb200_state_seqs": (SZ, [P]),
+    "tb200_forward_seq": (ctypes.c_int, [P, P, SZ, U32P, SZ, SZ, F32P, U32P]),
+    "tb200_forward_batch": (ctypes.c_int, [P, P, U32P, SZP, F32P, U32P]),
+    "tb200_generate_batch": (ctypes.c_int, [P, P, U32P, SZP, SZ, U32P]),
+    "tb200_decode_batch_enqueue": (ctypes.c_int, [P, P, U32P, SZP, SZ]),
+    "tb200_batch_read_kv": (ctypes.c_int, [P, SZ, SZ, ctypes.c_int, SZ, F32P]),
     "tb200_generate": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P]),
     "tb200_decode_enqueue": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ]),
     "tb200_enqueue_op": (ctypes.c_int, [P, P, ctypes.c_int, SZ]),

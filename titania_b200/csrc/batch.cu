@@ -1,0 +1,598 @@
+// batch.cu — kernels of the many-token forward (model/model.rs:93-149 run
+// over n tokens at once, and over many sequences at once): everything around
+// the tensor-core contractions of gemm.cu.
+//
+//   k_split_rows     x -> three bf16 planes, the operand form of gemm.cu
+//   k_norm_split     RMSNorm of each token row (cpu.rs:85-94), then the split
+//   k_qkv_post       per token: QK-norm of every q and k head, RoPE at the
+//                    token's position (cpu.rs:96-111), k and v appended to the
+//                    token's sequence cache (model.rs:119-120)
+//   k_attn_rows      decode attention, one query token per sequence: a CTA per
+//                    (token, kv group, run of cache positions), combined in
+//                    split order by the last CTA (cpu.rs:113-149)
+//   k_attn_prefill   causal attention for a run of tokens of one sequence,
+//                    tiled: 64 query rows against 64-position key/value tiles
+//                    with an online softmax
+//   k_argmax_rows    greedy choice per row of logits (sampler.rs:21-33 at
+//                    temperature 0, ties to the lowest id), advancing each
+//                    sequence's position for the device-side token loop
+//
+// The key/value cache of a batch is [sequence][layer][k|v][kv head][position]
+// [head_dim]; a sequence's block is the single-sequence layout, so the
+// single-token fused path reads the same cache.
+
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tb {
+
+namespace {
+
+constexpr int kD = 128;  // head_dim of the batched path (Qwen3)
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl, void (*kernel)(KArgs...),
+                Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---- operand split and RMSNorm -------------------------------------------------
+
+__global__ void k_split_rows(const float* __restrict__ x, uint16_t* __restrict__ out, size_t plane, size_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    store_split3(out, plane, i, x[i]);
+}
+
+// One CTA per output row r: x row (row0 + r) of width dim, normalised as
+// cpu.rs:85-94 (mean square, scale = 1/sqrt(ms + eps), v * (scale * w)),
+// written split to row r of the three planes.
+__global__ void __launch_bounds__(256) k_norm_split(const float* __restrict__ x, int row0, int dim,
+                                                   const uint16_t* __restrict__ w, float eps,
+                                                   uint16_t* __restrict__ out, size_t plane) {
+  __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float* xr = x + size_t(row0 + blockIdx.x) * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = xr[i];
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) tot += red[i];
+  const float scale = 1.0f / sqrtf(tot / float(dim) + eps);
+  const size_t row = size_t(blockIdx.x) * dim;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x)
+    store_split3(out, plane, row + i, __fmul_rn(xr[i], __fmul_rn(scale, bf16f(w[i]))));
+}
+
+// ---- QK-norm, RoPE, cache append -------------------------------------------------
+
+// One CTA (4 warps) per token; a warp takes one head at a time, lane l
+// holding elements 4l .. 4l+3, so a head's RoPE partner (i, i + 64) sits in
+// lane l ^ 16.
+__global__ void __launch_bounds__(128) k_qkv_post(QkvPostArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = a.pos[t], seq = a.seq[t];
+  if (pos < 0 || pos >= a.max_len || seq < 0 || seq >= a.n_seqs) {
+    if (threadIdx.x == 0) set_error(a.err, TB200_ERR_ARG);
+    return;
+  }
+  float* row = a.qkv + size_t(t) * a.ld;
+  const size_t cache_head = size_t(a.max_len) * kD;  // elements per kv head
+  const size_t v_off = size_t(a.n_kv_heads) * cache_head;
+  const size_t base = size_t(seq) * a.seq_stride + size_t(pos) * kD + 4 * lane;
+  // RoPE factors for this lane's four elements: pair index (4l + j) mod 64.
+  const int i0 = (4 * lane) & 63;
+  const float4 cs01 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kD + 2 * i0);
+  const float4 cs23 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kD + 2 * i0 + 4);
+  const float cs[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, sn[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
+  const bool first_half = lane < 16;
+  const int nq = a.n_heads, nk = a.n_kv_heads;
+  for (int h = warp; h < nq + 2 * nk; h += 4) {
+    float4 v = *reinterpret_cast<const float4*>(row + size_t(h) * kD + 4 * lane);
+    if (h >= nq + nk) {  // value head: into the cache as is
+      const size_t at = base + size_t(h - nq - nk) * cache_head + v_off;
+      if (a.kv_f32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.kv) + at) = v;
+      } else {
+        uint16_t* p = static_cast<uint16_t*>(a.kv) + at;
+        p[0] = f2bf(v.x); p[1] = f2bf(v.y); p[2] = f2bf(v.z); p[3] = f2bf(v.w);
+      }
+      continue;
+    }
+    const uint16_t* nw = h < nq ? a.q_norm : a.k_norm;
+    if (nw) {
+      const float s = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      const float scale = 1.0f / sqrtf(s / float(kD) + a.eps);
+      const uint2 wb = *reinterpret_cast<const uint2*>(nw + 4 * lane);
+      v.x = __fmul_rn(v.x, __fmul_rn(scale, bf_lo(wb.x)));
+      v.y = __fmul_rn(v.y, __fmul_rn(scale, bf_hi(wb.x)));
+      v.z = __fmul_rn(v.z, __fmul_rn(scale, bf_lo(wb.y)));
+      v.w = __fmul_rn(v.w, __fmul_rn(scale, bf_hi(wb.y)));
+    }
+    float e[4] = {v.x, v.y, v.z, v.w}, r[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float other = __shfl_xor_sync(0xffffffffu, e[j], 16);
+      r[j] = first_half ? __fsub_rn(__fmul_rn(e[j], cs[j]), __fmul_rn(other, sn[j]))
+                        : __fadd_rn(__fmul_rn(e[j], cs[j]), __fmul_rn(other, sn[j]));
+    }
+    const float4 o = make_float4(r[0], r[1], r[2], r[3]);
+    if (h < nq) {
+      *reinterpret_cast<float4*>(row + size_t(h) * kD + 4 * lane) = o;
+    } else {
+      const size_t at = base + size_t(h - nq) * cache_head;
+      if (a.kv_f32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.kv) + at) = o;
+      } else {
+        uint16_t* p = static_cast<uint16_t*>(a.kv) + at;
+        p[0] = f2bf(o.x); p[1] = f2bf(o.y); p[2] = f2bf(o.z); p[3] = f2bf(o.w);
+      }
+    }
+  }
+}
+
+// ---- decode attention: one query token per sequence ------------------------------
+
+template <bool F32KV>
+struct RowsCfg {
+  using KV = typename std::conditional<F32KV, float, uint16_t>::type;
+  static constexpr int kCh = F32KV ? 64 : 128;  // positions per CTA: 32 KB each of K and V
+  static constexpr size_t kSmem = size_t(2) * kCh * kD * sizeof(KV);
+};
+
+__device__ __forceinline__ void load4(const float* p, float (&o)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+__device__ __forceinline__ void load4(const uint16_t* p, float (&o)[4]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  o[0] = bf_lo(v.x); o[1] = bf_hi(v.x); o[2] = bf_lo(v.y); o[3] = bf_hi(v.y);
+}
+__device__ __forceinline__ float load1(const float* p) { return *p; }
+__device__ __forceinline__ float load1(const uint16_t* p) { return bf16f(*p); }
+
+// CTA (split, kv group g, token t): positions [split*kCh, ...) of the token's
+// sequence up to its position. Scores with a thread per (position, head),
+// reading key rows in rotated 4-element groups (conflict-free), the chunk's
+// softmax, then weighted values with a thread per dimension.
+template <int GRP, bool F32KV>
+__global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
+  using Cf = RowsCfg<F32KV>;
+  using KV = typename Cf::KV;
+  constexpr int CH = Cf::kCh;
+  extern __shared__ __align__(128) unsigned char smem[];
+  KV* ks = reinterpret_cast<KV*>(smem);
+  KV* vs = ks + size_t(CH) * kD;
+  __shared__ __align__(16) float qs[GRP][kD];
+  __shared__ float ps[GRP][CH];
+  __shared__ float stat[GRP][2];  // chunk max, chunk sum
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int is_last;
+
+  pdl_launch_dependents();
+  const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Positions and sequence ids change only between steps (the host, or the
+  // step's last kernel), so they can be read before the dependency wait.
+  const int pos = a.pos[t], seq = a.seq[t];
+  const bool ok = pos >= 0 && pos < a.max_len && seq >= 0 && seq < a.n_seqs;
+  const int ctx = pos + 1;
+  const int nsplit = (ctx + CH - 1) / CH;
+  const bool active = ok && split < nsplit && nsplit <= a.max_split;
+  const int p0 = split * CH, p1 = active ? min(ctx, p0 + CH) : p0;
+  const int n = p1 - p0;
+  const int cached = active ? max(0, min(p1, pos) - p0) : 0;  // rows written by earlier steps
+  const size_t head = size_t(seq) * a.seq_stride + size_t(g) * a.max_len * kD;
+  const size_t v_off = size_t(a.n_kv_heads) * a.max_len * kD;
+  const KV* kc = static_cast<const KV*>(a.kv) + head;
+  const KV* vc = kc + v_off;
+
+  if (active) {
+    if (tid == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0 && cached > 0) {
+      const uint32_t bytes = uint32_t(cached) * kD * sizeof(KV);
+      const uint64_t pol = l2_evict_first();
+      mbar_arrive_expect_tx(&bar, 2 * bytes);
+      bulk_g2s(ks, kc + size_t(p0) * kD, bytes, &bar, pol);
+      bulk_g2s(vs, vc + size_t(p0) * kD, bytes, &bar, pol);
+    }
+  }
+  pdl_wait();
+  if (!ok) {
+    if (split == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
+    return;
+  }
+  if (!active) return;
+  // The token's own key and value were appended by the previous kernel.
+  if (p1 == ctx) {
+    ks[size_t(pos - p0) * kD + tid] = kc[size_t(pos) * kD + tid];
+    vs[size_t(pos - p0) * kD + tid] = vc[size_t(pos) * kD + tid];
+  }
+  for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
+  if (cached > 0) {
+    // One thread waits with the time limit and the CTA follows its verdict.
+    if (tid == 0) is_last = mbar_wait(&bar, 0, a.err) ? 1 : 0;
+    __syncthreads();
+    if (!is_last) {
+      if (tid == 0) mbar_wait(&bar, 0, nullptr);  // one more bounded wait for the copy in flight
+      return;
+    }
+    mbar_wait(&bar, 0, nullptr);  // the phase is complete: returns at once
+  }
+  __syncthreads();
+
+  // Scores: thread -> (position p, head h); rotated groups of 4 elements.
+  const float scale = 1.0f / sqrtf(float(kD));
+  for (int i = tid; i < GRP * CH; i += 128) {
+    const int h = i / CH, p = i % CH;
+    float s = -INFINITY;
+    if (p < n) {
+      const KV* kr = ks + size_t(p) * kD;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int j = 0; j < 32; j++) {
+        const int c = 4 * ((j + p) & 31);
+        float k4[4];
+        load4(kr + c, k4);
+        const float4 q4 = *reinterpret_cast<const float4*>(&qs[h][c]);
+        acc = fmaf(q4.x, k4[0], acc);
+        acc = fmaf(q4.y, k4[1], acc);
+        acc = fmaf(q4.z, k4[2], acc);
+        acc = fmaf(q4.w, k4[3], acc);
+      }
+      s = scale * acc;
+    }
+    ps[h][p] = s;
+  }
+  __syncthreads();
+  // Chunk softmax statistics: warp w takes heads w, w + 4, ...
+  for (int h = warp; h < GRP; h += 4) {
+    float m = -INFINITY;
+    for (int p = lane; p < n; p += 32) m = fmaxf(m, ps[h][p]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int p = lane; p < n; p += 32) {
+      const float e = expf(ps[h][p] - m);
+      ps[h][p] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stat[h][0] = m;
+      stat[h][1] = l;
+    }
+  }
+  __syncthreads();
+  // Weighted values: thread d of every head.
+  float o[GRP];
+#pragma unroll
+  for (int h = 0; h < GRP; h++) o[h] = 0.f;
+  for (int p = 0; p < n; p++) {
+    const float v = load1(vs + size_t(p) * kD + tid);
+#pragma unroll
+    for (int h = 0; h < GRP; h++) o[h] = fmaf(ps[h][p], v, o[h]);
+  }
+  const size_t out_at = size_t(t) * a.ldo + size_t(g) * GRP * kD + tid;
+  if (nsplit == 1) {
+#pragma unroll
+    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, o[h] / stat[h][1]);
+    return;
+  }
+  const int stride = kD + 2;
+  float* part = a.part + ((size_t(t) * a.n_kv_heads + g) * a.max_split) * GRP * stride;
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    float* pp = part + (size_t(split) * GRP + h) * stride;
+    pp[2 + tid] = o[h];
+    if (tid == 0) {
+      pp[0] = stat[h][0];
+      pp[1] = stat[h][1];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  unsigned* ticket = a.ticket + size_t(t) * a.n_kv_heads + g;
+  if (tid == 0) is_last = atomicAdd(ticket, 1u) == unsigned(nsplit - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(part + (size_t(sp) * GRP + h) * stride));
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < nsplit; sp++) {
+      const float* pp = part + (size_t(sp) * GRP + h) * stride;
+      const float wt = expf(__ldcg(pp) - M);
+      L += __ldcg(pp + 1) * wt;
+      O += __ldcg(pp + 2 + tid) * wt;
+    }
+    store_split3(a.out, a.plane, out_at + size_t(h) * kD, O / L);
+  }
+  if (tid == 0) *ticket = 0u;
+}
+
+// ---- causal prefill attention -------------------------------------------------------
+
+constexpr int kPR = 64;     // query rows per CTA (tokens x heads of one kv group)
+constexpr int kPK = 64;     // cache positions per tile
+constexpr int kPPad = 68;   // padded row of the transposed tiles
+struct PrefillSmem {
+  float qt[kD][kPPad];   // queries, transposed: [dim][row]
+  float kt[kD][kPPad];   // keys, transposed:    [dim][position]
+  float vs[kPK][kD];     // values:              [position][dim]
+  float ps[kPR][kPPad];  // probabilities:       [row][position]
+};
+
+// CTA (query block, kv group g): rows r = token * GRP + head of kPR / GRP
+// consecutive tokens; 256 threads, thread (ty, tx) = (tid / 16, tid % 16)
+// owns rows 4ty .. 4ty+3, score columns 4tx .. 4tx+3 and output dimensions
+// 8tx .. 8tx+7.
+template <int GRP, bool F32KV>
+__global__ void __launch_bounds__(256) k_attn_prefill(AttnPrefillArgs a) {
+  using KV = typename std::conditional<F32KV, float, uint16_t>::type;
+  constexpr int QT = kPR / GRP;  // tokens per CTA
+  extern __shared__ __align__(128) unsigned char smem[];
+  PrefillSmem& S = *reinterpret_cast<PrefillSmem*>(smem);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int nqb = (a.T + QT - 1) / QT;
+  const int qb = nqb - 1 - int(blockIdx.x);  // longest rows first
+  const int g = blockIdx.y;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int tok0 = qb * QT;
+  const int qtok = min(QT, a.T - tok0);
+  const int kend = a.pos0 + tok0 + qtok;  // keys [0, kend) cover every row's causal window
+  const size_t v_off = size_t(a.n_kv_heads) * a.max_len * kD;
+  const KV* kc = static_cast<const KV*>(a.kv) + size_t(g) * a.max_len * kD;
+  const KV* vc = kc + v_off;
+
+  for (int i = tid; i < kPR * kD; i += 256) {
+    const int r = i / kD, d = i % kD;
+    const int tk = r / GRP, h = r % GRP;
+    S.qt[d][r] = tk < qtok ? a.q[size_t(tok0 + tk) * a.ldq + size_t(g * GRP + h) * kD + d] : 0.f;
+  }
+  float o[4][8], m[4], l[4];
+  int qpos[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+    qpos[i] = a.pos0 + tok0 + (4 * ty + i) / GRP;
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[i][j] = 0.f;
+  }
+  const float scale = 1.0f / sqrtf(float(kD));
+  const int ntiles = (kend + kPK - 1) / kPK;
+  for (int kt = 0; kt < ntiles; kt++) {
+    const int kp0 = kt * kPK;
+    const int kn = min(kPK, kend - kp0);
+    __syncthreads();  // previous tile's reads of kt / vs / ps are done
+    for (int i = tid; i < kPK * kD; i += 256) {
+      const int p = i / kD, d = i % kD;
+      float kv = 0.f, vv = 0.f;
+      if (p < kn) {
+        kv = load1(kc + size_t(kp0 + p) * kD + d);
+        vv = load1(vc + size_t(kp0 + p) * kD + d);
+      }
+      S.kt[d][p] = kv;
+      S.vs[p][d] = vv;
+    }
+    __syncthreads();
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < kD; d++) {
+      const float4 q4 = *reinterpret_cast<const float4*>(&S.qt[d][4 * ty]);
+      const float4 k4 = *reinterpret_cast<const float4*>(&S.kt[d][4 * tx]);
+      const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kp = kp0 + 4 * tx + j;
+        s[i][j] = (4 * tx + j < kn && kp <= qpos[i]) ? scale * s[i][j] : -INFINITY;
+        mx = fmaxf(mx, s[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[i], mx);
+      const float corr = expf(m[i] - mn);
+      float sum = 0.f;
+      float p4[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        p4[j] = expf(s[i][j] - mn);
+        sum += p4[j];
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l[i] = l[i] * corr + sum;
+      m[i] = mn;
+#pragma unroll
+      for (int j = 0; j < 8; j++) o[i][j] *= corr;
+      *reinterpret_cast<float4*>(&S.ps[4 * ty + i][4 * tx]) = make_float4(p4[0], p4[1], p4[2], p4[3]);
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int p = 0; p < kn; p++) {
+      const float4 va = *reinterpret_cast<const float4*>(&S.vs[p][8 * tx]);
+      const float4 vb = *reinterpret_cast<const float4*>(&S.vs[p][8 * tx + 4]);
+      const float vv[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float pr = S.ps[4 * ty + i][p];
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[i][j] = fmaf(pr, vv[j], o[i][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int r = 4 * ty + i, tk = r / GRP, h = r % GRP;
+    if (tk >= qtok) continue;
+    const size_t at = size_t(tok0 + tk) * a.ldo + size_t(g * GRP + h) * kD + 8 * tx;
+    const float inv = 1.0f / l[i];
+#pragma unroll
+    for (int j = 0; j < 8; j++) store_split3(a.out, a.plane, at + j, o[i][j] * inv);
+  }
+}
+
+// ---- greedy choice per row ----------------------------------------------------------
+
+__global__ void __launch_bounds__(1024) k_argmax_rows(ArgmaxRowsArgs a) {
+  __shared__ unsigned long long red[32];
+  __shared__ int step_s, is_last;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (threadIdx.x == 0) step_s = a.step ? *a.step : 0;
+  const float* x = a.logits + size_t(r) * a.V;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
+    const unsigned long long k = argmax_key(x[i], uint32_t(i));
+    best = k > best ? k : best;
+  }
+  best = warp_umax64(best);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long b = red[threadIdx.x];
+    b = warp_umax64(b);
+    if (threadIdx.x == 0) {
+      const int tok = int(argmax_index(b));
+      if (a.next) a.next[r] = tok;
+      if (a.tok) a.tok[r] = tok;
+      if (a.pos) a.pos[r] += 1;
+      if (a.out && step_s < a.out_cap) a.out[size_t(step_s) * gridDim.x + r] = tok;
+    }
+  }
+  if (!a.step) return;
+  // The last CTA advances the step counter, after every CTA has read it.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (is_last && threadIdx.x == 0) {
+    *a.step = step_s + 1;
+    *a.ticket = 0u;
+  }
+}
+
+template <int G, bool F>
+cudaError_t rows_attr() {
+  cudaError_t e = cudaFuncSetAttribute(k_attn_rows<G, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(RowsCfg<F>::kSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_prefill<G, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(sizeof(PrefillSmem)));
+  return e;
+}
+
+}  // namespace
+
+cudaError_t init_batch_kernels() {
+  cudaError_t e = cudaSuccess;
+#define TB_ATTR(G)                               \
+  if (e == cudaSuccess) e = rows_attr<G, true>(); \
+  if (e == cudaSuccess) e = rows_attr<G, false>();
+  TB_ATTR(1)
+  TB_ATTR(2)
+  TB_ATTR(4)
+  TB_ATTR(8)
+#undef TB_ATTR
+  return e;
+}
+
+bool batch_group_supported(int group) { return group == 1 || group == 2 || group == 4 || group == 8; }
+
+int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<false>::kCh; }
+
+void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t plane, size_t n, bool pdl) {
+  const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, 4096));
+  if (n) launch_pdl(s, dim3(grid), dim3(256), 0, pdl, k_split_rows, x, out, plane, n);
+}
+
+void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
+                       uint16_t* out, size_t plane, bool pdl) {
+  if (rows > 0) launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, row0, dim, w, eps, out, plane);
+}
+
+void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl) {
+  if (tokens > 0) launch_pdl(s, dim3(tokens), dim3(128), 0, pdl, k_qkv_post, a);
+}
+
+void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl) {
+  if (tokens <= 0) return;
+  const dim3 grid(unsigned(a.max_split), unsigned(a.n_kv_heads), unsigned(tokens));
+#define TB_ROWS(G)                                                                                   \
+  if (group == G) {                                                                                  \
+    if (a.kv_f32) launch_pdl(s, grid, dim3(128), RowsCfg<true>::kSmem, pdl, k_attn_rows<G, true>, a); \
+    else launch_pdl(s, grid, dim3(128), RowsCfg<false>::kSmem, pdl, k_attn_rows<G, false>, a);       \
+    return;                                                                                          \
+  }
+  TB_ROWS(1)
+  TB_ROWS(2)
+  TB_ROWS(4)
+  TB_ROWS(8)
+#undef TB_ROWS
+}
+
+void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bool pdl) {
+  if (a.T <= 0) return;
+  const int qt = kPR / group;
+  const dim3 grid(unsigned((a.T + qt - 1) / qt), unsigned(a.n_kv_heads));
+#define TB_PRE(G)                                                                                          \
+  if (group == G) {                                                                                        \
+    if (a.kv_f32) launch_pdl(s, grid, dim3(256), sizeof(PrefillSmem), pdl, k_attn_prefill<G, true>, a);   \
+    else launch_pdl(s, grid, dim3(256), sizeof(PrefillSmem), pdl, k_attn_prefill<G, false>, a);           \
+    return;                                                                                                \
+  }
+  TB_PRE(1)
+  TB_PRE(2)
+  TB_PRE(4)
+  TB_PRE(8)
+#undef TB_PRE
+}
+
+void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl) {
+  if (rows > 0) launch_pdl(s, dim3(rows), dim3(1024), 0, pdl, k_argmax_rows, a);
+}
+
+}  // namespace tb

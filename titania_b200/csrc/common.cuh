@@ -23,6 +23,20 @@ __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 
 // f32 -> bf16 bits, round to nearest even.
 __device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 
+// The operand form of the tensor-core contraction: v = x0 + x1 + x2 with
+// x0 = bf16(v), x1 = bf16(v - x0), x2 = bf16(v - x0 - x1) (exact for
+// |v| in 2^-100 .. 2^127; the subtractions are exact), stored to planes
+// p[at], p[plane + at], p[2 plane + at].
+__device__ __forceinline__ void store_split3(uint16_t* p, size_t plane, size_t at, float v) {
+  const uint16_t a = f2bf(v);
+  const float r = v - bf16f(a);
+  const uint16_t b = f2bf(r);
+  const uint16_t c = f2bf(r - bf16f(b));
+  p[at] = a;
+  p[plane + at] = b;
+  p[2 * plane + at] = c;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -1,0 +1,434 @@
+// gemm.cu — the tensor-core contraction for many tokens at once:
+//
+//     out[t][r] = Σ_c W[r][c] · x[t][c]          (model/cpu.rs:49-77, n > 1)
+//
+// W is the bf16 weight [M][K] exactly as uploaded; x is f32. The fifth
+// generation tensor cores multiply bf16 by bf16 (kind::f16, f32 accumulate),
+// so each activation is carried as three bf16 planes, x = x0 + x1 + x2 with
+// x0 = bf16(x), x1 = bf16(x - x0), x2 = bf16(x - x0 - x1): 3 x 8 significant
+// bits hold every f32 of magnitude 2^-100 .. 2^127 exactly, and every
+// bf16 x bf16 product is exact in f32, so W·x0 + W·x1 + W·x2 differs from the
+// reference's dot product only in the order and rounding of the f32
+// additions. The three products accumulate into one tensor-memory
+// accumulator: the split costs tensor-core time (three MMAs per K step) but
+// no extra passes over W — the contraction stays bound by streaming W from
+// HBM for a few dozen tokens, and by the tensor cores for long prompts.
+//
+// One CTA computes one 128-row × BN-token tile over one range of K (split-K
+// for short, wide matrices so that every SM streams weights):
+//   warp 0      TMA producer: 128×64 weight box + three BN×64 activation
+//               boxes per stage, 128-byte swizzle, into a ring of stages;
+//   warp 1      allocates BN tensor-memory columns, and one lane issues
+//               tcgen05.mma (M=128, N=BN, K=16) — 4 × 3 per 64-column stage —
+//               committing each stage back to the producer;
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, then store,
+//               residual add, or SiLU(gate)·up of interleaved row pairs split
+//               again into three bf16 planes for the next contraction.
+// Split-K partials go to a workspace; the last CTA of a tile (ticket) sums
+// them in split order, so results do not depend on scheduling.
+//
+// Every mbarrier wait is bounded (kWaitNs); on expiry the kernel records
+// TB200_ERR_TIMEOUT, lets what it issued drain (bounded), frees its tensor
+// memory on every path, and returns.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tb {
+
+namespace {
+
+constexpr int kBM = 128;          // weight rows per tile (MMA M)
+constexpr int kBK = 64;           // K per stage: one 128-byte swizzle row of bf16
+constexpr int kGemmThreads = 192;
+constexpr int kStageA = kBM * kBK * 2;  // 16 KB
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStageB = BN * kBK * 2;          // per activation plane
+  static constexpr int kStage = kStageA + 3 * kStageB;  // bytes per stage
+  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
+  // tiles + barriers + tensor-memory slot + flag, plus alignment slack
+  static constexpr size_t kSmem = size_t(kStages) * kStage + (2 * kStages + 1) * 8 + 64 + 1024;
+};
+
+// ---- tcgen05 / TMA wrappers -------------------------------------------------
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Whole warp: allocates `cols` tensor-memory columns, address written to *slot.
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t addr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(addr), "r"(cols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand whose rows are 128 bytes,
+// 128-byte swizzle, 8-row groups 1024 bytes apart (the layout a TMA box of
+// 64 bf16 columns with CU_TENSOR_MAP_SWIZZLE_128B writes). Bits: start
+// address >> 4 [0,14), leading byte offset >> 4 [16,30) (unused for this
+// layout, 1), stride byte offset >> 4 [32,46), descriptor version 1 [46,48),
+// base offset 0 [49,52) (tiles are 1024-byte aligned), layout 2 = 128-byte
+// swizzle [61,64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator [4,6) = 1, A and B bf16
+// ([7,10) = 1, [10,13) = 1), both K-major (bits 15, 16 zero), N >> 3 at
+// [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrives on `bar` once every tcgen05.mma this thread issued has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns of tensor memory per warp.
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(addr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D tiled TMA load of box (x = column, y = row) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// Applies the epilogue to one accumulator value: row `row` (< M), token t (< T).
+// kGemmSilu pairs lanes (2i, 2i+1) = (gate, up) of hidden row row/2: every
+// lane of the warp must call it with the same t.
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const GemmArgs& a, int row, int t, float v, bool valid) {
+  if (EPI == kGemmStore) {
+    if (valid) a.out[size_t(t) * a.ldo + row] = v;
+  } else if (EPI == kGemmResid) {
+    if (valid) {
+      float* p = a.out + size_t(t) * a.ldo + row;
+      *p = __fadd_rn(*p, v);
+    }
+  } else {  // kGemmSilu
+    const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (valid && (row & 1) == 0) store_split3(a.out_split, a.plane, size_t(t) * a.ldh + (row >> 1), silu_mul(v, u));
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx0,
+           const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2, GemmArgs a) {
+  using C = Cfg<BN>;
+  extern __shared__ unsigned char smem_raw[];
+  // The swizzled tiles need 1024-byte alignment.
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(C::kStages) * C::kStage);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* tfull = empty + C::kStages;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+  int* last_flag = reinterpret_cast<int*>(tslot + 1);
+  int* warp_ok = last_flag + 1;  // [4] per epilogue warp
+  auto sA = [&](int s) { return sm + size_t(s) * C::kStage; };
+  auto sB = [&](int s, int plane) { return sm + size_t(s) * C::kStage + kStageA + plane * C::kStageB; };
+
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x, nt = blockIdx.y, z = blockIdx.z;
+  const int m0 = mt * kBM, n0 = nt * BN;
+  const int nkb = (a.K + kBK - 1) / kBK;
+  const int kb0 = z * a.kb_per_split;
+  const int kb1 = min(nkb, kb0 + a.kb_per_split);
+  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tslot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer. Weights do not depend on earlier kernels: the first
+      // stages' weight boxes go out before the dependency wait.
+      const uint64_t pol_w = l2_evict_first(), pol_x = l2_evict_last();
+      const int pre = nk < C::kStages ? nk : C::kStages;
+      for (int i = 0; i < pre; i++) {
+        mbar_arrive_expect_tx(&full[i], C::kStage);
+        tma_load_2d(sA(i), &tw, (kb0 + i) * kBK, m0, &full[i], pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; i++) {
+        tma_load_2d(sB(i, 0), &tx0, (kb0 + i) * kBK, n0, &full[i], pol_x);
+        tma_load_2d(sB(i, 1), &tx1, (kb0 + i) * kBK, n0, &full[i], pol_x);
+        tma_load_2d(sB(i, 2), &tx2, (kb0 + i) * kBK, n0, &full[i], pol_x);
+      }
+      int issued = pre;
+      for (int i = pre; i < nk; i++) {
+        const int s = i % C::kStages;
+        if (!mbar_wait(&empty[s], ((i / C::kStages) & 1) ^ 1, a.err)) break;
+        mbar_arrive_expect_tx(&full[s], C::kStage);
+        tma_load_2d(sA(s), &tw, (kb0 + i) * kBK, m0, &full[s], pol_w);
+        tma_load_2d(sB(s, 0), &tx0, (kb0 + i) * kBK, n0, &full[s], pol_x);
+        tma_load_2d(sB(s, 1), &tx1, (kb0 + i) * kBK, n0, &full[s], pol_x);
+        tma_load_2d(sB(s, 2), &tx2, (kb0 + i) * kBK, n0, &full[s], pol_x);
+        issued = i + 1;
+      }
+      // Drain: every issued copy has landed before the CTA can exit (on the
+      // normal path the MMA warp already waited for each of them).
+      for (int i = issued - 1; i >= 0 && i >= issued - C::kStages; i--)
+        mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, nullptr);
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(kBM, BN);
+      for (int i = 0; i < nk; i++) {
+        const int s = i % C::kStages;
+        if (!mbar_wait(&full[s], (i / C::kStages) & 1, a.err)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s, 0));
+#pragma unroll
+        for (int k = 0; k < kBK / 16; k++) {
+          // K = 16 bf16 = 32 bytes per MMA inside the 128-byte swizzle row.
+          const uint64_t ad = sw128_desc(a0 + 32 * k);
+#pragma unroll
+          for (int p = 0; p < 3; p++)
+            mma_bf16(tmem, ad, sw128_desc(b0 + p * C::kStageB + 32 * k), idesc, (i > 0 || k > 0 || p > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      mma_commit(tfull);
+      // Tensor memory is freed below only after every MMA has completed.
+      mbar_wait(tfull, 0, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31.
+    pdl_wait();
+    const int q = warp & 3;
+    const int row = m0 + 32 * q + lane;
+    const bool row_ok = row < a.M;
+    bool ok = nk > 0 && mbar_wait(tfull, 0, a.err);
+    ok = __all_sync(0xffffffffu, ok);
+    // The four epilogue warps take the same branches below (named barriers).
+    if (lane == 0) warp_ok[q] = ok ? 1 : 0;
+    named_sync(1, 128);
+    ok = warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3];
+    tc_fence_after();
+    const uint32_t taddr = tmem + (uint32_t(32 * q) << 16);
+    if (ok && a.splits == 1) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(taddr + c, v);
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int t = n0 + c + j;
+          epilogue_store<EPI>(a, row, t, v[j], row_ok && t < a.T);
+        }
+      }
+    } else if (ok) {
+      // Split-K: this CTA's partial sums to the workspace [split][T][M].
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(taddr + c, v);
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int t = n0 + c + j;
+          if (row_ok && t < a.T) a.part[(size_t(z) * a.T + t) * a.M + row] = v[j];
+        }
+      }
+      __threadfence();
+      named_sync(1, 128);
+      unsigned* ticket = a.tickets + (size_t(mt) * gridDim.y + nt);
+      if (warp == 2 && lane == 0) *last_flag = atomicAdd(ticket, 1u) == unsigned(a.splits - 1);
+      named_sync(1, 128);
+      if (*last_flag) {
+        __threadfence();
+        const int tn = min(BN, a.T - n0);
+#pragma unroll 1
+        for (int j = 0; j < tn; j++) {
+          const int t = n0 + j;
+          float v = 0.f;
+          if (row_ok)
+            for (int zz = 0; zz < a.splits; zz++) v += __ldcg(a.part + (size_t(zz) * a.T + t) * a.M + row);
+          epilogue_store<EPI>(a, row, t, v, row_ok);
+        }
+        if (warp == 2 && lane == 0) *ticket = 0u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_free(tmem, C::kTmemCols);
+  }
+}
+
+// ---- host side -----------------------------------------------------------------
+
+std::mutex g_encode_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+template <int BN, int EPI>
+cudaError_t set_smem() {
+  return cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<BN>::kSmem));
+}
+
+template <int BN, int EPI>
+void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap* tx, const GemmArgs& a,
+                 bool pdl) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = p.grid;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = Cfg<BN>::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, k_gemm<BN, EPI>, tw, tx[0], tx[1], tx[2], a);
+}
+
+}  // namespace
+
+int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t cols, int box_rows,
+                     std::string* why) {
+  {
+    std::lock_guard<std::mutex> lock(g_encode_mu);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q{};
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        *why = "cuTensorMapEncodeTiled is not available from the driver";
+        return TB200_ERR_CUDA;
+      }
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || (cols * 2) % 16 != 0 || rows == 0 || cols == 0 ||
+      box_rows < 1 || box_rows > 256) {
+    *why = "tensor map: base must be 16-byte aligned and rows 16-byte multiples";
+    return TB200_ERR_ARG;
+  }
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols * 2)};
+  cuuint32_t box[2] = {cuuint32_t(kBK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *why = "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")";
+    return TB200_ERR_CUDA;
+  }
+  return TB200_OK;
+}
+
+int gemm_box_rows(int tokens) { return tokens <= 64 ? 64 : 128; }
+
+GemmPlan plan_gemm(int M, int K, int T, int sms) {
+  GemmPlan p{};
+  p.bn = gemm_box_rows(T);
+  const int mtiles = (M + kBM - 1) / kBM, ntiles = (T + p.bn - 1) / p.bn;
+  const int nkb = (K + kBK - 1) / kBK;
+  int splits = 1;
+  const int tiles = mtiles * ntiles;
+  if (tiles < sms) splits = std::max(1, std::min(nkb, sms / tiles));
+  p.kb_per_split = (nkb + splits - 1) / splits;
+  p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  p.grid = dim3(unsigned(mtiles), unsigned(ntiles), unsigned(p.splits));
+  return p;
+}
+
+size_t gemm_workspace_floats(const GemmPlan& p, int M, int T) {
+  return p.splits > 1 ? size_t(p.splits) * size_t(T) * size_t(M) : 0;
+}
+
+cudaError_t init_gemm_kernels() {
+  cudaError_t e = cudaSuccess;
+#define TB_GEMM_SMEM(BN)                                              \
+  if (e == cudaSuccess) e = set_smem<BN, kGemmStore>();              \
+  if (e == cudaSuccess) e = set_smem<BN, kGemmResid>();              \
+  if (e == cudaSuccess) e = set_smem<BN, kGemmSilu>();
+  TB_GEMM_SMEM(64)
+  TB_GEMM_SMEM(128)
+#undef TB_GEMM_SMEM
+  return e;
+}
+
+void launch_gemm(cudaStream_t s, const GemmPlan& p, int epi, const CUtensorMap& tw, const CUtensorMap* tx,
+                 const GemmArgs& a, bool pdl) {
+  GemmArgs b = a;
+  b.kb_per_split = p.kb_per_split;
+  b.splits = p.splits;
+#define TB_GEMM_CASE(BN)                                                        \
+  if (p.bn == BN) {                                                             \
+    if (epi == kGemmStore) launch_tile<BN, kGemmStore>(s, p, tw, tx, b, pdl);   \
+    if (epi == kGemmResid) launch_tile<BN, kGemmResid>(s, p, tw, tx, b, pdl);   \
+    if (epi == kGemmSilu) launch_tile<BN, kGemmSilu>(s, p, tw, tx, b, pdl);     \
+    return;                                                                     \
+  }
+  TB_GEMM_CASE(64)
+  TB_GEMM_CASE(128)
+#undef TB_GEMM_CASE
+}
+
+}  // namespace tb

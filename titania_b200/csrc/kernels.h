@@ -2,6 +2,7 @@
 // per Device-trait op; fused.cu: the fused decode path).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -153,5 +154,118 @@ void launch_interleave_rows(cudaStream_t s, uint16_t* dst, const uint16_t* a, co
                             size_t cols);
 // bf16 [rows][cols] -> f32, for reading the cache in tests.
 void launch_bf16_to_f32(cudaStream_t s, float* dst, const uint16_t* src, size_t n);
+
+// ---- tensor-core contraction for many tokens (gemm.cu) ---------------------
+
+enum GemmEpilogue {
+  kGemmStore = 0,  // out[t][r] = acc
+  kGemmResid,      // out[t][r] += acc                    (residual stream)
+  kGemmSilu,       // rows interleaved (gate, up): planes [t][r/2] = split3(silu(g) * u)
+};
+struct GemmArgs {
+  int M, K, T;              // weight rows, columns (reduction), tokens
+  int kb_per_split, splits;  // set by launch_gemm from the plan
+  float* out;               // kGemmStore / kGemmResid: [T][ldo]
+  int ldo;
+  uint16_t* out_split;      // kGemmSilu: three bf16 planes [T][ldh], `plane` elements apart
+  size_t plane;
+  int ldh;
+  float* part;              // split-K workspace, gemm_workspace_floats()
+  unsigned* tickets;        // split-K: one per tile, zero between launches
+  int* err;
+};
+struct GemmPlan {
+  int bn;            // tokens per tile (box rows of the activation maps)
+  int splits, kb_per_split;
+  dim3 grid;         // (row tiles, token tiles, splits)
+};
+// Tensor map of a row-major bf16 matrix [rows][cols] in boxes of 64 columns
+// by box_rows rows, 128-byte swizzle: the operand layout of the kernel.
+int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t cols, int box_rows,
+                     std::string* why);
+// Box rows of the activation maps for a contraction over `tokens` tokens.
+int gemm_box_rows(int tokens);
+GemmPlan plan_gemm(int M, int K, int T, int sms);
+size_t gemm_workspace_floats(const GemmPlan& p, int M, int T);
+// Most split-K workspace any plan needs on a GPU with `sms` SMs.
+inline size_t gemm_workspace_max_floats(int sms) { return size_t(sms) * 128 * 128; }
+cudaError_t init_gemm_kernels();
+// tw: weight map (box rows 128); tx[0..2]: the activation's three planes
+// (box rows p.bn).
+void launch_gemm(cudaStream_t s, const GemmPlan& p, int epilogue, const CUtensorMap& tw, const CUtensorMap* tx,
+                 const GemmArgs& a, bool pdl);
+
+// ---- many-token forward around the contractions (batch.cu) ------------------
+
+cudaError_t init_batch_kernels();
+// Query heads per kv head that the batched attention kernels handle.
+bool batch_group_supported(int group);
+// Cache positions per CTA of the decode attention (launch_attn_rows).
+int attn_rows_chunk(bool kv_f32);
+
+// x[0..n) -> three bf16 planes (store_split3), `plane` elements apart.
+void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t plane, size_t n, bool pdl);
+// planes row r = split3(rmsnorm(x row row0 + r, w)), r < rows; plane = elements between planes.
+void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
+                       uint16_t* out, size_t plane, bool pdl);
+
+struct QkvPostArgs {
+  float* qkv;               // [T][ld]: q heads | k heads | v heads; q rewritten in place
+  int ld;
+  const uint16_t* q_norm;   // [head_dim] or null
+  const uint16_t* k_norm;
+  float eps;
+  const float* rope;        // [max_len][head_dim] (cos, sin) pairs
+  void* kv;                 // this layer's cache block of sequence 0
+  size_t seq_stride;        // cache elements between sequences
+  int kv_f32, max_len, n_heads, n_kv_heads, n_seqs;
+  const int* pos;           // [T] position of each token
+  const int* seq;           // [T] sequence of each token
+  int* err;
+};
+void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl);
+
+struct AttnRowsArgs {
+  const float* q;           // [T][ldq], query heads (normed, rotated) from column 0
+  int ldq;
+  const void* kv;           // this layer's cache block of sequence 0
+  size_t seq_stride;
+  int kv_f32, max_len, n_kv_heads, n_seqs;
+  const int* pos;
+  const int* seq;
+  uint16_t* out;            // [3 planes][T][ldo] attention output, split3
+  size_t plane;
+  int ldo;
+  float* part;              // [T][Hkv][max_split][group][head_dim + 2]
+  unsigned* ticket;         // [T][Hkv], zero between launches
+  int max_split;            // ceil(max_len / attn_rows_chunk)
+  int* err;
+};
+void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl);
+
+struct AttnPrefillArgs {
+  const float* q;           // [T][ldq]
+  int ldq;
+  const void* kv;           // this layer's cache block of the sequence
+  int kv_f32, max_len, n_kv_heads;
+  int T, pos0;              // tokens at positions pos0 .. pos0 + T - 1, already in the cache
+  uint16_t* out;            // [3 planes][T][ldo]
+  size_t plane;
+  int ldo;
+};
+void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bool pdl);
+
+struct ArgmaxRowsArgs {
+  const float* logits;      // [rows][V]
+  int V;
+  int* next;                // [rows] greedy token, or null
+  int* tok;                 // [rows] next step's input token, or null
+  int* pos;                 // [rows] incremented, or null
+  int* out;                 // [out_cap][rows] tokens by step, or null
+  int* step;                // step counter (with out), or null
+  unsigned* ticket;         // with step: zero between launches
+  int out_cap;
+};
+void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl);
 
 }  // namespace tb

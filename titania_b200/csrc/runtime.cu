@@ -16,92 +16,18 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "runtime.h"
 
-struct tb200_device {
-  int ordinal = 0;
-  int sms = 0;
-  cudaStream_t stream = nullptr;
-  uint32_t* tokens = nullptr;  // device scratch for embed's token ids
-  size_t tokens_cap = 0;
-  unsigned long long* best = nullptr;  // argmax scratch
-};
-
-struct tb200_buffer {
-  float* ptr = nullptr;
-  size_t len = 0, cap = 0;
-};
-
-struct tb200_weight {
-  uint16_t* ptr = nullptr;
-  std::vector<size_t> shape;
-  size_t numel = 0;
-};
-
-struct FusedLayer {
-  const uint16_t *attn_norm, *mlp_norm, *q_norm, *k_norm;
-  uint16_t* wqkv = nullptr;  // [q_dim + 2 kv_dim][H], owned
-  uint16_t* wgu = nullptr;   // [2F][H] gate/up rows interleaved, owned
-  const uint16_t *wo, *wd;
-  uint16_t* wo_packed = nullptr;  // o_proj packed per (kv group, output slice), owned
-};
-
-struct tb200_model {
-  tb200_device* dev = nullptr;
-  int live_states = 0;          // states built on this model
-  bool free_requested = false;  // tb200_model_free came while states lived
-  tb200_config c{};
-  std::map<std::string, const tb200_weight*> bound;
-  bool finalized = false;
-  std::vector<FusedLayer> layers;
-  const uint16_t *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
-  size_t q_dim = 0, kv_dim = 0;
-  int attn_o_slices = 0;  // output slices per kv group of the fused attention + o_proj
-};
-
-struct tb200_state {
-  tb200_model* m = nullptr;
-  tb200_device* dev = nullptr;
-  size_t max_len = 0;
-  int kv_f32 = 0;          // cache element: 0 bf16, 1 f32
-  size_t host_pos = 0;     // the position the next step runs at, as the host knows it
-  unsigned char* kv = nullptr;  // [L][2][Hkv][max_len][head_dim], bf16 or f32
-  float* rope = nullptr;   // [max_len][head_dim]
-  float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
-  float *x2 = nullptr, *part_o = nullptr;  // mid-layer residual; per-group o_proj partials
-  float* part = nullptr;
-  unsigned* attn_ticket = nullptr;
-  unsigned long long* mv_partial = nullptr;
-  unsigned* mv_ticket = nullptr;
-  int* io = nullptr;          // device: [0] token, [1] pos, [2] step, [3] error
-  int* tokens_out = nullptr;  // device: [max_len]
-  int* io_host = nullptr;     // pinned: [max_len][2] staged (token, pos) + [4] readback
-  int max_split = 1;
-  tb::MvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_lm{};
-  tb::Trace trace{};       // device trace buffer while tracing
-  uint32_t trace_next = 0;  // next free record slot while capturing
-  cudaGraphExec_t graph = nullptr;        // positions >= kAttnOMaxCtx
-  cudaGraphExec_t graph_short = nullptr;  // positions < kAttnOMaxCtx (fused attention + o_proj)
-};
+namespace rt {
 
 namespace {
-
 thread_local std::string g_err;
+}  // namespace
 
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
 }
-
-#define CUDA_TRY(expr)                                                                      \
-  do {                                                                                      \
-    cudaError_t e_ = (expr);                                                                \
-    if (e_ != cudaSuccess) return fail(TB200_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
-  } while (0)
-
-#define ARG_CHECK(cond, msg)                         \
-  do {                                               \
-    if (!(cond)) return fail(TB200_ERR_ARG, (msg));  \
-  } while (0)
 
 int launched(const char* what) {
   cudaError_t e = cudaGetLastError();
@@ -113,12 +39,6 @@ int use(tb200_device* d) {
   if (!d) return fail(TB200_ERR_ARG, "null device");
   CUDA_TRY(cudaSetDevice(d->ordinal));
   return TB200_OK;
-}
-
-std::string shape_str(const std::vector<size_t>& s) {
-  std::string r = "[";
-  for (size_t i = 0; i < s.size(); i++) r += (i ? ", " : "") + std::to_string(s[i]);
-  return r + "]";
 }
 
 // model.rs:239-250, on the host exactly as the reference computes it.
@@ -136,13 +56,85 @@ std::vector<float> rope_table(size_t max_len, size_t head_dim, float theta) {
   return t;
 }
 
+const char* last_error() { return g_err.c_str(); }
+
+}  // namespace rt
+
+using rt::fail;
+using rt::launched;
+using rt::use;
+using rt::rope_table;
+
+namespace {
+
+std::string shape_str(const std::vector<size_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); i++) r += (i ? ", " : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
 }  // namespace
 
 int tb::record_error(int code, const std::string& msg) { return fail(code, msg); }
 
+namespace {
+
+// Several tokens: the tensor-core contraction (gemm.cu). The input is split
+// into three bf16 planes in device scratch; the weight's operand map is made
+// once.
+int matmul_tokens(tb200_device* d, tb200_buffer* out, const tb200_weight* w, const tb200_buffer* x, size_t rows,
+                  size_t cols, size_t n) {
+  cudaStream_t s = d->stream;
+  std::string why;
+  auto* wm = const_cast<tb200_weight*>(w);
+  if (!wm->has_map) {
+    if (int rc = tb::encode_tmap_bf16(&wm->map, w->ptr, rows, cols, 128, &why)) return fail(rc, "matmul: " + why);
+    wm->has_map = true;
+  }
+  const size_t need = n * cols;
+  if (need > d->split_cap) {
+    CUDA_TRY(cudaStreamSynchronize(s));
+    cudaFree(d->split);
+    d->split = nullptr;
+    d->split_cap = 0;
+    CUDA_TRY(cudaMalloc(&d->split, 3 * need * sizeof(uint16_t)));
+    d->split_cap = need;
+  }
+  const tb::GemmPlan p = tb::plan_gemm(int(rows), int(cols), int(n), d->sms);
+  CUtensorMap tx[3];
+  for (int i = 0; i < 3; i++)
+    if (int rc = tb::encode_tmap_bf16(&tx[i], d->split + i * d->split_cap, n, cols, p.bn, &why))
+      return fail(rc, "matmul: " + why);
+  ARG_CHECK(size_t(p.grid.x) * p.grid.y <= size_t(rt::kGemmTickets) || p.splits == 1, "matmul: too many tiles");
+  tb::launch_split_rows(s, x->ptr, d->split, d->split_cap, need, false);
+  if (int rc = launched("matmul split")) return rc;
+  tb::GemmArgs a{};
+  a.M = int(rows);
+  a.K = int(cols);
+  a.T = int(n);
+  a.out = out->ptr;
+  a.ldo = int(rows);
+  a.part = d->gemm_part;
+  a.tickets = d->gemm_tickets;
+  a.err = d->err;
+  tb::launch_gemm(s, p, tb::kGemmStore, wm->map, tx, a, false);
+  if (int rc = launched("matmul")) return rc;
+  // A kernel-side error (a wait that timed out) is reported here.
+  int err = 0;
+  CUDA_TRY(cudaMemcpyAsync(&err, d->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  CUDA_TRY(cudaStreamSynchronize(s));
+  if (err) {
+    cudaMemsetAsync(d->err, 0, sizeof(int), s);
+    return fail(TB200_ERR_TIMEOUT, "matmul: a wait inside the contraction timed out");
+  }
+  return TB200_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
-const char* tb200_last_error(void) { return g_err.c_str(); }
+const char* tb200_last_error(void) { return rt::last_error(); }
 
 int tb200_device_open(int ordinal, tb200_device** out) {
   ARG_CHECK(out, "null output handle");
@@ -155,14 +147,25 @@ int tb200_device_open(int ordinal, tb200_device** out) {
   if (prop.major != 10 || prop.minor != 0)
     return fail(TB200_ERR_CUDA, std::string("titania_b200 is built for sm_100a (B200); device is ") + prop.name +
                                     " sm_" + std::to_string(prop.major) + std::to_string(prop.minor));
-  if (cudaError_t e = tb::init_fused_kernels(int(prop.sharedMemPerBlockOptin)); e != cudaSuccess)
-    return fail(TB200_ERR_CUDA, std::string("kernel setup: ") + cudaGetErrorString(e));
+  cudaError_t e = tb::init_fused_kernels(int(prop.sharedMemPerBlockOptin));
+  if (e == cudaSuccess) e = tb::init_gemm_kernels();
+  if (e == cudaSuccess) e = tb::init_batch_kernels();
+  if (e != cudaSuccess) return fail(TB200_ERR_CUDA, std::string("kernel setup: ") + cudaGetErrorString(e));
   auto* d = new tb200_device;
   d->ordinal = ordinal;
   d->sms = prop.multiProcessorCount;
-  cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&d->best, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&d->gemm_part, tb::gemm_workspace_max_floats(d->sms) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&d->gemm_tickets, rt::kGemmTickets * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(d->gemm_tickets, 0, rt::kGemmTickets * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMalloc(&d->err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(d->err, 0, sizeof(int));
   if (e != cudaSuccess) {
+    cudaFree(d->best);
+    cudaFree(d->gemm_part);
+    cudaFree(d->gemm_tickets);
+    cudaFree(d->err);
     delete d;
     return fail(TB200_ERR_CUDA, std::string("device setup: ") + cudaGetErrorString(e));
   }
@@ -176,6 +179,10 @@ int tb200_device_close(tb200_device* d) {
   cudaStreamSynchronize(d->stream);
   cudaFree(d->tokens);
   cudaFree(d->best);
+  cudaFree(d->split);
+  cudaFree(d->gemm_part);
+  cudaFree(d->gemm_tickets);
+  cudaFree(d->err);
   cudaStreamDestroy(d->stream);
   delete d;
   return TB200_OK;
@@ -319,6 +326,8 @@ int tb200_matmul(tb200_device* d, tb200_buffer* out, const tb200_weight* w, cons
                                     std::to_string(cols) + "-wide rows");
   ARG_CHECK(out->len == n * rows, "matmul: output holds " + std::to_string(out->len) + ", expected " +
                                       std::to_string(n * rows));
+  if (n >= 2 && cols % 8 == 0 && rows < (size_t(1) << 31) && cols < (size_t(1) << 31) && n < (size_t(1) << 24))
+    return matmul_tokens(d, out, w, x, rows, cols, n);
   tb::launch_matmul(d->stream, out->ptr, w->ptr, rows, cols, x->ptr, n);
   return launched("matmul");
 }
@@ -517,7 +526,17 @@ int tb200_model_finalize(tb200_model* m) {
     CUDA_TRY(cudaMalloc(&L.wo_packed, H * m->q_dim * 2));
     tb::launch_pack_wo(s, L.wo_packed, o->ptr, int(H), int(c.num_key_value_heads), int(group), m->attn_o_slices);
     if (int rc2 = launched("pack o_proj")) return rc2;
+    std::string why;
+    int rc3 = tb::encode_tmap_bf16(&L.m_qkv, L.wqkv, rows, H, 128, &why);
+    if (!rc3) rc3 = tb::encode_tmap_bf16(&L.m_o, L.wo, H, m->q_dim, 128, &why);
+    if (!rc3) rc3 = tb::encode_tmap_bf16(&L.m_gu, L.wgu, 2 * F, H, 128, &why);
+    if (!rc3) rc3 = tb::encode_tmap_bf16(&L.m_down, L.wd, H, F, 128, &why);
+    if (rc3) return fail(rc3, "model: " + why);
     m->layers.push_back(L);
+  }
+  {
+    std::string why;
+    if (int rc = tb::encode_tmap_bf16(&m->m_lm, m->lm_head, V, H, 128, &why)) return fail(rc, "model: " + why);
   }
   CUDA_TRY(cudaStreamSynchronize(s));
   m->finalized = true;
@@ -780,8 +799,11 @@ int finish(tb200_state* st) {
 
 }  // namespace
 
-int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** out) {
+namespace {
+
+int state_create(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb200_state** out) {
   ARG_CHECK(m && out, "null argument");
+  ARG_CHECK(n_seqs > 0 && n_seqs <= 65536, "state: bad number of sequences");
   ARG_CHECK(m->finalized, "model not finalized");
   ARG_CHECK(!m->free_requested, "model already freed");
   ARG_CHECK(kv_dtype == TB200_KV_BF16 || kv_dtype == TB200_KV_F32, "unknown key/value cache type");
@@ -792,6 +814,7 @@ int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** 
   st->m = m;
   st->dev = m->dev;
   st->max_len = max_len;
+  st->n_seqs = n_seqs;
   st->kv_f32 = kv_dtype == TB200_KV_F32;
   m->live_states++;
   const int sms = m->dev->sms;
@@ -805,7 +828,8 @@ int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** 
     if (e == cudaSuccess) e = cudaMalloc(p, bytes);
     if (e == cudaSuccess) e = cudaMemsetAsync(*p, 0, bytes, m->dev->stream);
   };
-  A((void**)&st->kv, L * 2 * Hkv * max_len * D * (st->kv_f32 ? 4 : 2));
+  st->seq_stride = L * 2 * Hkv * max_len * D;
+  A((void**)&st->kv, n_seqs * st->seq_stride * (st->kv_f32 ? 4 : 2));
   A((void**)&st->rope, table.size() * 4);
   A((void**)&st->x, c.hidden_size * 4);
   A((void**)&st->qkv, (m->q_dim + 2 * m->kv_dim) * 4);
@@ -838,13 +862,28 @@ int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** 
     tb200_state_free(st);
     return fail(TB200_ERR_ARG, "hidden size too large for the residual kernels on this GPU");
   }
-  if (int rc = build_graph(st)) {
-    tb200_state_free(st);
-    return rc;
+  // The single-token graphs run sequence 0 of a one-sequence state.
+  if (n_seqs == 1) {
+    if (int rc = build_graph(st)) {
+      tb200_state_free(st);
+      return rc;
+    }
   }
   *out = st;
   return TB200_OK;
 }
+
+}  // namespace
+
+int tb200_state_new(tb200_model* m, size_t max_len, int kv_dtype, tb200_state** out) {
+  return state_create(m, 1, max_len, kv_dtype, out);
+}
+
+int tb200_batch_state_new(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb200_state** out) {
+  return state_create(m, n_seqs, max_len, kv_dtype, out);
+}
+
+size_t tb200_state_seqs(const tb200_state* st) { return st ? st->n_seqs : 0; }
 
 int tb200_state_free(tb200_state* st) {
   if (!st) return TB200_OK;
@@ -852,6 +891,7 @@ int tb200_state_free(tb200_state* st) {
   cudaStreamSynchronize(st->dev->stream);
   if (st->graph) cudaGraphExecDestroy(st->graph);
   if (st->graph_short) cudaGraphExecDestroy(st->graph_short);
+  rt::free_batch(st);
   void* ptrs[] = {st->kv, st->rope, st->x, st->qkv, st->att, st->h, st->logits, st->part, st->attn_ticket,
                   st->mv_partial, st->mv_ticket, st->io, st->tokens_out, st->x2, st->part_o};
   for (void* p : ptrs) cudaFree(p);
@@ -866,11 +906,18 @@ int tb200_state_free(tb200_state* st) {
 int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_t n, size_t pos, float* logits,
                   uint32_t* next_token) {
   ARG_CHECK(m && st && st->m == m, "bad model/state");
+  ARG_CHECK(st->n_seqs == 1, "tb200_forward runs one-sequence states; use tb200_forward_seq");
   ARG_CHECK(n > 0 && tokens, "no tokens to run");
   ARG_CHECK(pos + n <= st->max_len, "tokens past the end of the cache");
   if (int rc = use(m->dev)) return rc;
   for (size_t i = 0; i < n; i++)
     ARG_CHECK(tokens[i] < m->c.vocab_size, "token " + std::to_string(tokens[i]) + " is past the vocabulary");
+  // Several tokens (a prompt): the tensor-core path, all tokens at once.
+  if (n >= 2) {
+    if (int rc = rt::forward_tokens(st, 0, tokens, n, pos, logits, next_token)) return rc;
+    st->host_pos = pos + n;
+    return TB200_OK;
+  }
   cudaStream_t s = m->dev->stream;
   CUDA_TRY(cudaMemsetAsync(st->io + 2, 0, 2 * sizeof(int), s));  // step counter, error word
   for (size_t i = 0; i < n; i++) {
@@ -889,6 +936,7 @@ int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_
 
 int tb200_generate(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, size_t steps, uint32_t* out) {
   ARG_CHECK(m && st && st->m == m, "bad model/state");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(out || steps == 0, "null output");
   ARG_CHECK(pos + steps <= st->max_len, "tokens past the end of the cache");
   ARG_CHECK(token < m->c.vocab_size, "token past the vocabulary");
@@ -911,6 +959,7 @@ int tb200_generate(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, 
 
 int tb200_decode_enqueue(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, size_t steps) {
   ARG_CHECK(m && st && st->m == m, "bad model/state");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(pos + steps <= st->max_len, "decode steps past the end of the cache");
   ARG_CHECK(token < m->c.vocab_size, "token past the vocabulary");
   if (int rc = use(m->dev)) return rc;
@@ -923,6 +972,7 @@ int tb200_decode_enqueue(tb200_model* m, tb200_state* st, uint32_t token, size_t
 
 int tb200_enqueue_op(tb200_model* m, tb200_state* st, int op, size_t layer) {
   ARG_CHECK(m && st && st->m == m, "bad model/state");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(op >= TB200_OP_EMBED && op <= TB200_OP_GATE_UP_SUM, "unknown op");
   ARG_CHECK(layer < m->c.num_hidden_layers, "layer out of range");
   if (int rc = use(m->dev)) return rc;
@@ -932,6 +982,7 @@ int tb200_enqueue_op(tb200_model* m, tb200_state* st, int op, size_t layer) {
 
 int tb200_trace_start(tb200_state* st, size_t capacity) {
   ARG_CHECK(st && capacity > 0 && capacity < (size_t(1) << 31), "bad trace capacity");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(!st->trace.rec, "already tracing");
   if (int rc = use(st->dev)) return rc;
   CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
@@ -995,6 +1046,7 @@ int tb200_state_write(tb200_state* st, int which, const float* data, size_t n) {
 
 int tb200_state_set_position(tb200_state* st, uint32_t token, size_t pos) {
   ARG_CHECK(st, "null state");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(pos < st->max_len && token < st->m->c.vocab_size, "token or position out of range");
   if (int rc = use(st->dev)) return rc;
   tb::launch_set_io(st->dev->stream, st->io, int(token), int(pos));

@@ -1,0 +1,147 @@
+// runtime.h — the handles behind include/titania_b200.h and the helpers the
+// C ABI files share (runtime.cu: device, trait ops, single-token path;
+// forward.cu: the many-token and many-sequence paths).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+
+struct tb200_device {
+  int ordinal = 0;
+  int sms = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t* tokens = nullptr;  // device scratch for embed's token ids
+  size_t tokens_cap = 0;
+  unsigned long long* best = nullptr;  // argmax scratch
+  // matmul over several tokens: the input split into three bf16 planes,
+  // and the split-K workspace of the tensor-core contraction
+  uint16_t* split = nullptr;  // [3][split_cap]
+  size_t split_cap = 0;
+  float* gemm_part = nullptr;        // gemm_workspace_max_floats
+  unsigned* gemm_tickets = nullptr;  // [kGemmTickets]
+  int* err = nullptr;                // device error word of the trait ops
+};
+
+struct tb200_buffer {
+  float* ptr = nullptr;
+  size_t len = 0, cap = 0;
+};
+
+struct tb200_weight {
+  uint16_t* ptr = nullptr;
+  std::vector<size_t> shape;
+  size_t numel = 0;
+  bool has_map = false;
+  CUtensorMap map{};  // operand map of a matrix for the tensor-core contraction
+};
+
+struct FusedLayer {
+  const uint16_t *attn_norm, *mlp_norm, *q_norm, *k_norm;
+  uint16_t* wqkv = nullptr;  // [q_dim + 2 kv_dim][H], owned
+  uint16_t* wgu = nullptr;   // [2F][H] gate/up rows interleaved, owned
+  const uint16_t *wo, *wd;
+  uint16_t* wo_packed = nullptr;  // o_proj packed per (kv group, output slice), owned
+  // operand maps of the tensor-core contraction
+  CUtensorMap m_qkv{}, m_o{}, m_gu{}, m_down{};
+};
+
+struct tb200_model {
+  tb200_device* dev = nullptr;
+  int live_states = 0;          // states built on this model
+  bool free_requested = false;  // tb200_model_free came while states lived
+  tb200_config c{};
+  std::map<std::string, const tb200_weight*> bound;
+  bool finalized = false;
+  std::vector<FusedLayer> layers;
+  const uint16_t *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
+  CUtensorMap m_lm{};
+  size_t q_dim = 0, kv_dim = 0;
+  int attn_o_slices = 0;  // output slices per kv group of the fused attention + o_proj
+};
+
+// Operands of the many-token path's contractions, each three bf16 planes:
+// normalised residual [cap][H], attention output [cap][q_dim], silu(g)*u [cap][F].
+enum { kOpXn = 0, kOpAtt, kOpH, kOps };
+
+struct tb200_state {
+  tb200_model* m = nullptr;
+  tb200_device* dev = nullptr;
+  size_t max_len = 0;
+  size_t n_seqs = 1;       // sequences, each with its own cache
+  size_t seq_stride = 0;   // cache elements per sequence
+  int kv_f32 = 0;          // cache element: 0 bf16, 1 f32
+  size_t host_pos = 0;     // the position the next step runs at, as the host knows it
+  unsigned char* kv = nullptr;  // [seq][L][2][Hkv][max_len][head_dim], bf16 or f32
+  float* rope = nullptr;   // [max_len][head_dim]
+  float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+  float *x2 = nullptr, *part_o = nullptr;  // mid-layer residual; per-group o_proj partials
+  float* part = nullptr;
+  unsigned* attn_ticket = nullptr;
+  unsigned long long* mv_partial = nullptr;
+  unsigned* mv_ticket = nullptr;
+  int* io = nullptr;          // device: [0] token, [1] pos, [2] step, [3] error
+  int* tokens_out = nullptr;  // device: [max_len]
+  int* io_host = nullptr;     // pinned: [max_len][2] staged (token, pos) + [4] readback
+  int max_split = 1;
+  tb::MvPlan p_qkv{}, p_o{}, p_gu{}, p_down{}, p_lm{};
+  tb::Trace trace{};       // device trace buffer while tracing
+  uint32_t trace_next = 0;  // next free record slot while capturing
+  cudaGraphExec_t graph = nullptr;        // positions >= kAttnOMaxCtx
+  cudaGraphExec_t graph_short = nullptr;  // positions < kAttnOMaxCtx (fused attention + o_proj)
+
+  // ---- many-token / many-sequence path (forward.cu), allocated on first use
+  int cap = 0;                 // tokens per pass
+  float *bx = nullptr, *bqkv = nullptr, *blogits = nullptr;  // [cap][H], [cap][q+2kv], [n_seqs][V]
+  uint16_t* bact = nullptr;    // the kOps operands' planes, one allocation
+  int* bmeta = nullptr;        // device [3][cap]: token, position, sequence of each row
+  int* bmeta_host = nullptr;   // pinned [3][cap] + readback words
+  float* rows_part = nullptr;  // decode attention split partials
+  unsigned* rows_ticket = nullptr;
+  int rows_max_split = 0;
+  int* bstep = nullptr;        // device [0] step, [1] ticket
+  int* bout = nullptr;         // device [max_len][n_seqs] generated tokens
+  CUtensorMap act[2][kOps][3]{};  // per box height (64, 128 tokens), operand, plane
+  cudaGraphExec_t bgraph = nullptr;  // one decode step of every sequence
+};
+
+namespace rt {
+
+// Records `msg` for tb200_last_error and returns `code`.
+int fail(int code, const std::string& msg);
+// The last launch's error, recorded with `what`.
+int launched(const char* what);
+// Makes `d` the current device.
+int use(tb200_device* d);
+// model.rs:239-250, on the host.
+std::vector<float> rope_table(size_t max_len, size_t head_dim, float theta);
+const char* last_error();
+
+// forward.cu: Model::forward (model.rs:83-91) for `n` tokens of sequence
+// `seq` at positions pos.. through the tensor-core path; the last token's
+// logits go to `logits` (host, or null) and its greedy choice to *next.
+int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n, size_t pos, float* logits,
+                   uint32_t* next);
+// Frees what the many-token path allocated on a state.
+void free_batch(tb200_state* st);
+
+constexpr int kGemmTickets = 4096;
+
+}  // namespace rt
+
+#define CUDA_TRY(expr)                                                                                    \
+  do {                                                                                                    \
+    cudaError_t e_ = (expr);                                                                              \
+    if (e_ != cudaSuccess) return rt::fail(TB200_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define ARG_CHECK(cond, msg)                            \
+  do {                                                  \
+    if (!(cond)) return rt::fail(TB200_ERR_ARG, (msg)); \
+  } while (0)

@@ -284,6 +284,51 @@ class Model:
         """Enqueues one fused kernel of the decode step (TB200_OP_*)."""
         call("tb200_enqueue_op", self._h, state._h, int(op), int(layer))
 
+    # ---- many sequences ----------------------------------------------------
+
+    def batch_state(self, n_seqs: int, max_len: int, kv: str = "f32") -> "BatchState":
+        return BatchState(self, n_seqs, max_len, kv)
+
+    def forward_seq(self, state: "BatchState", seq: int, tokens, pos: int, logits: bool = True, out=None):
+        """Model::forward for sequence `seq` of a many-sequence state."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        nxt = ctypes.c_uint32()
+        if logits and out is None:
+            out = np.empty(self.config.vocab_size, dtype=np.float32)
+        call("tb200_forward_seq", self._h, state._h, int(seq), t.ctypes.data_as(_lib.U32P), t.size, int(pos),
+             out.ctypes.data_as(_lib.F32P) if logits else None, ctypes.byref(nxt))
+        self.last_token = int(nxt.value)
+        return out if logits else self.last_token
+
+    def forward_batch(self, state: "BatchState", tokens, positions, logits: bool = True, out=None):
+        """One decode step of every sequence (token i of sequence i at
+        positions[i]). Returns (logits [n_seqs][vocab] or None, next tokens)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uintp)
+        n = state.n_seqs
+        assert t.size == n and p.size == n
+        if logits and out is None:
+            out = np.empty((n, self.config.vocab_size), dtype=np.float32)
+        nxt = np.empty(n, dtype=np.uint32)
+        call("tb200_forward_batch", self._h, state._h, t.ctypes.data_as(_lib.U32P), p.ctypes.data_as(_lib.SZP),
+             out.ctypes.data_as(_lib.F32P) if logits else None, nxt.ctypes.data_as(_lib.U32P))
+        return (out if logits else None), nxt
+
+    def generate_batch(self, state: "BatchState", tokens, positions, steps: int) -> np.ndarray:
+        """Greedy decoding of every sequence on the device; [steps][n_seqs]."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uintp)
+        out = np.empty((steps, state.n_seqs), dtype=np.uint32)
+        call("tb200_generate_batch", self._h, state._h, t.ctypes.data_as(_lib.U32P), p.ctypes.data_as(_lib.SZP),
+             int(steps), out.ctypes.data_as(_lib.U32P))
+        return out
+
+    def decode_batch_enqueue(self, state: "BatchState", tokens, positions, steps: int) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uintp)
+        call("tb200_decode_batch_enqueue", self._h, state._h, t.ctypes.data_as(_lib.U32P),
+             p.ctypes.data_as(_lib.SZP), int(steps))
+
 
 KV_TYPES = {"bf16": 0, "f32": 1}
 
@@ -350,6 +395,35 @@ class State:
         c = self.model.config
         out = np.empty(c.num_key_value_heads * c.head_dim(), dtype=np.float32)
         call("tb200_state_read_kv", self._h, int(layer), int(which), int(pos), out.ctypes.data_as(_lib.F32P))
+        return out
+
+
+class BatchState:
+    """`n_seqs` independent sequences, each with its own key/value cache of
+    `max_len` positions (what n_seqs separate State::new would hold), run
+    together by Model.forward_batch / generate_batch."""
+
+    def __init__(self, model: Model, n_seqs: int, max_len: int, kv: str = "f32"):
+        if kv not in KV_TYPES:
+            raise ValueError(f"kv must be one of {sorted(KV_TYPES)}")
+        h = ctypes.c_void_p()
+        call("tb200_batch_state_new", model._h, int(n_seqs), int(max_len), KV_TYPES[kv], ctypes.byref(h))
+        self._h = h.value
+        self.model = model
+        self.n_seqs = n_seqs
+        self.max_len = max_len
+        self.kv = kv
+
+    def __del__(self):
+        if getattr(self, "_h", None) and not sys.is_finalizing():
+            _lib.lib().tb200_state_free(self._h)
+        self._h = None
+
+    def read_kv(self, seq: int, layer: int, which: int, pos: int) -> np.ndarray:
+        c = self.model.config
+        out = np.empty(c.num_key_value_heads * c.head_dim(), dtype=np.float32)
+        call("tb200_batch_read_kv", self._h, int(seq), int(layer), int(which), int(pos),
+             out.ctypes.data_as(_lib.F32P))
         return out
 
 
