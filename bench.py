@@ -427,6 +427,22 @@ def profile_op(args):
     print(json.dumps({"profile_op": args.profile_op, "launches": args.launches}))
 
 
+def profile_bs64(args):
+    """For ncu: config 3's 64 x 1024-token prefill (64 passes of 228 kernels),
+    then `--launches` batched decode steps (228 kernels each)."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    dev = tb.B200(0)
+    m = tb.Model.load(synth.cached_model("qwen3-0.6b", seed=0), dev)
+    V = synth.QWEN3_0_6B["vocab_size"]
+    bs = m.batch_state(BS64_SEQS, BS64_CTX + BS64_GEN, kv="bf16")
+    first = [m.forward_seq(bs, i, synth.prompt_tokens(BS64_CTX, V, seed=1000 + i), 0, logits=False)
+             for i in range(BS64_SEQS)]
+    m.decode_batch_enqueue(bs, first, [BS64_CTX] * BS64_SEQS, args.launches)
+    dev.sync()
+    print(json.dumps({"profile_bs64": True, "steps": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,9 +457,14 @@ def main():
     ap.add_argument("--profile-op", choices=["qkv", "attention", "o", "gate_up", "down", "lm_head"],
                     help="small case for ncu: launch one fused kernel only")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--profile-bs64", action="store_true",
+                    help="small case for ncu: the bs64 prefill, then --launches batched decode steps")
     args = ap.parse_args()
     if args.profile_op:
         profile_op(args)
+        return
+    if args.profile_bs64:
+        profile_bs64(args)
         return
     args.warmup = max(args.warmup, 3)
 

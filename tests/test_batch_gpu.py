@@ -139,6 +139,25 @@ def test_tiny_batch_generate(tiny, kv):
         assert [first[i]] + out[:, i].tolist() == expected[i][0][:steps + 1], f"sequence {i}"
 
 
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_tiny_batch_long_contexts(tiny, kv):
+    """Few sequences with long contexts: the decode attention splits each
+    context into parts and combines them (contexts of 1 to 5 parts)."""
+    m, ref = tiny
+    prompts = [synth.prompt_tokens(k, 1024, seed=200 + k) for k in (150, 300, 20)]
+    steps = 4
+    bs = m.batch_state(len(prompts), 400, kv=kv)
+    first = [m.forward_seq(bs, i, p, 0, logits=False) for i, p in enumerate(prompts)]
+    expected = [orc.greedy_generate(ref, p, steps + 1, max_len=400) for p in prompts]
+    tokens, positions = list(first), [len(p) for p in prompts]
+    for step in range(steps):
+        logits, nxt = m.forward_batch(bs, tokens, positions)
+        for i in range(len(prompts)):
+            close(logits[i], expected[i][1][step + 1], REL, ABS)
+            assert int(nxt[i]) == expected[i][0][step + 1]
+        tokens, positions = nxt.tolist(), [p + 1 for p in positions]
+
+
 def test_tiny_batch_forward_logits(tiny):
     """One step of every sequence at once returns each sequence's logits."""
     m, ref = tiny

@@ -8,8 +8,9 @@
 //                    token's position (cpu.rs:96-111), k and v appended to the
 //                    token's sequence cache (model.rs:119-120)
 //   k_attn_rows      decode attention, one query token per sequence: a CTA per
-//                    (token, kv group, run of cache positions), combined in
-//                    split order by the last CTA (cpu.rs:113-149)
+//                    (token, kv group[, part of the context]) streaming the
+//                    cache through a ring of bulk copies with an online
+//                    softmax (cpu.rs:113-149)
 //   k_attn_prefill   causal attention for a run of tokens of one sequence,
 //                    tiled: 64 query rows against 64-position key/value tiles
 //                    with an online softmax
@@ -159,8 +160,10 @@ __global__ void __launch_bounds__(128) k_qkv_post(QkvPostArgs a) {
 template <bool F32KV>
 struct RowsCfg {
   using KV = typename std::conditional<F32KV, float, uint16_t>::type;
-  static constexpr int kCh = F32KV ? 64 : 128;  // positions per CTA: 32 KB each of K and V
-  static constexpr size_t kSmem = size_t(2) * kCh * kD * sizeof(KV);
+  static constexpr int kCh = F32KV ? 32 : 64;  // positions per chunk: 16 KB each of K and V
+  static constexpr int kStages = 3;            // chunks in flight
+  static constexpr size_t kStageBytes = size_t(2) * kCh * kD * sizeof(KV);
+  static constexpr size_t kSmem = kStages * kStageBytes;
 };
 
 __device__ __forceinline__ void load4(const float* p, float (&o)[4]) {
@@ -174,162 +177,190 @@ __device__ __forceinline__ void load4(const uint16_t* p, float (&o)[4]) {
 __device__ __forceinline__ float load1(const float* p) { return *p; }
 __device__ __forceinline__ float load1(const uint16_t* p) { return bf16f(*p); }
 
-// CTA (split, kv group g, token t): positions [split*kCh, ...) of the token's
-// sequence up to its position. Scores with a thread per (position, head),
-// reading key rows in rotated 4-element groups (conflict-free), the chunk's
-// softmax, then weighted values with a thread per dimension.
+// CTA (part, kv group g, token t): the token's sequence from position
+// part * span up to its own position, in chunks of kCh positions streamed by
+// bulk copy through a ring of kStages chunks, with an online softmax
+// (running max and sum per head). Per chunk: scores with a thread per
+// (position, head) reading key rows in rotated 4-element groups
+// (conflict-free), the chunk's statistics per head (a warp per head), then
+// the weighted values with a thread per dimension. One part covers the
+// whole context when the batch alone fills the GPU; otherwise the parts'
+// partial results are combined in part order by the last CTA.
 template <int GRP, bool F32KV>
 __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   using Cf = RowsCfg<F32KV>;
   using KV = typename Cf::KV;
-  constexpr int CH = Cf::kCh;
+  constexpr int CH = Cf::kCh, NS = Cf::kStages;
   extern __shared__ __align__(128) unsigned char smem[];
-  KV* ks = reinterpret_cast<KV*>(smem);
-  KV* vs = ks + size_t(CH) * kD;
   __shared__ __align__(16) float qs[GRP][kD];
   __shared__ float ps[GRP][CH];
-  __shared__ float stat[GRP][2];  // chunk max, chunk sum
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ int is_last;
+  __shared__ float corr_s[GRP], m_s[GRP], l_s[GRP];
+  __shared__ __align__(8) uint64_t bar[NS];
+  __shared__ int verdict, is_last;
+  auto kst = [&](int s) { return reinterpret_cast<KV*>(smem + size_t(s) * Cf::kStageBytes); };
+  auto vst = [&](int s) { return kst(s) + size_t(CH) * kD; };
 
   pdl_launch_dependents();
-  const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Positions and sequence ids change only between steps (the host, or the
   // step's last kernel), so they can be read before the dependency wait.
   const int pos = a.pos[t], seq = a.seq[t];
   const bool ok = pos >= 0 && pos < a.max_len && seq >= 0 && seq < a.n_seqs;
   const int ctx = pos + 1;
-  const int nsplit = (ctx + CH - 1) / CH;
-  const bool active = ok && split < nsplit && nsplit <= a.max_split;
-  const int p0 = split * CH, p1 = active ? min(ctx, p0 + CH) : p0;
-  const int n = p1 - p0;
-  const int cached = active ? max(0, min(p1, pos) - p0) : 0;  // rows written by earlier steps
+  const int span = ((ctx + a.parts - 1) / a.parts + CH - 1) / CH * CH;  // positions per part, whole chunks
+  const int nparts = (ctx + span - 1) / span;
+  const bool active = ok && part < nparts;
+  const int p0 = part * span, p1 = active ? min(ctx, p0 + span) : p0;
+  const int nchunks = (p1 - p0 + CH - 1) / CH;
   const size_t head = size_t(seq) * a.seq_stride + size_t(g) * a.max_len * kD;
   const size_t v_off = size_t(a.n_kv_heads) * a.max_len * kD;
   const KV* kc = static_cast<const KV*>(a.kv) + head;
   const KV* vc = kc + v_off;
+  const uint64_t pol = l2_evict_first();
+  // Chunk i -> stage i % NS, completing on bar[i % NS].
+  auto issue = [&](int i) {
+    const int c0 = p0 + i * CH, n = min(CH, p1 - c0);
+    const uint32_t bytes = uint32_t(n) * kD * sizeof(KV);
+    uint64_t* b = &bar[i % NS];
+    mbar_arrive_expect_tx(b, 2 * bytes);
+    bulk_g2s(kst(i % NS), kc + size_t(c0) * kD, bytes, b, pol);
+    bulk_g2s(vst(i % NS), vc + size_t(c0) * kD, bytes, b, pol);
+  };
 
+  int issued = 0;
   if (active) {
     if (tid == 0) {
-      mbar_init(&bar, 1);
+      for (int s = 0; s < NS; s++) mbar_init(&bar[s], 1);
       fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0 && cached > 0) {
-      const uint32_t bytes = uint32_t(cached) * kD * sizeof(KV);
-      const uint64_t pol = l2_evict_first();
-      mbar_arrive_expect_tx(&bar, 2 * bytes);
-      bulk_g2s(ks, kc + size_t(p0) * kD, bytes, &bar, pol);
-      bulk_g2s(vs, vc + size_t(p0) * kD, bytes, &bar, pol);
+      // Chunks before the token's own position were written by earlier
+      // steps: they go out before the dependency wait.
+      while (issued < NS && issued < nchunks && p0 + (issued + 1) * CH <= pos) issue(issued++);
     }
   }
   pdl_wait();
   if (!ok) {
-    if (split == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
+    if (part == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
     return;
   }
   if (!active) return;
-  // The token's own key and value were appended by the previous kernel.
-  if (p1 == ctx) {
-    ks[size_t(pos - p0) * kD + tid] = kc[size_t(pos) * kD + tid];
-    vs[size_t(pos - p0) * kD + tid] = vc[size_t(pos) * kD + tid];
-  }
+  if (tid == 0)
+    while (issued < NS && issued < nchunks) issue(issued++);
   for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
-  if (cached > 0) {
-    // One thread waits with the time limit and the CTA follows its verdict.
-    if (tid == 0) is_last = mbar_wait(&bar, 0, a.err) ? 1 : 0;
-    __syncthreads();
-    if (!is_last) {
-      if (tid == 0) mbar_wait(&bar, 0, nullptr);  // one more bounded wait for the copy in flight
-      return;
-    }
-    mbar_wait(&bar, 0, nullptr);  // the phase is complete: returns at once
+  if (tid < GRP) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.f;
   }
-  __syncthreads();
 
-  // Scores: thread -> (position p, head h); rotated groups of 4 elements.
   const float scale = 1.0f / sqrtf(float(kD));
-  for (int i = tid; i < GRP * CH; i += 128) {
-    const int h = i / CH, p = i % CH;
-    float s = -INFINITY;
-    if (p < n) {
-      const KV* kr = ks + size_t(p) * kD;
-      float acc = 0.f;
+  float acc[GRP];
+#pragma unroll
+  for (int h = 0; h < GRP; h++) acc[h] = 0.f;
+  bool failed = false;
+  for (int i = 0; i < nchunks; i++) {
+    const int s = i % NS;
+    const int c0 = p0 + i * CH, n = min(CH, p1 - c0);
+    // One thread waits with the time limit and the CTA follows its verdict.
+    if (tid == 0) verdict = mbar_wait(&bar[s], (i / NS) & 1, a.err) ? 1 : 0;
+    __syncthreads();  // also: qs and the previous chunk's statistics are visible
+    if (!verdict) {
+      failed = true;
+      break;
+    }
+    mbar_wait(&bar[s], (i / NS) & 1, nullptr);  // the phase is complete: returns at once
+    const KV* ks = kst(s);
+    const KV* vs = vst(s);
+    for (int idx = tid; idx < GRP * CH; idx += 128) {
+      const int h = idx / CH, p = idx % CH;
+      float sc = -INFINITY;
+      if (p < n) {
+        const KV* kr = ks + size_t(p) * kD;
+        float d = 0.f;
 #pragma unroll 8
-      for (int j = 0; j < 32; j++) {
-        const int c = 4 * ((j + p) & 31);
-        float k4[4];
-        load4(kr + c, k4);
-        const float4 q4 = *reinterpret_cast<const float4*>(&qs[h][c]);
-        acc = fmaf(q4.x, k4[0], acc);
-        acc = fmaf(q4.y, k4[1], acc);
-        acc = fmaf(q4.z, k4[2], acc);
-        acc = fmaf(q4.w, k4[3], acc);
+        for (int j = 0; j < 32; j++) {
+          const int c = 4 * ((j + p) & 31);
+          float k4[4];
+          load4(kr + c, k4);
+          const float4 q4 = *reinterpret_cast<const float4*>(&qs[h][c]);
+          d = fmaf(q4.x, k4[0], d);
+          d = fmaf(q4.y, k4[1], d);
+          d = fmaf(q4.z, k4[2], d);
+          d = fmaf(q4.w, k4[3], d);
+        }
+        sc = scale * d;
       }
-      s = scale * acc;
+      ps[h][p] = sc;
     }
-    ps[h][p] = s;
-  }
-  __syncthreads();
-  // Chunk softmax statistics: warp w takes heads w, w + 4, ...
-  for (int h = warp; h < GRP; h += 4) {
-    float m = -INFINITY;
-    for (int p = lane; p < n; p += 32) m = fmaxf(m, ps[h][p]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int p = lane; p < n; p += 32) {
-      const float e = expf(ps[h][p] - m);
-      ps[h][p] = e;
-      l += e;
+    __syncthreads();
+    for (int h = warp; h < GRP; h += 4) {
+      float mx = -INFINITY;
+      for (int p = lane; p < n; p += 32) mx = fmaxf(mx, ps[h][p]);
+      mx = warp_max(mx);
+      const float mo = m_s[h];
+      const float mn = fmaxf(mo, mx);
+      float sum = 0.f;
+      for (int p = lane; p < n; p += 32) {
+        const float e = expf(ps[h][p] - mn);
+        ps[h][p] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        const float c = expf(mo - mn);  // 0 on the first chunk (mo = -inf)
+        corr_s[h] = c;
+        m_s[h] = mn;
+        l_s[h] = l_s[h] * c + sum;
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      stat[h][0] = m;
-      stat[h][1] = l;
-    }
-  }
-  __syncthreads();
-  // Weighted values: thread d of every head.
-  float o[GRP];
+    __syncthreads();
 #pragma unroll
-  for (int h = 0; h < GRP; h++) o[h] = 0.f;
-  for (int p = 0; p < n; p++) {
-    const float v = load1(vs + size_t(p) * kD + tid);
+    for (int h = 0; h < GRP; h++) acc[h] *= corr_s[h];
+    for (int p = 0; p < n; p++) {
+      const float v = load1(vs + size_t(p) * kD + tid);
 #pragma unroll
-    for (int h = 0; h < GRP; h++) o[h] = fmaf(ps[h][p], v, o[h]);
+      for (int h = 0; h < GRP; h++) acc[h] = fmaf(ps[h][p], v, acc[h]);
+    }
+    __syncthreads();  // every thread is done with stage s and ps
+    if (tid == 0 && issued < nchunks) issue(issued++);
   }
+  if (failed) {
+    // Let the copies in flight land (bounded) before the CTA's memory goes.
+    if (tid == 0)
+      for (int i = max(0, issued - NS); i < issued; i++) mbar_wait(&bar[i % NS], (i / NS) & 1, nullptr);
+    return;
+  }
+
   const size_t out_at = size_t(t) * a.ldo + size_t(g) * GRP * kD + tid;
-  if (nsplit == 1) {
+  if (nparts == 1) {
 #pragma unroll
-    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, o[h] / stat[h][1]);
+    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, acc[h] / l_s[h]);
     return;
   }
   const int stride = kD + 2;
-  float* part = a.part + ((size_t(t) * a.n_kv_heads + g) * a.max_split) * GRP * stride;
+  float* pbase = a.part + ((size_t(t) * a.n_kv_heads + g) * a.parts) * GRP * stride;
 #pragma unroll
   for (int h = 0; h < GRP; h++) {
-    float* pp = part + (size_t(split) * GRP + h) * stride;
-    pp[2 + tid] = o[h];
+    float* pp = pbase + (size_t(part) * GRP + h) * stride;
+    pp[2 + tid] = acc[h];
     if (tid == 0) {
-      pp[0] = stat[h][0];
-      pp[1] = stat[h][1];
+      pp[0] = m_s[h];
+      pp[1] = l_s[h];
     }
   }
   __threadfence();
   __syncthreads();
   unsigned* ticket = a.ticket + size_t(t) * a.n_kv_heads + g;
-  if (tid == 0) is_last = atomicAdd(ticket, 1u) == unsigned(nsplit - 1);
+  if (tid == 0) is_last = atomicAdd(ticket, 1u) == unsigned(nparts - 1);
   __syncthreads();
   if (!is_last) return;
   __threadfence();
 #pragma unroll
   for (int h = 0; h < GRP; h++) {
     float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(part + (size_t(sp) * GRP + h) * stride));
+    for (int sp = 0; sp < nparts; sp++) M = fmaxf(M, __ldcg(pbase + (size_t(sp) * GRP + h) * stride));
     float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < nsplit; sp++) {
-      const float* pp = part + (size_t(sp) * GRP + h) * stride;
+    for (int sp = 0; sp < nparts; sp++) {
+      const float* pp = pbase + (size_t(sp) * GRP + h) * stride;
       const float wt = expf(__ldcg(pp) - M);
       L += __ldcg(pp + 1) * wt;
       O += __ldcg(pp + 2 + tid) * wt;
@@ -515,6 +546,31 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(ArgmaxRowsArgs a) {
   }
 }
 
+// One CTA: the token ids from the keys a contraction folded into best[],
+// which it zeroes for the next step.
+__global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigned long long* best, int rows) {
+  __shared__ int step_s;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x == 0) step_s = a.step ? *a.step : 0;
+  __syncthreads();
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    const unsigned long long k = best[r];
+    best[r] = 0ull;
+    int tok = int(argmax_index(k));
+    if (k == 0ull || tok < 0 || tok >= a.V) {  // no key arrived: a contraction failed
+      set_error(a.err, TB200_ERR_TIMEOUT);
+      tok = 0;
+    }
+    if (a.next) a.next[r] = tok;
+    if (a.tok) a.tok[r] = tok;
+    if (a.pos) a.pos[r] += 1;
+    if (a.out && step_s < a.out_cap) a.out[size_t(step_s) * rows + r] = tok;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && a.step) *a.step = step_s + 1;
+}
+
 template <int G, bool F>
 cudaError_t rows_attr() {
   cudaError_t e = cudaFuncSetAttribute(k_attn_rows<G, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -544,6 +600,14 @@ bool batch_group_supported(int group) { return group == 1 || group == 2 || group
 
 int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<false>::kCh; }
 
+int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms) {
+  // Enough CTAs for two per SM; never a part shorter than one chunk.
+  const int units = std::max(1, tokens * n_kv_heads);
+  const int want = (2 * sms + units - 1) / units;
+  const int chunks = (max_len + attn_rows_chunk(kv_f32) - 1) / attn_rows_chunk(kv_f32);
+  return std::max(1, std::min(want, chunks));
+}
+
 void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t plane, size_t n, bool pdl) {
   const unsigned grid = unsigned(std::min<size_t>((n + 255) / 256, 4096));
   if (n) launch_pdl(s, dim3(grid), dim3(256), 0, pdl, k_split_rows, x, out, plane, n);
@@ -560,7 +624,7 @@ void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl)
 
 void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl) {
   if (tokens <= 0) return;
-  const dim3 grid(unsigned(a.max_split), unsigned(a.n_kv_heads), unsigned(tokens));
+  const dim3 grid(unsigned(a.parts), unsigned(a.n_kv_heads), unsigned(tokens));
 #define TB_ROWS(G)                                                                                   \
   if (group == G) {                                                                                  \
     if (a.kv_f32) launch_pdl(s, grid, dim3(128), RowsCfg<true>::kSmem, pdl, k_attn_rows<G, true>, a); \
@@ -589,6 +653,10 @@ void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bo
   TB_PRE(4)
   TB_PRE(8)
 #undef TB_PRE
+}
+
+void launch_argmax_finish(cudaStream_t s, const ArgmaxRowsArgs& a, unsigned long long* best, int rows, bool pdl) {
+  if (rows > 0) launch_pdl(s, dim3(1), dim3(256), 0, pdl, k_argmax_finish, a, best, rows);
 }
 
 void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl) {

@@ -70,8 +70,8 @@ int ensure_batch(tb200_state* st) {
   ARG_CHECK(tb::batch_group_supported(int(group)), "the many-token path needs 1, 2, 4 or 8 query heads per kv head");
   const size_t cap = round_up(std::max(st->n_seqs, std::min<size_t>(st->max_len, 1024)), 128);
   const size_t qkv_w = m->q_dim + 2 * m->kv_dim;
-  const int chunk = tb::attn_rows_chunk(st->kv_f32 != 0);
-  const size_t max_split = (st->max_len + chunk - 1) / chunk;
+  const size_t parts = size_t(tb::attn_rows_parts(int(st->n_seqs), int(Hkv), int(st->max_len), st->kv_f32 != 0,
+                                                      m->dev->sms));
   cudaStream_t s = m->dev->stream;
   cudaError_t e = cudaSuccess;
   auto A = [&](void** p, size_t bytes) {
@@ -84,9 +84,10 @@ int ensure_batch(tb200_state* st) {
   A((void**)&st->blogits, st->n_seqs * V * 4);
   A((void**)&st->bact, 3 * cap * (H + m->q_dim + F) * 2);
   A((void**)&st->bmeta, 3 * cap * 4);
-  A((void**)&st->rows_part, st->n_seqs * Hkv * max_split * group * (D + 2) * 4);
+  A((void**)&st->rows_part, st->n_seqs * Hkv * parts * group * (D + 2) * 4);
   A((void**)&st->rows_ticket, st->n_seqs * Hkv * 4);
   A((void**)&st->bstep, 4 * 4);
+  A((void**)&st->bbest, st->n_seqs * 8);
   A((void**)&st->bout, st->max_len * st->n_seqs * 4);
   // Staging: a region per prompt position (passes of one call never share
   // one), then a decode step's rows.
@@ -98,7 +99,7 @@ int ensure_batch(tb200_state* st) {
     rt::free_batch(st);
     return fail(TB200_ERR_CUDA, std::string("batch workspace: ") + cudaGetErrorString(e));
   }
-  st->rows_max_split = int(max_split);
+  st->rows_parts = int(parts);
   for (int b = 0; b < 2; b++)
     for (int op = 0; op < kOps; op++)
       for (int pl = 0; pl < 3; pl++) {
@@ -118,9 +119,9 @@ int* readback(tb200_state* st) { return st->bmeta_host + 3 * (st->max_len + size
 // One contraction over T rows: weights `w`, activation operand `op`; the
 // kGemmSilu epilogue writes operand kOpH.
 void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, int epi, float* out, int ldo,
-          bool pdl) {
+          bool pdl, unsigned long long* best = nullptr) {
   tb200_device* d = st->dev;
-  const tb::GemmPlan p = tb::plan_gemm(M, K, T, d->sms);
+  const tb::GemmPlan p = tb::plan_gemm(M, K, T, d->sms, d->max_cluster);
   const int bi = p.bn == 64 ? 0 : 1;
   tb::GemmArgs a{};
   a.M = M;
@@ -133,9 +134,8 @@ void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, in
     a.plane = plane(st, kOpH);
     a.ldh = int(width(st, kOpH));
   }
-  a.part = d->gemm_part;
-  a.tickets = d->gemm_tickets;
   a.err = st->io + 3;
+  a.best = best;
   tb::launch_gemm(d->stream, p, epi, w, st->act[bi][op], a, pdl);
 }
 
@@ -208,7 +208,7 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
       a.ldo = qd;
       a.part = st->rows_part;
       a.ticket = st->rows_ticket;
-      a.max_split = st->rows_max_split;
+      a.parts = st->rows_parts;
       a.err = err;
       tb::launch_attn_rows(s, a, T, group, pdl);
     }
@@ -221,14 +221,17 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
 
 // Final norm, lm_head and greedy choice for rows row0 .. row0 + rows - 1 of
 // the pass (model.rs:144-147); logits land in blogits rows 0 .. rows - 1.
-void enqueue_head(tb200_state* st, int row0, int rows, const tb::ArgmaxRowsArgs& am, bool pdl) {
+// The contraction folds each row's argmax key into bbest as it stores the
+// logits; a one-CTA kernel turns the keys into token ids.
+void enqueue_head(tb200_state* st, int row0, int rows, tb::ArgmaxRowsArgs am, bool pdl) {
   tb200_model* m = st->m;
   const tb200_config& c = m->c;
   const int H = int(c.hidden_size), V = int(c.vocab_size);
   cudaStream_t s = m->dev->stream;
   tb::launch_norm_split(s, st->bx, row0, rows, H, m->norm, c.rms_norm_eps, operand(st, kOpXn), plane(st, kOpXn), pdl);
-  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl);
-  tb::launch_argmax_rows(s, am, rows, pdl);
+  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest);
+  am.err = st->io + 3;
+  tb::launch_argmax_finish(s, am, st->bbest, rows, pdl);
 }
 
 // One decode step of every sequence; rows' tokens and positions in bmeta.
@@ -320,12 +323,13 @@ void free_batch(tb200_state* st) {
   if (st->bgraph) cudaGraphExecDestroy(st->bgraph);
   st->bgraph = nullptr;
   void* ptrs[] = {st->bx, st->bqkv, st->blogits, st->bact, st->bmeta, st->rows_part, st->rows_ticket, st->bstep,
-                  st->bout};
+                  st->bout, st->bbest};
   for (void* p : ptrs) cudaFree(p);
   if (st->bmeta_host) cudaFreeHost(st->bmeta_host);
   st->bx = st->bqkv = st->blogits = st->rows_part = nullptr;
   st->bact = nullptr;
   st->bmeta = st->bmeta_host = st->bstep = st->bout = nullptr;
+  st->bbest = nullptr;
   st->rows_ticket = nullptr;
   st->cap = 0;
 }

@@ -24,8 +24,9 @@
 //   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, then store,
 //               residual add, or SiLU(gate)·up of interleaved row pairs split
 //               again into three bf16 planes for the next contraction.
-// Split-K partials go to a workspace; the last CTA of a tile (ticket) sums
-// them in split order, so results do not depend on scheduling.
+// Split-K runs the K ranges of a tile as the CTAs of one thread-block
+// cluster, which sum their partial tiles over distributed shared memory in
+// split order, so results do not depend on scheduling.
 //
 // Every mbarrier wait is bounded (kWaitNs); on expiry the kernel records
 // TB200_ERR_TIMEOUT, lets what it issued drain (bounded), frees its tensor
@@ -34,6 +35,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 
@@ -48,6 +51,9 @@ constexpr int kBM = 128;          // weight rows per tile (MMA M)
 constexpr int kBK = 64;           // K per stage: one 128-byte swizzle row of bf16
 constexpr int kGemmThreads = 192;
 constexpr int kStageA = kBM * kBK * 2;  // 16 KB
+// Shared memory after the barriers: tensor-memory slot, flags, and the
+// epilogue warps' argmax keys [4][128].
+constexpr size_t kExtra = 64 + 4 * 128 * 8;
 
 template <int BN>
 struct Cfg {
@@ -55,8 +61,8 @@ struct Cfg {
   static constexpr int kStage = kStageA + 3 * kStageB;  // bytes per stage
   static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  // tiles + barriers + tensor-memory slot + flag, plus alignment slack
-  static constexpr size_t kSmem = size_t(kStages) * kStage + (2 * kStages + 1) * 8 + 64 + 1024;
+  // tiles + barriers + tensor-memory slot + flags + argmax keys, plus alignment slack
+  static constexpr size_t kSmem = size_t(kStages) * kStage + (2 * kStages + 1) * 8 + kExtra + 1024;
 };
 
 // ---- tcgen05 / TMA wrappers -------------------------------------------------
@@ -155,6 +161,30 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& a, int row, int t
   }
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster; orders shared-memory writes
+// before the barrier with reads by other CTAs after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float in the shared memory of cluster CTA `rank`, at this CTA's offset `saddr`.
+__device__ __forceinline__ float ld_cluster(uint32_t saddr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// One CTA per (row tile, token tile, K range). With a.splits > 1 the K
+// ranges of a tile are the CTAs of one cluster (cluster dims 1 x 1 x splits):
+// each leaves its partial tile in its own shared memory and cluster CTA r
+// sums the splits, in split order, for its slice of the tokens (DSMEM), so
+// the reduction runs on every CTA of the cluster at once.
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx0,
@@ -164,12 +194,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // The swizzled tiles need 1024-byte alignment.
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(C::kStages) * C::kStage);
-  uint64_t* empty = full + C::kStages;
-  uint64_t* tfull = empty + C::kStages;
+  const int stages = a.stages;  // 1 .. C::kStages, sized by the host to the K range
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * C::kStage);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
-  int* last_flag = reinterpret_cast<int*>(tslot + 1);
-  int* warp_ok = last_flag + 1;  // [4] per epilogue warp
+  int* warp_ok = reinterpret_cast<int*>(tslot + 1);  // [4] per epilogue warp, then [4] the verdict
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(tfull + 8);  // [4][128] argmax keys
   auto sA = [&](int s) { return sm + size_t(s) * C::kStage; };
   auto sB = [&](int s, int plane) { return sm + size_t(s) * C::kStage + kStageA + plane * C::kStageB; };
 
@@ -183,11 +214,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; s++) {
+    for (int s = 0; s < stages; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
+    warp_ok[4] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tslot, C::kTmemCols);
@@ -201,7 +233,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Producer. Weights do not depend on earlier kernels: the first
       // stages' weight boxes go out before the dependency wait.
       const uint64_t pol_w = l2_evict_first(), pol_x = l2_evict_last();
-      const int pre = nk < C::kStages ? nk : C::kStages;
+      const int pre = nk < stages ? nk : stages;
       for (int i = 0; i < pre; i++) {
         mbar_arrive_expect_tx(&full[i], C::kStage);
         tma_load_2d(sA(i), &tw, (kb0 + i) * kBK, m0, &full[i], pol_w);
@@ -214,8 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       int issued = pre;
       for (int i = pre; i < nk; i++) {
-        const int s = i % C::kStages;
-        if (!mbar_wait(&empty[s], ((i / C::kStages) & 1) ^ 1, a.err)) break;
+        const int s = i % stages;
+        if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, a.err)) break;
         mbar_arrive_expect_tx(&full[s], C::kStage);
         tma_load_2d(sA(s), &tw, (kb0 + i) * kBK, m0, &full[s], pol_w);
         tma_load_2d(sB(s, 0), &tx0, (kb0 + i) * kBK, n0, &full[s], pol_x);
@@ -225,8 +257,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       // Drain: every issued copy has landed before the CTA can exit (on the
       // normal path the MMA warp already waited for each of them).
-      for (int i = issued - 1; i >= 0 && i >= issued - C::kStages; i--)
-        mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1, nullptr);
+      for (int i = issued - 1; i >= 0 && i >= issued - stages; i--)
+        mbar_wait(&full[i % stages], (i / stages) & 1, nullptr);
     } else {
       pdl_wait();
     }
@@ -235,8 +267,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(kBM, BN);
       for (int i = 0; i < nk; i++) {
-        const int s = i % C::kStages;
-        if (!mbar_wait(&full[s], (i / C::kStages) & 1, a.err)) break;
+        const int s = i % stages;
+        if (!mbar_wait(&full[s], (i / stages) & 1, a.err)) break;
         tc_fence_after();
         const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s, 0));
 #pragma unroll
@@ -262,10 +294,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool row_ok = row < a.M;
     bool ok = nk > 0 && mbar_wait(tfull, 0, a.err);
     ok = __all_sync(0xffffffffu, ok);
-    // The four epilogue warps take the same branches below (named barriers).
+    // The four epilogue warps take the same branches below.
     if (lane == 0) warp_ok[q] = ok ? 1 : 0;
     named_sync(1, 128);
     ok = warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3];
+    if (warp == 2 && lane == 0) warp_ok[4] = ok ? 1 : 0;
     tc_fence_after();
     const uint32_t taddr = tmem + (uint32_t(32 * q) << 16);
     if (ok && a.splits == 1) {
@@ -277,39 +310,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int j = 0; j < 16; j++) {
           const int t = n0 + c + j;
           epilogue_store<EPI>(a, row, t, v[j], row_ok && t < a.T);
+          if (EPI == kGemmStore && a.best) {
+            const unsigned long long k = warp_umax64(row_ok ? argmax_key(v[j], uint32_t(row)) : 0ull);
+            if (lane == 0) keys[q * 128 + c + j] = k;
+          }
+        }
+      }
+      if (EPI == kGemmStore && a.best) {
+        // One atomic per token and CTA: the best of the four warps' rows.
+        named_sync(1, 128);
+        const int j = threadIdx.x - 64;
+        if (j < BN && n0 + j < a.T) {
+          unsigned long long k = keys[j];
+#pragma unroll
+          for (int w = 1; w < 4; w++) k = keys[w * 128 + j] > k ? keys[w * 128 + j] : k;
+          atomicMax(a.best + n0 + j, k);
         }
       }
     } else if (ok) {
-      // Split-K: this CTA's partial sums to the workspace [split][T][M].
+      // This split's partial tile into the (now idle) stage memory, [token][row].
+      float* red = reinterpret_cast<float*>(sm);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float v[16];
         tmem_ld16(taddr + c, v);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int t = n0 + c + j;
-          if (row_ok && t < a.T) a.part[(size_t(z) * a.T + t) * a.M + row] = v[j];
-        }
-      }
-      __threadfence();
-      named_sync(1, 128);
-      unsigned* ticket = a.tickets + (size_t(mt) * gridDim.y + nt);
-      if (warp == 2 && lane == 0) *last_flag = atomicAdd(ticket, 1u) == unsigned(a.splits - 1);
-      named_sync(1, 128);
-      if (*last_flag) {
-        __threadfence();
-        const int tn = min(BN, a.T - n0);
-#pragma unroll 1
-        for (int j = 0; j < tn; j++) {
-          const int t = n0 + j;
-          float v = 0.f;
-          if (row_ok)
-            for (int zz = 0; zz < a.splits; zz++) v += __ldcg(a.part + (size_t(zz) * a.T + t) * a.M + row);
-          epilogue_store<EPI>(a, row, t, v, row_ok);
-        }
-        if (warp == 2 && lane == 0) *ticket = 0u;
+        for (int j = 0; j < 16; j++) red[(c + j) * kBM + 32 * q + lane] = v[j];
       }
     }
+  }
+
+  if (a.splits > 1) {
+    __syncwarp();
+    cluster_sync_all();  // every split's partial tile is in place
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const int row = m0 + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      const int per = (BN + a.splits - 1) / a.splits;
+      const int j0 = int(cluster_rank()) * per, j1 = min(BN, j0 + per);
+      const uint32_t base = smem_u32(sm) + uint32_t(32 * q + lane) * 4;
+      if (warp_ok[4]) {
+#pragma unroll 1
+        for (int j = j0; j < j1; j++) {
+          const uint32_t at = base + uint32_t(j * kBM) * 4;
+          float v = 0.f;
+#pragma unroll 4
+          for (int r = 0; r < a.splits; r++) v += ld_cluster(at, uint32_t(r));
+          const int t = n0 + j;
+          epilogue_store<EPI>(a, row, t, v, row_ok && t < a.T);
+          if (EPI == kGemmStore && a.best) {
+            const unsigned long long k = warp_umax64(row_ok ? argmax_key(v, uint32_t(row)) : 0ull);
+            if (lane == 0 && t < a.T) atomicMax(a.best + t, k);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while another still reads its tile
   }
 
   tc_fence_before();
@@ -327,7 +385,15 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 template <int BN, int EPI>
 cudaError_t set_smem() {
-  return cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<BN>::kSmem));
+  cudaError_t e =
+      cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<BN>::kSmem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
+template <int BN>
+size_t smem_for(int stages) {
+  return size_t(stages) * Cfg<BN>::kStage + (2 * size_t(stages) + 1) * 8 + kExtra + 1024;
 }
 
 template <int BN, int EPI>
@@ -336,13 +402,24 @@ void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = p.grid;
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = Cfg<BN>::kSmem;
+  cfg.dynamicSmemBytes = smem_for<BN>(p.stages);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (p.splits > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = unsigned(p.splits);
+    n++;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, k_gemm<BN, EPI>, tw, tx[0], tx[1], tx[2], a);
 }
 
@@ -384,22 +461,21 @@ int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t col
 
 int gemm_box_rows(int tokens) { return tokens <= 64 ? 64 : 128; }
 
-GemmPlan plan_gemm(int M, int K, int T, int sms) {
+GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster) {
   GemmPlan p{};
   p.bn = gemm_box_rows(T);
   const int mtiles = (M + kBM - 1) / kBM, ntiles = (T + p.bn - 1) / p.bn;
   const int nkb = (K + kBK - 1) / kBK;
   int splits = 1;
   const int tiles = mtiles * ntiles;
-  if (tiles < sms) splits = std::max(1, std::min(nkb, sms / tiles));
+  // Split K across the CTAs of a cluster when the tiles alone leave SMs idle.
+  if (tiles < sms) splits = std::max(1, std::min({nkb, sms / tiles, max_cluster}));
   p.kb_per_split = (nkb + splits - 1) / splits;
   p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  const int max_stages = p.bn == 64 ? Cfg<64>::kStages : Cfg<128>::kStages;
+  p.stages = std::min(max_stages, p.kb_per_split);
   p.grid = dim3(unsigned(mtiles), unsigned(ntiles), unsigned(p.splits));
   return p;
-}
-
-size_t gemm_workspace_floats(const GemmPlan& p, int M, int T) {
-  return p.splits > 1 ? size_t(p.splits) * size_t(T) * size_t(M) : 0;
 }
 
 cudaError_t init_gemm_kernels() {
@@ -414,11 +490,33 @@ cudaError_t init_gemm_kernels() {
   return e;
 }
 
+int gemm_max_cluster() {
+  for (unsigned n : {16u, 8u, 4u, 2u}) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1, 1, n);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg<64>::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = n;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k_gemm<64, kGemmStore>, &cfg) == cudaSuccess && clusters > 0)
+      return int(n);
+    cudaGetLastError();  // an unsupported size is not an error of ours
+  }
+  return 1;
+}
+
 void launch_gemm(cudaStream_t s, const GemmPlan& p, int epi, const CUtensorMap& tw, const CUtensorMap* tx,
                  const GemmArgs& a, bool pdl) {
   GemmArgs b = a;
   b.kb_per_split = p.kb_per_split;
   b.splits = p.splits;
+  b.stages = p.stages;
 #define TB_GEMM_CASE(BN)                                                        \
   if (p.bn == BN) {                                                             \
     if (epi == kGemmStore) launch_tile<BN, kGemmStore>(s, p, tw, tx, b, pdl);   \

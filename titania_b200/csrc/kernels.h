@@ -164,19 +164,21 @@ enum GemmEpilogue {
 };
 struct GemmArgs {
   int M, K, T;              // weight rows, columns (reduction), tokens
-  int kb_per_split, splits;  // set by launch_gemm from the plan
+  int kb_per_split, splits, stages;  // set by launch_gemm from the plan
   float* out;               // kGemmStore / kGemmResid: [T][ldo]
   int ldo;
   uint16_t* out_split;      // kGemmSilu: three bf16 planes [T][ldh], `plane` elements apart
   size_t plane;
   int ldh;
-  float* part;              // split-K workspace, gemm_workspace_floats()
-  unsigned* tickets;        // split-K: one per tile, zero between launches
+  unsigned long long* best;  // kGemmStore: per token, the argmax key (argmax_key) of its
+                             // outputs is folded in with atomicMax; null: none
   int* err;
 };
 struct GemmPlan {
   int bn;            // tokens per tile (box rows of the activation maps)
-  int splits, kb_per_split;
+  int splits;        // K ranges per tile = cluster size (1: no cluster)
+  int kb_per_split;  // 64-column K blocks per range
+  int stages;        // shared-memory ring depth
   dim3 grid;         // (row tiles, token tiles, splits)
 };
 // Tensor map of a row-major bf16 matrix [rows][cols] in boxes of 64 columns
@@ -185,11 +187,13 @@ int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t col
                      std::string* why);
 // Box rows of the activation maps for a contraction over `tokens` tokens.
 int gemm_box_rows(int tokens);
-GemmPlan plan_gemm(int M, int K, int T, int sms);
-size_t gemm_workspace_floats(const GemmPlan& p, int M, int T);
-// Most split-K workspace any plan needs on a GPU with `sms` SMs.
-inline size_t gemm_workspace_max_floats(int sms) { return size_t(sms) * 128 * 128; }
+// max_cluster: the largest cluster the GPU schedules for this kernel
+// (gemm_max_cluster).
+GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster);
 cudaError_t init_gemm_kernels();
+// Largest split-K cluster (<= 16) with every CTA at full shared memory that
+// the device can run.
+int gemm_max_cluster();
 // tw: weight map (box rows 128); tx[0..2]: the activation's three planes
 // (box rows p.bn).
 void launch_gemm(cudaStream_t s, const GemmPlan& p, int epilogue, const CUtensorMap& tw, const CUtensorMap* tx,
@@ -200,7 +204,7 @@ void launch_gemm(cudaStream_t s, const GemmPlan& p, int epilogue, const CUtensor
 cudaError_t init_batch_kernels();
 // Query heads per kv head that the batched attention kernels handle.
 bool batch_group_supported(int group);
-// Cache positions per CTA of the decode attention (launch_attn_rows).
+// Cache positions per chunk of the decode attention (launch_attn_rows).
 int attn_rows_chunk(bool kv_f32);
 
 // x[0..n) -> three bf16 planes (store_split3), `plane` elements apart.
@@ -236,11 +240,14 @@ struct AttnRowsArgs {
   uint16_t* out;            // [3 planes][T][ldo] attention output, split3
   size_t plane;
   int ldo;
-  float* part;              // [T][Hkv][max_split][group][head_dim + 2]
+  float* part;              // [T][Hkv][parts][group][head_dim + 2]
   unsigned* ticket;         // [T][Hkv], zero between launches
-  int max_split;            // ceil(max_len / attn_rows_chunk)
+  int parts;                // CTAs per (token, kv group): attn_rows_parts
   int* err;
 };
+// Context parts per (token, kv group) for launch_attn_rows: one when the
+// batch alone gives two CTAs per SM.
+int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms);
 void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl);
 
 struct AttnPrefillArgs {
@@ -255,6 +262,12 @@ struct AttnPrefillArgs {
 };
 void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bool pdl);
 
+// The greedy choice after a contraction that folded argmax keys into
+// best[rows] (GemmArgs::best): writes the token ids as launch_argmax_rows
+// does and zeroes best.
+void launch_argmax_finish(cudaStream_t s, const struct ArgmaxRowsArgs& a, unsigned long long* best, int rows,
+                          bool pdl);
+
 struct ArgmaxRowsArgs {
   const float* logits;      // [rows][V]
   int V;
@@ -265,6 +278,7 @@ struct ArgmaxRowsArgs {
   int* step;                // step counter (with out), or null
   unsigned* ticket;         // with step: zero between launches
   int out_cap;
+  int* err;                 // launch_argmax_finish: set when a row got no key
 };
 void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl);
 

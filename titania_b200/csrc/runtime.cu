@@ -6,6 +6,7 @@
 // them (model/cpu.rs, model/titania.rs) and returns TB200_ERR_ARG with a
 // message instead of panicking.
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -100,12 +101,11 @@ int matmul_tokens(tb200_device* d, tb200_buffer* out, const tb200_weight* w, con
     CUDA_TRY(cudaMalloc(&d->split, 3 * need * sizeof(uint16_t)));
     d->split_cap = need;
   }
-  const tb::GemmPlan p = tb::plan_gemm(int(rows), int(cols), int(n), d->sms);
+  const tb::GemmPlan p = tb::plan_gemm(int(rows), int(cols), int(n), d->sms, d->max_cluster);
   CUtensorMap tx[3];
   for (int i = 0; i < 3; i++)
     if (int rc = tb::encode_tmap_bf16(&tx[i], d->split + i * d->split_cap, n, cols, p.bn, &why))
       return fail(rc, "matmul: " + why);
-  ARG_CHECK(size_t(p.grid.x) * p.grid.y <= size_t(rt::kGemmTickets) || p.splits == 1, "matmul: too many tiles");
   tb::launch_split_rows(s, x->ptr, d->split, d->split_cap, need, false);
   if (int rc = launched("matmul split")) return rc;
   tb::GemmArgs a{};
@@ -114,8 +114,6 @@ int matmul_tokens(tb200_device* d, tb200_buffer* out, const tb200_weight* w, con
   a.T = int(n);
   a.out = out->ptr;
   a.ldo = int(rows);
-  a.part = d->gemm_part;
-  a.tickets = d->gemm_tickets;
   a.err = d->err;
   tb::launch_gemm(s, p, tb::kGemmStore, wm->map, tx, a, false);
   if (int rc = launched("matmul")) return rc;
@@ -156,19 +154,15 @@ int tb200_device_open(int ordinal, tb200_device** out) {
   d->sms = prop.multiProcessorCount;
   e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&d->best, sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMalloc(&d->gemm_part, tb::gemm_workspace_max_floats(d->sms) * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&d->gemm_tickets, rt::kGemmTickets * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(d->gemm_tickets, 0, rt::kGemmTickets * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMalloc(&d->err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(d->err, 0, sizeof(int));
   if (e != cudaSuccess) {
     cudaFree(d->best);
-    cudaFree(d->gemm_part);
-    cudaFree(d->gemm_tickets);
     cudaFree(d->err);
     delete d;
     return fail(TB200_ERR_CUDA, std::string("device setup: ") + cudaGetErrorString(e));
   }
+  d->max_cluster = std::min(8, tb::gemm_max_cluster());
   *out = d;
   return TB200_OK;
 }
@@ -180,8 +174,6 @@ int tb200_device_close(tb200_device* d) {
   cudaFree(d->tokens);
   cudaFree(d->best);
   cudaFree(d->split);
-  cudaFree(d->gemm_part);
-  cudaFree(d->gemm_tickets);
   cudaFree(d->err);
   cudaStreamDestroy(d->stream);
   delete d;

@@ -20,13 +20,11 @@ struct tb200_device {
   uint32_t* tokens = nullptr;  // device scratch for embed's token ids
   size_t tokens_cap = 0;
   unsigned long long* best = nullptr;  // argmax scratch
-  // matmul over several tokens: the input split into three bf16 planes,
-  // and the split-K workspace of the tensor-core contraction
+  // matmul over several tokens: the input split into three bf16 planes
   uint16_t* split = nullptr;  // [3][split_cap]
   size_t split_cap = 0;
-  float* gemm_part = nullptr;        // gemm_workspace_max_floats
-  unsigned* gemm_tickets = nullptr;  // [kGemmTickets]
-  int* err = nullptr;                // device error word of the trait ops
+  int max_cluster = 1;        // largest split-K cluster (gemm_max_cluster, at most 8)
+  int* err = nullptr;         // device error word of the trait ops
 };
 
 struct tb200_buffer {
@@ -104,7 +102,8 @@ struct tb200_state {
   int* bmeta_host = nullptr;   // pinned [3][cap] + readback words
   float* rows_part = nullptr;  // decode attention split partials
   unsigned* rows_ticket = nullptr;
-  int rows_max_split = 0;
+  int rows_parts = 0;
+  unsigned long long* bbest = nullptr;  // device [n_seqs] argmax keys of the lm_head contraction
   int* bstep = nullptr;        // device [0] step, [1] ticket
   int* bout = nullptr;         // device [max_len][n_seqs] generated tokens
   CUtensorMap act[2][kOps][3]{};  // per box height (64, 128 tokens), operand, plane
@@ -130,8 +129,6 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
                    uint32_t* next);
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);
-
-constexpr int kGemmTickets = 4096;
 
 }  // namespace rt
 
