@@ -443,6 +443,29 @@ def profile_bs64(args):
     print(json.dumps({"profile_bs64": True, "steps": args.launches}))
 
 
+GEMM_SHAPES = [(151936, 1024, 64), (6144, 1024, 64), (4096, 1024, 64), (1024, 2048, 64), (1024, 3072, 64),
+               (151936, 1024, 1), (6144, 1024, 512)]
+
+
+def profile_gemm(args):
+    """For ncu: the tensor-core contraction (through the trait matmul over
+    several tokens) at the batched decode's shapes, `--launches` times each."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    dev = tb.B200(0)
+    rng = np.random.default_rng(0)
+    for rows, cols, n in GEMM_SHAPES:
+        w = dev.upload(tb.Tensor([rows, cols], synth.f32_to_bf16_bits(
+            rng.normal(0, 0.02, size=(rows, cols)).astype(np.float32)).reshape(rows, cols)))
+        x = dev.alloc(n * cols)
+        dev.write(x, rng.standard_normal(n * cols, dtype=np.float32))
+        out = dev.alloc(n * rows)
+        for _ in range(args.launches):
+            dev.matmul(out, w, x)
+    dev.sync()
+    print(json.dumps({"profile_gemm": GEMM_SHAPES, "launches": args.launches}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,7 +482,12 @@ def main():
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--profile-bs64", action="store_true",
                     help="small case for ncu: the bs64 prefill, then --launches batched decode steps")
+    ap.add_argument("--profile-gemm", action="store_true",
+                    help="small case for ncu: the tensor-core contraction at the batched shapes")
     args = ap.parse_args()
+    if args.profile_gemm:
+        profile_gemm(args)
+        return
     if args.profile_op:
         profile_op(args)
         return

@@ -253,9 +253,9 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   }
 
   const float scale = 1.0f / sqrtf(float(kD));
-  float acc[GRP];
+  float acc[GRP], acc2[GRP];  // even and odd positions: two independent chains
 #pragma unroll
-  for (int h = 0; h < GRP; h++) acc[h] = 0.f;
+  for (int h = 0; h < GRP; h++) acc[h] = acc2[h] = 0.f;
   bool failed = false;
   for (int i = 0; i < nchunks; i++) {
     const int s = i % NS;
@@ -275,19 +275,19 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
       float sc = -INFINITY;
       if (p < n) {
         const KV* kr = ks + size_t(p) * kD;
-        float d = 0.f;
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four independent chains
 #pragma unroll 8
         for (int j = 0; j < 32; j++) {
           const int c = 4 * ((j + p) & 31);
           float k4[4];
           load4(kr + c, k4);
           const float4 q4 = *reinterpret_cast<const float4*>(&qs[h][c]);
-          d = fmaf(q4.x, k4[0], d);
-          d = fmaf(q4.y, k4[1], d);
-          d = fmaf(q4.z, k4[2], d);
-          d = fmaf(q4.w, k4[3], d);
+          d0 = fmaf(q4.x, k4[0], d0);
+          d1 = fmaf(q4.y, k4[1], d1);
+          d2 = fmaf(q4.z, k4[2], d2);
+          d3 = fmaf(q4.w, k4[3], d3);
         }
-        sc = scale * d;
+        sc = scale * ((d0 + d1) + (d2 + d3));
       }
       ps[h][p] = sc;
     }
@@ -314,11 +314,25 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
     }
     __syncthreads();
 #pragma unroll
-    for (int h = 0; h < GRP; h++) acc[h] *= corr_s[h];
-    for (int p = 0; p < n; p++) {
-      const float v = load1(vs + size_t(p) * kD + tid);
+    for (int h = 0; h < GRP; h++) {
+      acc[h] *= corr_s[h];
+      acc2[h] *= corr_s[h];
+    }
+    int p = 0;
+#pragma unroll 2
+    for (; p + 1 < n; p += 2) {
+      const float v0 = load1(vs + size_t(p) * kD + tid);
+      const float v1 = load1(vs + size_t(p + 1) * kD + tid);
 #pragma unroll
-      for (int h = 0; h < GRP; h++) acc[h] = fmaf(ps[h][p], v, acc[h]);
+      for (int h = 0; h < GRP; h++) {
+        acc[h] = fmaf(ps[h][p], v0, acc[h]);
+        acc2[h] = fmaf(ps[h][p + 1], v1, acc2[h]);
+      }
+    }
+    if (p < n) {
+      const float v0 = load1(vs + size_t(p) * kD + tid);
+#pragma unroll
+      for (int h = 0; h < GRP; h++) acc[h] = fmaf(ps[h][p], v0, acc[h]);
     }
     __syncthreads();  // every thread is done with stage s and ps
     if (tid == 0 && issued < nchunks) issue(issued++);
@@ -330,6 +344,8 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
     return;
   }
 
+#pragma unroll
+  for (int h = 0; h < GRP; h++) acc[h] += acc2[h];
   const size_t out_at = size_t(t) * a.ldo + size_t(g) * GRP * kD + tid;
   if (nparts == 1) {
 #pragma unroll

@@ -100,16 +100,15 @@ int ensure_batch(tb200_state* st) {
     return fail(TB200_ERR_CUDA, std::string("batch workspace: ") + cudaGetErrorString(e));
   }
   st->rows_parts = int(parts);
-  for (int b = 0; b < 2; b++)
-    for (int op = 0; op < kOps; op++)
-      for (int pl = 0; pl < 3; pl++) {
-        std::string why;
-        uint16_t* base = operand(st, op) + pl * plane(st, op);
-        if (int rc = tb::encode_tmap_bf16(&st->act[b][op][pl], base, cap, width(st, op), b == 0 ? 64 : 128, &why)) {
-          rt::free_batch(st);
-          return fail(rc, "batch workspace: " + why);
-        }
+  for (int op = 0; op < kOps; op++)
+    for (int pl = 0; pl < 3; pl++) {
+      std::string why;
+      uint16_t* base = operand(st, op) + pl * plane(st, op);
+      if (int rc = tb::encode_tmap_bf16(&st->act[op][pl], base, cap, width(st, op), tb::gemm_box_rows(), &why)) {
+        rt::free_batch(st);
+        return fail(rc, "batch workspace: " + why);
       }
+    }
   return TB200_OK;
 }
 
@@ -122,7 +121,6 @@ void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, in
           bool pdl, unsigned long long* best = nullptr) {
   tb200_device* d = st->dev;
   const tb::GemmPlan p = tb::plan_gemm(M, K, T, d->sms, d->max_cluster);
-  const int bi = p.bn == 64 ? 0 : 1;
   tb::GemmArgs a{};
   a.M = M;
   a.K = K;
@@ -136,7 +134,7 @@ void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, in
   }
   a.err = st->io + 3;
   a.best = best;
-  tb::launch_gemm(d->stream, p, epi, w, st->act[bi][op], a, pdl);
+  tb::launch_gemm(d->stream, p, epi, w, st->act[op], a, pdl);
 }
 
 // The transformer layers over T rows whose token, position and sequence are

@@ -9,24 +9,31 @@
 // bits hold every f32 of magnitude 2^-100 .. 2^127 exactly, and every
 // bf16 x bf16 product is exact in f32, so W·x0 + W·x1 + W·x2 differs from the
 // reference's dot product only in the order and rounding of the f32
-// additions. The three products accumulate into one tensor-memory
-// accumulator: the split costs tensor-core time (three MMAs per K step) but
-// no extra passes over W — the contraction stays bound by streaming W from
-// HBM for a few dozen tokens, and by the tensor cores for long prompts.
+// additions. A tile of 64 tokens stacks its three planes as the 192 columns
+// of one MMA (M=128, N=192, K=16), so each weight tile is read from shared
+// memory once per K step; the epilogue adds the three column groups.
 //
-// One CTA computes one 128-row × BN-token tile over one range of K (split-K
-// for short, wide matrices so that every SM streams weights):
-//   warp 0      TMA producer: 128×64 weight box + three BN×64 activation
-//               boxes per stage, 128-byte swizzle, into a ring of stages;
-//   warp 1      allocates BN tensor-memory columns, and one lane issues
-//               tcgen05.mma (M=128, N=BN, K=16) — 4 × 3 per 64-column stage —
-//               committing each stage back to the producer;
-//   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, then store,
-//               residual add, or SiLU(gate)·up of interleaved row pairs split
-//               again into three bf16 planes for the next contraction.
-// Split-K runs the K ranges of a tile as the CTAs of one thread-block
-// cluster, which sum their partial tiles over distributed shared memory in
-// split order, so results do not depend on scheduling.
+// Roles (192 threads):
+//   warp 0      TMA producer: a 128x64 weight box and three 64x64 activation
+//               boxes (128-byte swizzle) per stage, into a ring of stages;
+//   warp 1      allocates 512 tensor-memory columns (two accumulators of
+//               192), and one lane issues tcgen05.mma, committing each stage
+//               back to the producer and each finished tile to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, then store
+//               (optionally folding each token's argmax key), residual add,
+//               or SiLU(gate)·up of interleaved row pairs split again into
+//               three bf16 planes for the next contraction.
+// Two schedules:
+//   persistent  (enough tiles for every SM) one CTA per SM walks tiles
+//               blockIdx.x, + gridDim.x, ...; the producer runs ahead across
+//               tiles and the two accumulators let the epilogue of one tile
+//               overlap the MMAs of the next;
+//   split-K     (few tiles: short, wide matrices at decode batch sizes) the
+//               K ranges of a tile are the CTAs of one thread-block cluster,
+//               which sum their partial tiles over distributed shared memory
+//               in split order, so results do not depend on scheduling.
+// Every CTA takes more than half an SM's shared memory, so no two share an
+// SM and the 512-column allocation never waits.
 //
 // Every mbarrier wait is bounded (kWaitNs); on expiry the kernel records
 // TB200_ERR_TIMEOUT, lets what it issued drain (bounded), frees its tensor
@@ -47,23 +54,28 @@ namespace tb {
 
 namespace {
 
-constexpr int kBM = 128;          // weight rows per tile (MMA M)
-constexpr int kBK = 64;           // K per stage: one 128-byte swizzle row of bf16
+constexpr int kBM = 128;                 // weight rows per tile (MMA M)
+constexpr int kBK = 64;                  // K per stage: one 128-byte swizzle row of bf16
+constexpr int kBN = 64;                  // tokens per tile
+constexpr int kNP = 3 * kBN;             // MMA N: the tile's three activation planes
 constexpr int kGemmThreads = 192;
-constexpr int kStageA = kBM * kBK * 2;  // 16 KB
-// Shared memory after the barriers: tensor-memory slot, flags, and the
-// epilogue warps' argmax keys [4][128].
-constexpr size_t kExtra = 64 + 4 * 128 * 8;
+constexpr int kStageA = kBM * kBK * 2;   // 16 KB
+constexpr int kStageB = kNP * kBK * 2;   // 24 KB (three 8 KB plane boxes)
+constexpr int kStage = kStageA + kStageB;
+constexpr int kMaxStages = 5;
+constexpr int kAccCols = 256;            // tensor-memory columns per accumulator
+constexpr int kTmemCols = 2 * kAccCols;
+// Floor of the dynamic shared memory: more than half of an SM's 228 KB.
+constexpr size_t kMinSmem = 116 * 1024;
 
-template <int BN>
-struct Cfg {
-  static constexpr int kStageB = BN * kBK * 2;          // per activation plane
-  static constexpr int kStage = kStageA + 3 * kStageB;  // bytes per stage
-  static constexpr int kStages = (200 * 1024) / kStage > 8 ? 8 : (200 * 1024) / kStage;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;
-  // tiles + barriers + tensor-memory slot + flags + argmax keys, plus alignment slack
-  static constexpr size_t kSmem = size_t(kStages) * kStage + (2 * kStages + 1) * 8 + kExtra + 1024;
-};
+// Shared memory: `stages` tiles, then 8-byte slots: full[stages],
+// empty[stages], tfull[2], tempty[2], mdone, the tensor-memory address and
+// flags (6 slots), then the epilogue warps' argmax keys [4][kBN]; plus
+// alignment slack.
+size_t smem_for(int stages) {
+  const size_t need = size_t(stages) * kStage + (2 * size_t(stages) + 11) * 8 + 4 * kBN * 8 + 1024;
+  return need > kMinSmem ? need : kMinSmem;
+}
 
 // ---- tcgen05 / TMA wrappers -------------------------------------------------
 
@@ -180,49 +192,63 @@ __device__ __forceinline__ float ld_cluster(uint32_t saddr, uint32_t rank) {
   return v;
 }
 
-// One CTA per (row tile, token tile, K range). With a.splits > 1 the K
-// ranges of a tile are the CTAs of one cluster (cluster dims 1 x 1 x splits):
-// each leaves its partial tile in its own shared memory and cluster CTA r
-// sums the splits, in split order, for its slice of the tokens (DSMEM), so
-// the reduction runs on every CTA of the cluster at once.
-template <int BN, int EPI>
+// Sums the three plane column groups of accumulator columns [c, c + 16)
+// for this warp's 32 lanes: v[j] = token (c + j) of the tile.
+__device__ __forceinline__ void tmem_ld_tokens(uint32_t taddr, int c, float (&v)[16]) {
+  float p1[16], p2[16];
+  tmem_ld16(taddr + c, v);
+  tmem_ld16(taddr + kBN + c, p1);
+  tmem_ld16(taddr + 2 * kBN + c, p2);
+#pragma unroll
+  for (int j = 0; j < 16; j++) v[j] = (v[j] + p1[j]) + p2[j];
+}
+
+template <int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx0,
            const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2, GemmArgs a) {
-  using C = Cfg<BN>;
   extern __shared__ unsigned char smem_raw[];
   // The swizzled tiles need 1024-byte alignment.
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const int stages = a.stages;  // 1 .. C::kStages, sized by the host to the K range
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * C::kStage);
+  const int stages = a.stages;  // 1 .. kMaxStages
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * kStage);
   uint64_t* empty = full + stages;
-  uint64_t* tfull = empty + stages;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
-  int* warp_ok = reinterpret_cast<int*>(tslot + 1);  // [4] per epilogue warp, then [4] the verdict
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(tfull + 8);  // [4][128] argmax keys
-  auto sA = [&](int s) { return sm + size_t(s) * C::kStage; };
-  auto sB = [&](int s, int plane) { return sm + size_t(s) * C::kStage + kStageA + plane * C::kStageB; };
+  uint64_t* tfull = empty + stages;  // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;      // [2] accumulator drained
+  uint64_t* mdone = tempty + 2;      // every MMA of the CTA completed
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
+  int* flags = reinterpret_cast<int*>(tslot + 1);  // [0..3] per epilogue warp, [4] verdict
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(mdone + 6);  // [4][kBN]
+  auto sA = [&](int s) { return sm + size_t(s) * kStage; };
+  auto sB = [&](int s) { return sm + size_t(s) * kStage + kStageA; };
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mt = blockIdx.x, nt = blockIdx.y, z = blockIdx.z;
-  const int m0 = mt * kBM, n0 = nt * BN;
+  const bool split = a.splits > 1;
   const int nkb = (a.K + kBK - 1) / kBK;
-  const int kb0 = z * a.kb_per_split;
-  const int kb1 = min(nkb, kb0 + a.kb_per_split);
-  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+  // Tile sequence of this CTA: split-K, one tile (blockIdx) and one K range;
+  // persistent, tiles blockIdx.x, blockIdx.x + gridDim.x, ... over all of K.
+  const int ntiles = split ? 1 : (a.mtiles * a.ntiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+  const int kb0 = split ? int(blockIdx.z) * a.kb_per_split : 0;
+  const int nk = split ? max(0, min(nkb, kb0 + a.kb_per_split) - kb0) : nkb;
+  auto tile_m = [&](int ti) { return split ? int(blockIdx.x) : (int(blockIdx.x) + ti * int(gridDim.x)) % a.mtiles; };
+  auto tile_n = [&](int ti) { return split ? int(blockIdx.y) : (int(blockIdx.x) + ti * int(gridDim.x)) / a.mtiles; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 1);
-    warp_ok[4] = 0;
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(mdone, 1);
+    flags[4] = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tslot, C::kTmemCols);
+  if (warp == 1) tmem_alloc(tslot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -231,126 +257,154 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // Producer. Weights do not depend on earlier kernels: the first
-      // stages' weight boxes go out before the dependency wait.
+      // tile's first stages of weights go out before the dependency wait.
       const uint64_t pol_w = l2_evict_first(), pol_x = l2_evict_last();
-      const int pre = nk < stages ? nk : stages;
+      auto load_b = [&](int s, int kb, int n0) {
+        tma_load_2d(sB(s), &tx0, kb * kBK, n0, &full[s], pol_x);
+        tma_load_2d(sB(s) + kBN * 128, &tx1, kb * kBK, n0, &full[s], pol_x);
+        tma_load_2d(sB(s) + 2 * kBN * 128, &tx2, kb * kBK, n0, &full[s], pol_x);
+      };
+      const int pre = ntiles > 0 ? min(nk, stages) : 0;
       for (int i = 0; i < pre; i++) {
-        mbar_arrive_expect_tx(&full[i], C::kStage);
-        tma_load_2d(sA(i), &tw, (kb0 + i) * kBK, m0, &full[i], pol_w);
+        mbar_arrive_expect_tx(&full[i], kStage);
+        tma_load_2d(sA(i), &tw, (kb0 + i) * kBK, tile_m(0) * kBM, &full[i], pol_w);
       }
       pdl_wait();
-      for (int i = 0; i < pre; i++) {
-        tma_load_2d(sB(i, 0), &tx0, (kb0 + i) * kBK, n0, &full[i], pol_x);
-        tma_load_2d(sB(i, 1), &tx1, (kb0 + i) * kBK, n0, &full[i], pol_x);
-        tma_load_2d(sB(i, 2), &tx2, (kb0 + i) * kBK, n0, &full[i], pol_x);
-      }
-      int issued = pre;
-      for (int i = pre; i < nk; i++) {
-        const int s = i % stages;
-        if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, a.err)) break;
-        mbar_arrive_expect_tx(&full[s], C::kStage);
-        tma_load_2d(sA(s), &tw, (kb0 + i) * kBK, m0, &full[s], pol_w);
-        tma_load_2d(sB(s, 0), &tx0, (kb0 + i) * kBK, n0, &full[s], pol_x);
-        tma_load_2d(sB(s, 1), &tx1, (kb0 + i) * kBK, n0, &full[s], pol_x);
-        tma_load_2d(sB(s, 2), &tx2, (kb0 + i) * kBK, n0, &full[s], pol_x);
-        issued = i + 1;
+      for (int i = 0; i < pre; i++) load_b(i, kb0 + i, tile_n(0) * kBN);
+      int i = 0, issued = pre;  // i: this CTA's k-block counter over all its tiles
+      bool ok = true;
+      for (int ti = 0; ti < ntiles && ok; ti++) {
+        const int m0 = tile_m(ti) * kBM, n0 = tile_n(ti) * kBN;
+        for (int k = 0; k < nk; k++, i++) {
+          if (i < pre) continue;
+          const int s = i % stages;
+          if (!mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, a.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kStage);
+          tma_load_2d(sA(s), &tw, (kb0 + k) * kBK, m0, &full[s], pol_w);
+          load_b(s, kb0 + k, n0);
+          issued = i + 1;
+        }
       }
       // Drain: every issued copy has landed before the CTA can exit (on the
       // normal path the MMA warp already waited for each of them).
-      for (int i = issued - 1; i >= 0 && i >= issued - stages; i--)
-        mbar_wait(&full[i % stages], (i / stages) & 1, nullptr);
+      for (int j = issued - 1; j >= 0 && j >= issued - stages; j--)
+        mbar_wait(&full[j % stages], (j / stages) & 1, nullptr);
     } else {
       pdl_wait();
     }
   } else if (warp == 1) {
     pdl_wait();
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(kBM, BN);
-      for (int i = 0; i < nk; i++) {
-        const int s = i % stages;
-        if (!mbar_wait(&full[s], (i / stages) & 1, a.err)) break;
+      constexpr uint32_t idesc = idesc_bf16(kBM, kNP);
+      int i = 0;
+      bool ok = true;
+      for (int ti = 0; ti < ntiles && ok; ti++) {
+        const int b = ti & 1;
+        // The epilogue has drained this accumulator's previous tile.
+        if (!mbar_wait(&tempty[b], ((ti >> 1) - 1) & 1, a.err)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s, 0));
+        const uint32_t acc = tmem + uint32_t(b * kAccCols);
+        for (int k = 0; k < nk; k++, i++) {
+          const int s = i % stages;
+          if (!mbar_wait(&full[s], (i / stages) & 1, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
 #pragma unroll
-        for (int k = 0; k < kBK / 16; k++) {
-          // K = 16 bf16 = 32 bytes per MMA inside the 128-byte swizzle row.
-          const uint64_t ad = sw128_desc(a0 + 32 * k);
-#pragma unroll
-          for (int p = 0; p < 3; p++)
-            mma_bf16(tmem, ad, sw128_desc(b0 + p * C::kStageB + 32 * k), idesc, (i > 0 || k > 0 || p > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; kk++)  // K = 16 bf16 = 32 bytes per MMA in the 128-byte row
+            mma_bf16(acc, sw128_desc(a0 + 32 * kk), sw128_desc(b0 + 32 * kk), idesc, (k > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
-        mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        mma_commit(&tfull[b]);
       }
-      mma_commit(tfull);
-      // Tensor memory is freed below only after every MMA has completed.
-      mbar_wait(tfull, 0, nullptr);
+      // Tensor memory is freed below only after every MMA has completed:
+      // a last commit tracks all of them.
+      mma_commit(mdone);
+      mbar_wait(mdone, 0, nullptr);
     }
     __syncwarp();
   } else {
     // Epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31.
     pdl_wait();
     const int q = warp & 3;
-    const int row = m0 + 32 * q + lane;
-    const bool row_ok = row < a.M;
-    bool ok = nk > 0 && mbar_wait(tfull, 0, a.err);
-    ok = __all_sync(0xffffffffu, ok);
-    // The four epilogue warps take the same branches below.
-    if (lane == 0) warp_ok[q] = ok ? 1 : 0;
-    named_sync(1, 128);
-    ok = warp_ok[0] && warp_ok[1] && warp_ok[2] && warp_ok[3];
-    if (warp == 2 && lane == 0) warp_ok[4] = ok ? 1 : 0;
-    tc_fence_after();
-    const uint32_t taddr = tmem + (uint32_t(32 * q) << 16);
-    if (ok && a.splits == 1) {
+    for (int ti = 0; ti < ntiles; ti++) {
+      const int b = ti & 1;
+      const int m0 = tile_m(ti) * kBM, n0 = tile_n(ti) * kBN;
+      const int row = m0 + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      bool ok = nk > 0 && mbar_wait(&tfull[b], (ti >> 1) & 1, a.err);
+      ok = __all_sync(0xffffffffu, ok);
+      // The four epilogue warps take the same branches below.
+      if (lane == 0) flags[q] = ok ? 1 : 0;
+      named_sync(1, 128);
+      ok = flags[0] && flags[1] && flags[2] && flags[3];
+      named_sync(1, 128);  // flags[0..3] read before the next tile writes them
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + uint32_t(b * kAccCols) + (uint32_t(32 * q) << 16);
+      if (!split) {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
+        for (int c = 0; c < kBN; c += 16) {
+          float v[16];
+          tmem_ld_tokens(taddr, c, v);
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int t = n0 + c + j;
-          epilogue_store<EPI>(a, row, t, v[j], row_ok && t < a.T);
-          if (EPI == kGemmStore && a.best) {
-            const unsigned long long k = warp_umax64(row_ok ? argmax_key(v[j], uint32_t(row)) : 0ull);
-            if (lane == 0) keys[q * 128 + c + j] = k;
+          for (int j = 0; j < 16; j++) {
+            const int t = n0 + c + j;
+            epilogue_store<EPI>(a, row, t, v[j], row_ok && t < a.T);
+            if (EPI == kGemmStore && a.best) {
+              const unsigned long long key = warp_umax64(row_ok ? argmax_key(v[j], uint32_t(row)) : 0ull);
+              if (lane == 0) keys[q * kBN + c + j] = key;
+            }
           }
         }
-      }
-      if (EPI == kGemmStore && a.best) {
-        // One atomic per token and CTA: the best of the four warps' rows.
-        named_sync(1, 128);
-        const int j = threadIdx.x - 64;
-        if (j < BN && n0 + j < a.T) {
-          unsigned long long k = keys[j];
+        // The accumulator is drained: the MMA warp may refill it.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+        if (EPI == kGemmStore && a.best) {
+          // One atomic per token and tile: the best of the four warps' rows.
+          named_sync(1, 128);
+          const int j = threadIdx.x - 64;
+          if (j < kBN && n0 + j < a.T) {
+            unsigned long long key = keys[j];
 #pragma unroll
-          for (int w = 1; w < 4; w++) k = keys[w * 128 + j] > k ? keys[w * 128 + j] : k;
-          atomicMax(a.best + n0 + j, k);
+            for (int w = 1; w < 4; w++) key = keys[w * kBN + j] > key ? keys[w * kBN + j] : key;
+            atomicMax(a.best + n0 + j, key);
+          }
+          named_sync(1, 128);  // keys read before the next tile writes them
         }
-      }
-    } else if (ok) {
-      // This split's partial tile into the (now idle) stage memory, [token][row].
-      float* red = reinterpret_cast<float*>(sm);
+      } else {
+        // This split's partial tile into the (now idle) stage memory, [token][row].
+        float* red = reinterpret_cast<float*>(sm);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
+        for (int c = 0; c < kBN; c += 16) {
+          float v[16];
+          tmem_ld_tokens(taddr, c, v);
 #pragma unroll
-        for (int j = 0; j < 16; j++) red[(c + j) * kBM + 32 * q + lane] = v[j];
+          for (int j = 0; j < 16; j++) red[(c + j) * kBM + 32 * q + lane] = v[j];
+        }
+        if (warp == 2 && lane == 0) flags[4] = 1;
       }
     }
   }
 
-  if (a.splits > 1) {
+  if (split) {
     __syncwarp();
     cluster_sync_all();  // every split's partial tile is in place
     if (warp >= 2) {
       const int q = warp & 3;
+      const int m0 = int(blockIdx.x) * kBM, n0 = int(blockIdx.y) * kBN;
       const int row = m0 + 32 * q + lane;
       const bool row_ok = row < a.M;
-      const int per = (BN + a.splits - 1) / a.splits;
-      const int j0 = int(cluster_rank()) * per, j1 = min(BN, j0 + per);
+      const int per = (kBN + a.splits - 1) / a.splits;
+      const int j0 = int(cluster_rank()) * per, j1 = min(kBN, j0 + per);
       const uint32_t base = smem_u32(sm) + uint32_t(32 * q + lane) * 4;
-      if (warp_ok[4]) {
+      if (flags[4]) {
 #pragma unroll 1
         for (int j = j0; j < j1; j++) {
           const uint32_t at = base + uint32_t(j * kBM) * 4;
@@ -360,8 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int t = n0 + j;
           epilogue_store<EPI>(a, row, t, v, row_ok && t < a.T);
           if (EPI == kGemmStore && a.best) {
-            const unsigned long long k = warp_umax64(row_ok ? argmax_key(v, uint32_t(row)) : 0ull);
-            if (lane == 0 && t < a.T) atomicMax(a.best + t, k);
+            const unsigned long long key = warp_umax64(row_ok ? argmax_key(v, uint32_t(row)) : 0ull);
+            if (lane == 0 && t < a.T) atomicMax(a.best + t, key);
           }
         }
       }
@@ -374,7 +428,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_free(tmem, C::kTmemCols);
+    tmem_free(tmem, kTmemCols);
   }
 }
 
@@ -383,26 +437,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 std::mutex g_encode_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-template <int BN, int EPI>
-cudaError_t set_smem() {
-  cudaError_t e =
-      cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg<BN>::kSmem));
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<BN, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+template <int EPI>
+cudaError_t set_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(k_gemm<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem_for(kMaxStages)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
 
-template <int BN>
-size_t smem_for(int stages) {
-  return size_t(stages) * Cfg<BN>::kStage + (2 * size_t(stages) + 1) * 8 + kExtra + 1024;
-}
-
-template <int BN, int EPI>
+template <int EPI>
 void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap* tx, const GemmArgs& a,
                  bool pdl) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = p.grid;
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = smem_for<BN>(p.stages);
+  cfg.dynamicSmemBytes = smem_for(p.stages);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
@@ -420,7 +469,7 @@ void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaLaunchKernelEx(&cfg, k_gemm<BN, EPI>, tw, tx[0], tx[1], tx[2], a);
+  cudaLaunchKernelEx(&cfg, k_gemm<EPI>, tw, tx[0], tx[1], tx[2], a);
 }
 
 }  // namespace
@@ -459,34 +508,37 @@ int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t col
   return TB200_OK;
 }
 
-int gemm_box_rows(int tokens) { return tokens <= 64 ? 64 : 128; }
+int gemm_box_rows() { return kBN; }
 
 GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster) {
   GemmPlan p{};
-  p.bn = gemm_box_rows(T);
-  const int mtiles = (M + kBM - 1) / kBM, ntiles = (T + p.bn - 1) / p.bn;
+  p.mtiles = (M + kBM - 1) / kBM;
+  p.ntiles = (T + kBN - 1) / kBN;
   const int nkb = (K + kBK - 1) / kBK;
+  const int tiles = p.mtiles * p.ntiles;
   int splits = 1;
-  const int tiles = mtiles * ntiles;
-  // Split K across the CTAs of a cluster when the tiles alone leave SMs idle.
-  if (tiles < sms) splits = std::max(1, std::min({nkb, sms / tiles, max_cluster}));
+  // Split K across the CTAs of a cluster (a power of two) when the tiles
+  // alone leave SMs idle.
+  if (tiles < sms) {
+    const int want = std::max(1, std::min({nkb, sms / tiles, max_cluster}));
+    while (splits * 2 <= want) splits *= 2;
+  }
   p.kb_per_split = (nkb + splits - 1) / splits;
   p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
-  const int max_stages = p.bn == 64 ? Cfg<64>::kStages : Cfg<128>::kStages;
-  p.stages = std::min(max_stages, p.kb_per_split);
-  p.grid = dim3(unsigned(mtiles), unsigned(ntiles), unsigned(p.splits));
+  if (p.splits > 1) {
+    p.stages = std::min(kMaxStages, p.kb_per_split);
+    p.grid = dim3(unsigned(p.mtiles), unsigned(p.ntiles), unsigned(p.splits));
+  } else {
+    p.stages = kMaxStages;
+    p.grid = dim3(unsigned(std::min(tiles, sms)), 1, 1);
+  }
   return p;
 }
 
 cudaError_t init_gemm_kernels() {
-  cudaError_t e = cudaSuccess;
-#define TB_GEMM_SMEM(BN)                                              \
-  if (e == cudaSuccess) e = set_smem<BN, kGemmStore>();              \
-  if (e == cudaSuccess) e = set_smem<BN, kGemmResid>();              \
-  if (e == cudaSuccess) e = set_smem<BN, kGemmSilu>();
-  TB_GEMM_SMEM(64)
-  TB_GEMM_SMEM(128)
-#undef TB_GEMM_SMEM
+  cudaError_t e = set_attrs<kGemmStore>();
+  if (e == cudaSuccess) e = set_attrs<kGemmResid>();
+  if (e == cudaSuccess) e = set_attrs<kGemmSilu>();
   return e;
 }
 
@@ -495,7 +547,7 @@ int gemm_max_cluster() {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1, 1, n);
     cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = Cfg<64>::kSmem;
+    cfg.dynamicSmemBytes = smem_for(kMaxStages);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
@@ -504,7 +556,7 @@ int gemm_max_cluster() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k_gemm<64, kGemmStore>, &cfg) == cudaSuccess && clusters > 0)
+    if (cudaOccupancyMaxActiveClusters(&clusters, k_gemm<kGemmStore>, &cfg) == cudaSuccess && clusters > 0)
       return int(n);
     cudaGetLastError();  // an unsupported size is not an error of ours
   }
@@ -517,16 +569,11 @@ void launch_gemm(cudaStream_t s, const GemmPlan& p, int epi, const CUtensorMap& 
   b.kb_per_split = p.kb_per_split;
   b.splits = p.splits;
   b.stages = p.stages;
-#define TB_GEMM_CASE(BN)                                                        \
-  if (p.bn == BN) {                                                             \
-    if (epi == kGemmStore) launch_tile<BN, kGemmStore>(s, p, tw, tx, b, pdl);   \
-    if (epi == kGemmResid) launch_tile<BN, kGemmResid>(s, p, tw, tx, b, pdl);   \
-    if (epi == kGemmSilu) launch_tile<BN, kGemmSilu>(s, p, tw, tx, b, pdl);     \
-    return;                                                                     \
-  }
-  TB_GEMM_CASE(64)
-  TB_GEMM_CASE(128)
-#undef TB_GEMM_CASE
+  b.mtiles = p.mtiles;
+  b.ntiles = p.ntiles;
+  if (epi == kGemmStore) launch_tile<kGemmStore>(s, p, tw, tx, b, pdl);
+  if (epi == kGemmResid) launch_tile<kGemmResid>(s, p, tw, tx, b, pdl);
+  if (epi == kGemmSilu) launch_tile<kGemmSilu>(s, p, tw, tx, b, pdl);
 }
 
 }  // namespace tb

@@ -164,7 +164,7 @@ enum GemmEpilogue {
 };
 struct GemmArgs {
   int M, K, T;              // weight rows, columns (reduction), tokens
-  int kb_per_split, splits, stages;  // set by launch_gemm from the plan
+  int kb_per_split, splits, stages, mtiles, ntiles;  // set by launch_gemm from the plan
   float* out;               // kGemmStore / kGemmResid: [T][ldo]
   int ldo;
   uint16_t* out_split;      // kGemmSilu: three bf16 planes [T][ldh], `plane` elements apart
@@ -175,18 +175,18 @@ struct GemmArgs {
   int* err;
 };
 struct GemmPlan {
-  int bn;            // tokens per tile (box rows of the activation maps)
-  int splits;        // K ranges per tile = cluster size (1: no cluster)
-  int kb_per_split;  // 64-column K blocks per range
-  int stages;        // shared-memory ring depth
-  dim3 grid;         // (row tiles, token tiles, splits)
+  int mtiles, ntiles;  // 128-row weight tiles, 64-token tiles
+  int splits;          // K ranges per tile = cluster size (1: persistent CTAs over all tiles)
+  int kb_per_split;    // 64-column K blocks per range
+  int stages;          // shared-memory ring depth
+  dim3 grid;           // split-K: (row tiles, token tiles, splits); persistent: (CTAs)
 };
 // Tensor map of a row-major bf16 matrix [rows][cols] in boxes of 64 columns
 // by box_rows rows, 128-byte swizzle: the operand layout of the kernel.
 int encode_tmap_bf16(CUtensorMap* map, const void* base, size_t rows, size_t cols, int box_rows,
                      std::string* why);
-// Box rows of the activation maps for a contraction over `tokens` tokens.
-int gemm_box_rows(int tokens);
+// Box rows (tokens per tile) of the activation maps.
+int gemm_box_rows();
 // max_cluster: the largest cluster the GPU schedules for this kernel
 // (gemm_max_cluster).
 GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster);
@@ -195,7 +195,7 @@ cudaError_t init_gemm_kernels();
 // the device can run.
 int gemm_max_cluster();
 // tw: weight map (box rows 128); tx[0..2]: the activation's three planes
-// (box rows p.bn).
+// (box rows gemm_box_rows()).
 void launch_gemm(cudaStream_t s, const GemmPlan& p, int epilogue, const CUtensorMap& tw, const CUtensorMap* tx,
                  const GemmArgs& a, bool pdl);
 

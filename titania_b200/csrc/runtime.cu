@@ -104,7 +104,7 @@ int matmul_tokens(tb200_device* d, tb200_buffer* out, const tb200_weight* w, con
   const tb::GemmPlan p = tb::plan_gemm(int(rows), int(cols), int(n), d->sms, d->max_cluster);
   CUtensorMap tx[3];
   for (int i = 0; i < 3; i++)
-    if (int rc = tb::encode_tmap_bf16(&tx[i], d->split + i * d->split_cap, n, cols, p.bn, &why))
+    if (int rc = tb::encode_tmap_bf16(&tx[i], d->split + i * d->split_cap, n, cols, tb::gemm_box_rows(), &why))
       return fail(rc, "matmul: " + why);
   tb::launch_split_rows(s, x->ptr, d->split, d->split_cap, need, false);
   if (int rc = launched("matmul split")) return rc;

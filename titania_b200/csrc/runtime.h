@@ -106,7 +106,7 @@ struct tb200_state {
   unsigned long long* bbest = nullptr;  // device [n_seqs] argmax keys of the lm_head contraction
   int* bstep = nullptr;        // device [0] step, [1] ticket
   int* bout = nullptr;         // device [max_len][n_seqs] generated tokens
-  CUtensorMap act[2][kOps][3]{};  // per box height (64, 128 tokens), operand, plane
+  CUtensorMap act[kOps][3]{};  // per operand and plane
   cudaGraphExec_t bgraph = nullptr;  // one decode step of every sequence
 };
 
