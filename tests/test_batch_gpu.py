@@ -173,6 +173,32 @@ def test_tiny_batch_forward_logits(tiny):
         positions = [p + 1 for p in positions]
 
 
+@pytest.mark.parametrize("heads,kv_heads", [(2, 2), (8, 2)])
+@pytest.mark.parametrize("kv", ["f32", "bf16"])
+def test_tiny_batch_group_sizes(b200, heads, kv_heads, kv):
+    """1 and 4 query heads per kv head (the tensor-core decode attention
+    takes 1 and 2; 4 runs on the CUDA cores), prompt and batched decode."""
+    import os
+    from conftest import ROOT
+    cfg = dict(synth.TINY, num_attention_heads=heads, num_key_value_heads=kv_heads)
+    d = os.path.join(ROOT, "_build", f"tiny-h{heads}-kv{kv_heads}")
+    synth.write_model(d, cfg, seed=5)
+    m, ref = tb.Model.load(d, b200), orc.Model(d)
+    prompts = [synth.prompt_tokens(k, 1024, seed=300 + k) for k in (70, 5, 130)]
+    steps = 3
+    bs = m.batch_state(len(prompts), 160, kv=kv)
+    first = [m.forward_seq(bs, i, p, 0, logits=False) for i, p in enumerate(prompts)]
+    expected = [orc.greedy_generate(ref, p, steps + 1, max_len=160) for p in prompts]
+    assert first == [e[0][0] for e in expected]
+    tokens, positions = list(first), [len(p) for p in prompts]
+    for step in range(steps):
+        logits, nxt = m.forward_batch(bs, tokens, positions)
+        for i in range(len(prompts)):
+            close(logits[i], expected[i][1][step + 1], REL, ABS)
+            assert int(nxt[i]) == expected[i][0][step + 1]
+        tokens, positions = nxt.tolist(), [p + 1 for p in positions]
+
+
 def test_batch_state_bounds(tiny):
     m, _ = tiny
     bs = m.batch_state(3, 16)

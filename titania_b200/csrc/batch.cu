@@ -386,6 +386,316 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   if (tid == 0) *ticket = 0u;
 }
 
+// ---- decode attention on the tensor cores (bf16 cache) ---------------------------
+//
+// The same work as k_attn_rows for a bf16 cache, with the two products on
+// mma.sync m16n8k16 (bf16 in, f32 accumulate):
+//   scores   S[p][c] = K[p][:] . qc[:]   A = 16 cached keys (ldmatrix), B = the
+//            query as 8 columns (column 2j + h: plane j of head h, q = q0 + q1 +
+//            q2; columns 6, 7 and absent heads zero), kept in registers;
+//   values   O[d][c] = V[:][d] . Pc[:]   A = 16 dimensions x 16 positions of V
+//            (ldmatrix.trans), B = the probabilities split the same way.
+// Every product is exact (bf16 x bf16 in f32) and the planes make q and P
+// exact, so only the f32 accumulation order differs from k_attn_rows. Keys
+// and values arrive by TMA (128-byte swizzle, so ldmatrix is conflict-free)
+// in chunks of 64 positions; warp w owns positions 16w .. 16w+15 of every
+// chunk and keeps its own running max, sum and output, and the four warps
+// are combined once at the end.
+
+constexpr int kTcCh = 64;                         // positions per chunk
+constexpr int kTcStages = 3;
+constexpr int kTcBox = kTcCh * 64 * 2;            // one 64-position x 64-dim box: 8 KB
+constexpr int kTcStage = 4 * kTcBox;              // K lo/hi dims, V lo/hi dims: 32 KB
+constexpr size_t kTcSmem = size_t(kTcStages) * kTcStage + 1024;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Byte offset of (row r, 16-byte unit u) in a 128-byte-swizzled box.
+__device__ __forceinline__ uint32_t sw128(int r, int u) { return uint32_t(r * 128 + ((u ^ (r & 7)) << 4)); }
+__device__ __forceinline__ uint16_t plane_of(float v, int j) {
+  const uint16_t a = f2bf(v);
+  if (j == 0) return a;
+  const float r = v - bf16f(a);
+  const uint16_t b = f2bf(r);
+  return j == 1 ? b : f2bf(r - bf16f(b));
+}
+
+template <int GRP>
+__global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CUtensorMap cache, AttnRowsArgs a) {
+  static_assert(GRP == 1 || GRP == 2, "three planes per head in 8 columns");
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // swizzled boxes: 1024-byte aligned
+  __shared__ __align__(16) float qs[GRP][kD];
+  __shared__ __align__(16) uint16_t pw[4][8][16];  // per warp: probabilities [column][position]
+  __shared__ float wm[4][GRP], wl[4][GRP];
+  __shared__ __align__(16) float wo[4][GRP][kD];
+  __shared__ __align__(8) uint64_t bar[kTcStages];
+  __shared__ int verdict, is_last;
+
+  pdl_launch_dependents();
+  const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Positions and sequence ids change only between steps (the host, or the
+  // step's last kernel), so they can be read before the dependency wait.
+  const int pos = a.pos[t], seq = a.seq[t];
+  const bool ok = pos >= 0 && pos < a.max_len && seq >= 0 && seq < a.n_seqs;
+  const int ctx = pos + 1;
+  const int span = ((ctx + a.parts - 1) / a.parts + kTcCh - 1) / kTcCh * kTcCh;
+  const int nparts = (ctx + span - 1) / span;
+  const bool active = ok && part < nparts;
+  const int p0 = part * span, p1 = active ? min(ctx, p0 + span) : p0;
+  const int nchunks = (p1 - p0 + kTcCh - 1) / kTcCh;
+  // Cache rows (of head_dim elements) of this (sequence, layer, kv head).
+  const int krow = int(size_t(seq) * a.seq_stride / kD) + a.layer_rows + g * a.max_len;
+  const int vrow = krow + a.n_kv_heads * a.max_len;
+  const uint64_t pol = l2_evict_first();
+  auto issue = [&](int i) {
+    unsigned char* st = sm + size_t(i % kTcStages) * kTcStage;
+    uint64_t* b = &bar[i % kTcStages];
+    const int c0 = p0 + i * kTcCh;
+    mbar_arrive_expect_tx(b, kTcStage);
+    tma_load_2d(st, &cache, 0, krow + c0, b, pol);
+    tma_load_2d(st + kTcBox, &cache, 64, krow + c0, b, pol);
+    tma_load_2d(st + 2 * kTcBox, &cache, 0, vrow + c0, b, pol);
+    tma_load_2d(st + 3 * kTcBox, &cache, 64, vrow + c0, b, pol);
+  };
+
+  int issued = 0;
+  if (active && tid == 0) {
+    for (int s = 0; s < kTcStages; s++) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+    // Chunks wholly before the token's own position were written by earlier
+    // steps: they go out before the dependency wait.
+    while (issued < kTcStages && issued < nchunks && p0 + (issued + 1) * kTcCh <= pos) issue(issued++);
+  }
+  pdl_wait();
+  if (!ok) {
+    if (part == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
+    return;
+  }
+  if (!active) return;
+  if (tid == 0)
+    while (issued < kTcStages && issued < nchunks) issue(issued++);
+  for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
+  for (int i = tid; i < 4 * 8 * 16; i += 128) (&pw[0][0][0])[i] = 0;  // columns 6, 7 stay zero
+  __syncthreads();
+
+  // The query as B fragments: column c = lane / 4, k = dims 16 kb + 2 (lane % 4) (+1, +8, +9).
+  const int col = lane >> 2, kq = 2 * (lane & 3);
+  const int qh = col & 1, qj = col >> 1;  // column c = 2 plane + head
+  const bool qlive = qj < 3 && qh < GRP;
+  uint32_t qb[8][2];
+#pragma unroll
+  for (int kb = 0; kb < 8; kb++)
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+      const int d = 16 * kb + kq + 8 * hf;
+      const uint32_t lo = qlive ? plane_of(qs[qh][d], qj) : 0u;
+      const uint32_t hi = qlive ? plane_of(qs[qh][d + 1], qj) : 0u;
+      qb[kb][hf] = lo | (hi << 16);
+    }
+
+  const float scale = 1.0f / sqrtf(float(kD));
+  float m[GRP], l[GRP];
+  float o[8][4];  // O^T fragments: dims 16 mb + lane / 4 (+8), columns 2 (lane % 4) (+1)
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+  }
+#pragma unroll
+  for (int mb = 0; mb < 8; mb++) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
+  const int r = lane >> 2;  // this lane's score rows: positions r and r + 8 of the warp's 16
+  bool failed = false;
+  for (int i = 0; i < nchunks; i++) {
+    const int s = i % kTcStages;
+    const int c0 = p0 + i * kTcCh;
+    if (tid == 0) verdict = mbar_wait(&bar[s], (i / kTcStages) & 1, a.err) ? 1 : 0;
+    __syncthreads();
+    if (!verdict) {
+      failed = true;
+      break;
+    }
+    mbar_wait(&bar[s], (i / kTcStages) & 1, nullptr);  // the phase is complete: returns at once
+    const uint32_t kbase = smem_u32(sm + size_t(s) * kTcStage), vbase = kbase + 2 * kTcBox;
+    const int pw0 = 16 * warp;  // the warp's first position in the chunk
+    // Scores for positions pw0 .. pw0 + 15.
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int ar = pw0 + (lane & 7) + 8 * ((lane >> 3) & 1), au = lane >> 4;
+#pragma unroll
+      for (int kb = 0; kb < 8; kb++) {
+        uint32_t af[4];
+        ldsm_x4(kbase + (kb >> 2) * kTcBox + sw128(ar, 2 * (kb & 3) + au), af);
+        mma16816(sc, af, qb[kb][0], qb[kb][1]);
+      }
+    }
+    // Sum the three planes (lanes 4r .. 4r+3 hold columns 0-1, 2-3, 4-5, 6-7).
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 1);
+      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
+    }
+    // sc: [0] (row r, head 0) [1] (row r, head 1) [2] (row r+8, head 0) [3] (row r+8, head 1)
+    const int n = min(kTcCh, p1 - c0);
+    float pv[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int p = pw0 + r + 8 * (e >> 1);
+      pv[e] = p < n ? scale * sc[e] : -INFINITY;
+    }
+#pragma unroll
+    for (int h = 0; h < GRP; h++) {
+      float mx = fmaxf(pv[h], pv[2 + h]);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[h], mx);
+      const float corr = m[h] == -INFINITY ? 0.f : expf(m[h] - mn);
+      const float e0 = pv[h] == -INFINITY ? 0.f : expf(pv[h] - mn);
+      const float e1 = pv[2 + h] == -INFINITY ? 0.f : expf(pv[2 + h] - mn);
+      pv[h] = e0;
+      pv[2 + h] = e1;
+      float sum = e0 + e1;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l[h] = l[h] * corr + sum;
+      m[h] = mn;
+#pragma unroll
+      for (int mb = 0; mb < 8; mb++) {
+        o[mb][h] *= corr;      // column 2 (lane % 4) + h: head h (GRP 2) ...
+        o[mb][2 + h] *= corr;  // ... rows d and d + 8
+      }
+    }
+    // Probabilities as B fragments: plane (lane % 4) of each head, via the warp's pw.
+    if ((lane & 3) < 3) {
+      const int j = lane & 3;
+#pragma unroll
+      for (int h = 0; h < GRP; h++) {
+        const int c = 2 * j + h;
+        pw[warp][c][r] = plane_of(pv[h], j);
+        pw[warp][c][r + 8] = plane_of(pv[2 + h], j);
+      }
+    }
+    __syncwarp();
+    const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&pw[warp][col][kq]);
+    const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&pw[warp][col][kq + 8]);
+    {
+      const int vr = pw0 + (lane & 7) + 8 * (lane >> 4), vu = (lane >> 3) & 1;
+#pragma unroll
+      for (int mb = 0; mb < 8; mb++) {
+        uint32_t af[4];
+        ldsm_x4_t(vbase + (mb >> 2) * kTcBox + sw128(vr, 2 * (mb & 3) + vu), af);
+        mma16816(o[mb], af, pb0, pb1);
+      }
+    }
+    __syncthreads();  // every warp is done with stage s (and its pw)
+    if (tid == 0 && issued < nchunks) issue(issued++);
+  }
+  if (failed) {
+    // Let the copies in flight land (bounded) before the CTA's memory goes.
+    if (tid == 0)
+      for (int i = max(0, issued - kTcStages); i < issued; i++)
+        mbar_wait(&bar[i % kTcStages], (i / kTcStages) & 1, nullptr);
+    return;
+  }
+
+  // Per warp: add the planes (lanes 4r .. 4r+2) and publish (m, l, O).
+#pragma unroll
+  for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      o[mb][e] += __shfl_xor_sync(0xffffffffu, o[mb][e], 1);
+      o[mb][e] += __shfl_xor_sync(0xffffffffu, o[mb][e], 2);
+    }
+  if ((lane & 3) == 0) {
+#pragma unroll
+    for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+      for (int h = 0; h < GRP; h++) {
+        wo[warp][h][16 * mb + r] = o[mb][h];
+        wo[warp][h][16 * mb + r + 8] = o[mb][2 + h];
+      }
+  }
+  if (lane == 0)
+#pragma unroll
+    for (int h = 0; h < GRP; h++) {
+      wm[warp][h] = m[h];
+      wl[warp][h] = l[h];
+    }
+  __syncthreads();
+  float res[GRP], rm[GRP], rl[GRP];
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w][h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      const float wt = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+      L += wl[w][h] * wt;
+      O += wo[w][h][tid] * wt;
+    }
+    res[h] = O;
+    rm[h] = M;
+    rl[h] = L;
+  }
+  const size_t out_at = size_t(t) * a.ldo + size_t(g) * GRP * kD + tid;
+  if (nparts == 1) {
+#pragma unroll
+    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, res[h] / rl[h]);
+    return;
+  }
+  const int stride = kD + 2;
+  float* pbase = a.part + ((size_t(t) * a.n_kv_heads + g) * a.parts) * GRP * stride;
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    float* pp = pbase + (size_t(part) * GRP + h) * stride;
+    pp[2 + tid] = res[h];
+    if (tid == 0) {
+      pp[0] = rm[h];
+      pp[1] = rl[h];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  unsigned* ticket = a.ticket + size_t(t) * a.n_kv_heads + g;
+  if (tid == 0) is_last = atomicAdd(ticket, 1u) == unsigned(nparts - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < nparts; sp++) M = fmaxf(M, __ldcg(pbase + (size_t(sp) * GRP + h) * stride));
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < nparts; sp++) {
+      const float* pp = pbase + (size_t(sp) * GRP + h) * stride;
+      const float wt = expf(__ldcg(pp) - M);
+      L += __ldcg(pp + 1) * wt;
+      O += __ldcg(pp + 2 + tid) * wt;
+    }
+    store_split3(a.out, a.plane, out_at + size_t(h) * kD, O / L);
+  }
+  if (tid == 0) *ticket = 0u;
+}
+
 // ---- causal prefill attention -------------------------------------------------------
 
 constexpr int kPR = 64;     // query rows per CTA (tokens x heads of one kv group)
@@ -587,6 +897,11 @@ __global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigne
   if (threadIdx.x == 0 && a.step) *a.step = step_s + 1;
 }
 
+template <int G>
+cudaError_t tc_attr() {
+  return cudaFuncSetAttribute(k_attn_rows_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
+}
+
 template <int G, bool F>
 cudaError_t rows_attr() {
   cudaError_t e = cudaFuncSetAttribute(k_attn_rows<G, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -609,6 +924,8 @@ cudaError_t init_batch_kernels() {
   TB_ATTR(4)
   TB_ATTR(8)
 #undef TB_ATTR
+  if (e == cudaSuccess) e = tc_attr<1>();
+  if (e == cudaSuccess) e = tc_attr<2>();
   return e;
 }
 
@@ -617,10 +934,12 @@ bool batch_group_supported(int group) { return group == 1 || group == 2 || group
 int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<false>::kCh; }
 
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms) {
-  // Enough CTAs for two per SM; never a part shorter than one chunk.
+  // Enough CTAs for two per SM; never a part shorter than one chunk (the
+  // tensor-core kernel's chunk is at least as long as the other's).
   const int units = std::max(1, tokens * n_kv_heads);
   const int want = (2 * sms + units - 1) / units;
-  const int chunks = (max_len + attn_rows_chunk(kv_f32) - 1) / attn_rows_chunk(kv_f32);
+  const int chunk = std::max(attn_rows_chunk(kv_f32), kTcCh);
+  const int chunks = (max_len + chunk - 1) / chunk;
   return std::max(1, std::min(want, chunks));
 }
 
@@ -638,9 +957,16 @@ void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl)
   if (tokens > 0) launch_pdl(s, dim3(tokens), dim3(128), 0, pdl, k_qkv_post, a);
 }
 
+bool attn_rows_tensor_cores(bool kv_f32, int group) { return !kv_f32 && (group == 1 || group == 2); }
+
 void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl) {
   if (tokens <= 0) return;
   const dim3 grid(unsigned(a.parts), unsigned(a.n_kv_heads), unsigned(tokens));
+  if (attn_rows_tensor_cores(a.kv_f32 != 0, group) && a.cache_map) {
+    if (group == 1) launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<1>, *a.cache_map, a);
+    else launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<2>, *a.cache_map, a);
+    return;
+  }
 #define TB_ROWS(G)                                                                                   \
   if (group == G) {                                                                                  \
     if (a.kv_f32) launch_pdl(s, grid, dim3(128), RowsCfg<true>::kSmem, pdl, k_attn_rows<G, true>, a); \

@@ -100,6 +100,15 @@ int ensure_batch(tb200_state* st) {
     return fail(TB200_ERR_CUDA, std::string("batch workspace: ") + cudaGetErrorString(e));
   }
   st->rows_parts = int(parts);
+  if (!st->kv_f32) {
+    std::string why;
+    const size_t rows = st->n_seqs * st->seq_stride / D;
+    if (int rc = tb::encode_tmap_bf16(&st->cache_map, st->kv, rows, D, 64, &why)) {
+      rt::free_batch(st);
+      return fail(rc, "batch workspace: " + why);
+    }
+    st->has_cache_map = true;
+  }
   for (int op = 0; op < kOps; op++)
     for (int pl = 0; pl < 3; pl++) {
       std::string why;
@@ -208,6 +217,8 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
       a.ticket = st->rows_ticket;
       a.parts = st->rows_parts;
       a.err = err;
+      a.cache_map = st->has_cache_map ? &st->cache_map : nullptr;
+      a.layer_rows = int(l * kv_layer / c.head_dim);
       tb::launch_attn_rows(s, a, T, group, pdl);
     }
     gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl);

@@ -244,7 +244,15 @@ struct AttnRowsArgs {
   unsigned* ticket;         // [T][Hkv], zero between launches
   int parts;                // CTAs per (token, kv group): attn_rows_parts
   int* err;
+  // bf16 cache on the tensor cores (attn_rows_tensor_cores): a map of the
+  // whole cache as rows of head_dim (box 64 x 64, 128-byte swizzle), and the
+  // row of this layer's block of sequence 0.
+  const CUtensorMap* cache_map;
+  int layer_rows;
 };
+// Whether launch_attn_rows runs the tensor-core kernel (bf16 cache, 1 or 2
+// query heads per kv head; it needs AttnRowsArgs::cache_map).
+bool attn_rows_tensor_cores(bool kv_f32, int group);
 // Context parts per (token, kv group) for launch_attn_rows: one when the
 // batch alone gives two CTAs per SM.
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms);

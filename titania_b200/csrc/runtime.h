@@ -107,6 +107,8 @@ struct tb200_state {
   int* bstep = nullptr;        // device [0] step, [1] ticket
   int* bout = nullptr;         // device [max_len][n_seqs] generated tokens
   CUtensorMap act[kOps][3]{};  // per operand and plane
+  CUtensorMap cache_map{};     // bf16 cache as rows of head_dim, for the tensor-core decode attention
+  bool has_cache_map = false;
   cudaGraphExec_t bgraph = nullptr;  // one decode step of every sequence
 };
 
