@@ -274,17 +274,35 @@ enum {
   TB200_TRACE_LAST_WEIGHTS = 6, /* the CTA's last weight chunk is in shared memory */
 };
 
-/* One trace record: tag = op << 16 | layer (TB200_OP_*), the CTA index, the
- * event, the SM, and the GPU's global timer in nanoseconds. */
+/* Kernels of a state's batched decode step (tb200_forward_batch and friends),
+ * as the op half of their trace tags. */
+enum {
+  TB200_TRACE_OP_NORM = 17,     /* rmsnorm + split before q|k|v */
+  TB200_TRACE_OP_QKV = 18,      /* q|k|v contraction */
+  TB200_TRACE_OP_QKV_POST = 19, /* QK-norm, RoPE, cache append */
+  TB200_TRACE_OP_ATTENTION = 20,
+  TB200_TRACE_OP_O = 21,        /* o_proj contraction (+ residual) */
+  TB200_TRACE_OP_NORM2 = 22,    /* rmsnorm + split before gate|up */
+  TB200_TRACE_OP_GATE_UP = 23,  /* gate|up contraction (+ silu) */
+  TB200_TRACE_OP_DOWN = 24,     /* down contraction (+ residual) */
+  TB200_TRACE_OP_FINAL_NORM = 25,
+  TB200_TRACE_OP_LM_HEAD = 26,  /* lm_head contraction (+ argmax keys) */
+  TB200_TRACE_OP_ARGMAX = 27,
+};
+
+/* One trace record: tag = op << 16 | layer (TB200_OP_* for the single-token
+ * step, TB200_TRACE_OP_* for the batched one), the CTA index, the event, the
+ * SM, and the GPU's global timer in nanoseconds. */
 typedef struct tb200_trace_record {
   uint32_t tag, cta, event, sm;
   uint64_t ns;
 } tb200_trace_record;
 
-/* Starts recording the state's decode step: every kernel of the step's graph
- * owns fixed record slots (8 per CTA), so a replay overwrites the previous
- * one and the buffer holds the last step. `capacity` records are allocated;
- * the graph is rebuilt to carry the buffer. */
+/* Starts recording the state's decode step (the single-token step of a
+ * one-sequence state, and the batched step of any state): every kernel of the
+ * step's graph owns fixed record slots (8 per CTA), so a replay overwrites
+ * the previous one and the buffer holds the last step. `capacity` records
+ * are allocated; the graphs are rebuilt to carry the buffer. */
 TB200_API int tb200_trace_start(tb200_state* state, size_t capacity);
 /* Stops recording, copies up to `cap` record slots to `out` (slots with
  * ns == 0 were not written) and the number of slots one step uses to `*n`. */

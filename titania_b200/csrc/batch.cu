@@ -63,10 +63,12 @@ __global__ void k_split_rows(const float* __restrict__ x, uint16_t* __restrict__
 // written split to row r of the three planes.
 __global__ void __launch_bounds__(256) k_norm_split(const float* __restrict__ x, int row0, int dim,
                                                    const uint16_t* __restrict__ w, float eps,
-                                                   uint16_t* __restrict__ out, size_t plane) {
+                                                   uint16_t* __restrict__ out, size_t plane, TraceAt tr) {
   __shared__ float red[8];
   pdl_launch_dependents();
+  if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_START);
   pdl_wait();
+  if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_WAITED);
   const float* xr = x + size_t(row0 + blockIdx.x) * dim;
   float ss = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -83,6 +85,7 @@ __global__ void __launch_bounds__(256) k_norm_split(const float* __restrict__ x,
   const size_t row = size_t(blockIdx.x) * dim;
   for (int i = threadIdx.x; i < dim; i += blockDim.x)
     store_split3(out, plane, row + i, __fmul_rn(xr[i], __fmul_rn(scale, bf16f(w[i]))));
+  if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_DONE);
 }
 
 // ---- QK-norm, RoPE, cache append -------------------------------------------------
@@ -92,7 +95,9 @@ __global__ void __launch_bounds__(256) k_norm_split(const float* __restrict__ x,
 // lane l ^ 16.
 __global__ void __launch_bounds__(128) k_qkv_post(QkvPostArgs a) {
   pdl_launch_dependents();
+  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_START);
   pdl_wait();
+  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_WAITED);
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pos = a.pos[t], seq = a.seq[t];
@@ -153,6 +158,8 @@ __global__ void __launch_bounds__(128) k_qkv_post(QkvPostArgs a) {
       }
     }
   }
+  __syncthreads();
+  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_DONE);
 }
 
 // ---- decode attention: one query token per sequence ------------------------------
@@ -202,6 +209,8 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
 
   pdl_launch_dependents();
   const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_START);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Positions and sequence ids change only between steps (the host, or the
   // step's last kernel), so they can be read before the dependency wait.
@@ -239,6 +248,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
     }
   }
   pdl_wait();
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_WAITED);
   if (!ok) {
     if (part == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
     return;
@@ -350,6 +360,7 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   if (nparts == 1) {
 #pragma unroll
     for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, acc[h] / l_s[h]);
+    if (tid == 0) a.trace.at(cta, TB200_TRACE_DONE);
     return;
   }
   const int stride = kD + 2;
@@ -450,6 +461,8 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
 
   pdl_launch_dependents();
   const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_START);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Positions and sequence ids change only between steps (the host, or the
   // step's last kernel), so they can be read before the dependency wait.
@@ -485,6 +498,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     while (issued < kTcStages && issued < nchunks && p0 + (issued + 1) * kTcCh <= pos) issue(issued++);
   }
   pdl_wait();
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_WAITED);
   if (!ok) {
     if (part == 0 && g == 0 && tid == 0) set_error(a.err, TB200_ERR_ARG);
     return;
@@ -660,6 +674,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   if (nparts == 1) {
 #pragma unroll
     for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, res[h] / rl[h]);
+    if (tid == 0) a.trace.at(cta, TB200_TRACE_DONE);
     return;
   }
   const int stride = kD + 2;
@@ -877,7 +892,9 @@ __global__ void __launch_bounds__(1024) k_argmax_rows(ArgmaxRowsArgs a) {
 __global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigned long long* best, int rows) {
   __shared__ int step_s;
   pdl_launch_dependents();
+  if (threadIdx.x == 0) a.trace.at(0, TB200_TRACE_START);
   pdl_wait();
+  if (threadIdx.x == 0) a.trace.at(0, TB200_TRACE_WAITED);
   if (threadIdx.x == 0) step_s = a.step ? *a.step : 0;
   __syncthreads();
   for (int r = threadIdx.x; r < rows; r += blockDim.x) {
@@ -895,6 +912,7 @@ __global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigne
   }
   __syncthreads();
   if (threadIdx.x == 0 && a.step) *a.step = step_s + 1;
+  if (threadIdx.x == 0) a.trace.at(0, TB200_TRACE_DONE);
 }
 
 template <int G>
@@ -949,8 +967,8 @@ void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t pla
 }
 
 void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
-                       uint16_t* out, size_t plane, bool pdl) {
-  if (rows > 0) launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, row0, dim, w, eps, out, plane);
+                       uint16_t* out, size_t plane, bool pdl, const TraceAt& tr) {
+  if (rows > 0) launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, row0, dim, w, eps, out, plane, tr);
 }
 
 void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl) {

@@ -96,6 +96,21 @@ __device__ __forceinline__ uint32_t sm_id() {
   return r;
 }
 
+// Writes event `ev` of CTA `cta` into the launch's fixed slots (base + cta
+// * kTraceEvents + ev), when tracing.
+__device__ __forceinline__ void trace_at(const Trace& t, uint32_t base, uint32_t tag, uint32_t cta, uint32_t ev) {
+  if (t.rec) {
+    const uint32_t i = base + cta * kTraceEvents + ev;
+    if (i < t.cap) t.rec[i] = TraceRec{tag, cta, ev, sm_id(), global_ns()};
+  }
+}
+// A launch's trace slots: the buffer, its first slot and its tag (op << 16 | layer).
+struct TraceAt {
+  Trace t;
+  uint32_t base, tag;
+  __device__ __forceinline__ void at(uint32_t cta, uint32_t ev) const { trace_at(t, base, tag, cta, ev); }
+};
+
 __device__ __forceinline__ void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

@@ -126,8 +126,17 @@ int* readback(tb200_state* st) { return st->bmeta_host + 3 * (st->max_len + size
 
 // One contraction over T rows: weights `w`, activation operand `op`; the
 // kGemmSilu epilogue writes operand kOpH.
+// Trace slots for a launch of `ctas` CTAs (kTraceEvents each) while a
+// traced graph is captured; no slots otherwise.
+tb::TraceAt trace_slots(tb200_state* st, bool on, int op, size_t layer, uint32_t ctas) {
+  if (!on || !st->trace.rec) return tb::TraceAt{};
+  tb::TraceAt t{st->trace, st->trace_next, (uint32_t(op) << 16) | uint32_t(layer)};
+  st->trace_next += ctas * tb::kTraceEvents;
+  return t;
+}
+
 void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, int epi, float* out, int ldo,
-          bool pdl, unsigned long long* best = nullptr) {
+          bool pdl, unsigned long long* best = nullptr, bool traced = false, int top = 0, size_t layer = 0) {
   tb200_device* d = st->dev;
   const tb::GemmPlan p = tb::plan_gemm(M, K, T, d->sms, d->max_cluster);
   tb::GemmArgs a{};
@@ -143,6 +152,7 @@ void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, in
   }
   a.err = st->io + 3;
   a.best = best;
+  a.trace = trace_slots(st, traced, top, layer, p.grid.x * p.grid.y * p.grid.z);
   tb::launch_gemm(d->stream, p, epi, w, st->act[op], a, pdl);
 }
 
@@ -159,13 +169,15 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
   const size_t eb = st->kv_f32 ? 4 : 2;
   const size_t kv_layer = 2 * c.num_key_value_heads * st->max_len * c.head_dim;
   int* err = st->io + 3;
+  const bool tr = !prefill;  // the batched step is traced (its graph is captured once)
   uint16_t* xn = operand(st, kOpXn);
   uint16_t* att = operand(st, kOpAtt);
   const size_t xn_plane = plane(st, kOpXn), att_plane = plane(st, kOpAtt);
   for (size_t l = 0; l < c.num_hidden_layers; l++) {
     const FusedLayer& L = m->layers[l];
-    tb::launch_norm_split(s, st->bx, 0, T, H, L.attn_norm, c.rms_norm_eps, xn, xn_plane, pdl);
-    gemm(st, T, qkv_w, H, L.m_qkv, kOpXn, tb::kGemmStore, st->bqkv, qkv_w, pdl);
+    tb::launch_norm_split(s, st->bx, 0, T, H, L.attn_norm, c.rms_norm_eps, xn, xn_plane, pdl,
+                          trace_slots(st, tr, TB200_TRACE_OP_NORM, l, uint32_t(T)));
+    gemm(st, T, qkv_w, H, L.m_qkv, kOpXn, tb::kGemmStore, st->bqkv, qkv_w, pdl, nullptr, tr, TB200_TRACE_OP_QKV, l);
     tb::QkvPostArgs q{};
     q.qkv = st->bqkv;
     q.ld = qkv_w;
@@ -183,6 +195,7 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
     q.pos = meta_pos(st);
     q.seq = meta_seq(st);
     q.err = err;
+    q.trace = trace_slots(st, tr, TB200_TRACE_OP_QKV_POST, l, uint32_t(T));
     tb::launch_qkv_post(s, q, T, pdl);
     if (prefill) {
       tb::AttnPrefillArgs a{};
@@ -219,12 +232,15 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
       a.err = err;
       a.cache_map = st->has_cache_map ? &st->cache_map : nullptr;
       a.layer_rows = int(l * kv_layer / c.head_dim);
+      a.trace = trace_slots(st, tr, TB200_TRACE_OP_ATTENTION, l,
+                            uint32_t(a.parts) * uint32_t(c.num_key_value_heads) * uint32_t(T));
       tb::launch_attn_rows(s, a, T, group, pdl);
     }
-    gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl);
-    tb::launch_norm_split(s, st->bx, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane, pdl);
-    gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl);
-    gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResid, st->bx, H, pdl);
+    gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
+    tb::launch_norm_split(s, st->bx, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane, pdl,
+                          trace_slots(st, tr, TB200_TRACE_OP_NORM2, l, uint32_t(T)));
+    gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl, nullptr, tr, TB200_TRACE_OP_GATE_UP, l);
+    gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
   }
 }
 
@@ -232,14 +248,16 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
 // the pass (model.rs:144-147); logits land in blogits rows 0 .. rows - 1.
 // The contraction folds each row's argmax key into bbest as it stores the
 // logits; a one-CTA kernel turns the keys into token ids.
-void enqueue_head(tb200_state* st, int row0, int rows, tb::ArgmaxRowsArgs am, bool pdl) {
+void enqueue_head(tb200_state* st, int row0, int rows, tb::ArgmaxRowsArgs am, bool pdl, bool tr) {
   tb200_model* m = st->m;
   const tb200_config& c = m->c;
   const int H = int(c.hidden_size), V = int(c.vocab_size);
   cudaStream_t s = m->dev->stream;
-  tb::launch_norm_split(s, st->bx, row0, rows, H, m->norm, c.rms_norm_eps, operand(st, kOpXn), plane(st, kOpXn), pdl);
-  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest);
+  tb::launch_norm_split(s, st->bx, row0, rows, H, m->norm, c.rms_norm_eps, operand(st, kOpXn), plane(st, kOpXn), pdl,
+                        trace_slots(st, tr, TB200_TRACE_OP_FINAL_NORM, 0, uint32_t(rows)));
+  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest, tr, TB200_TRACE_OP_LM_HEAD, 0);
   am.err = st->io + 3;
+  am.trace = trace_slots(st, tr, TB200_TRACE_OP_ARGMAX, 0, 1);
   tb::launch_argmax_finish(s, am, st->bbest, rows, pdl);
 }
 
@@ -248,6 +266,7 @@ int enqueue_decode_step(tb200_state* st) {
   const bool pdl = use_pdl();
   tb200_model* m = st->m;
   const int T = int(st->n_seqs);
+  st->trace_next = 0;
   tb::launch_embed(m->dev->stream, st->bx, m->embed, m->c.hidden_size, reinterpret_cast<const uint32_t*>(meta_tok(st)),
                    size_t(T));
   enqueue_layers(st, T, false, 0, 0, pdl);
@@ -260,7 +279,7 @@ int enqueue_decode_step(tb200_state* st) {
   am.step = st->bstep;
   am.ticket = reinterpret_cast<unsigned*>(st->bstep + 1);
   am.out_cap = int(st->max_len);
-  enqueue_head(st, 0, T, am, pdl);
+  enqueue_head(st, 0, T, am, pdl, true);
   return launched("batched decode step");
 }
 
@@ -328,9 +347,13 @@ int check_rows(tb200_state* st, const uint32_t* tokens, const size_t* positions,
 
 namespace rt {
 
-void free_batch(tb200_state* st) {
+void drop_batch_graph(tb200_state* st) {
   if (st->bgraph) cudaGraphExecDestroy(st->bgraph);
   st->bgraph = nullptr;
+}
+
+void free_batch(tb200_state* st) {
+  drop_batch_graph(st);
   void* ptrs[] = {st->bx, st->bqkv, st->blogits, st->bact, st->bmeta, st->rows_part, st->rows_ticket, st->bstep,
                   st->bout, st->bbest};
   for (void* p : ptrs) cudaFree(p);
@@ -371,7 +394,7 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
   am.logits = st->blogits;
   am.V = int(m->c.vocab_size);
   am.next = st->bstep + 2;
-  enqueue_head(st, int(last) - 1, 1, am, pdl);
+  enqueue_head(st, int(last) - 1, 1, am, pdl, false);
   if (int rc = launched("prompt pass")) return rc;
   if (logits) CUDA_TRY(cudaMemcpyAsync(logits, st->blogits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
   int* back = readback(st) + 1;

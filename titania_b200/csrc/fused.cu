@@ -44,13 +44,6 @@ __device__ __forceinline__ int xperm(int i) { return (i & ~255) + ((i >> 2) & 1)
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Trace slots are fixed per (launch, CTA, event): no atomics on the path.
-__device__ __forceinline__ void trace_at(const Trace& t, uint32_t base, uint32_t tag, uint32_t cta, uint32_t ev) {
-  if (t.rec) {
-    const uint32_t i = base + cta * kTraceEvents + ev;
-    if (i < t.cap) t.rec[i] = TraceRec{tag, cta, ev, sm_id(), global_ns()};
-  }
-}
-
 // Each CTA owns rows [r0, r1). The producer warp copies them in stages of
 // `stage_rows` rows (large bulk copies: a TMA copy's cost is mostly per copy,
 // so a few tens of KB per copy reach far higher per-SM bandwidth than rows

@@ -141,21 +141,42 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
-// Applies the epilogue to one accumulator value: row `row` (< M), token t (< T).
-// kGemmSilu pairs lanes (2i, 2i+1) = (gate, up) of hidden row row/2: every
-// lane of the warp must call it with the same t.
-template <int EPI>
-__device__ __forceinline__ void epilogue_store(const GemmArgs& a, int row, int t, float v, bool valid) {
+// Applies the epilogue to N consecutive tokens t0 .. t0 + N - 1 of one row
+// (v[j] = accumulator of token t0 + j). Residual reads are all issued before
+// any write. kGemmSilu pairs lanes (2i, 2i+1) = (gate, up) of hidden row
+// row/2: every lane of the warp calls it with the same t0.
+template <int EPI, int N>
+__device__ __forceinline__ void epilogue_tokens(const GemmArgs& a, int row, bool row_ok, int t0, const float (&v)[N]) {
   if (EPI == kGemmStore) {
-    if (valid) a.out[size_t(t) * a.ldo + row] = v;
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = v[j];
   } else if (EPI == kGemmResid) {
-    if (valid) {
-      float* p = a.out + size_t(t) * a.ldo + row;
-      *p = __fadd_rn(*p, v);
-    }
+    float x[N];
+#pragma unroll
+    for (int j = 0; j < N; j++) x[j] = row_ok && t0 + j < a.T ? a.out[size_t(t0 + j) * a.ldo + row] : 0.f;
+#pragma unroll
+    for (int j = 0; j < N; j++)
+      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = __fadd_rn(x[j], v[j]);
   } else {  // kGemmSilu
-    const float u = __shfl_xor_sync(0xffffffffu, v, 1);
-    if (valid && (row & 1) == 0) store_split3(a.out_split, a.plane, size_t(t) * a.ldh + (row >> 1), silu_mul(v, u));
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+      const float u = __shfl_xor_sync(0xffffffffu, v[j], 1);
+      if (row_ok && t0 + j < a.T && (row & 1) == 0)
+        store_split3(a.out_split, a.plane, size_t(t0 + j) * a.ldh + (row >> 1), silu_mul(v[j], u));
+    }
+  }
+}
+
+// Folds each token's argmax key over this warp's 32 rows into best[] (one
+// atomic per token and warp); all lanes call it.
+template <int N>
+__device__ __forceinline__ void argmax_tokens(const GemmArgs& a, int row, bool row_ok, int t0, const float (&v)[N],
+                                              int lane) {
+#pragma unroll
+  for (int j = 0; j < N; j++) {
+    const unsigned long long key = warp_umax64(row_ok ? argmax_key(v[j], uint32_t(row)) : 0ull);
+    if (lane == 0 && t0 + j < a.T) atomicMax(a.best + t0 + j, key);
   }
 }
 
@@ -189,7 +210,7 @@ __device__ __forceinline__ void tmem_ld_tokens(uint32_t taddr, int c, float (&v)
   for (int j = 0; j < 16; j++) v[j] = (v[j] + p1[j]) + p2[j];
 }
 
-template <int EPI>
+template <int EPI, int S>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx0,
            const __grid_constant__ CUtensorMap tx1, const __grid_constant__ CUtensorMap tx2, GemmArgs a) {
@@ -211,7 +232,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool split = a.splits > 1;
+  const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_START);
+  constexpr bool split = S > 1;  // a.splits == S
   const int nkb = (a.K + kBK - 1) / kBK;
   // Tile sequence of this CTA: split-K, one tile (blockIdx) and one K range;
   // persistent, tiles blockIdx.x, blockIdx.x + gridDim.x, ... over all of K.
@@ -274,6 +297,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           issued = i + 1;
         }
       }
+      a.trace.at(cta, TB200_TRACE_ISSUED);
       // Drain: every issued copy has landed before the CTA can exit (on the
       // normal path the MMA warp already waited for each of them).
       for (int j = issued - 1; j >= 0 && j >= issued - stages; j--)
@@ -299,6 +323,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
+          if (i == 0) a.trace.at(cta, TB200_TRACE_WEIGHTS);
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA(s)), b0 = smem_u32(sB(s));
 #pragma unroll
@@ -308,6 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         mma_commit(&tfull[b]);
       }
+      a.trace.at(cta, TB200_TRACE_LAST_WEIGHTS);
       // Tensor memory is freed below only after every MMA has completed:
       // a last commit tracks all of them.
       mma_commit(mdone);
@@ -317,8 +343,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // Epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. + 31.
     pdl_wait();
+    if (warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_WAITED);
     const int q = warp & 3;
-    for (int ti = 0; ti < ntiles; ti++) {
+    if (split && nk == 0) {
+      // A split past the end of K: its partial tile is zero.
+      float* red = reinterpret_cast<float*>(sm);
+      for (int j = 0; j < kBN; j++) red[j * kBM + 32 * q + lane] = 0.f;
+      if (warp == 2 && lane == 0) flags[4] = 1;
+    }
+    for (int ti = 0; ti < ntiles && nk > 0; ti++) {
       const int b = ti & 1;
       const int m0 = tile_m(ti) * kBM, n0 = tile_n(ti) * kBN;
       const int row = m0 + 32 * q + lane;
@@ -331,6 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ok = flags[0] && flags[1] && flags[2] && flags[3];
       named_sync(1, 128);  // flags[0..3] read before the next tile writes them
       if (!ok) break;
+      if (ti == 0 && warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_INPUT);
       tc_fence_after();
       const uint32_t taddr = tmem + uint32_t(b * kAccCols) + (uint32_t(32 * q) << 16);
       if (!split) {
@@ -338,11 +372,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int c = 0; c < kBN; c += 16) {
           float v[16];
           tmem_ld_tokens(taddr, c, v);
+          epilogue_tokens<EPI, 16>(a, row, row_ok, n0 + c, v);
+          if (EPI == kGemmStore && a.best) {
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            const int t = n0 + c + j;
-            epilogue_store<EPI>(a, row, t, v[j], row_ok && t < a.T);
-            if (EPI == kGemmStore && a.best) {
+            for (int j = 0; j < 16; j++) {
               const unsigned long long key = warp_umax64(row_ok ? argmax_key(v[j], uint32_t(row)) : 0ull);
               if (lane == 0) keys[q * kBN + c + j] = key;
             }
@@ -382,29 +415,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (split) {
     __syncwarp();
     cluster_sync_all();  // every split's partial tile is in place
-    if (warp >= 2) {
+    if (warp >= 2 && flags[4]) {
+      // Cluster CTA r sums the S partial tiles for tokens r PER .. + PER - 1,
+      // in split order: every partial load is issued before any is used.
+      constexpr int PER = kBN / S;
       const int q = warp & 3;
       const int m0 = int(blockIdx.x) * kBM, n0 = int(blockIdx.y) * kBN;
       const int row = m0 + 32 * q + lane;
       const bool row_ok = row < a.M;
-      const int per = (kBN + a.splits - 1) / a.splits;
-      const int j0 = int(cluster_rank()) * per, j1 = min(kBN, j0 + per);
-      const uint32_t base = smem_u32(sm) + uint32_t(32 * q + lane) * 4;
-      if (flags[4]) {
-#pragma unroll 1
-        for (int j = j0; j < j1; j++) {
-          const uint32_t at = base + uint32_t(j * kBM) * 4;
-          float v = 0.f;
-#pragma unroll 4
-          for (int r = 0; r < a.splits; r++) v += ld_cluster(at, uint32_t(r));
-          const int t = n0 + j;
-          epilogue_store<EPI>(a, row, t, v, row_ok && t < a.T);
-          if (EPI == kGemmStore && a.best) {
-            const unsigned long long key = warp_umax64(row_ok ? argmax_key(v, uint32_t(row)) : 0ull);
-            if (lane == 0 && t < a.T) atomicMax(a.best + t, key);
-          }
-        }
+      const int j0 = int(cluster_rank()) * PER;
+      const uint32_t base = smem_u32(sm) + uint32_t((j0 * kBM + 32 * q + lane) * 4);
+      float pv[S][PER];
+#pragma unroll
+      for (int r = 0; r < S; r++)
+#pragma unroll
+        for (int j = 0; j < PER; j++) pv[r][j] = ld_cluster(base + uint32_t(j * kBM * 4), uint32_t(r));
+      float v[PER];
+#pragma unroll
+      for (int j = 0; j < PER; j++) {
+        v[j] = pv[0][j];
+#pragma unroll
+        for (int r = 1; r < S; r++) v[j] += pv[r][j];
       }
+      epilogue_tokens<EPI, PER>(a, row, row_ok, n0 + j0, v);
+      if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + j0, v, lane);
     }
     __syncwarp();
     cluster_sync_all();  // no CTA leaves while another still reads its tile
@@ -412,6 +446,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_DONE);
   if (warp == 1) {
     tc_fence_after();
     tmem_free(tmem, kTmemCols);
@@ -423,15 +458,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 std::mutex g_encode_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+template <int EPI, int S>
+cudaError_t set_attrs_one() {
+  cudaError_t e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem_for(kMaxStages)));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
 template <int EPI>
 cudaError_t set_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(k_gemm<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem_for(kMaxStages)));
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = set_attrs_one<EPI, 1>();
+  if (e == cudaSuccess) e = set_attrs_one<EPI, 2>();
+  if (e == cudaSuccess) e = set_attrs_one<EPI, 4>();
+  if (e == cudaSuccess) e = set_attrs_one<EPI, 8>();
+  if (e == cudaSuccess) e = set_attrs_one<EPI, 16>();
   return e;
 }
 
-template <int EPI>
+template <int EPI, int S>
 void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const CUtensorMap* tx, const GemmArgs& a,
                  bool pdl) {
   cudaLaunchConfig_t cfg{};
@@ -455,7 +499,7 @@ void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaLaunchKernelEx(&cfg, k_gemm<EPI>, tw, tx[0], tx[1], tx[2], a);
+  cudaLaunchKernelEx(&cfg, k_gemm<EPI, S>, tw, tx[0], tx[1], tx[2], a);
 }
 
 }  // namespace
@@ -510,7 +554,7 @@ GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster) {
     while (splits * 2 <= want) splits *= 2;
   }
   p.kb_per_split = (nkb + splits - 1) / splits;
-  p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  p.splits = splits;  // a power of two; a split past the end of K contributes zeros
   if (p.splits > 1) {
     p.stages = std::min(kMaxStages, p.kb_per_split);
     p.grid = dim3(unsigned(p.mtiles), unsigned(p.ntiles), unsigned(p.splits));
@@ -542,7 +586,7 @@ int gemm_max_cluster() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, k_gemm<kGemmStore>, &cfg) == cudaSuccess && clusters > 0)
+    if (cudaOccupancyMaxActiveClusters(&clusters, k_gemm<kGemmStore, 2>, &cfg) == cudaSuccess && clusters > 0)
       return int(n);
     cudaGetLastError();  // an unsupported size is not an error of ours
   }
@@ -557,9 +601,18 @@ void launch_gemm(cudaStream_t s, const GemmPlan& p, int epi, const CUtensorMap& 
   b.stages = p.stages;
   b.mtiles = p.mtiles;
   b.ntiles = p.ntiles;
-  if (epi == kGemmStore) launch_tile<kGemmStore>(s, p, tw, tx, b, pdl);
-  if (epi == kGemmResid) launch_tile<kGemmResid>(s, p, tw, tx, b, pdl);
-  if (epi == kGemmSilu) launch_tile<kGemmSilu>(s, p, tw, tx, b, pdl);
+#define TB_GEMM_S(EPI)                                                      \
+  if (epi == EPI) {                                                         \
+    if (p.splits == 1) launch_tile<EPI, 1>(s, p, tw, tx, b, pdl);           \
+    if (p.splits == 2) launch_tile<EPI, 2>(s, p, tw, tx, b, pdl);           \
+    if (p.splits == 4) launch_tile<EPI, 4>(s, p, tw, tx, b, pdl);           \
+    if (p.splits == 8) launch_tile<EPI, 8>(s, p, tw, tx, b, pdl);           \
+    if (p.splits == 16) launch_tile<EPI, 16>(s, p, tw, tx, b, pdl);         \
+  }
+  TB_GEMM_S(kGemmStore)
+  TB_GEMM_S(kGemmResid)
+  TB_GEMM_S(kGemmSilu)
+#undef TB_GEMM_S
 }
 
 }  // namespace tb

@@ -173,6 +173,7 @@ struct GemmArgs {
   unsigned long long* best;  // kGemmStore: per token, the argmax key (argmax_key) of its
                              // outputs is folded in with atomicMax; null: none
   int* err;
+  TraceAt trace;  // CTA index blockIdx.x + gridDim.x (blockIdx.y + gridDim.y blockIdx.z)
 };
 struct GemmPlan {
   int mtiles, ntiles;  // 128-row weight tiles, 64-token tiles
@@ -211,7 +212,7 @@ int attn_rows_chunk(bool kv_f32);
 void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t plane, size_t n, bool pdl);
 // planes row r = split3(rmsnorm(x row row0 + r, w)), r < rows; plane = elements between planes.
 void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
-                       uint16_t* out, size_t plane, bool pdl);
+                       uint16_t* out, size_t plane, bool pdl, const TraceAt& tr = TraceAt{});
 
 struct QkvPostArgs {
   float* qkv;               // [T][ld]: q heads | k heads | v heads; q rewritten in place
@@ -226,6 +227,7 @@ struct QkvPostArgs {
   const int* pos;           // [T] position of each token
   const int* seq;           // [T] sequence of each token
   int* err;
+  TraceAt trace;
 };
 void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl);
 
@@ -249,6 +251,7 @@ struct AttnRowsArgs {
   // row of this layer's block of sequence 0.
   const CUtensorMap* cache_map;
   int layer_rows;
+  TraceAt trace;  // CTA index blockIdx.x + gridDim.x (blockIdx.y + gridDim.y blockIdx.z)
 };
 // Whether launch_attn_rows runs the tensor-core kernel (bf16 cache, 1 or 2
 // query heads per kv head; it needs AttnRowsArgs::cache_map).
@@ -287,6 +290,7 @@ struct ArgmaxRowsArgs {
   unsigned* ticket;         // with step: zero between launches
   int out_cap;
   int* err;                 // launch_argmax_finish: set when a row got no key
+  TraceAt trace;
 };
 void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl);
 

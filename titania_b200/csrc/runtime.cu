@@ -974,14 +974,14 @@ int tb200_enqueue_op(tb200_model* m, tb200_state* st, int op, size_t layer) {
 
 int tb200_trace_start(tb200_state* st, size_t capacity) {
   ARG_CHECK(st && capacity > 0 && capacity < (size_t(1) << 31), "bad trace capacity");
-  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
   ARG_CHECK(!st->trace.rec, "already tracing");
   if (int rc = use(st->dev)) return rc;
   CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
   CUDA_TRY(cudaMalloc(&st->trace.rec, capacity * sizeof(tb::TraceRec)));
   CUDA_TRY(cudaMemset(st->trace.rec, 0, capacity * sizeof(tb::TraceRec)));
   st->trace.cap = unsigned(capacity);
-  return build_graph(st);
+  rt::drop_batch_graph(st);  // recaptured with the buffer on next use
+  return st->n_seqs == 1 ? build_graph(st) : TB200_OK;
 }
 
 int tb200_trace_stop(tb200_state* st, tb200_trace_record* out, size_t cap, size_t* n) {
@@ -995,7 +995,8 @@ int tb200_trace_stop(tb200_state* st, tb200_trace_record* out, size_t cap, size_
   if (k) CUDA_TRY(cudaMemcpy(out, st->trace.rec, k * sizeof(tb::TraceRec), cudaMemcpyDeviceToHost));
   cudaFree(st->trace.rec);
   st->trace = tb::Trace{};
-  return build_graph(st);
+  rt::drop_batch_graph(st);
+  return st->n_seqs == 1 ? build_graph(st) : TB200_OK;
 }
 
 static int state_buffer(tb200_state* st, int which, float** p, size_t* len) {

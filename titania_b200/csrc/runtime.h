@@ -131,6 +131,8 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
                    uint32_t* next);
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);
+// Destroys the batched decode graph (it is captured again on next use).
+void drop_batch_graph(tb200_state* st);
 
 }  // namespace rt
 

@@ -426,6 +426,18 @@ class BatchState:
              out.ctypes.data_as(_lib.F32P))
         return out
 
+    def trace_start(self, capacity: int = 1 << 20) -> None:
+        """Records the batched decode step's kernels (TB200_TRACE_OP_* tags)."""
+        call("tb200_trace_start", self._h, int(capacity))
+        self._trace_cap = int(capacity)
+
+    def trace_stop(self) -> np.ndarray:
+        out = np.zeros(self._trace_cap, dtype=State.TRACE_DTYPE)
+        n = ctypes.c_size_t()
+        call("tb200_trace_stop", self._h, out.ctypes.data_as(ctypes.c_void_p), out.size, ctypes.byref(n))
+        out = out[:min(n.value, out.size)]
+        return out[out["ns"] != 0]
+
 
 class Sampler:
     """model/sampler.rs: top-k, then top-p, at a temperature; temperature 0 is
