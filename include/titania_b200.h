@@ -53,6 +53,7 @@ typedef struct tb200_buffer tb200_buffer; /* Device::Buffer, f32 (model/device.r
 typedef struct tb200_weight tb200_weight; /* Device::Weight, bf16 (model/device.rs:15) */
 typedef struct tb200_model tb200_model;   /* fused-path model (no trait counterpart) */
 typedef struct tb200_state tb200_state;   /* fused-path State (model/model.rs:156-172) */
+typedef struct tb200_tp tb200_tp;         /* a tensor-parallel group (one rank per process and GPU) */
 
 /* Message for the last nonzero return on this thread. */
 TB200_API const char* tb200_last_error(void);
@@ -185,6 +186,34 @@ TB200_API int tb200_state_free(tb200_state* state);
  * be NULL) and the greedy choice to `next_token` (may be NULL). */
 TB200_API int tb200_forward(tb200_model* model, tb200_state* state, const uint32_t* tokens, size_t n, size_t pos,
                   float* logits, uint32_t* next_token);
+
+/* ---- tensor parallelism (no counterpart in the reference) ------------------- */
+
+/* A model split over `world` GPUs of one node, one process per GPU
+ * (Megatron-style): rank r holds q/k/v rows of its num_key_value_heads/world
+ * kv heads and their query heads, the matching o_proj columns, gate/up rows
+ * r*F/world .. (r+1)*F/world and the matching down_proj columns; norms,
+ * embedding and lm_head are replicated. o_proj and down_proj then produce
+ * partial sums, which are added over the group (NCCL all-reduce over NVLink)
+ * before they join the residual stream; every rank computes the same logits.
+ *
+ * Rank 0 makes a group id (tb200_tp_unique_id, 128 bytes) and the caller
+ * hands it to every rank (for instance with torch.distributed); every rank
+ * then calls tb200_tp_init at the same time. A rank's model is created with
+ * its local head and FFN counts (the config divided by world), its local
+ * tensors are bound, and tb200_model_set_tp attaches the group before
+ * tb200_model_finalize. All ranks must then make the same calls in the same
+ * order (each forward step runs the group's collectives). NCCL is loaded at
+ * run time (libnccl.so.2). */
+TB200_API int tb200_tp_unique_id(uint8_t* out, size_t len);
+TB200_API int tb200_tp_init(tb200_device* dev, int rank, int world, const uint8_t* id, size_t len, tb200_tp** out);
+TB200_API int tb200_tp_free(tb200_tp* tp);
+TB200_API int tb200_tp_rank(const tb200_tp* tp);
+TB200_API int tb200_tp_world(const tb200_tp* tp);
+/* Sums a buffer over the group in place (all ranks call it); waits. */
+TB200_API int tb200_tp_allreduce(tb200_tp* tp, tb200_buffer* buf);
+/* Attaches the group to a model before tb200_model_finalize. */
+TB200_API int tb200_model_set_tp(tb200_model* model, tb200_tp* tp);
 
 /* ---- many sequences ------------------------------------------------------- */
 

@@ -81,6 +81,13 @@ SIGNATURES = {
     "tb200_state_free": (ctypes.c_int, [P]),
     "tb200_forward": (ctypes.c_int, [P, P, U32P, SZ, SZ, F32P, U32P]),
     "tb200_batch_state_new": (ctypes.c_int, [P, SZ, SZ, ctypes.c_int, PP]),
+    "tb200_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p, SZ]),
+    "tb200_tp_init": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, SZ, PP]),
+    "tb200_tp_free": (ctypes.c_int, [P]),
+    "tb200_tp_rank": (ctypes.c_int, [P]),
+    "tb200_tp_world": (ctypes.c_int, [P]),
+    "tb200_tp_allreduce": (ctypes.c_int, [P, P]),
+    "tb200_model_set_tp": (ctypes.c_int, [P, P]),
     "tb200_state_seqs": (SZ, [P]),
     "tb200_forward_seq": (ctypes.c_int, [P, P, SZ, U32P, SZ, SZ, F32P, U32P]),
     "tb200_forward_batch": (ctypes.c_int, [P, P, U32P, SZP, F32P, U32P]),

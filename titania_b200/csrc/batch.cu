@@ -60,16 +60,23 @@ __global__ void k_split_rows(const float* __restrict__ x, uint16_t* __restrict__
 
 // One CTA per output row r: x row (row0 + r) of width dim, normalised as
 // cpu.rs:85-94 (mean square, scale = 1/sqrt(ms + eps), v * (scale * w)),
-// written split to row r of the three planes.
-__global__ void __launch_bounds__(256) k_norm_split(const float* __restrict__ x, int row0, int dim,
-                                                   const uint16_t* __restrict__ w, float eps,
+// written split to row r of the three planes. With `add`, the row of `add`
+// is first added to x (the residual update x += o, model.rs:121-123) and x
+// written back.
+__global__ void __launch_bounds__(256) k_norm_split(float* __restrict__ x, const float* __restrict__ add, int row0,
+                                                   int dim, const uint16_t* __restrict__ w, float eps,
                                                    uint16_t* __restrict__ out, size_t plane, TraceAt tr) {
   __shared__ float red[8];
   pdl_launch_dependents();
   if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_START);
   pdl_wait();
   if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_WAITED);
-  const float* xr = x + size_t(row0 + blockIdx.x) * dim;
+  float* xr = x + size_t(row0 + blockIdx.x) * dim;
+  if (add) {
+    const float* ar = add + size_t(row0 + blockIdx.x) * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) xr[i] = __fadd_rn(xr[i], ar[i]);
+    __syncthreads();
+  }
   float ss = 0.f;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
     const float v = xr[i];
@@ -966,9 +973,10 @@ void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t pla
   if (n) launch_pdl(s, dim3(grid), dim3(256), 0, pdl, k_split_rows, x, out, plane, n);
 }
 
-void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
-                       uint16_t* out, size_t plane, bool pdl, const TraceAt& tr) {
-  if (rows > 0) launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, row0, dim, w, eps, out, plane, tr);
+void launch_norm_split(cudaStream_t s, float* x, const float* add, int row0, int rows, int dim, const uint16_t* w,
+                       float eps, uint16_t* out, size_t plane, bool pdl, const TraceAt& tr) {
+  if (rows > 0)
+    launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, add, row0, dim, w, eps, out, plane, tr);
 }
 
 void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl) {

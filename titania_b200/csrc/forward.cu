@@ -81,6 +81,7 @@ int ensure_batch(tb200_state* st) {
   st->cap = int(cap);
   A((void**)&st->bx, cap * H * 4);
   A((void**)&st->bqkv, cap * qkv_w * 4);
+  if (m->tp) A((void**)&st->bpart, cap * H * 4);
   A((void**)&st->blogits, st->n_seqs * V * 4);
   A((void**)&st->bact, 3 * cap * (H + m->q_dim + F) * 2);
   A((void**)&st->bmeta, 3 * cap * 4);
@@ -159,7 +160,7 @@ void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, in
 // The transformer layers over T rows whose token, position and sequence are
 // in bmeta. prefill: the rows are tokens pos0 .. pos0 + T - 1 of sequence
 // `seq`; otherwise each row is one token of its own sequence.
-void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos0, bool pdl) {
+int enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos0, bool pdl) {
   tb200_model* m = st->m;
   const tb200_config& c = m->c;
   cudaStream_t s = m->dev->stream;
@@ -175,8 +176,9 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
   const size_t xn_plane = plane(st, kOpXn), att_plane = plane(st, kOpAtt);
   for (size_t l = 0; l < c.num_hidden_layers; l++) {
     const FusedLayer& L = m->layers[l];
-    tb::launch_norm_split(s, st->bx, 0, T, H, L.attn_norm, c.rms_norm_eps, xn, xn_plane, pdl,
-                          trace_slots(st, tr, TB200_TRACE_OP_NORM, l, uint32_t(T)));
+    // Tensor parallel: the previous layer's reduced down_proj partial joins x here.
+    tb::launch_norm_split(s, st->bx, m->tp && l > 0 ? st->bpart : nullptr, 0, T, H, L.attn_norm, c.rms_norm_eps, xn,
+                          xn_plane, pdl, trace_slots(st, tr, TB200_TRACE_OP_NORM, l, uint32_t(T)));
     gemm(st, T, qkv_w, H, L.m_qkv, kOpXn, tb::kGemmStore, st->bqkv, qkv_w, pdl, nullptr, tr, TB200_TRACE_OP_QKV, l);
     tb::QkvPostArgs q{};
     q.qkv = st->bqkv;
@@ -236,12 +238,23 @@ void enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos
                             uint32_t(a.parts) * uint32_t(c.num_key_value_heads) * uint32_t(T));
       tb::launch_attn_rows(s, a, T, group, pdl);
     }
-    gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
-    tb::launch_norm_split(s, st->bx, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane, pdl,
-                          trace_slots(st, tr, TB200_TRACE_OP_NORM2, l, uint32_t(T)));
+    if (m->tp) {  // partial sums, reduced over the group, added to x by the norm
+      gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmStore, st->bpart, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
+      if (int rc = rt::tp_allreduce(m->tp, st->bpart, size_t(T) * H, s)) return rc;
+    } else {
+      gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
+    }
+    tb::launch_norm_split(s, st->bx, m->tp ? st->bpart : nullptr, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane,
+                          pdl, trace_slots(st, tr, TB200_TRACE_OP_NORM2, l, uint32_t(T)));
     gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl, nullptr, tr, TB200_TRACE_OP_GATE_UP, l);
-    gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
+    if (m->tp) {
+      gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmStore, st->bpart, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
+      if (int rc = rt::tp_allreduce(m->tp, st->bpart, size_t(T) * H, s)) return rc;
+    } else {
+      gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
+    }
   }
+  return TB200_OK;
 }
 
 // Final norm, lm_head and greedy choice for rows row0 .. row0 + rows - 1 of
@@ -253,7 +266,8 @@ void enqueue_head(tb200_state* st, int row0, int rows, tb::ArgmaxRowsArgs am, bo
   const tb200_config& c = m->c;
   const int H = int(c.hidden_size), V = int(c.vocab_size);
   cudaStream_t s = m->dev->stream;
-  tb::launch_norm_split(s, st->bx, row0, rows, H, m->norm, c.rms_norm_eps, operand(st, kOpXn), plane(st, kOpXn), pdl,
+  tb::launch_norm_split(s, st->bx, m->tp ? st->bpart : nullptr, row0, rows, H, m->norm, c.rms_norm_eps,
+                        operand(st, kOpXn), plane(st, kOpXn), pdl,
                         trace_slots(st, tr, TB200_TRACE_OP_FINAL_NORM, 0, uint32_t(rows)));
   gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest, tr, TB200_TRACE_OP_LM_HEAD, 0);
   am.err = st->io + 3;
@@ -269,7 +283,7 @@ int enqueue_decode_step(tb200_state* st) {
   st->trace_next = 0;
   tb::launch_embed(m->dev->stream, st->bx, m->embed, m->c.hidden_size, reinterpret_cast<const uint32_t*>(meta_tok(st)),
                    size_t(T));
-  enqueue_layers(st, T, false, 0, 0, pdl);
+  if (int rc = enqueue_layers(st, T, false, 0, 0, pdl)) return rc;
   tb::ArgmaxRowsArgs am{};
   am.logits = st->blogits;
   am.V = int(m->c.vocab_size);
@@ -355,13 +369,14 @@ void drop_batch_graph(tb200_state* st) {
 void free_batch(tb200_state* st) {
   drop_batch_graph(st);
   void* ptrs[] = {st->bx, st->bqkv, st->blogits, st->bact, st->bmeta, st->rows_part, st->rows_ticket, st->bstep,
-                  st->bout, st->bbest};
+                  st->bout, st->bbest, st->bpart};
   for (void* p : ptrs) cudaFree(p);
   if (st->bmeta_host) cudaFreeHost(st->bmeta_host);
   st->bx = st->bqkv = st->blogits = st->rows_part = nullptr;
   st->bact = nullptr;
   st->bmeta = st->bmeta_host = st->bstep = st->bout = nullptr;
   st->bbest = nullptr;
+  st->bpart = nullptr;
   st->rows_ticket = nullptr;
   st->cap = 0;
 }
@@ -387,7 +402,7 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
     CUDA_TRY(cudaMemcpyAsync(st->bmeta + cap, h + T, T * sizeof(int), cudaMemcpyHostToDevice, s));
     CUDA_TRY(cudaMemcpyAsync(st->bmeta + 2 * cap, h + 2 * T, T * sizeof(int), cudaMemcpyHostToDevice, s));
     tb::launch_embed(s, st->bx, m->embed, m->c.hidden_size, reinterpret_cast<const uint32_t*>(st->bmeta), T);
-    enqueue_layers(st, int(T), true, seq, pos + c0, pdl);
+    if (int rc = enqueue_layers(st, int(T), true, seq, pos + c0, pdl)) return rc;
     last = T;
   }
   tb::ArgmaxRowsArgs am{};

@@ -210,9 +210,10 @@ int attn_rows_chunk(bool kv_f32);
 
 // x[0..n) -> three bf16 planes (store_split3), `plane` elements apart.
 void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t plane, size_t n, bool pdl);
-// planes row r = split3(rmsnorm(x row row0 + r, w)), r < rows; plane = elements between planes.
-void launch_norm_split(cudaStream_t s, const float* x, int row0, int rows, int dim, const uint16_t* w, float eps,
-                       uint16_t* out, size_t plane, bool pdl, const TraceAt& tr = TraceAt{});
+// planes row r = split3(rmsnorm(x row row0 + r, w)), r < rows; plane =
+// elements between planes. With `add` (may be null), x row += add row first.
+void launch_norm_split(cudaStream_t s, float* x, const float* add, int row0, int rows, int dim, const uint16_t* w,
+                       float eps, uint16_t* out, size_t plane, bool pdl, const TraceAt& tr = TraceAt{});
 
 struct QkvPostArgs {
   float* qkv;               // [T][ld]: q heads | k heads | v heads; q rewritten in place

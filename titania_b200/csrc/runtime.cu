@@ -435,6 +435,13 @@ int tb200_model_create(tb200_device* d, const tb200_config* c, tb200_model** out
   return TB200_OK;
 }
 
+int tb200_model_set_tp(tb200_model* m, tb200_tp* tp) {
+  ARG_CHECK(m, "null model");
+  ARG_CHECK(!m->finalized, "set the tensor-parallel group before finalizing the model");
+  m->tp = tp;
+  return TB200_OK;
+}
+
 int tb200_model_bind(tb200_model* m, const char* name, const tb200_weight* w) {
   ARG_CHECK(m && name && w, "null argument");
   ARG_CHECK(!m->finalized, "model already finalized");
@@ -596,6 +603,12 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.rows = int(m->q_dim + 2 * m->kv_dim);
       a.cols = H;
       a.x = st->x;
+      if (m->tp && l > 0) {  // x = x2 + the previous layer's reduced down_proj partial
+        a.x = st->x2;
+        a.partials = st->part_tp2;
+        a.npartials = 1;
+        a.x_out = st->x;
+      }
       a.norm_w = L.attn_norm;
       a.out = st->qkv;
       a.trace_base = slots_for(st->p_qkv.grid);
@@ -664,6 +677,11 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.x = st->att;
       a.out = st->x;
       a.trace_base = slots_for(st->p_o.grid);
+      if (m->tp) {  // this rank's partial sum; reduced over the group next
+        a.out = st->part_tp;
+        tb::launch_mv(s, st->p_o, tb::kMvStore, a, pdl);
+        return;
+      }
       tb::launch_mv(s, st->p_o, tb::kMvResidual, a, pdl);
       return;
     }
@@ -678,6 +696,9 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       if (op == TB200_OP_GATE_UP_SUM) {
         a.partials = st->part_o;
         a.npartials = int(c.num_key_value_heads);
+      } else if (m->tp) {  // x + the reduced o_proj partial
+        a.partials = st->part_tp;
+        a.npartials = 1;
       }
       a.norm_w = m->layers[l].mlp_norm;
       a.out = st->h;
@@ -693,6 +714,12 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.out = st->x;
       a.resid_src = st->x2;
       a.trace_base = slots_for(st->p_down.grid);
+      if (m->tp) {  // this rank's partial sum; the next kernel adds it to x2 once reduced
+        a.out = st->part_tp2;
+        a.resid_src = nullptr;
+        tb::launch_mv(s, st->p_down, tb::kMvStore, a, pdl);
+        return;
+      }
       tb::launch_mv(s, st->p_down, tb::kMvResidual, a, pdl);
       return;
     }
@@ -701,6 +728,11 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.rows = int(c.vocab_size);
       a.cols = H;
       a.x = st->x;
+      if (m->tp) {
+        a.x = st->x2;
+        a.partials = st->part_tp2;
+        a.npartials = 1;
+      }
       a.norm_w = m->norm;
       a.out = st->logits;
       a.partial = st->mv_partial;
@@ -725,18 +757,27 @@ int enqueue_step(tb200_state* st, bool short_ctx) {
   // dependent launch (each waits for the previous to finish): a diagnostic
   // for ordering questions, slower but otherwise identical.
   static const bool pdl = !(getenv("TB200_SERIAL") && getenv("TB200_SERIAL")[0] == '1');
+  tb200_model* m = st->m;
+  cudaStream_t s = m->dev->stream;
+  const size_t H = m->c.hidden_size, Hkv = m->c.num_key_value_heads;
   enqueue_op(st, TB200_OP_EMBED, 0, pdl);
-  for (size_t l = 0; l < st->m->c.num_hidden_layers; l++) {
+  for (size_t l = 0; l < m->c.num_hidden_layers; l++) {
     enqueue_op(st, TB200_OP_QKV, l, pdl);
     if (short_ctx) {
       enqueue_op(st, TB200_OP_ATTENTION_O, l, pdl);
+      if (m->tp)
+        if (int rc = rt::tp_allreduce(m->tp, st->part_o, Hkv * H, s)) return rc;
       enqueue_op(st, TB200_OP_GATE_UP_SUM, l, pdl);
     } else {
       enqueue_op(st, TB200_OP_ATTENTION, l, pdl);
       enqueue_op(st, TB200_OP_O, l, pdl);
+      if (m->tp)
+        if (int rc = rt::tp_allreduce(m->tp, st->part_tp, H, s)) return rc;
       enqueue_op(st, TB200_OP_GATE_UP, l, pdl);
     }
     enqueue_op(st, TB200_OP_DOWN, l, pdl);
+    if (m->tp)
+      if (int rc = rt::tp_allreduce(m->tp, st->part_tp2, H, s)) return rc;
   }
   enqueue_op(st, TB200_OP_LM_HEAD, 0, pdl);
   return launched("decode step");
@@ -829,6 +870,10 @@ int state_create(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb
   A((void**)&st->h, c.intermediate_size * 4);
   A((void**)&st->x2, c.hidden_size * 4);
   A((void**)&st->part_o, Hkv * c.hidden_size * 4);
+  if (m->tp) {
+    A((void**)&st->part_tp, c.hidden_size * 4);
+    A((void**)&st->part_tp2, c.hidden_size * 4);
+  }
   A((void**)&st->logits, c.vocab_size * 4);
   A((void**)&st->part, Hkv * st->max_split * group * (D + 2) * 4);
   A((void**)&st->attn_ticket, Hkv * 4);
@@ -885,7 +930,8 @@ int tb200_state_free(tb200_state* st) {
   if (st->graph_short) cudaGraphExecDestroy(st->graph_short);
   rt::free_batch(st);
   void* ptrs[] = {st->kv, st->rope, st->x, st->qkv, st->att, st->h, st->logits, st->part, st->attn_ticket,
-                  st->mv_partial, st->mv_ticket, st->io, st->tokens_out, st->x2, st->part_o};
+                  st->mv_partial, st->mv_ticket, st->io, st->tokens_out, st->x2, st->part_o, st->part_tp,
+                  st->part_tp2};
   for (void* p : ptrs) cudaFree(p);
   if (st->io_host) cudaFreeHost(st->io_host);
   tb200_model* m = st->m;

@@ -13,6 +13,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+struct tb200_tp;  // tp.cu
+
 struct tb200_device {
   int ordinal = 0;
   int sms = 0;
@@ -60,6 +62,7 @@ struct tb200_model {
   std::vector<FusedLayer> layers;
   const uint16_t *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
   CUtensorMap m_lm{};
+  tb200_tp* tp = nullptr;  // tensor-parallel group: this model holds one rank's heads and FFN columns
   size_t q_dim = 0, kv_dim = 0;
   int attn_o_slices = 0;  // output slices per kv group of the fused attention + o_proj
 };
@@ -80,6 +83,7 @@ struct tb200_state {
   float* rope = nullptr;   // [max_len][head_dim]
   float *x = nullptr, *qkv = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
   float *x2 = nullptr, *part_o = nullptr;  // mid-layer residual; per-group o_proj partials
+  float *part_tp = nullptr, *part_tp2 = nullptr;  // tensor parallel: o_proj / down_proj partial sums [H]
   float* part = nullptr;
   unsigned* attn_ticket = nullptr;
   unsigned long long* mv_partial = nullptr;
@@ -97,6 +101,7 @@ struct tb200_state {
   // ---- many-token / many-sequence path (forward.cu), allocated on first use
   int cap = 0;                 // tokens per pass
   float *bx = nullptr, *bqkv = nullptr, *blogits = nullptr;  // [cap][H], [cap][q+2kv], [n_seqs][V]
+  float* bpart = nullptr;      // tensor parallel: o_proj / down_proj partial sums [cap][H]
   uint16_t* bact = nullptr;    // the kOps operands' planes, one allocation
   int* bmeta = nullptr;        // device [3][cap]: token, position, sequence of each row
   int* bmeta_host = nullptr;   // pinned [3][cap] + readback words
@@ -129,6 +134,9 @@ const char* last_error();
 // logits go to `logits` (host, or null) and its greedy choice to *next.
 int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n, size_t pos, float* logits,
                    uint32_t* next);
+// Sums `n` floats at `buf` over the tensor-parallel group, on stream `s`.
+int tp_allreduce(tb200_tp* tp, float* buf, size_t n, cudaStream_t s);
+
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);
 // Destroys the batched decode graph (it is captured again on next use).

@@ -229,14 +229,16 @@ class Model:
     """Model<B200> with the fused decode path (no trait counterpart in the
     reference; its forward pass computes what model/model.rs:93-149 does)."""
 
-    def __init__(self, config: Config, device: B200, weights: dict):
-        self.config, self.device, self.weights = config, device, weights
+    def __init__(self, config: Config, device: B200, weights: dict, tp=None):
+        self.config, self.device, self.weights, self.tp = config, device, weights, tp
         h = ctypes.c_void_p()
         cfg = config.to_c()
         call("tb200_model_create", device._h, ctypes.byref(cfg), ctypes.byref(h))
         self._h = h.value
         for name, wt in weights.items():
             call("tb200_model_bind", self._h, name.encode(), wt._h)
+        if tp is not None:  # a tensor-parallel rank (titania_b200.tp): partial sums are reduced over the group
+            call("tb200_model_set_tp", self._h, tp._h)
         call("tb200_model_finalize", self._h)
 
     @classmethod
