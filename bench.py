@@ -237,14 +237,114 @@ def run_bs64(args, tb, m, dev, cfg, torch, world):
     }
 
 
+def cached_model_all_ranks(name, rank, world, torch):
+    """The seeded checkpoint, written once (rank 0) while the others wait."""
+    from titania_b200 import synth
+    if rank == 0:
+        path = synth.cached_model(name, seed=0)
+    if world > 1:
+        torch.distributed.barrier()
+    return synth.cached_model(name, seed=0) if rank != 0 else path
+
+
+TP_CTX, TP_GEN, TP_BATCH = 2048, 32, 256  # config 4
+
+
+def run_tp(args, rank, world, torch):
+    """Config 4: Qwen3-4B-shaped random-init weights, tensor-parallel over the
+    `world` GPUs of this node (one rank per GPU; world 1 is the single-GPU
+    baseline). bs1: a 2048-token prompt, then TP_GEN greedy steps (contexts
+    2048..2079), replayed; bs256: 256 sequences, each prefilled with 2048
+    ids, then TP_GEN steps of all at once (bf16 K/V). The all-reduces after
+    o_proj and down_proj are NCCL calls captured in the decode graphs.
+    Device time, max over ranks."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    from titania_b200.tp import TPGroup, load_tp_model
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = tb.B200(local)
+    path = cached_model_all_ranks("qwen3-4b", rank, world, torch)
+    cfg = dict(synth.QWEN3_4B)
+    uid = [TPGroup.unique_id() if rank == 0 else None]
+    if world > 1:
+        torch.distributed.broadcast_object_list(uid, src=0)
+    group = TPGroup(dev, rank, world, uid[0])
+    m = load_tp_model(path, dev, group)
+    stream = torch.cuda.ExternalStream(dev.stream)
+    V = cfg["vocab_size"]
+
+    def timed(fn, warm):
+        fn(warm)
+        dev.sync()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        steps = fn(None)
+        e1.record(stream)
+        dev.sync()
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) * 1e-3
+        if world > 1:
+            t = torch.tensor([secs], dtype=torch.float64, device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            secs = t.item()
+        return steps, secs
+
+    weights, kv_per_pos = model_bytes(cfg, kv_bytes=2)
+    weights32, kv_per_pos32 = model_bytes(cfg, kv_bytes=4)
+    out = {"model": "Qwen3-4B architecture (random-init bf16)", "tp": world, "ctx": [TP_CTX, TP_CTX + TP_GEN - 1]}
+
+    # bs1 (f32 cache, as the reference)
+    st = m.state(TP_CTX + TP_GEN + 1)
+    first = m.forward(st, synth.prompt_tokens(TP_CTX, V, seed=7), 0, logits=False)
+
+    def bs1(warm):
+        n = 1 if warm else max(1, args.tp_gens)
+        for _ in range(n):
+            m.decode_enqueue(st, first, TP_CTX, TP_GEN)
+        return n * TP_GEN
+    steps, secs = timed(bs1, True)
+    step_bytes = weights32 + kv_per_pos32 * (TP_CTX + TP_GEN / 2)
+    out["bs1"] = {"tok_s": steps / secs, "ms_per_step": secs / steps * 1e3, "kv_cache": "f32",
+                  "hbm_frac_of_8tbs_x_n": step_bytes * steps / secs / (NOMINAL_HBM_GBS * 1e9 * world)}
+    del st
+
+    # bs256 (bf16 cache)
+    if args.tp_batch > 0:
+        B = args.tp_batch
+        bs = m.batch_state(B, TP_CTX + TP_GEN, kv="bf16")
+        t0 = time.perf_counter()
+        bfirst = [m.forward_seq(bs, i, synth.prompt_tokens(TP_CTX, V, seed=2000 + i), 0, logits=False)
+                  for i in range(B)]
+        prefill_s = time.perf_counter() - t0
+        pos = [TP_CTX] * B
+
+        def bsn(warm):
+            n = 1 if warm else max(1, args.tp_gens)
+            for _ in range(n):
+                m.decode_batch_enqueue(bs, bfirst, pos, TP_GEN)
+            return n * TP_GEN
+        steps, secs = timed(bsn, True)
+        step_bytes = weights + B * kv_per_pos * (TP_CTX + TP_GEN / 2)
+        out[f"bs{B}"] = {"tok_s": steps * B / secs, "ms_per_step": secs / steps * 1e3, "kv_cache": "bf16",
+                         "prefill_seconds": prefill_s,
+                         "hbm_frac_of_8tbs_x_n": step_bytes * steps / secs / (NOMINAL_HBM_GBS * 1e9 * world)}
+        del bs
+    del m
+    group.close()
+    return out
+
+
 def run_ours(args, rank, world, torch):
     import titania_b200 as tb
     from titania_b200 import synth
 
-    dev = tb.B200(rank if world > 1 else 0)
+    dev = tb.B200(int(os.environ.get("LOCAL_RANK", rank)) if world > 1 else 0)
     torch.cuda.set_device(dev.ordinal)
     cfg = dict(synth.QWEN3_0_6B)
-    path = synth.cached_model("qwen3-0.6b", seed=0)
+    path = cached_model_all_ranks("qwen3-0.6b", rank, world, torch)
     m = tb.Model.load(path, dev)
     prompt = synth.prompt_tokens(PROMPT, cfg["vocab_size"], seed=1)
     st = m.state(PROMPT + GEN + 1)
@@ -347,6 +447,9 @@ def run_ours(args, rank, world, torch):
         result["kernels"] = kern
     if rank == 0 and world == 1 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline(path, prompt, budget_s=args.cpu_seconds)
+    if args.tp4b or (world > 1 and not args.no_tp):
+        del st, m
+        result["tp4b"] = run_tp(args, rank, world, torch)
     return result
 
 
@@ -477,6 +580,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-bs64", action="store_true", help="skip the batch-64 decode (config 3)")
     ap.add_argument("--bs64-gens", type=int, default=2, help="timed 128-step generations of the bs64 decode")
+    ap.add_argument("--tp4b", action="store_true",
+                    help="also run config 4 (Qwen3-4B, tensor-parallel over the ranks; default when N > 1)")
+    ap.add_argument("--no-tp", action="store_true", help="skip config 4 when N > 1")
+    ap.add_argument("--tp-gens", type=int, default=2, help="timed 32-step generations of config 4")
+    ap.add_argument("--tp-batch", type=int, default=TP_BATCH, help="config 4's large batch (0: skip it)")
     ap.add_argument("--profile-op", choices=["qkv", "attention", "o", "gate_up", "down", "lm_head"],
                     help="small case for ncu: launch one fused kernel only")
     ap.add_argument("--launches", type=int, default=3)

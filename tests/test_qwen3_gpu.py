@@ -154,3 +154,35 @@ def test_qwen3_0_6b_greedy_32_steps(b200, qwen06b, qwen06b_oracle, kv, rel, abs_
     st2 = m.state(64, kv=kv)
     first = m.forward(st2, prompt, 0, logits=False)
     assert [first] + m.generate(st2, first, 16, 31) == ref_tokens
+
+
+@pytest.fixture(scope="module")
+def qwen4b():
+    return synth.cached_model("qwen3-4b", seed=0)
+
+
+@pytest.mark.slow
+def test_qwen3_4b_single_token_and_batched(b200, qwen4b):
+    """Qwen3-4B shapes (hidden 2560, 4 query heads per kv
+    head, FFN 9728): a 16-token prompt and 4 greedy steps on the single-token
+    path, and two sequences decoded together, against the oracle."""
+    prompt = synth.prompt_tokens(16, 151936, seed=5)
+    steps = 4
+    ref = orc.Model(qwen4b)
+    ref_tokens, ref_logits = orc.greedy_generate(ref, prompt, steps + 1, max_len=32)
+    m = tb.Model.load(qwen4b, b200)
+    st = m.state(32)
+    logits = m.forward(st, prompt, 0)
+    pos = len(prompt)
+    for i in range(steps + 1):
+        close(logits, ref_logits[i], REL, ABS)
+        t = int(np.argmax(logits))
+        assert t == ref_tokens[i], f"step {i}"
+        if i < steps:
+            logits = m.forward(st, [t], pos)
+            pos += 1
+    bs = m.batch_state(2, 32, kv="bf16")
+    first = [m.forward_seq(bs, i, prompt, 0, logits=False) for i in range(2)]
+    out = m.generate_batch(bs, first, [16, 16], steps)
+    for i in range(2):
+        assert [first[i]] + out[:, i].tolist() == ref_tokens, f"sequence {i}"

@@ -409,10 +409,12 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
 // The same work as k_attn_rows for a bf16 cache, with the two products on
 // mma.sync m16n8k16 (bf16 in, f32 accumulate):
 //   scores   S[p][c] = K[p][:] . qc[:]   A = 16 cached keys (ldmatrix), B = the
-//            query as 8 columns (column 2j + h: plane j of head h, q = q0 + q1 +
-//            q2; columns 6, 7 and absent heads zero), kept in registers;
+//            query as columns (column GRP j + h: plane j of head h, q = q0 + q1
+//            + q2; padded to blocks of 8 with zeros), kept in registers;
 //   values   O[d][c] = V[:][d] . Pc[:]   A = 16 dimensions x 16 positions of V
 //            (ldmatrix.trans), B = the probabilities split the same way.
+// Scores and outputs are regrouped by head through small per-warp tiles in
+// shared memory.
 // Every product is exact (bf16 x bf16 in f32) and the planes make q and P
 // exact, so only the f32 accumulation order differs from k_attn_rows. Keys
 // and values arrive by TMA (128-byte swizzle, so ldmatrix is conflict-free)
@@ -455,14 +457,17 @@ __device__ __forceinline__ uint16_t plane_of(float v, int j) {
 
 template <int GRP>
 __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CUtensorMap cache, AttnRowsArgs a) {
-  static_assert(GRP == 1 || GRP == 2, "three planes per head in 8 columns");
+  constexpr int NC = 3 * GRP;        // live columns: plane j of head h at column GRP j + h
+  constexpr int NB = (NC + 7) / 8;   // MMA column blocks of 8
+  constexpr int HP = (GRP + 1) / 2;  // (position, head) pairs per lane: 16 positions x GRP heads / 32 lanes
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // swizzled boxes: 1024-byte aligned
   __shared__ __align__(16) float qs[GRP][kD];
-  __shared__ __align__(16) uint16_t pw[4][8][16];  // per warp: probabilities [column][position]
+  __shared__ __align__(16) uint16_t pw[4][8 * NB][16];  // per warp: probabilities [column][position]
+  __shared__ float sw[4][16][8 * NB + 1];               // per warp: scores [position][column]
+  __shared__ float corr_w[4][GRP];
   __shared__ float wm[4][GRP], wl[4][GRP];
-  __shared__ __align__(16) float wo[4][GRP][kD];
   __shared__ __align__(8) uint64_t bar[kTcStages];
   __shared__ int verdict, is_last;
 
@@ -514,35 +519,44 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   if (tid == 0)
     while (issued < kTcStages && issued < nchunks) issue(issued++);
   for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
-  for (int i = tid; i < 4 * 8 * 16; i += 128) (&pw[0][0][0])[i] = 0;  // columns 6, 7 stay zero
+  for (int i = tid; i < 4 * 8 * NB * 16; i += 128) (&pw[0][0][0])[i] = 0;  // pad columns stay zero
   __syncthreads();
 
-  // The query as B fragments: column c = lane / 4, k = dims 16 kb + 2 (lane % 4) (+1, +8, +9).
-  const int col = lane >> 2, kq = 2 * (lane & 3);
-  const int qh = col & 1, qj = col >> 1;  // column c = 2 plane + head
-  const bool qlive = qj < 3 && qh < GRP;
-  uint32_t qb[8][2];
+  // The query as B fragments: column c = 8 nb + lane / 4, k = dims 16 kb + 2 (lane % 4) (+1, +8, +9).
+  const int kq = 2 * (lane & 3);
+  uint32_t qb[NB][8][2];
 #pragma unroll
-  for (int kb = 0; kb < 8; kb++)
+  for (int nb = 0; nb < NB; nb++) {
+    const int c = 8 * nb + (lane >> 2);
+    const int qj = c / GRP, qh = c % GRP;
+    const bool live = c < NC;
 #pragma unroll
-    for (int hf = 0; hf < 2; hf++) {
-      const int d = 16 * kb + kq + 8 * hf;
-      const uint32_t lo = qlive ? plane_of(qs[qh][d], qj) : 0u;
-      const uint32_t hi = qlive ? plane_of(qs[qh][d + 1], qj) : 0u;
-      qb[kb][hf] = lo | (hi << 16);
-    }
+    for (int kb = 0; kb < 8; kb++)
+#pragma unroll
+      for (int hf = 0; hf < 2; hf++) {
+        const int d = 16 * kb + kq + 8 * hf;
+        const uint32_t lo = live ? plane_of(qs[qh][d], qj) : 0u;
+        const uint32_t hi = live ? plane_of(qs[qh][d + 1], qj) : 0u;
+        qb[nb][kb][hf] = lo | (hi << 16);
+      }
+  }
 
   const float scale = 1.0f / sqrtf(float(kD));
-  float m[GRP], l[GRP];
-  float o[8][4];  // O^T fragments: dims 16 mb + lane / 4 (+8), columns 2 (lane % 4) (+1)
+  // This lane's (position, head) pairs: position rr of the warp's 16, heads
+  // hb + 2 i. Its running max and sum per head.
+  const int rr = lane & 15, hb = lane >> 4;
+  float m[HP], l[HP];
 #pragma unroll
-  for (int h = 0; h < GRP; h++) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
+  for (int i = 0; i < HP; i++) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
   }
+  float o[8][NB][4];  // O^T fragments: dims 16 mb + lane / 4 (+8), columns 8 nb + 2 (lane % 4) (+1)
 #pragma unroll
-  for (int mb = 0; mb < 8; mb++) o[mb][0] = o[mb][1] = o[mb][2] = o[mb][3] = 0.f;
-  const int r = lane >> 2;  // this lane's score rows: positions r and r + 8 of the warp's 16
+  for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+    for (int nb = 0; nb < NB; nb++) o[mb][nb][0] = o[mb][nb][1] = o[mb][nb][2] = o[mb][nb][3] = 0.f;
+  const int r = lane >> 2;
   bool failed = false;
   for (int i = 0; i < nchunks; i++) {
     const int s = i % kTcStages;
@@ -556,76 +570,85 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     mbar_wait(&bar[s], (i / kTcStages) & 1, nullptr);  // the phase is complete: returns at once
     const uint32_t kbase = smem_u32(sm + size_t(s) * kTcStage), vbase = kbase + 2 * kTcBox;
     const int pw0 = 16 * warp;  // the warp's first position in the chunk
-    // Scores for positions pw0 .. pw0 + 15.
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
     {
+      float sc[NB][4];
+#pragma unroll
+      for (int nb = 0; nb < NB; nb++) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
       const int ar = pw0 + (lane & 7) + 8 * ((lane >> 3) & 1), au = lane >> 4;
 #pragma unroll
       for (int kb = 0; kb < 8; kb++) {
         uint32_t af[4];
         ldsm_x4(kbase + (kb >> 2) * kTcBox + sw128(ar, 2 * (kb & 3) + au), af);
-        mma16816(sc, af, qb[kb][0], qb[kb][1]);
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) mma16816(sc[nb], af, qb[nb][kb][0], qb[nb][kb][1]);
       }
-    }
-    // Sum the three planes (lanes 4r .. 4r+3 hold columns 0-1, 2-3, 4-5, 6-7).
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 1);
-      sc[e] += __shfl_xor_sync(0xffffffffu, sc[e], 2);
-    }
-    // sc: [0] (row r, head 0) [1] (row r, head 1) [2] (row r+8, head 0) [3] (row r+8, head 1)
-    const int n = min(kTcCh, p1 - c0);
-    float pv[4];
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int p = pw0 + r + 8 * (e >> 1);
-      pv[e] = p < n ? scale * sc[e] : -INFINITY;
-    }
-#pragma unroll
-    for (int h = 0; h < GRP; h++) {
-      float mx = fmaxf(pv[h], pv[2 + h]);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[h], mx);
-      const float corr = m[h] == -INFINITY ? 0.f : expf(m[h] - mn);
-      const float e0 = pv[h] == -INFINITY ? 0.f : expf(pv[h] - mn);
-      const float e1 = pv[2 + h] == -INFINITY ? 0.f : expf(pv[2 + h] - mn);
-      pv[h] = e0;
-      pv[2 + h] = e1;
-      float sum = e0 + e1;
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      l[h] = l[h] * corr + sum;
-      m[h] = mn;
-#pragma unroll
-      for (int mb = 0; mb < 8; mb++) {
-        o[mb][h] *= corr;      // column 2 (lane % 4) + h: head h (GRP 2) ...
-        o[mb][2 + h] *= corr;  // ... rows d and d + 8
-      }
-    }
-    // Probabilities as B fragments: plane (lane % 4) of each head, via the warp's pw.
-    if ((lane & 3) < 3) {
-      const int j = lane & 3;
-#pragma unroll
-      for (int h = 0; h < GRP; h++) {
-        const int c = 2 * j + h;
-        pw[warp][c][r] = plane_of(pv[h], j);
-        pw[warp][c][r + 8] = plane_of(pv[2 + h], j);
+      for (int nb = 0; nb < NB; nb++) {
+        sw[warp][r][8 * nb + kq] = sc[nb][0];
+        sw[warp][r][8 * nb + kq + 1] = sc[nb][1];
+        sw[warp][r + 8][8 * nb + kq] = sc[nb][2];
+        sw[warp][r + 8][8 * nb + kq + 1] = sc[nb][3];
       }
     }
     __syncwarp();
-    const uint32_t pb0 = *reinterpret_cast<const uint32_t*>(&pw[warp][col][kq]);
-    const uint32_t pb1 = *reinterpret_cast<const uint32_t*>(&pw[warp][col][kq + 8]);
+    const int n = min(kTcCh, p1 - c0);
+    const bool live_pos = pw0 + rr < n;
+    float pv[HP];
+#pragma unroll
+    for (int i2 = 0; i2 < HP; i2++) {
+      const int h = hb + 2 * i2;
+      float sc = -INFINITY;
+      if (h < GRP && live_pos) sc = scale * ((sw[warp][rr][h] + sw[warp][rr][GRP + h]) + sw[warp][rr][2 * GRP + h]);
+      // Running statistics of head h over this warp's positions (lanes with the same hb).
+      float mx = sc;
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[i2], mx);
+      const float corr = (m[i2] == -INFINITY || mn == -INFINITY) ? 0.f : expf(m[i2] - mn);
+      const float e = sc == -INFINITY ? 0.f : expf(sc - mn);
+      float sum = e;
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l[i2] = l[i2] * corr + sum;
+      m[i2] = mn;
+      pv[i2] = e;
+      if (rr == 0 && h < GRP) corr_w[warp][h] = corr;
+    }
+    // Probabilities as B fragments (three planes per head), via the warp's pw.
+#pragma unroll
+    for (int i2 = 0; i2 < HP; i2++) {
+      const int h = hb + 2 * i2;
+      if (h < GRP)
+#pragma unroll
+        for (int j = 0; j < 3; j++) pw[warp][GRP * j + h][rr] = plane_of(pv[i2], j);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+      for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int c = 8 * nb + kq + (e & 1);
+          o[mb][nb][e] *= c < NC ? corr_w[warp][c % GRP] : 0.f;
+        }
     {
       const int vr = pw0 + (lane & 7) + 8 * (lane >> 4), vu = (lane >> 3) & 1;
+      uint32_t pb[NB][2];
+#pragma unroll
+      for (int nb = 0; nb < NB; nb++) {
+        pb[nb][0] = *reinterpret_cast<const uint32_t*>(&pw[warp][8 * nb + (lane >> 2)][kq]);
+        pb[nb][1] = *reinterpret_cast<const uint32_t*>(&pw[warp][8 * nb + (lane >> 2)][kq + 8]);
+      }
 #pragma unroll
       for (int mb = 0; mb < 8; mb++) {
         uint32_t af[4];
         ldsm_x4_t(vbase + (mb >> 2) * kTcBox + sw128(vr, 2 * (mb & 3) + vu), af);
-        mma16816(o[mb], af, pb0, pb1);
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) mma16816(o[mb][nb], af, pb[nb][0], pb[nb][1]);
       }
     }
-    __syncthreads();  // every warp is done with stage s (and its pw)
+    __syncthreads();  // every warp is done with stage s (and its pw, sw)
     if (tid == 0 && issued < nchunks) issue(issued++);
   }
   if (failed) {
@@ -636,28 +659,26 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     return;
   }
 
-  // Per warp: add the planes (lanes 4r .. 4r+2) and publish (m, l, O).
+  // Per warp: publish (m, l) per head and O per (column, dim) into the idle
+  // stage memory, then thread d combines the warps and the planes.
+  float* ow = reinterpret_cast<float*>(sm);  // [4][8 NB][kD]
 #pragma unroll
   for (int mb = 0; mb < 8; mb++)
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      o[mb][e] += __shfl_xor_sync(0xffffffffu, o[mb][e], 1);
-      o[mb][e] += __shfl_xor_sync(0xffffffffu, o[mb][e], 2);
-    }
-  if ((lane & 3) == 0) {
+    for (int nb = 0; nb < NB; nb++)
 #pragma unroll
-    for (int mb = 0; mb < 8; mb++)
-#pragma unroll
-      for (int h = 0; h < GRP; h++) {
-        wo[warp][h][16 * mb + r] = o[mb][h];
-        wo[warp][h][16 * mb + r + 8] = o[mb][2 + h];
+      for (int e = 0; e < 4; e++) {
+        const int c = 8 * nb + kq + (e & 1), d = 16 * mb + r + 8 * (e >> 1);
+        ow[(warp * 8 * NB + c) * kD + d] = o[mb][nb][e];
       }
-  }
-  if (lane == 0)
+  if (rr == 0)
 #pragma unroll
-    for (int h = 0; h < GRP; h++) {
-      wm[warp][h] = m[h];
-      wl[warp][h] = l[h];
+    for (int i2 = 0; i2 < HP; i2++) {
+      const int h = hb + 2 * i2;
+      if (h < GRP) {
+        wm[warp][h] = m[i2];
+        wl[warp][h] = l[i2];
+      }
     }
   __syncthreads();
   float res[GRP], rm[GRP], rl[GRP];
@@ -670,8 +691,10 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
 #pragma unroll
     for (int w = 0; w < 4; w++) {
       const float wt = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+      const float* ob = ow + size_t(w * 8 * NB) * kD + tid;
+      const float ov = (ob[size_t(h) * kD] + ob[size_t(GRP + h) * kD]) + ob[size_t(2 * GRP + h) * kD];
       L += wl[w][h] * wt;
-      O += wo[w][h][tid] * wt;
+      O += ov * wt;
     }
     res[h] = O;
     rm[h] = M;
@@ -951,6 +974,8 @@ cudaError_t init_batch_kernels() {
 #undef TB_ATTR
   if (e == cudaSuccess) e = tc_attr<1>();
   if (e == cudaSuccess) e = tc_attr<2>();
+  if (e == cudaSuccess) e = tc_attr<4>();
+  if (e == cudaSuccess) e = tc_attr<8>();
   return e;
 }
 
@@ -983,14 +1008,18 @@ void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl)
   if (tokens > 0) launch_pdl(s, dim3(tokens), dim3(128), 0, pdl, k_qkv_post, a);
 }
 
-bool attn_rows_tensor_cores(bool kv_f32, int group) { return !kv_f32 && (group == 1 || group == 2); }
+bool attn_rows_tensor_cores(bool kv_f32, int group) {
+  return !kv_f32 && (group == 1 || group == 2 || group == 4 || group == 8);
+}
 
 void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl) {
   if (tokens <= 0) return;
   const dim3 grid(unsigned(a.parts), unsigned(a.n_kv_heads), unsigned(tokens));
   if (attn_rows_tensor_cores(a.kv_f32 != 0, group) && a.cache_map) {
     if (group == 1) launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<1>, *a.cache_map, a);
-    else launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<2>, *a.cache_map, a);
+    if (group == 2) launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<2>, *a.cache_map, a);
+    if (group == 4) launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<4>, *a.cache_map, a);
+    if (group == 8) launch_pdl(s, grid, dim3(128), kTcSmem, pdl, k_attn_rows_tc<8>, *a.cache_map, a);
     return;
   }
 #define TB_ROWS(G)                                                                                   \

@@ -111,7 +111,7 @@ def write_model(dirpath: str, config: dict, seed: int = 0, std: float = 0.02) ->
     hbytes = json.dumps(header, separators=(",", ":")).encode()
     hbytes += b" " * ((-len(hbytes)) % 8)
     h = hashlib.sha256()
-    tmp = os.path.join(dirpath, "model.safetensors.tmp")
+    tmp = os.path.join(dirpath, f"model.safetensors.{os.getpid()}.tmp")  # concurrent writers never share it
     with open(tmp, "wb") as fh:
         pre = struct.pack("<Q", len(hbytes)) + hbytes
         fh.write(pre)
