@@ -370,15 +370,15 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
     if (tid == 0) a.trace.at(cta, TB200_TRACE_DONE);
     return;
   }
-  const int stride = kD + 2;
+  const int stride = kPartStride;
   float* pbase = a.part + ((size_t(t) * a.n_kv_heads + g) * a.parts) * GRP * stride;
 #pragma unroll
   for (int h = 0; h < GRP; h++) {
     float* pp = pbase + (size_t(part) * GRP + h) * stride;
-    pp[2 + tid] = acc[h];
+    pp[tid] = acc[h];
     if (tid == 0) {
-      pp[0] = m_s[h];
-      pp[1] = l_s[h];
+      pp[kD] = m_s[h];
+      pp[kD + 1] = l_s[h];
     }
   }
   __threadfence();
@@ -388,18 +388,14 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  {
+    // The staging ring is free now: it holds the merge weights, then the merged heads.
+    __shared__ float hsum[GRP];
+    float* wbuf = reinterpret_cast<float*>(smem);
+    float(*merged)[128] = reinterpret_cast<float(*)[128]>(wbuf + ((nparts * GRP + 3) & ~3));  // 16-byte aligned
+    merge_splits<GRP>(pbase, nparts, wbuf, hsum, merged);
 #pragma unroll
-  for (int h = 0; h < GRP; h++) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nparts; sp++) M = fmaxf(M, __ldcg(pbase + (size_t(sp) * GRP + h) * stride));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < nparts; sp++) {
-      const float* pp = pbase + (size_t(sp) * GRP + h) * stride;
-      const float wt = expf(__ldcg(pp) - M);
-      L += __ldcg(pp + 1) * wt;
-      O += __ldcg(pp + 2 + tid) * wt;
-    }
-    store_split3(a.out, a.plane, out_at + size_t(h) * kD, O / L);
+    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, merged[h][tid]);
   }
   if (tid == 0) *ticket = 0u;
 }
@@ -707,15 +703,15 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     if (tid == 0) a.trace.at(cta, TB200_TRACE_DONE);
     return;
   }
-  const int stride = kD + 2;
+  const int stride = kPartStride;
   float* pbase = a.part + ((size_t(t) * a.n_kv_heads + g) * a.parts) * GRP * stride;
 #pragma unroll
   for (int h = 0; h < GRP; h++) {
     float* pp = pbase + (size_t(part) * GRP + h) * stride;
-    pp[2 + tid] = res[h];
+    pp[tid] = res[h];
     if (tid == 0) {
-      pp[0] = rm[h];
-      pp[1] = rl[h];
+      pp[kD] = rm[h];
+      pp[kD + 1] = rl[h];
     }
   }
   __threadfence();
@@ -725,18 +721,14 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  {
+    // The staging ring is free now: it holds the merge weights, then the merged heads.
+    __shared__ float hsum[GRP];
+    float* wbuf = reinterpret_cast<float*>(sm);
+    float(*merged)[128] = reinterpret_cast<float(*)[128]>(wbuf + ((nparts * GRP + 3) & ~3));  // 16-byte aligned
+    merge_splits<GRP>(pbase, nparts, wbuf, hsum, merged);
 #pragma unroll
-  for (int h = 0; h < GRP; h++) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nparts; sp++) M = fmaxf(M, __ldcg(pbase + (size_t(sp) * GRP + h) * stride));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < nparts; sp++) {
-      const float* pp = pbase + (size_t(sp) * GRP + h) * stride;
-      const float wt = expf(__ldcg(pp) - M);
-      L += __ldcg(pp + 1) * wt;
-      O += __ldcg(pp + 2 + tid) * wt;
-    }
-    store_split3(a.out, a.plane, out_at + size_t(h) * kD, O / L);
+    for (int h = 0; h < GRP; h++) store_split3(a.out, a.plane, out_at + size_t(h) * kD, merged[h][tid]);
   }
   if (tid == 0) *ticket = 0u;
 }

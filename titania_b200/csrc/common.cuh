@@ -210,6 +210,56 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// A partial attention result of one head over a run of positions: the 128
+// output dimensions (unnormalised), then the run's max and sum; 132 floats
+// so that every record starts on a 16-byte boundary.
+constexpr int kPartStride = 132;
+
+// The merge of `n` partial attention results of GRP heads (split s, head h
+// at part + (s GRP + h) kPartStride), run by the last CTA of a
+// split-context attention (128 threads): all threads read the splits'
+// maxima at once, a warp per head turns them into weights exp(m_s - M)
+// (kept in `w`, n GRP floats of shared memory) and the sum L, then a warp
+// per head sums the splits' outputs, lane l taking dimensions 4l .. 4l+3
+// with one 16-byte load per split, every load independent. The merged head
+// h is left in out[h][0..128) (shared memory).
+template <int GRP>
+__device__ __forceinline__ void merge_splits(const float* part, int n, float* w, float* hsum, float (*out)[128]) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = int(blockDim.x) >> 5;
+  for (int i = tid; i < n * GRP; i += blockDim.x) w[i] = __ldcg(part + size_t(i) * kPartStride + 128);
+  __syncthreads();
+  for (int h = warp; h < GRP; h += nwarps) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < n; sp += 32) M = fmaxf(M, w[sp * GRP + h]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int sp = lane; sp < n; sp += 32) {
+      const float mm = w[sp * GRP + h];
+      const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
+      L += __ldcg(part + size_t(sp * GRP + h) * kPartStride + 129) * wt;
+      w[sp * GRP + h] = wt;
+    }
+    L = warp_sum(L);
+    if (lane == 0) hsum[h] = L;
+  }
+  __syncthreads();
+  for (int h = warp; h < GRP; h += nwarps) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int sp = 0; sp < n; sp++) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(part + size_t(sp * GRP + h) * kPartStride) + lane);
+      const float wt = w[sp * GRP + h];
+      acc.x += v.x * wt;
+      acc.y += v.y * wt;
+      acc.z += v.z * wt;
+      acc.w += v.w * wt;
+    }
+    const float inv = 1.0f / hsum[h];
+    *reinterpret_cast<float4*>(&out[h][4 * lane]) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  }
+  __syncthreads();
+}
+
 // 8 bf16 weights (one 16-byte word) dotted with 8 f32 activations, in the
 // order w0*x0 + ... accumulated into acc.
 __device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {

@@ -85,7 +85,7 @@ int ensure_batch(tb200_state* st) {
   A((void**)&st->blogits, st->n_seqs * V * 4);
   A((void**)&st->bact, 3 * cap * (H + m->q_dim + F) * 2);
   A((void**)&st->bmeta, 3 * cap * 4);
-  A((void**)&st->rows_part, st->n_seqs * Hkv * parts * group * (D + 2) * 4);
+  A((void**)&st->rows_part, st->n_seqs * Hkv * parts * group * tb::kPartStride * 4);
   A((void**)&st->rows_ticket, st->n_seqs * Hkv * 4);
   A((void**)&st->bstep, 4 * 4);
   A((void**)&st->bbest, st->n_seqs * 8);

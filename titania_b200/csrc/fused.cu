@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
   __syncthreads();
 
   // Merge the four warps: thread d of each head.
-  const int stride = kHd + 2;
+  const int stride = kPartStride;
   for (int h = 0; h < GRP; h++) {
     float M = -INFINITY;
 #pragma unroll
@@ -583,10 +583,10 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
       a.out[size_t(g * GRP + h) * kHd + tid] = o / L;
     } else {
       float* pp = a.part + ((size_t(g) * a.max_split + split) * GRP + h) * stride;
-      pp[2 + tid] = o;
+      pp[tid] = o;
       if (tid == 0) {
-        pp[0] = M;
-        pp[1] = L;
+        pp[kHd] = M;
+        pp[kHd + 1] = L;
       }
     }
   }
@@ -600,19 +600,14 @@ __global__ void __launch_bounds__(128) attn_decode(AttnArgs a) {
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int h = 0; h < GRP; h++) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; sp++)
-      M = fmaxf(M, __ldcg(a.part + ((size_t(g) * a.max_split + sp) * GRP + h) * stride));
-    float L = 0.f, o = 0.f;
-    for (int sp = 0; sp < nsplit; sp++) {
-      const float* pp = a.part + ((size_t(g) * a.max_split + sp) * GRP + h) * stride;
-      const float mm = __ldcg(pp);
-      const float wt = mm == -INFINITY ? 0.f : expf(mm - M);
-      L += __ldcg(pp + 1) * wt;
-      o += __ldcg(pp + 2 + tid) * wt;
-    }
-    a.out[size_t(g * GRP + h) * kHd + tid] = o / L;
+  {
+    // The key/value staging area is free now: it holds the merge weights.
+    __shared__ float hsum[GRP];
+    float(*merged)[128] = reinterpret_cast<float(*)[128]>(wacc);  // the warp sums are consumed
+    merge_splits<GRP>(a.part + size_t(g) * a.max_split * GRP * stride, nsplit, reinterpret_cast<float*>(smem), hsum,
+                      merged);
+#pragma unroll
+    for (int h = 0; h < GRP; h++) a.out[size_t(g * GRP + h) * kHd + tid] = merged[h][tid];
   }
   if (tid == 0) a.ticket[g] = 0u;
 }

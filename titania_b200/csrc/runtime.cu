@@ -853,8 +853,16 @@ int state_create(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb
   const int sms = m->dev->sms;
   const size_t Hkv = c.num_key_value_heads, D = c.head_dim, L = c.num_hidden_layers;
   const size_t group = c.num_attention_heads / Hkv;
-  // Attention splits of kAttnChunk positions cover the whole cache.
+  // Attention splits of kAttnChunk positions cover the whole cache; their
+  // merge keeps one weight per (split, head) in the kernel's staging memory.
   st->max_split = int((max_len + tb::kAttnChunk - 1) / tb::kAttnChunk);
+  if (size_t(st->max_split) * group * 4 > tb::attn_smem_bytes(kv_dtype == TB200_KV_F32)) {
+    m->live_states--;
+    delete st;
+    return fail(TB200_ERR_ARG, "state: max_len " + std::to_string(max_len) + " is past the longest context (" +
+                                   std::to_string(tb::attn_smem_bytes(kv_dtype == TB200_KV_F32) / 4 / group *
+                                                  tb::kAttnChunk) + ") of this model's attention kernels");
+  }
   std::vector<float> table = rope_table(max_len, D, c.rope_theta);
   cudaError_t e = cudaSuccess;
   auto A = [&](void** p, size_t bytes) {
@@ -875,7 +883,7 @@ int state_create(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb
     A((void**)&st->part_tp2, c.hidden_size * 4);
   }
   A((void**)&st->logits, c.vocab_size * 4);
-  A((void**)&st->part, Hkv * st->max_split * group * (D + 2) * 4);
+  A((void**)&st->part, Hkv * st->max_split * group * tb::kPartStride * 4);
   A((void**)&st->attn_ticket, Hkv * 4);
   A((void**)&st->mv_partial, size_t(sms) * 8);
   A((void**)&st->mv_ticket, 4);
