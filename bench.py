@@ -531,19 +531,21 @@ def profile_op(args):
 
 
 def profile_bs64(args):
-    """For ncu: config 3's 64 x 1024-token prefill (64 passes of 228 kernels),
-    then `--launches` batched decode steps (228 kernels each)."""
+    """For ncu: config 3's prefill (`--profile-seqs` sequences x
+    `--profile-ctx` tokens, one pass of 228 kernels each at the defaults), then
+    `--launches` batched decode steps (228 kernels each). Smaller sequence
+    counts and contexts keep full captures to a few GB on the device."""
     import titania_b200 as tb
     from titania_b200 import synth
     dev = tb.B200(0)
     m = tb.Model.load(synth.cached_model("qwen3-0.6b", seed=0), dev)
     V = synth.QWEN3_0_6B["vocab_size"]
-    bs = m.batch_state(BS64_SEQS, BS64_CTX + BS64_GEN, kv="bf16")
-    first = [m.forward_seq(bs, i, synth.prompt_tokens(BS64_CTX, V, seed=1000 + i), 0, logits=False)
-             for i in range(BS64_SEQS)]
-    m.decode_batch_enqueue(bs, first, [BS64_CTX] * BS64_SEQS, args.launches)
+    n, ctx = args.profile_seqs, args.profile_ctx
+    bs = m.batch_state(n, ctx + BS64_GEN, kv="bf16")
+    first = [m.forward_seq(bs, i, synth.prompt_tokens(ctx, V, seed=1000 + i), 0, logits=False) for i in range(n)]
+    m.decode_batch_enqueue(bs, first, [ctx] * n, args.launches)
     dev.sync()
-    print(json.dumps({"profile_bs64": True, "steps": args.launches}))
+    print(json.dumps({"profile_bs64": True, "seqs": n, "ctx": ctx, "steps": args.launches}))
 
 
 GEMM_SHAPES = [(151936, 1024, 64), (6144, 1024, 64), (4096, 1024, 64), (1024, 2048, 64), (1024, 3072, 64),
@@ -590,6 +592,8 @@ def main():
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--profile-bs64", action="store_true",
                     help="small case for ncu: the bs64 prefill, then --launches batched decode steps")
+    ap.add_argument("--profile-seqs", type=int, default=BS64_SEQS)
+    ap.add_argument("--profile-ctx", type=int, default=BS64_CTX)
     ap.add_argument("--profile-gemm", action="store_true",
                     help="small case for ncu: the tensor-core contraction at the batched shapes")
     args = ap.parse_args()

@@ -301,20 +301,22 @@ enum {
   TB200_TRACE_DONE = 4,         /* the CTA finished its rows */
   TB200_TRACE_ISSUED = 5,       /* the CTA's last weight copy was issued */
   TB200_TRACE_LAST_WEIGHTS = 6, /* the CTA's last weight chunk is in shared memory */
+  TB200_TRACE_REDUCE = 7,       /* a split-K CTA's cluster holds every partial tile (reduction starts) */
 };
 
 /* Kernels of a state's batched decode step (tb200_forward_batch and friends),
  * as the op half of their trace tags. */
 enum {
-  TB200_TRACE_OP_NORM = 17,     /* rmsnorm + split before q|k|v */
+  TB200_TRACE_OP_EMBED = 16,    /* embedding + the first RMSNorm's input */
+  TB200_TRACE_OP_NORM = 17,     /* rmsnorm + split before q|k|v (tensor parallel) */
   TB200_TRACE_OP_QKV = 18,      /* q|k|v contraction */
-  TB200_TRACE_OP_QKV_POST = 19, /* QK-norm, RoPE, cache append */
+  TB200_TRACE_OP_QKV_POST = 19, /* (no longer launched: QK-norm, RoPE and the cache append run in the q|k|v epilogue) */
   TB200_TRACE_OP_ATTENTION = 20,
   TB200_TRACE_OP_O = 21,        /* o_proj contraction (+ residual) */
-  TB200_TRACE_OP_NORM2 = 22,    /* rmsnorm + split before gate|up */
+  TB200_TRACE_OP_NORM2 = 22,    /* rmsnorm + split before gate|up (tensor parallel) */
   TB200_TRACE_OP_GATE_UP = 23,  /* gate|up contraction (+ silu) */
   TB200_TRACE_OP_DOWN = 24,     /* down contraction (+ residual) */
-  TB200_TRACE_OP_FINAL_NORM = 25,
+  TB200_TRACE_OP_FINAL_NORM = 25, /* (tensor parallel) */
   TB200_TRACE_OP_LM_HEAD = 26,  /* lm_head contraction (+ argmax keys) */
   TB200_TRACE_OP_ARGMAX = 27,
 };

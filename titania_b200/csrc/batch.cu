@@ -95,6 +95,42 @@ __global__ void __launch_bounds__(256) k_norm_split(float* __restrict__ x, const
   if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_DONE);
 }
 
+// One CTA per token: x row = the embedding row of the token (cpu.rs:38-47),
+// then the first RMSNorm's input as the contraction consumes it: planes of
+// x * w and the row's sum of squares (ssq[t], one part).
+__global__ void __launch_bounds__(256) k_embed_split(float* __restrict__ x, const uint16_t* __restrict__ table,
+                                                    int dim, const int* __restrict__ tok, int vocab,
+                                                    const uint16_t* __restrict__ w, uint16_t* __restrict__ out,
+                                                    size_t plane, float* __restrict__ ssq, int* err, TraceAt tr) {
+  __shared__ float red[8];
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) tr.at(blockIdx.x, TB200_TRACE_START);
+  pdl_wait();
+  int id = tok[blockIdx.x];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_error(err, TB200_ERR_ARG);
+    id = 0;
+  }
+  const uint16_t* er = table + size_t(id) * dim;
+  float* xr = x + size_t(blockIdx.x) * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = bf16f(er[i]);
+    xr[i] = v;
+    ss = fmaf(v, v, ss);
+    store_split3(out, plane, size_t(blockIdx.x) * dim + i, __fmul_rn(v, bf16f(w[i])));
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int i = 0; i < int(blockDim.x >> 5); i++) tot += red[i];
+    ssq[blockIdx.x] = tot;
+    tr.at(blockIdx.x, TB200_TRACE_DONE);
+  }
+}
+
 // ---- QK-norm, RoPE, cache append -------------------------------------------------
 
 // One CTA (4 warps) per token; a warp takes one head at a time, lane l
@@ -994,6 +1030,14 @@ void launch_norm_split(cudaStream_t s, float* x, const float* add, int row0, int
                        float eps, uint16_t* out, size_t plane, bool pdl, const TraceAt& tr) {
   if (rows > 0)
     launch_pdl(s, dim3(rows), dim3(256), 0, pdl, k_norm_split, x, add, row0, dim, w, eps, out, plane, tr);
+}
+
+void launch_embed_split(cudaStream_t s, float* x, const uint16_t* table, int dim, const int* tok, int vocab,
+                        const uint16_t* w, uint16_t* out, size_t plane, float* ssq, int* err, int tokens, bool pdl,
+                        const TraceAt& tr) {
+  if (tokens > 0)
+    launch_pdl(s, dim3(tokens), dim3(256), 0, pdl, k_embed_split, x, table, dim, tok, vocab, w, out, plane, ssq, err,
+               tr);
 }
 
 void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl) {

@@ -12,13 +12,19 @@
 //               independent Model::forward calls would run), captured as a
 //               CUDA graph, and a greedy token loop on the device.
 //
-// A pass over T tokens, per layer l (model.rs:100-141):
-//   norm_split(x) -> xn          gemm(qkv, xn) -> qkv
-//   qkv_post(qkv) -> q, cache    attention(q, cache) -> att (three planes)
-//   gemm(o, att) += x            norm_split(x) -> xn
-//   gemm(gate|up, xn) -> h       gemm(down, h) += x
-// then the final norm, lm_head and greedy choice for the rows that need
-// logits (model.rs:144-147).
+// A pass over T tokens (model.rs:100-147), five kernels per layer:
+//   embed: x, and the first RMSNorm's input (planes of x * w, sums of squares)
+//   gemm(qkv, xn) * norm scale, QK-norm, RoPE  -> q, cache
+//   attention(q, cache)                        -> att (three planes)
+//   gemm(o, att): x += o, the MLP norm's input  -> xn, sums of squares
+//   gemm(gate|up, xn) * norm scale, silu * up   -> h
+//   gemm(down, h): x += d, the next norm's input -> xn, sums of squares
+// then lm_head (* the final norm's scale, argmax keys folded in) and the
+// greedy choice for the rows that need logits. Each RMSNorm (cpu.rs:85-94)
+// is split between the kernel that produces its input (x * w and per-tile
+// sums of squares) and the contraction that consumes it (the per-token
+// scale applied to the accumulator). Tensor parallel runs the norms as
+// kernels of their own, after the all-reduce of the partial sums.
 
 #include <algorithm>
 #include <cstdlib>
@@ -82,6 +88,9 @@ int ensure_batch(tb200_state* st) {
   A((void**)&st->bx, cap * H * 4);
   A((void**)&st->bqkv, cap * qkv_w * 4);
   if (m->tp) A((void**)&st->bpart, cap * H * 4);
+  const size_t hparts = std::max<size_t>(1, (H + 127) / 128);
+  A((void**)&st->ssq_a, cap * hparts * 4);
+  A((void**)&st->ssq_b, cap * hparts * 4);
   A((void**)&st->blogits, st->n_seqs * V * 4);
   A((void**)&st->bact, 3 * cap * (H + m->q_dim + F) * 2);
   A((void**)&st->bmeta, 3 * cap * 4);
@@ -137,10 +146,11 @@ tb::TraceAt trace_slots(tb200_state* st, bool on, int op, size_t layer, uint32_t
 }
 
 void gemm(tb200_state* st, int T, int M, int K, const CUtensorMap& w, int op, int epi, float* out, int ldo,
-          bool pdl, unsigned long long* best = nullptr, bool traced = false, int top = 0, size_t layer = 0) {
+          bool pdl, unsigned long long* best = nullptr, bool traced = false, int top = 0, size_t layer = 0,
+          const tb::GemmArgs* extra = nullptr) {
   tb200_device* d = st->dev;
   const tb::GemmPlan p = tb::plan_gemm(M, K, T, d->sms, d->max_cluster);
-  tb::GemmArgs a{};
+  tb::GemmArgs a = extra ? *extra : tb::GemmArgs{};
   a.M = M;
   a.K = K;
   a.T = T;
@@ -167,25 +177,27 @@ int enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos0
   const int H = int(c.hidden_size), F = int(c.intermediate_size);
   const int qkv_w = int(m->q_dim + 2 * m->kv_dim), qd = int(m->q_dim);
   const int group = int(c.num_attention_heads / c.num_key_value_heads);
+  const int hparts = std::max(1, (H + 127) / 128);
   const size_t eb = st->kv_f32 ? 4 : 2;
   const size_t kv_layer = 2 * c.num_key_value_heads * st->max_len * c.head_dim;
   int* err = st->io + 3;
   const bool tr = !prefill;  // the batched step is traced (its graph is captured once)
+  const bool fused = !m->tp;  // RMSNorms folded into the contractions (tensor parallel adds partials first)
   uint16_t* xn = operand(st, kOpXn);
   uint16_t* att = operand(st, kOpAtt);
   const size_t xn_plane = plane(st, kOpXn), att_plane = plane(st, kOpAtt);
+  if (fused)
+    tb::launch_embed_split(s, st->bx, m->embed, H, meta_tok(st), int(c.vocab_size), m->layers[0].attn_norm, xn,
+                           xn_plane, st->ssq_a, err, T, pdl, trace_slots(st, tr, TB200_TRACE_OP_EMBED, 0, uint32_t(T)));
+  else
+    tb::launch_embed(s, st->bx, m->embed, c.hidden_size, reinterpret_cast<const uint32_t*>(meta_tok(st)), size_t(T));
   for (size_t l = 0; l < c.num_hidden_layers; l++) {
     const FusedLayer& L = m->layers[l];
-    // Tensor parallel: the previous layer's reduced down_proj partial joins x here.
-    tb::launch_norm_split(s, st->bx, m->tp && l > 0 ? st->bpart : nullptr, 0, T, H, L.attn_norm, c.rms_norm_eps, xn,
-                          xn_plane, pdl, trace_slots(st, tr, TB200_TRACE_OP_NORM, l, uint32_t(T)));
-    gemm(st, T, qkv_w, H, L.m_qkv, kOpXn, tb::kGemmStore, st->bqkv, qkv_w, pdl, nullptr, tr, TB200_TRACE_OP_QKV, l);
-    tb::QkvPostArgs q{};
-    q.qkv = st->bqkv;
-    q.ld = qkv_w;
+    // q|k|v with QK-norm, RoPE and the cache append in its epilogue.
+    tb::GemmArgs q{};
+    q.eps = c.rms_norm_eps;
     q.q_norm = L.q_norm;
     q.k_norm = L.k_norm;
-    q.eps = c.rms_norm_eps;
     q.rope = st->rope;
     q.kv = st->kv + l * kv_layer * eb;
     q.seq_stride = st->seq_stride;
@@ -194,11 +206,18 @@ int enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos0
     q.n_heads = int(c.num_attention_heads);
     q.n_kv_heads = int(c.num_key_value_heads);
     q.n_seqs = int(st->n_seqs);
-    q.pos = meta_pos(st);
-    q.seq = meta_seq(st);
-    q.err = err;
-    q.trace = trace_slots(st, tr, TB200_TRACE_OP_QKV_POST, l, uint32_t(T));
-    tb::launch_qkv_post(s, q, T, pdl);
+    q.tok_pos = meta_pos(st);
+    q.tok_seq = meta_seq(st);
+    if (fused) {
+      q.in_ssq = st->ssq_a;
+      q.in_parts = l == 0 ? 1 : hparts;
+      q.in_dim = H;
+    } else {
+      // Tensor parallel: the previous layer's reduced down_proj partial joins x here.
+      tb::launch_norm_split(s, st->bx, l > 0 ? st->bpart : nullptr, 0, T, H, L.attn_norm, c.rms_norm_eps, xn,
+                            xn_plane, pdl, trace_slots(st, tr, TB200_TRACE_OP_NORM, l, uint32_t(T)));
+    }
+    gemm(st, T, qkv_w, H, L.m_qkv, kOpXn, tb::kGemmQkv, st->bqkv, qkv_w, pdl, nullptr, tr, TB200_TRACE_OP_QKV, l, &q);
     if (prefill) {
       tb::AttnPrefillArgs a{};
       a.q = st->bqkv;
@@ -238,20 +257,37 @@ int enqueue_layers(tb200_state* st, int T, bool prefill, size_t seq, size_t pos0
                             uint32_t(a.parts) * uint32_t(c.num_key_value_heads) * uint32_t(T));
       tb::launch_attn_rows(s, a, T, group, pdl);
     }
-    if (m->tp) {  // partial sums, reduced over the group, added to x by the norm
+    if (fused) {
+      // x += o_proj; then the MLP RMSNorm's input (planes of x * w, sums of squares).
+      tb::GemmArgs o{};
+      o.next_w = L.mlp_norm;
+      o.next_split = xn;
+      o.next_plane = xn_plane;
+      o.out_ssq = st->ssq_b;
+      gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResidNorm, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l, &o);
+      tb::GemmArgs gu{};
+      gu.in_ssq = st->ssq_b;
+      gu.in_parts = hparts;
+      gu.in_dim = H;
+      gu.eps = c.rms_norm_eps;
+      gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl, nullptr, tr, TB200_TRACE_OP_GATE_UP, l,
+           &gu);
+      // x += down_proj; then the next layer's (or the final) RMSNorm's input.
+      tb::GemmArgs dn{};
+      dn.next_w = l + 1 < c.num_hidden_layers ? m->layers[l + 1].attn_norm : m->norm;
+      dn.next_split = xn;
+      dn.next_plane = xn_plane;
+      dn.out_ssq = st->ssq_a;
+      gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResidNorm, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l,
+           &dn);
+    } else {  // partial sums, reduced over the group, added to x by the norm
       gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmStore, st->bpart, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
       if (int rc = rt::tp_allreduce(m->tp, st->bpart, size_t(T) * H, s)) return rc;
-    } else {
-      gemm(st, T, H, qd, L.m_o, kOpAtt, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_O, l);
-    }
-    tb::launch_norm_split(s, st->bx, m->tp ? st->bpart : nullptr, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane,
-                          pdl, trace_slots(st, tr, TB200_TRACE_OP_NORM2, l, uint32_t(T)));
-    gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl, nullptr, tr, TB200_TRACE_OP_GATE_UP, l);
-    if (m->tp) {
+      tb::launch_norm_split(s, st->bx, st->bpart, 0, T, H, L.mlp_norm, c.rms_norm_eps, xn, xn_plane, pdl,
+                            trace_slots(st, tr, TB200_TRACE_OP_NORM2, l, uint32_t(T)));
+      gemm(st, T, 2 * F, H, L.m_gu, kOpXn, tb::kGemmSilu, nullptr, 0, pdl, nullptr, tr, TB200_TRACE_OP_GATE_UP, l);
       gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmStore, st->bpart, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
       if (int rc = rt::tp_allreduce(m->tp, st->bpart, size_t(T) * H, s)) return rc;
-    } else {
-      gemm(st, T, H, F, L.m_down, kOpH, tb::kGemmResid, st->bx, H, pdl, nullptr, tr, TB200_TRACE_OP_DOWN, l);
     }
   }
   return TB200_OK;
@@ -266,10 +302,20 @@ void enqueue_head(tb200_state* st, int row0, int rows, tb::ArgmaxRowsArgs am, bo
   const tb200_config& c = m->c;
   const int H = int(c.hidden_size), V = int(c.vocab_size);
   cudaStream_t s = m->dev->stream;
-  tb::launch_norm_split(s, st->bx, m->tp ? st->bpart : nullptr, row0, rows, H, m->norm, c.rms_norm_eps,
-                        operand(st, kOpXn), plane(st, kOpXn), pdl,
-                        trace_slots(st, tr, TB200_TRACE_OP_FINAL_NORM, 0, uint32_t(rows)));
-  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest, tr, TB200_TRACE_OP_LM_HEAD, 0);
+  tb::GemmArgs h{};
+  if (m->tp) {
+    tb::launch_norm_split(s, st->bx, st->bpart, row0, rows, H, m->norm, c.rms_norm_eps, operand(st, kOpXn),
+                          plane(st, kOpXn), pdl, trace_slots(st, tr, TB200_TRACE_OP_FINAL_NORM, 0, uint32_t(rows)));
+  } else {
+    // The last down_proj left x * w_final as planes at rows row0 ..; the scale comes from the sums of squares.
+    h.in_ssq = st->ssq_a;
+    h.in_parts = std::max(1, (H + 127) / 128);
+    h.in_dim = H;
+    h.eps = c.rms_norm_eps;
+    h.act_row0 = row0;
+  }
+  gemm(st, rows, V, H, m->m_lm, kOpXn, tb::kGemmStore, st->blogits, V, pdl, st->bbest, tr, TB200_TRACE_OP_LM_HEAD, 0,
+       &h);
   am.err = st->io + 3;
   am.trace = trace_slots(st, tr, TB200_TRACE_OP_ARGMAX, 0, 1);
   tb::launch_argmax_finish(s, am, st->bbest, rows, pdl);
@@ -281,8 +327,6 @@ int enqueue_decode_step(tb200_state* st) {
   tb200_model* m = st->m;
   const int T = int(st->n_seqs);
   st->trace_next = 0;
-  tb::launch_embed(m->dev->stream, st->bx, m->embed, m->c.hidden_size, reinterpret_cast<const uint32_t*>(meta_tok(st)),
-                   size_t(T));
   if (int rc = enqueue_layers(st, T, false, 0, 0, pdl)) return rc;
   tb::ArgmaxRowsArgs am{};
   am.logits = st->blogits;
@@ -369,14 +413,14 @@ void drop_batch_graph(tb200_state* st) {
 void free_batch(tb200_state* st) {
   drop_batch_graph(st);
   void* ptrs[] = {st->bx, st->bqkv, st->blogits, st->bact, st->bmeta, st->rows_part, st->rows_ticket, st->bstep,
-                  st->bout, st->bbest, st->bpart};
+                  st->bout, st->bbest, st->bpart, st->ssq_a, st->ssq_b};
   for (void* p : ptrs) cudaFree(p);
   if (st->bmeta_host) cudaFreeHost(st->bmeta_host);
   st->bx = st->bqkv = st->blogits = st->rows_part = nullptr;
   st->bact = nullptr;
   st->bmeta = st->bmeta_host = st->bstep = st->bout = nullptr;
   st->bbest = nullptr;
-  st->bpart = nullptr;
+  st->bpart = st->ssq_a = st->ssq_b = nullptr;
   st->rows_ticket = nullptr;
   st->cap = 0;
 }
@@ -401,7 +445,6 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
     CUDA_TRY(cudaMemcpyAsync(st->bmeta, h, T * sizeof(int), cudaMemcpyHostToDevice, s));
     CUDA_TRY(cudaMemcpyAsync(st->bmeta + cap, h + T, T * sizeof(int), cudaMemcpyHostToDevice, s));
     CUDA_TRY(cudaMemcpyAsync(st->bmeta + 2 * cap, h + 2 * T, T * sizeof(int), cudaMemcpyHostToDevice, s));
-    tb::launch_embed(s, st->bx, m->embed, m->c.hidden_size, reinterpret_cast<const uint32_t*>(st->bmeta), T);
     if (int rc = enqueue_layers(st, int(T), true, seq, pos + c0, pdl)) return rc;
     last = T;
   }

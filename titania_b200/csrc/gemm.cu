@@ -68,12 +68,21 @@ constexpr int kTmemCols = 2 * kAccCols;
 // Floor of the dynamic shared memory: more than half of an SM's 228 KB.
 constexpr size_t kMinSmem = 116 * 1024;
 
+// The epilogue warps' scratch for a group of up to 32 tokens: per-warp
+// partial sums, per-token scales, and one head's values per token.
+struct EpiScratch {
+  float red[4][32];
+  float scale[32];
+  float tile[32][128];
+};
+
 // Shared memory: `stages` tiles, then 8-byte slots: full[stages],
 // empty[stages], tfull[2], tempty[2], mdone, the tensor-memory address and
-// flags (6 slots), then the epilogue warps' argmax keys [4][kBN]; plus
-// alignment slack.
+// flags (6 slots), then the epilogue warps' argmax keys [4][kBN] and their
+// EpiScratch; plus alignment slack.
 size_t smem_for(int stages) {
-  const size_t need = size_t(stages) * kStage + (2 * size_t(stages) + 11) * 8 + 4 * kBN * 8 + 1024;
+  const size_t need =
+      size_t(stages) * kStage + (2 * size_t(stages) + 11) * 8 + 4 * kBN * 8 + sizeof(EpiScratch) + 1024;
   return need > kMinSmem ? need : kMinSmem;
 }
 
@@ -139,31 +148,137 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
 }
 
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+// silu(g) * u = g / (1 + exp(-g)) * u (cpu.rs:151-155), with the fast
+// exponential and division (a few ulp from libm's; within every parity bar).
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
-// Applies the epilogue to N consecutive tokens t0 .. t0 + N - 1 of one row
-// (v[j] = accumulator of token t0 + j). Residual reads are all issued before
-// any write. kGemmSilu pairs lanes (2i, 2i+1) = (gate, up) of hidden row
-// row/2: every lane of the warp calls it with the same t0.
+// The epilogue of N consecutive tokens t0 .. t0 + N - 1 (N <= 32) of row
+// `row` = m0 + 32 q + lane of row tile `mt`: v[j] is the accumulator of
+// token t0 + j. All 128 epilogue threads call it together (named barrier 1);
+// residual reads are issued before any write. On return v holds the values
+// the epilogue produced from (after the input scale; kGemmQkv: after
+// QK-norm and RoPE).
 template <int EPI, int N>
-__device__ __forceinline__ void epilogue_tokens(const GemmArgs& a, int row, bool row_ok, int t0, const float (&v)[N]) {
+__device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bool row_ok, int q, int lane, int t0,
+                                          float (&v)[N], EpiScratch& es) {
+  static_assert(N <= 32, "scratch holds 32 tokens");
+  const int e = int(threadIdx.x) - 64;  // 0 .. 127 over the epilogue warps
+  if (a.in_ssq) {
+    // The input's RMSNorm (cpu.rs:85-94): the scale of each token, from the
+    // partial sums of squares the producer of the input left, in order.
+    if (e < N && t0 + e < a.T) {
+      const float* p = a.in_ssq + size_t(a.act_row0 + t0 + e) * a.in_parts;
+      float ss = 0.f;
+      for (int i = 0; i < a.in_parts; i++) ss += p[i];
+      es.scale[e] = 1.0f / sqrtf(ss / float(a.in_dim) + a.eps);
+    }
+    named_sync(1, 128);
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] *= es.scale[j];
+    named_sync(1, 128);
+  }
   if (EPI == kGemmStore) {
 #pragma unroll
     for (int j = 0; j < N; j++)
       if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = v[j];
-  } else if (EPI == kGemmResid) {
+  } else if (EPI == kGemmResid || EPI == kGemmResidNorm) {
     float x[N];
 #pragma unroll
     for (int j = 0; j < N; j++) x[j] = row_ok && t0 + j < a.T ? a.out[size_t(t0 + j) * a.ldo + row] : 0.f;
 #pragma unroll
-    for (int j = 0; j < N; j++)
-      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = __fadd_rn(x[j], v[j]);
-  } else {  // kGemmSilu
+    for (int j = 0; j < N; j++) {
+      x[j] = __fadd_rn(x[j], v[j]);
+      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = x[j];
+    }
+    if (EPI == kGemmResidNorm) {
+      // The next RMSNorm's input: x * w as planes, and this tile's sum of
+      // squares of x per token (its consumer divides by the row length).
+      const float w = row_ok ? bf16f(a.next_w[row]) : 0.f;
+#pragma unroll
+      for (int j = 0; j < N; j++) {
+        const float sq = warp_sum(row_ok ? x[j] * x[j] : 0.f);
+        if (lane == 0) es.red[q][j] = sq;
+        if (row_ok && t0 + j < a.T)
+          store_split3(a.next_split, a.next_plane, size_t(t0 + j) * a.ldo + row, __fmul_rn(x[j], w));
+      }
+      named_sync(1, 128);
+      if (e < N && t0 + e < a.T)
+        a.out_ssq[size_t(t0 + e) * a.mtiles + mt] = ((es.red[0][e] + es.red[1][e]) + es.red[2][e]) + es.red[3][e];
+      named_sync(1, 128);
+    }
+#pragma unroll
+    for (int j = 0; j < N; j++) v[j] = x[j];
+  } else if (EPI == kGemmSilu) {
+    // Lanes 2i (gate) and 2i+1 (up) of hidden row i share tokens: the even
+    // lane finishes token j, the odd lane token j + 1.
+    static_assert(N % 2 == 0, "token pairs");
+    const bool even = (row & 1) == 0;
+#pragma unroll
+    for (int j = 0; j < N; j += 2) {
+      const float other = __shfl_xor_sync(0xffffffffu, even ? v[j + 1] : v[j], 1);
+      const float g = even ? v[j] : other, u = even ? other : v[j + 1];
+      const int t = t0 + j + (even ? 0 : 1);
+      if (row_ok && t < a.T) store_split3(a.out_split, a.plane, size_t(t) * a.ldh + (row >> 1), silu_mul(g, u));
+    }
+  } else {  // kGemmQkv: tile mt is query head mt, key head mt - nq, or value head mt - nq - nk
+    const int nq = a.n_heads, nk = a.n_kv_heads;
+    const int d = 32 * q + lane;  // the head dimension of this row
+    const bool is_v = mt >= nq + nk;
+    if (!is_v) {
+      const uint16_t* nw = mt < nq ? a.q_norm : a.k_norm;
+      if (nw) {
+        // QK-norm over the head (model.rs:111-116 with cpu.rs:85-94).
+#pragma unroll
+        for (int j = 0; j < N; j++) {
+          const float sq = warp_sum(v[j] * v[j]);
+          if (lane == 0) es.red[q][j] = sq;
+        }
+        named_sync(1, 128);
+        const float w = bf16f(nw[d]);
+#pragma unroll
+        for (int j = 0; j < N; j++) {
+          const float ss = ((es.red[0][j] + es.red[1][j]) + es.red[2][j]) + es.red[3][j];
+          const float sc = 1.0f / sqrtf(ss / 128.0f + a.eps);
+          v[j] = __fmul_rn(v[j], __fmul_rn(sc, w));
+        }
+        named_sync(1, 128);
+      }
+      // RoPE (cpu.rs:96-111): element d pairs with d ^ 64.
+#pragma unroll
+      for (int j = 0; j < N; j++) es.tile[j][d] = v[j];
+      named_sync(1, 128);
+      const int i = d & 63;
+#pragma unroll
+      for (int j = 0; j < N; j++) {
+        if (t0 + j >= a.T) continue;
+        const float other = es.tile[j][d ^ 64];
+        const int pos = a.tok_pos[a.act_row0 + t0 + j];
+        const float2 cs = (pos >= 0 && pos < a.max_len)
+                              ? *reinterpret_cast<const float2*>(a.rope + size_t(pos) * 128 + 2 * i)
+                              : make_float2(1.f, 0.f);
+        v[j] = d < 64 ? __fsub_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y))
+                      : __fadd_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y));
+      }
+      named_sync(1, 128);
+    }
 #pragma unroll
     for (int j = 0; j < N; j++) {
-      const float u = __shfl_xor_sync(0xffffffffu, v[j], 1);
-      if (row_ok && t0 + j < a.T && (row & 1) == 0)
-        store_split3(a.out_split, a.plane, size_t(t0 + j) * a.ldh + (row >> 1), silu_mul(v[j], u));
+      const int t = t0 + j;
+      if (t >= a.T) continue;
+      if (mt < nq) {
+        a.out[size_t(t) * a.ldo + row] = v[j];
+        continue;
+      }
+      const int pos = a.tok_pos[a.act_row0 + t], sq = a.tok_seq[a.act_row0 + t];
+      if (pos < 0 || pos >= a.max_len || sq < 0 || sq >= a.n_seqs) {
+        if (d == 0) set_error(a.err, TB200_ERR_ARG);
+        continue;
+      }
+      const int kh = is_v ? mt - nq - nk : mt - nq;
+      const size_t at = size_t(sq) * a.seq_stride + (is_v ? size_t(nk) * a.max_len * 128 : 0) +
+                        (size_t(kh) * a.max_len + pos) * 128 + d;
+      if (a.kv_f32) static_cast<float*>(a.kv)[at] = v[j];
+      else static_cast<uint16_t*>(a.kv)[at] = f2bf(v[j]);
     }
   }
 }
@@ -227,6 +342,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
   int* flags = reinterpret_cast<int*>(tslot + 1);  // [0..3] per epilogue warp, [4] verdict
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(mdone + 6);  // [4][kBN]
+  EpiScratch& es = *reinterpret_cast<EpiScratch*>(keys + 4 * kBN);
   auto sA = [&](int s) { return sm + size_t(s) * kStage; };
   auto sB = [&](int s) { return sm + size_t(s) * kStage + kStageA; };
 
@@ -269,9 +385,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // tile's first stages of weights go out before the dependency wait.
       const uint64_t pol_w = l2_evict_first(), pol_x = l2_evict_last();
       auto load_b = [&](int s, int kb, int n0) {
-        tma_load_2d(sB(s), &tx0, kb * kBK, n0, &full[s], pol_x);
-        tma_load_2d(sB(s) + kBN * 128, &tx1, kb * kBK, n0, &full[s], pol_x);
-        tma_load_2d(sB(s) + 2 * kBN * 128, &tx2, kb * kBK, n0, &full[s], pol_x);
+        const int y = a.act_row0 + n0;
+        tma_load_2d(sB(s), &tx0, kb * kBK, y, &full[s], pol_x);
+        tma_load_2d(sB(s) + kBN * 128, &tx1, kb * kBK, y, &full[s], pol_x);
+        tma_load_2d(sB(s) + 2 * kBN * 128, &tx2, kb * kBK, y, &full[s], pol_x);
       };
       const int pre = ntiles > 0 ? min(nk, stages) : 0;
       for (int i = 0; i < pre; i++) {
@@ -372,7 +489,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int c = 0; c < kBN; c += 16) {
           float v[16];
           tmem_ld_tokens(taddr, c, v);
-          epilogue_tokens<EPI, 16>(a, row, row_ok, n0 + c, v);
+          epi_group<EPI, 16>(a, tile_m(ti), row, row_ok, q, lane, n0 + c, v, es);
           if (EPI == kGemmStore && a.best) {
 #pragma unroll
             for (int j = 0; j < 16; j++) {
@@ -412,9 +529,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
-  if (split) {
+  if constexpr (split) {
     __syncwarp();
     cluster_sync_all();  // every split's partial tile is in place
+    if (threadIdx.x == 64) a.trace.at(cta, TB200_TRACE_REDUCE);
     if (warp >= 2 && flags[4]) {
       // Cluster CTA r sums the S partial tiles for tokens r PER .. + PER - 1,
       // in split order: every partial load is issued before any is used.
@@ -437,7 +555,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int r = 1; r < S; r++) v[j] += pv[r][j];
       }
-      epilogue_tokens<EPI, PER>(a, row, row_ok, n0 + j0, v);
+      epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + j0, v, es);
       if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + j0, v, lane);
     }
     __syncwarp();
@@ -569,6 +687,8 @@ cudaError_t init_gemm_kernels() {
   cudaError_t e = set_attrs<kGemmStore>();
   if (e == cudaSuccess) e = set_attrs<kGemmResid>();
   if (e == cudaSuccess) e = set_attrs<kGemmSilu>();
+  if (e == cudaSuccess) e = set_attrs<kGemmResidNorm>();
+  if (e == cudaSuccess) e = set_attrs<kGemmQkv>();
   return e;
 }
 
@@ -612,6 +732,8 @@ void launch_gemm(cudaStream_t s, const GemmPlan& p, int epi, const CUtensorMap& 
   TB_GEMM_S(kGemmStore)
   TB_GEMM_S(kGemmResid)
   TB_GEMM_S(kGemmSilu)
+  TB_GEMM_S(kGemmResidNorm)
+  TB_GEMM_S(kGemmQkv)
 #undef TB_GEMM_S
 }
 

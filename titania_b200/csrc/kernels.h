@@ -161,6 +161,10 @@ enum GemmEpilogue {
   kGemmStore = 0,  // out[t][r] = acc
   kGemmResid,      // out[t][r] += acc                    (residual stream)
   kGemmSilu,       // rows interleaved (gate, up): planes [t][r/2] = split3(silu(g) * u)
+  kGemmResidNorm,  // out[t][r] += acc, then the next RMSNorm's input: planes of
+                   // out[t][r] * next_w[r] and per-tile sums of squares out_ssq[t][tile]
+  kGemmQkv,        // q|k|v rows, 128-row tile = one head: QK-norm, RoPE at the
+                   // token's position; q to out[t][r], k and v into the cache
 };
 struct GemmArgs {
   int M, K, T;              // weight rows, columns (reduction), tokens
@@ -172,6 +176,27 @@ struct GemmArgs {
   int ldh;
   unsigned long long* best;  // kGemmStore: per token, the argmax key (argmax_key) of its
                              // outputs is folded in with atomicMax; null: none
+  // The input's RMSNorm scale, folded into every epilogue: acc *= 1 /
+  // sqrt(sum_p in_ssq[act_row0 + t][p] / in_dim + eps); null: none.
+  const float* in_ssq;
+  int in_parts, in_dim;
+  float eps;
+  int act_row0;             // first activation row (token) the contraction reads
+  // kGemmResidNorm: the next RMSNorm's weight, its input planes (`next_plane`
+  // apart, rows of ldo) and the sums of squares [T][mtiles].
+  const uint16_t* next_w;
+  uint16_t* next_split;
+  size_t next_plane;
+  float* out_ssq;
+  // kGemmQkv (QkvPostArgs' meaning): norms, RoPE table, cache, token rows.
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const float* rope;
+  void* kv;                 // this layer's cache block of sequence 0
+  size_t seq_stride;
+  int kv_f32, max_len, n_heads, n_kv_heads, n_seqs;
+  const int* tok_pos;
+  const int* tok_seq;
   int* err;
   TraceAt trace;  // CTA index blockIdx.x + gridDim.x (blockIdx.y + gridDim.y blockIdx.z)
 };
@@ -214,6 +239,12 @@ void launch_split_rows(cudaStream_t s, const float* x, uint16_t* out, size_t pla
 // elements between planes. With `add` (may be null), x row += add row first.
 void launch_norm_split(cudaStream_t s, float* x, const float* add, int row0, int rows, int dim, const uint16_t* w,
                        float eps, uint16_t* out, size_t plane, bool pdl, const TraceAt& tr = TraceAt{});
+
+// x rows = embedding rows of tok[0..tokens), planes of x * w, ssq[t] = sum of
+// squares of row t (the first RMSNorm's input in the fused layer sequence).
+void launch_embed_split(cudaStream_t s, float* x, const uint16_t* table, int dim, const int* tok, int vocab,
+                        const uint16_t* w, uint16_t* out, size_t plane, float* ssq, int* err, int tokens, bool pdl,
+                        const TraceAt& tr = TraceAt{});
 
 struct QkvPostArgs {
   float* qkv;               // [T][ld]: q heads | k heads | v heads; q rewritten in place

@@ -102,6 +102,8 @@ struct tb200_state {
   int cap = 0;                 // tokens per pass
   float *bx = nullptr, *bqkv = nullptr, *blogits = nullptr;  // [cap][H], [cap][q+2kv], [n_seqs][V]
   float* bpart = nullptr;      // tensor parallel: o_proj / down_proj partial sums [cap][H]
+  float* ssq_a = nullptr;      // [cap][H/128] partial sums of squares of x before attention (RMSNorm input)
+  float* ssq_b = nullptr;      // ... and before the MLP
   uint16_t* bact = nullptr;    // the kOps operands' planes, one allocation
   int* bmeta = nullptr;        // device [3][cap]: token, position, sequence of each row
   int* bmeta_host = nullptr;   // pinned [3][cap] + readback words
