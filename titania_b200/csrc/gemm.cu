@@ -71,9 +71,9 @@ constexpr size_t kMinSmem = 116 * 1024;
 // The epilogue warps' scratch for a group of up to 32 tokens: per-warp
 // partial sums, per-token scales, and one head's values per token.
 struct EpiScratch {
-  float red[4][32];
   float scale[32];
-  float tile[32][128];
+  int pos[32], seq[32];
+  float tile[32 * 132];  // [token][row], row stride 128 + 128 / tokens (tile_token_sum)
 };
 
 // Shared memory: `stages` tiles, then 8-byte slots: full[stages],
@@ -158,6 +158,24 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(
 // residual reads are issued before any write. On return v holds the values
 // the epilogue produced from (after the input scale; kGemmQkv: after
 // QK-norm and RoPE).
+// Per-token sums over a tile's 128 rows. Epilogue thread e (row e) left its
+// value for token j at tile[j * (128 + G) + e]; then G = 128 / N threads share
+// a token, each adding every G-th row, and a G-lane shuffle tree (G-lane groups
+// sit inside one warp) finishes the sum, returned on every lane of the group.
+// The padded row stride puts the G-thread groups of different tokens on
+// distinct banks. One barrier and no per-token warp-wide dependency chain.
+template <int N>
+__device__ __forceinline__ float tile_token_sum(const float* tile, int e) {
+  constexpr int G = 128 / N, ST = 128 + G;
+  const int j = e / G, p = e % G;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < N; k++) s += tile[j * ST + p + k * G];
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
 template <int EPI, int N>
 __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bool row_ok, int q, int lane, int t0,
                                           float (&v)[N], EpiScratch& es) {
@@ -169,6 +187,7 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     if (e < N && t0 + e < a.T) {
       const float* p = a.in_ssq + size_t(a.act_row0 + t0 + e) * a.in_parts;
       float ss = 0.f;
+#pragma unroll 4
       for (int i = 0; i < a.in_parts; i++) ss += p[i];
       es.scale[e] = 1.0f / sqrtf(ss / float(a.in_dim) + a.eps);
     }
@@ -193,18 +212,18 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     if (EPI == kGemmResidNorm) {
       // The next RMSNorm's input: x * w as planes, and this tile's sum of
       // squares of x per token (its consumer divides by the row length).
+      constexpr int G = 128 / N, ST = 128 + G;
       const float w = row_ok ? bf16f(a.next_w[row]) : 0.f;
 #pragma unroll
       for (int j = 0; j < N; j++) {
-        const float sq = warp_sum(row_ok ? x[j] * x[j] : 0.f);
-        if (lane == 0) es.red[q][j] = sq;
+        es.tile[j * ST + e] = row_ok ? x[j] * x[j] : 0.f;
         if (row_ok && t0 + j < a.T)
           store_split3(a.next_split, a.next_plane, size_t(t0 + j) * a.ldo + row, __fmul_rn(x[j], w));
       }
       named_sync(1, 128);
-      if (e < N && t0 + e < a.T)
-        a.out_ssq[size_t(t0 + e) * a.mtiles + mt] = ((es.red[0][e] + es.red[1][e]) + es.red[2][e]) + es.red[3][e];
-      named_sync(1, 128);
+      const float ss = tile_token_sum<N>(es.tile, e);
+      if (e % G == 0 && t0 + e / G < a.T) a.out_ssq[size_t(t0 + e / G) * a.mtiles + mt] = ss;
+      named_sync(1, 128);  // the tile is read before the next group writes it
     }
 #pragma unroll
     for (int j = 0; j < N; j++) v[j] = x[j];
@@ -222,44 +241,47 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     }
   } else {  // kGemmQkv: tile mt is query head mt, key head mt - nq, or value head mt - nq - nk
     const int nq = a.n_heads, nk = a.n_kv_heads;
-    const int d = 32 * q + lane;  // the head dimension of this row
+    const int d = 32 * q + lane;  // the head dimension of this row (e is not: warp 2 reads lanes 64..95)
     const bool is_v = mt >= nq + nk;
+    // The tokens' positions and sequences, once per group.
+    if (e < N) {
+      const bool t_ok = t0 + e < a.T;
+      es.pos[e] = t_ok ? a.tok_pos[a.act_row0 + t0 + e] : -1;
+      es.seq[e] = t_ok ? a.tok_seq[a.act_row0 + t0 + e] : -1;
+    }
     if (!is_v) {
       const uint16_t* nw = mt < nq ? a.q_norm : a.k_norm;
       if (nw) {
         // QK-norm over the head (model.rs:111-116 with cpu.rs:85-94).
+        constexpr int G = 128 / N, ST = 128 + G;
 #pragma unroll
-        for (int j = 0; j < N; j++) {
-          const float sq = warp_sum(v[j] * v[j]);
-          if (lane == 0) es.red[q][j] = sq;
-        }
+        for (int j = 0; j < N; j++) es.tile[j * ST + d] = v[j] * v[j];
+        named_sync(1, 128);
+        const float ss = tile_token_sum<N>(es.tile, e);
+        if (e % G == 0) es.scale[e / G] = 1.0f / sqrtf(ss / 128.0f + a.eps);
         named_sync(1, 128);
         const float w = bf16f(nw[d]);
 #pragma unroll
-        for (int j = 0; j < N; j++) {
-          const float ss = ((es.red[0][j] + es.red[1][j]) + es.red[2][j]) + es.red[3][j];
-          const float sc = 1.0f / sqrtf(ss / 128.0f + a.eps);
-          v[j] = __fmul_rn(v[j], __fmul_rn(sc, w));
-        }
-        named_sync(1, 128);
+        for (int j = 0; j < N; j++) v[j] = __fmul_rn(v[j], __fmul_rn(es.scale[j], w));
       }
       // RoPE (cpu.rs:96-111): element d pairs with d ^ 64.
 #pragma unroll
-      for (int j = 0; j < N; j++) es.tile[j][d] = v[j];
+      for (int j = 0; j < N; j++) es.tile[j * 128 + d] = v[j];
       named_sync(1, 128);
       const int i = d & 63;
 #pragma unroll
       for (int j = 0; j < N; j++) {
         if (t0 + j >= a.T) continue;
-        const float other = es.tile[j][d ^ 64];
-        const int pos = a.tok_pos[a.act_row0 + t0 + j];
+        const float other = es.tile[j * 128 + (d ^ 64)];
+        const int pos = es.pos[j];
         const float2 cs = (pos >= 0 && pos < a.max_len)
                               ? *reinterpret_cast<const float2*>(a.rope + size_t(pos) * 128 + 2 * i)
                               : make_float2(1.f, 0.f);
         v[j] = d < 64 ? __fsub_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y))
                       : __fadd_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y));
       }
-      named_sync(1, 128);
+    } else {
+      named_sync(1, 128);  // es.pos / es.seq in place
     }
 #pragma unroll
     for (int j = 0; j < N; j++) {
@@ -269,7 +291,7 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
         a.out[size_t(t) * a.ldo + row] = v[j];
         continue;
       }
-      const int pos = a.tok_pos[a.act_row0 + t], sq = a.tok_seq[a.act_row0 + t];
+      const int pos = es.pos[j], sq = es.seq[j];
       if (pos < 0 || pos >= a.max_len || sq < 0 || sq >= a.n_seqs) {
         if (d == 0) set_error(a.err, TB200_ERR_ARG);
         continue;
@@ -280,6 +302,7 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
       if (a.kv_f32) static_cast<float*>(a.kv)[at] = v[j];
       else static_cast<uint16_t*>(a.kv)[at] = f2bf(v[j]);
     }
+    named_sync(1, 128);  // es.tile / es.pos / es.seq read before the next group writes them
   }
 }
 
