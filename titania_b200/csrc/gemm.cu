@@ -328,6 +328,9 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync_all, for work placed between them.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // A float in the shared memory of cluster CTA `rank`, at this CTA's offset `saddr`.
 __device__ __forceinline__ float ld_cluster(uint32_t saddr, uint32_t rank) {
   uint32_t remote;
@@ -578,11 +581,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int r = 1; r < S; r++) v[j] += pv[r][j];
       }
+      // This CTA's reads of the cluster's tiles are done: it arrives now and
+      // waits only before exiting, so the barrier overlaps the epilogue (a
+      // release arrive after the epilogue's global stores would wait for them).
+      cluster_arrive();
       epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + j0, v, es);
       if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + j0, v, lane);
+    } else {
+      cluster_arrive();
     }
     __syncwarp();
-    cluster_sync_all();  // no CTA leaves while another still reads its tile
+    cluster_wait();  // no CTA leaves while another still reads its tile
   }
 
   tc_fence_before();
