@@ -501,7 +501,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   __shared__ float corr_w[4][GRP];
   __shared__ float wm[4][GRP], wl[4][GRP];
   __shared__ __align__(8) uint64_t bar[kTcStages];
-  __shared__ int verdict, is_last;
+  __shared__ int consumed[kTcStages], issued_sh, is_last;
 
   pdl_launch_dependents();
   const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
@@ -535,7 +535,10 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
 
   int issued = 0;
   if (active && tid == 0) {
-    for (int s = 0; s < kTcStages; s++) mbar_init(&bar[s], 1);
+    for (int s = 0; s < kTcStages; s++) {
+      mbar_init(&bar[s], 1);
+      consumed[s] = 0;
+    }
     fence_mbar_init();
     // Chunks wholly before the token's own position were written by earlier
     // steps: they go out before the dependency wait.
@@ -548,8 +551,10 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     return;
   }
   if (!active) return;
-  if (tid == 0)
+  if (tid == 0) {
     while (issued < kTcStages && issued < nchunks) issue(issued++);
+    issued_sh = issued;
+  }
   for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
   for (int i = tid; i < 4 * 8 * NB * 16; i += 128) (&pw[0][0][0])[i] = 0;  // pad columns stay zero
   __syncthreads();
@@ -573,9 +578,11 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
       }
   }
 
-  const float scale = 1.0f / sqrtf(float(kD));
+  // Scores are kept in base-2 units (scaled by log2 e) so the exponentials are exp2.
+  const float scale2 = 1.4426950408889634f / sqrtf(float(kD));
   // This lane's (position, head) pairs: position rr of the warp's 16, heads
-  // hb + 2 i. Its running max and sum per head.
+  // hb + 2 i. The running max per head (shared by the 16 lanes of the head)
+  // and this lane's share of the running sum (added up once at the end).
   const int rr = lane & 15, hb = lane >> 4;
   float m[HP], l[HP];
 #pragma unroll
@@ -590,12 +597,15 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     for (int nb = 0; nb < NB; nb++) o[mb][nb][0] = o[mb][nb][1] = o[mb][nb][2] = o[mb][nb][3] = 0.f;
   const int r = lane >> 2;
   bool failed = false;
+  // The warps go through the chunks independently: each waits for a chunk
+  // itself, and the last warp done with a stage issues the chunk kTcStages
+  // ahead into it (no block-wide barrier per chunk).
   for (int i = 0; i < nchunks; i++) {
     const int s = i % kTcStages;
     const int c0 = p0 + i * kTcCh;
-    if (tid == 0) verdict = mbar_wait(&bar[s], (i / kTcStages) & 1, a.err) ? 1 : 0;
-    __syncthreads();
-    if (!verdict) {
+    int got = 1;
+    if (lane == 0) got = mbar_wait(&bar[s], (i / kTcStages) & 1, a.err) ? 1 : 0;
+    if (!__shfl_sync(0xffffffffu, got, 0)) {
       failed = true;
       break;
     }
@@ -603,23 +613,26 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     const uint32_t kbase = smem_u32(sm + size_t(s) * kTcStage), vbase = kbase + 2 * kTcBox;
     const int pw0 = 16 * warp;  // the warp's first position in the chunk
     {
-      float sc[NB][4];
-#pragma unroll
-      for (int nb = 0; nb < NB; nb++) sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.f;
+      // All eight key fragments first, then two independent accumulation chains.
       const int ar = pw0 + (lane & 7) + 8 * ((lane >> 3) & 1), au = lane >> 4;
+      uint32_t af[8][4];
 #pragma unroll
-      for (int kb = 0; kb < 8; kb++) {
-        uint32_t af[4];
-        ldsm_x4(kbase + (kb >> 2) * kTcBox + sw128(ar, 2 * (kb & 3) + au), af);
+      for (int kb = 0; kb < 8; kb++) ldsm_x4(kbase + (kb >> 2) * kTcBox + sw128(ar, 2 * (kb & 3) + au), af[kb]);
+      float sc[2][NB][4];
 #pragma unroll
-        for (int nb = 0; nb < NB; nb++) mma16816(sc[nb], af, qb[nb][kb][0], qb[nb][kb][1]);
-      }
+      for (int h2 = 0; h2 < 2; h2++)
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) sc[h2][nb][0] = sc[h2][nb][1] = sc[h2][nb][2] = sc[h2][nb][3] = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < 8; kb++)
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) mma16816(sc[kb & 1][nb], af[kb], qb[nb][kb][0], qb[nb][kb][1]);
 #pragma unroll
       for (int nb = 0; nb < NB; nb++) {
-        sw[warp][r][8 * nb + kq] = sc[nb][0];
-        sw[warp][r][8 * nb + kq + 1] = sc[nb][1];
-        sw[warp][r + 8][8 * nb + kq] = sc[nb][2];
-        sw[warp][r + 8][8 * nb + kq + 1] = sc[nb][3];
+        sw[warp][r][8 * nb + kq] = sc[0][nb][0] + sc[1][nb][0];
+        sw[warp][r][8 * nb + kq + 1] = sc[0][nb][1] + sc[1][nb][1];
+        sw[warp][r + 8][8 * nb + kq] = sc[0][nb][2] + sc[1][nb][2];
+        sw[warp][r + 8][8 * nb + kq + 1] = sc[0][nb][3] + sc[1][nb][3];
       }
     }
     __syncwarp();
@@ -630,18 +643,15 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     for (int i2 = 0; i2 < HP; i2++) {
       const int h = hb + 2 * i2;
       float sc = -INFINITY;
-      if (h < GRP && live_pos) sc = scale * ((sw[warp][rr][h] + sw[warp][rr][GRP + h]) + sw[warp][rr][2 * GRP + h]);
-      // Running statistics of head h over this warp's positions (lanes with the same hb).
+      if (h < GRP && live_pos) sc = scale2 * ((sw[warp][rr][h] + sw[warp][rr][GRP + h]) + sw[warp][rr][2 * GRP + h]);
+      // Running max of head h over this warp's positions (lanes with the same hb).
       float mx = sc;
 #pragma unroll
       for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float mn = fmaxf(m[i2], mx);
-      const float corr = (m[i2] == -INFINITY || mn == -INFINITY) ? 0.f : expf(m[i2] - mn);
-      const float e = sc == -INFINITY ? 0.f : expf(sc - mn);
-      float sum = e;
-#pragma unroll
-      for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      l[i2] = l[i2] * corr + sum;
+      const float corr = (m[i2] == -INFINITY || mn == -INFINITY) ? 0.f : exp2f(m[i2] - mn);
+      const float e = sc == -INFINITY ? 0.f : exp2f(sc - mn);
+      l[i2] = l[i2] * corr + e;
       m[i2] = mn;
       pv[i2] = e;
       if (rr == 0 && h < GRP) corr_w[warp][h] = corr;
@@ -655,17 +665,11 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
         for (int j = 0; j < 3; j++) pw[warp][GRP * j + h][rr] = plane_of(pv[i2], j);
     }
     __syncwarp();
-#pragma unroll
-    for (int mb = 0; mb < 8; mb++)
-#pragma unroll
-      for (int nb = 0; nb < NB; nb++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int c = 8 * nb + kq + (e & 1);
-          o[mb][nb][e] *= c < NC ? corr_w[warp][c % GRP] : 0.f;
-        }
     {
       const int vr = pw0 + (lane & 7) + 8 * (lane >> 4), vu = (lane >> 3) & 1;
+      uint32_t af[8][4];
+#pragma unroll
+      for (int mb = 0; mb < 8; mb++) ldsm_x4_t(vbase + (mb >> 2) * kTcBox + sw128(vr, 2 * (mb & 3) + vu), af[mb]);
       uint32_t pb[NB][2];
 #pragma unroll
       for (int nb = 0; nb < NB; nb++) {
@@ -673,23 +677,50 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
         pb[nb][1] = *reinterpret_cast<const uint32_t*>(&pw[warp][8 * nb + (lane >> 2)][kq + 8]);
       }
 #pragma unroll
-      for (int mb = 0; mb < 8; mb++) {
-        uint32_t af[4];
-        ldsm_x4_t(vbase + (mb >> 2) * kTcBox + sw128(vr, 2 * (mb & 3) + vu), af);
+      for (int mb = 0; mb < 8; mb++)
 #pragma unroll
-        for (int nb = 0; nb < NB; nb++) mma16816(o[mb][nb], af, pb[nb][0], pb[nb][1]);
+        for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int c = 8 * nb + kq + (e & 1);
+            o[mb][nb][e] *= c < NC ? corr_w[warp][c % GRP] : 0.f;
+          }
+#pragma unroll
+      for (int mb = 0; mb < 8; mb++)
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) mma16816(o[mb][nb], af[mb], pb[nb][0], pb[nb][1]);
+    }
+    // This warp is done with stage s (its fragments are in registers). The
+    // fourth warp to get here refills the stage.
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&consumed[s], 1) == 3) {
+        consumed[s] = 0;
+        if (i + kTcStages < nchunks) {
+          issue(i + kTcStages);
+          atomicMax(&issued_sh, i + kTcStages + 1);
+        }
       }
     }
-    __syncthreads();  // every warp is done with stage s (and its pw, sw)
-    if (tid == 0 && issued < nchunks) issue(issued++);
   }
+  // Every warp is out of the loop (and done reading the stages) before the
+  // stage memory is reused below; a failure anywhere fails the CTA.
+  failed = __syncthreads_or(failed);
   if (failed) {
     // Let the copies in flight land (bounded) before the CTA's memory goes.
-    if (tid == 0)
-      for (int i = max(0, issued - kTcStages); i < issued; i++)
+    if (tid == 0) {
+      const int n_issued = issued_sh;
+      for (int i = max(0, n_issued - kTcStages); i < n_issued; i++)
         mbar_wait(&bar[i % kTcStages], (i / kTcStages) & 1, nullptr);
+    }
     return;
   }
+  // The sums of the 16 lanes of each head.
+#pragma unroll
+  for (int i2 = 0; i2 < HP; i2++)
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) l[i2] += __shfl_xor_sync(0xffffffffu, l[i2], off);
 
   // Per warp: publish (m, l) per head and O per (column, dim) into the idle
   // stage memory, then thread d combines the warps and the planes.
@@ -722,7 +753,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     float L = 0.f, O = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; w++) {
-      const float wt = wm[w][h] == -INFINITY ? 0.f : expf(wm[w][h] - M);
+      const float wt = wm[w][h] == -INFINITY ? 0.f : exp2f(wm[w][h] - M);  // base-2 units
       const float* ob = ow + size_t(w * 8 * NB) * kD + tid;
       const float ov = (ob[size_t(h) * kD] + ob[size_t(GRP + h) * kD]) + ob[size_t(2 * GRP + h) * kD];
       L += wl[w][h] * wt;
@@ -746,7 +777,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     float* pp = pbase + (size_t(part) * GRP + h) * stride;
     pp[tid] = res[h];
     if (tid == 0) {
-      pp[kD] = rm[h];
+      pp[kD] = rm[h] * 0.6931471805599453f;  // the partial records hold natural-log maxima
       pp[kD + 1] = rl[h];
     }
   }
