@@ -152,12 +152,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
 // exponential and division (a few ulp from libm's; within every parity bar).
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
-// The epilogue of N consecutive tokens t0 .. t0 + N - 1 (N <= 32) of row
-// `row` = m0 + 32 q + lane of row tile `mt`: v[j] is the accumulator of
-// token t0 + j. All 128 epilogue threads call it together (named barrier 1);
-// residual reads are issued before any write. On return v holds the values
-// the epilogue produced from (after the input scale; kGemmQkv: after
-// QK-norm and RoPE).
 // Per-token sums over a tile's 128 rows. Epilogue thread e (row e) left its
 // value for token j at tile[j * (128 + G) + e]; then G = 128 / N threads share
 // a token, each adding every G-th row, and a G-lane shuffle tree (G-lane groups
@@ -176,22 +170,72 @@ __device__ __forceinline__ float tile_token_sum(const float* tile, int e) {
   return s;
 }
 
+// What an epilogue group reads besides its accumulators. The split-K kernel
+// loads it while the contraction runs; the persistent one just before use.
+template <int N>
+struct EpiPre {
+  float x[N];    // kGemmResid, kGemmResidNorm: the residual rows of the N tokens
+  float w;       // kGemmResidNorm: the next norm's weight; kGemmQkv: the QK-norm weight
+  float2 cs[N];  // kGemmQkv: RoPE cos / sin of each token's position
+};
+
+// Loads the EpiPre of N tokens t0 .. of row `row` of tile `mt`, and leaves
+// in `es` the input scale per token (in_ssq) and, for kGemmQkv, the tokens'
+// positions and sequences. Only results of earlier kernels are read (after
+// the dependency wait). es is read only after a later named barrier.
+template <int EPI, int N>
+__device__ __forceinline__ void epi_prefetch(const GemmArgs& a, int mt, int row, bool row_ok, int q, int lane,
+                                             int t0, EpiPre<N>& pre, EpiScratch& es) {
+  const int e = int(threadIdx.x) - 64;
+  if (a.in_ssq && e < N && t0 + e < a.T) {
+    // The input's RMSNorm (cpu.rs:85-94): the scale of each token, from the
+    // partial sums of squares the producer of the input left, in order.
+    const float* p = a.in_ssq + size_t(a.act_row0 + t0 + e) * a.in_parts;
+    float ss = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < a.in_parts; i++) ss += p[i];
+    es.scale[e] = 1.0f / sqrtf(ss / float(a.in_dim) + a.eps);
+  }
+  if (EPI == kGemmResid || EPI == kGemmResidNorm) {
+#pragma unroll
+    for (int j = 0; j < N; j++) pre.x[j] = row_ok && t0 + j < a.T ? a.out[size_t(t0 + j) * a.ldo + row] : 0.f;
+    if (EPI == kGemmResidNorm) pre.w = row_ok ? bf16f(a.next_w[row]) : 0.f;
+  }
+  if (EPI == kGemmQkv) {
+    const int nq = a.n_heads, nk = a.n_kv_heads;
+    const int d = 32 * q + lane;
+    if (e < N) {
+      const bool t_ok = t0 + e < a.T;
+      es.pos[e] = t_ok ? a.tok_pos[a.act_row0 + t0 + e] : -1;
+      es.seq[e] = t_ok ? a.tok_seq[a.act_row0 + t0 + e] : -1;
+    }
+    const uint16_t* nw = mt < nq ? a.q_norm : mt < nq + nk ? a.k_norm : nullptr;
+    pre.w = nw ? bf16f(nw[d]) : 1.f;
+    if (mt < nq + nk) {
+      const int i = d & 63;
+#pragma unroll
+      for (int j = 0; j < N; j++) {
+        const int pos = t0 + j < a.T ? a.tok_pos[a.act_row0 + t0 + j] : -1;
+        pre.cs[j] = (pos >= 0 && pos < a.max_len) ? *reinterpret_cast<const float2*>(a.rope + size_t(pos) * 128 + 2 * i)
+                                                  : make_float2(1.f, 0.f);
+      }
+    }
+  }
+}
+
+// The epilogue of N consecutive tokens t0 .. t0 + N - 1 (N <= 32) of row
+// `row` = m0 + 32 q + lane of row tile `mt`: v[j] is the accumulator of
+// token t0 + j, `pre` what epi_prefetch loaded for the same tokens. All 128
+// epilogue threads call it together (named barrier 1). On return v holds the
+// values the epilogue produced from (after the input scale; kGemmQkv: after
+// QK-norm and RoPE).
 template <int EPI, int N>
 __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bool row_ok, int q, int lane, int t0,
-                                          float (&v)[N], EpiScratch& es) {
+                                          float (&v)[N], const EpiPre<N>& pre, EpiScratch& es) {
   static_assert(N <= 32, "scratch holds 32 tokens");
   const int e = int(threadIdx.x) - 64;  // 0 .. 127 over the epilogue warps
   if (a.in_ssq) {
-    // The input's RMSNorm (cpu.rs:85-94): the scale of each token, from the
-    // partial sums of squares the producer of the input left, in order.
-    if (e < N && t0 + e < a.T) {
-      const float* p = a.in_ssq + size_t(a.act_row0 + t0 + e) * a.in_parts;
-      float ss = 0.f;
-#pragma unroll 4
-      for (int i = 0; i < a.in_parts; i++) ss += p[i];
-      es.scale[e] = 1.0f / sqrtf(ss / float(a.in_dim) + a.eps);
-    }
-    named_sync(1, 128);
+    named_sync(1, 128);  // es.scale in place
 #pragma unroll
     for (int j = 0; j < N; j++) v[j] *= es.scale[j];
     named_sync(1, 128);
@@ -203,17 +247,15 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
   } else if (EPI == kGemmResid || EPI == kGemmResidNorm) {
     float x[N];
 #pragma unroll
-    for (int j = 0; j < N; j++) x[j] = row_ok && t0 + j < a.T ? a.out[size_t(t0 + j) * a.ldo + row] : 0.f;
-#pragma unroll
     for (int j = 0; j < N; j++) {
-      x[j] = __fadd_rn(x[j], v[j]);
+      x[j] = __fadd_rn(pre.x[j], v[j]);
       if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = x[j];
     }
     if (EPI == kGemmResidNorm) {
       // The next RMSNorm's input: x * w as planes, and this tile's sum of
       // squares of x per token (its consumer divides by the row length).
       constexpr int G = 128 / N, ST = 128 + G;
-      const float w = row_ok ? bf16f(a.next_w[row]) : 0.f;
+      const float w = pre.w;
 #pragma unroll
       for (int j = 0; j < N; j++) {
         es.tile[j * ST + e] = row_ok ? x[j] * x[j] : 0.f;
@@ -243,12 +285,6 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     const int nq = a.n_heads, nk = a.n_kv_heads;
     const int d = 32 * q + lane;  // the head dimension of this row (e is not: warp 2 reads lanes 64..95)
     const bool is_v = mt >= nq + nk;
-    // The tokens' positions and sequences, once per group.
-    if (e < N) {
-      const bool t_ok = t0 + e < a.T;
-      es.pos[e] = t_ok ? a.tok_pos[a.act_row0 + t0 + e] : -1;
-      es.seq[e] = t_ok ? a.tok_seq[a.act_row0 + t0 + e] : -1;
-    }
     if (!is_v) {
       const uint16_t* nw = mt < nq ? a.q_norm : a.k_norm;
       if (nw) {
@@ -260,7 +296,7 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
         const float ss = tile_token_sum<N>(es.tile, e);
         if (e % G == 0) es.scale[e / G] = 1.0f / sqrtf(ss / 128.0f + a.eps);
         named_sync(1, 128);
-        const float w = bf16f(nw[d]);
+        const float w = pre.w;
 #pragma unroll
         for (int j = 0; j < N; j++) v[j] = __fmul_rn(v[j], __fmul_rn(es.scale[j], w));
       }
@@ -268,15 +304,11 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
 #pragma unroll
       for (int j = 0; j < N; j++) es.tile[j * 128 + d] = v[j];
       named_sync(1, 128);
-      const int i = d & 63;
 #pragma unroll
       for (int j = 0; j < N; j++) {
         if (t0 + j >= a.T) continue;
         const float other = es.tile[j * 128 + (d ^ 64)];
-        const int pos = es.pos[j];
-        const float2 cs = (pos >= 0 && pos < a.max_len)
-                              ? *reinterpret_cast<const float2*>(a.rope + size_t(pos) * 128 + 2 * i)
-                              : make_float2(1.f, 0.f);
+        const float2 cs = pre.cs[j];
         v[j] = d < 64 ? __fsub_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y))
                       : __fadd_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y));
       }
@@ -331,11 +363,16 @@ __device__ __forceinline__ void cluster_sync_all() {
 // The two halves of cluster_sync_all, for work placed between them.
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// A float in the shared memory of cluster CTA `rank`, at this CTA's offset `saddr`.
-__device__ __forceinline__ float ld_cluster(uint32_t saddr, uint32_t rank) {
+// The shared::cluster address of offset `saddr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_cluster(uint32_t saddr, uint32_t rank) {
   uint32_t remote;
-  float v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
+  return remote;
+}
+// A float at a shared::cluster address. (Scalar loads, 128 contiguous bytes
+// per warp instruction, measured faster here than 16-byte vector loads.)
+__device__ __forceinline__ float ld_cluster(uint32_t remote) {
+  float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
 }
@@ -377,6 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_START);
   constexpr bool split = S > 1;  // a.splits == S
+  constexpr int PER = split ? kBN / S : 16;  // split-K: the tokens of the tile this CTA finishes
+  EpiPre<PER> pre;                           // split-K: that slice's epilogue inputs
   const int nkb = (a.K + kBK - 1) / kBK;
   // Tile sequence of this CTA: split-K, one tile (blockIdx) and one K range;
   // persistent, tiles blockIdx.x, blockIdx.x + gridDim.x, ... over all of K.
@@ -488,11 +527,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     pdl_wait();
     if (warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_WAITED);
     const int q = warp & 3;
-    if (split && nk == 0) {
-      // A split past the end of K: its partial tile is zero.
-      float* red = reinterpret_cast<float*>(sm);
-      for (int j = 0; j < kBN; j++) red[j * kBM + 32 * q + lane] = 0.f;
-      if (warp == 2 && lane == 0) flags[4] = 1;
+    if constexpr (split) {
+      // The epilogue's other inputs, loaded while the contraction runs.
+      epi_prefetch<EPI, PER>(a, int(blockIdx.x), int(blockIdx.x) * kBM + 32 * q + lane,
+                             int(blockIdx.x) * kBM + 32 * q + lane < a.M, q, lane,
+                             int(blockIdx.y) * kBN + int(cluster_rank()) * PER, pre, es);
+      if (nk == 0) {
+        // A split past the end of K: its partial tile is zero.
+        float* red = reinterpret_cast<float*>(sm);
+        for (int j = 0; j < kBN; j++) red[j * kBM + 32 * q + lane] = 0.f;
+        if (warp == 2 && lane == 0) flags[4] = 1;
+      }
     }
     for (int ti = 0; ti < ntiles && nk > 0; ti++) {
       const int b = ti & 1;
@@ -514,8 +559,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c = 0; c < kBN; c += 16) {
           float v[16];
+          EpiPre<16> pre16;
+          epi_prefetch<EPI, 16>(a, tile_m(ti), row, row_ok, q, lane, n0 + c, pre16, es);
           tmem_ld_tokens(taddr, c, v);
-          epi_group<EPI, 16>(a, tile_m(ti), row, row_ok, q, lane, n0 + c, v, es);
+          epi_group<EPI, 16>(a, tile_m(ti), row, row_ok, q, lane, n0 + c, v, pre16, es);
           if (EPI == kGemmStore && a.best) {
 #pragma unroll
             for (int j = 0; j < 16; j++) {
@@ -562,7 +609,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp >= 2 && flags[4]) {
       // Cluster CTA r sums the S partial tiles for tokens r PER .. + PER - 1,
       // in split order: every partial load is issued before any is used.
-      constexpr int PER = kBN / S;
       const int q = warp & 3;
       const int m0 = int(blockIdx.x) * kBM, n0 = int(blockIdx.y) * kBN;
       const int row = m0 + 32 * q + lane;
@@ -571,9 +617,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t base = smem_u32(sm) + uint32_t((j0 * kBM + 32 * q + lane) * 4);
       float pv[S][PER];
 #pragma unroll
-      for (int r = 0; r < S; r++)
+      for (int r = 0; r < S; r++) {
+        const uint32_t remote = mapa_cluster(base, uint32_t(r));
 #pragma unroll
-        for (int j = 0; j < PER; j++) pv[r][j] = ld_cluster(base + uint32_t(j * kBM * 4), uint32_t(r));
+        for (int j = 0; j < PER; j++) pv[r][j] = ld_cluster(remote + uint32_t(j * kBM * 4));
+      }
       float v[PER];
 #pragma unroll
       for (int j = 0; j < PER; j++) {
@@ -585,7 +633,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // waits only before exiting, so the barrier overlaps the epilogue (a
       // release arrive after the epilogue's global stores would wait for them).
       cluster_arrive();
-      epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + j0, v, es);
+      epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + j0, v, pre, es);
       if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + j0, v, lane);
     } else {
       cluster_arrive();
