@@ -63,6 +63,8 @@ constexpr int kStageA = kBM * kBK * 2;   // 16 KB
 constexpr int kStageB = kNP * kBK * 2;   // 24 KB (three 8 KB plane boxes)
 constexpr int kStage = kStageA + kStageB;
 constexpr int kMaxStages = 5;
+constexpr int kMaxSplitStages = 4;               // split-K: room for the receive buffer
+constexpr size_t kRecvBytes = size_t(kBN) * kBM * 4;  // split-K: S slices of 64 / S tokens x 128 rows
 constexpr int kAccCols = 256;            // tensor-memory columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
 // Floor of the dynamic shared memory: more than half of an SM's 228 KB.
@@ -76,13 +78,14 @@ struct EpiScratch {
   float tile[32 * 132];  // [token][row], row stride 128 + 128 / tokens (tile_token_sum)
 };
 
-// Shared memory: `stages` tiles, then 8-byte slots: full[stages],
-// empty[stages], tfull[2], tempty[2], mdone, the tensor-memory address and
-// flags (6 slots), then the epilogue warps' argmax keys [4][kBN] and their
-// EpiScratch; plus alignment slack.
-size_t smem_for(int stages) {
-  const size_t need =
-      size_t(stages) * kStage + (2 * size_t(stages) + 11) * 8 + 4 * kBN * 8 + sizeof(EpiScratch) + 1024;
+// Shared memory: `stages` tiles, (split-K) the receive buffer, then 8-byte
+// slots: full[stages], empty[stages], tfull[2], tempty[2], mdone, the
+// tensor-memory address and flags, the receive barrier (6 slots), then the
+// epilogue warps' argmax keys [4][kBN] and their EpiScratch; plus alignment
+// slack.
+size_t smem_for(int stages, bool split) {
+  const size_t need = size_t(stages) * kStage + (split ? kRecvBytes : 0) + (2 * size_t(stages) + 11) * 8 +
+                      4 * kBN * 8 + sizeof(EpiScratch) + 1024;
   return need > kMinSmem ? need : kMinSmem;
 }
 
@@ -355,26 +358,47 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// Every thread of every CTA of the cluster; orders shared-memory writes
-// before the barrier with reads by other CTAs after it.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+// The two halves of a cluster barrier, for work placed between them.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
-// The two halves of cluster_sync_all, for work placed between them.
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// An asynchronous 4-byte store into the shared memory of another CTA of the
+// cluster, counted (complete_tx) on that CTA's barrier at `rbar`.
+__device__ __forceinline__ void st_async_f32(uint32_t remote, float x, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote),
+               "r"(__float_as_uint(x)), "r"(rbar)
+               : "memory");
+}
+// mbar_wait with acquire at cluster scope: what other CTAs' st.async
+// delivered before the phase completed is visible afterwards.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (global_ns() - t0 > kWaitNs) {
+      set_error(err, TB200_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
 // The shared::cluster address of offset `saddr` in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t mapa_cluster(uint32_t saddr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(saddr), "r"(rank));
   return remote;
-}
-// A float at a shared::cluster address. (Scalar loads, 128 contiguous bytes
-// per warp instruction, measured faster here than 16-byte vector loads.)
-__device__ __forceinline__ float ld_cluster(uint32_t remote) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
 }
 
 // Sums the three plane column groups of accumulator columns [c, c + 16)
@@ -396,14 +420,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // The swizzled tiles need 1024-byte alignment.
   const uint32_t raw = smem_u32(smem_raw);
   unsigned char* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const int stages = a.stages;  // 1 .. kMaxStages
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * kStage);
+  constexpr bool split = S > 1;  // a.splits == S
+  const int stages = a.stages;  // 1 .. kMaxStages (split-K: .. kMaxSplitStages)
+  // Split-K: the receive buffer of the other CTAs' partial sums follows the stages.
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * kStage + (split ? kRecvBytes : 0));
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;  // [2] accumulator ready
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained
   uint64_t* mdone = tempty + 2;      // every MMA of the CTA completed
+  uint64_t* rbar = mdone + 5;        // split-K: the other CTAs' partial sums have landed
   uint32_t* tslot = reinterpret_cast<uint32_t*>(mdone + 1);
-  int* flags = reinterpret_cast<int*>(tslot + 1);  // [0..3] per epilogue warp, [4] verdict
+  int* flags = reinterpret_cast<int*>(tslot + 1);  // [0..3] per epilogue warp
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(mdone + 6);  // [4][kBN]
   EpiScratch& es = *reinterpret_cast<EpiScratch*>(keys + 4 * kBN);
   auto sA = [&](int s) { return sm + size_t(s) * kStage; };
@@ -413,7 +440,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   if (threadIdx.x == 0) a.trace.at(cta, TB200_TRACE_START);
-  constexpr bool split = S > 1;  // a.splits == S
   constexpr int PER = split ? kBN / S : 16;  // split-K: the tokens of the tile this CTA finishes
   EpiPre<PER> pre;                           // split-K: that slice's epilogue inputs
   const int nkb = (a.K + kBK - 1) / kBK;
@@ -435,7 +461,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], 4);  // one arrival per epilogue warp
     }
     mbar_init(mdone, 1);
-    flags[4] = 0;
+    if (split) {
+      mbar_init(rbar, 1);
+      mbar_arrive_expect_tx(rbar, uint32_t((S - 1) * PER * kBM * 4));
+    }
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tslot, kTmemCols);
@@ -443,6 +472,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // Split-K: the receive barriers are initialized before any CTA of the
+  // cluster sends to them (every thread waits on this arrival later).
+  if constexpr (split) cluster_arrive_relaxed();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -527,35 +559,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     pdl_wait();
     if (warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_WAITED);
     const int q = warp & 3;
-    if constexpr (split) {
-      // The epilogue's other inputs, loaded while the contraction runs.
-      epi_prefetch<EPI, PER>(a, int(blockIdx.x), int(blockIdx.x) * kBM + 32 * q + lane,
-                             int(blockIdx.x) * kBM + 32 * q + lane < a.M, q, lane,
-                             int(blockIdx.y) * kBN + int(cluster_rank()) * PER, pre, es);
-      if (nk == 0) {
-        // A split past the end of K: its partial tile is zero.
-        float* red = reinterpret_cast<float*>(sm);
-        for (int j = 0; j < kBN; j++) red[j * kBM + 32 * q + lane] = 0.f;
-        if (warp == 2 && lane == 0) flags[4] = 1;
-      }
-    }
-    for (int ti = 0; ti < ntiles && nk > 0; ti++) {
-      const int b = ti & 1;
-      const int m0 = tile_m(ti) * kBM, n0 = tile_n(ti) * kBN;
-      const int row = m0 + 32 * q + lane;
-      const bool row_ok = row < a.M;
-      bool ok = nk > 0 && mbar_wait(&tfull[b], (ti >> 1) & 1, a.err);
+    // The four epilogue warps take the same branches: a verdict is shared.
+    auto all_ok = [&](bool ok) {
       ok = __all_sync(0xffffffffu, ok);
-      // The four epilogue warps take the same branches below.
       if (lane == 0) flags[q] = ok ? 1 : 0;
       named_sync(1, 128);
       ok = flags[0] && flags[1] && flags[2] && flags[3];
-      named_sync(1, 128);  // flags[0..3] read before the next tile writes them
-      if (!ok) break;
-      if (ti == 0 && warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_INPUT);
-      tc_fence_after();
-      const uint32_t taddr = tmem + uint32_t(b * kAccCols) + (uint32_t(32 * q) << 16);
-      if (!split) {
+      named_sync(1, 128);  // flags[0..3] read before they are written again
+      return ok;
+    };
+    if constexpr (split) {
+      // Split-K over the cluster: cluster CTA R finishes tokens R PER .. +
+      // PER - 1 of the tile. Every CTA pushes the other CTAs' token slices of
+      // its partial sums into their receive buffers (st.async, counted on the
+      // receiver's barrier) and keeps its own; then each CTA sums the S slices
+      // of its tokens in split order from its own shared memory. No CTA reads
+      // another's memory, and each waits for every byte sent to it before it
+      // leaves.
+      const int R = int(cluster_rank());
+      const int rl = 32 * q + lane, row = int(blockIdx.x) * kBM + rl, n0 = int(blockIdx.y) * kBN;
+      const bool row_ok = row < a.M;
+      float* recv = reinterpret_cast<float*>(sm + size_t(stages) * kStage);  // [source][token][row]
+      const uint32_t recv_s = smem_u32(recv), rbar_s = smem_u32(rbar);
+      // The epilogue's other inputs, loaded while the contraction runs.
+      epi_prefetch<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + R * PER, pre, es);
+      cluster_wait();  // every receive barrier of the cluster is initialized
+      auto push = [&](int jt, float x) {
+        const int dst = jt / PER;
+        const uint32_t off = uint32_t(((R * PER + jt % PER) * kBM + rl) * 4);
+        if (dst == R) recv[off / 4] = x;
+        else st_async_f32(mapa_cluster(recv_s + off, uint32_t(dst)), x, mapa_cluster(rbar_s, uint32_t(dst)));
+      };
+      bool ok = true;
+      if (nk > 0) {
+        ok = all_ok(mbar_wait(&tfull[0], 0, a.err));
+        if (ok) {
+          if (warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_INPUT);
+          tc_fence_after();
+          const uint32_t taddr = tmem + (uint32_t(32 * q) << 16);
+#pragma unroll 1
+          for (int c = 0; c < kBN; c += 16) {
+            float v[16];
+            tmem_ld_tokens(taddr, c, v);
+#pragma unroll
+            for (int j = 0; j < 16; j++) push(c + j, v[j]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int jt = 0; jt < kBN; jt++) push(jt, 0.f);  // a split past the end of K adds zeros
+      }
+      // Every byte sent here lands before the CTA goes, whatever its verdict.
+      const bool got = all_ok(mbar_wait_cluster(rbar, 0, a.err));
+      if (ok && got) {
+        if (threadIdx.x == 64) a.trace.at(cta, TB200_TRACE_REDUCE);
+        float v[PER];
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+          v[j] = recv[j * kBM + rl];
+#pragma unroll
+          for (int r = 1; r < S; r++) v[j] += recv[(r * PER + j) * kBM + rl];
+        }
+        epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + R * PER, v, pre, es);
+        if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + R * PER, v, lane);
+      }
+    } else {
+      for (int ti = 0; ti < ntiles; ti++) {
+        const int b = ti & 1;
+        const int m0 = tile_m(ti) * kBM, n0 = tile_n(ti) * kBN;
+        const int row = m0 + 32 * q + lane;
+        const bool row_ok = row < a.M;
+        if (!all_ok(mbar_wait(&tfull[b], (ti >> 1) & 1, a.err))) break;
+        if (ti == 0 && warp == 2 && lane == 0) a.trace.at(cta, TB200_TRACE_INPUT);
+        tc_fence_after();
+        const uint32_t taddr = tmem + uint32_t(b * kAccCols) + (uint32_t(32 * q) << 16);
 #pragma unroll 1
         for (int c = 0; c < kBN; c += 16) {
           float v[16];
@@ -587,59 +664,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           named_sync(1, 128);  // keys read before the next tile writes them
         }
-      } else {
-        // This split's partial tile into the (now idle) stage memory, [token][row].
-        float* red = reinterpret_cast<float*>(sm);
-#pragma unroll 1
-        for (int c = 0; c < kBN; c += 16) {
-          float v[16];
-          tmem_ld_tokens(taddr, c, v);
-#pragma unroll
-          for (int j = 0; j < 16; j++) red[(c + j) * kBM + 32 * q + lane] = v[j];
-        }
-        if (warp == 2 && lane == 0) flags[4] = 1;
       }
     }
   }
-
   if constexpr (split) {
-    __syncwarp();
-    cluster_sync_all();  // every split's partial tile is in place
-    if (threadIdx.x == 64) a.trace.at(cta, TB200_TRACE_REDUCE);
-    if (warp >= 2 && flags[4]) {
-      // Cluster CTA r sums the S partial tiles for tokens r PER .. + PER - 1,
-      // in split order: every partial load is issued before any is used.
-      const int q = warp & 3;
-      const int m0 = int(blockIdx.x) * kBM, n0 = int(blockIdx.y) * kBN;
-      const int row = m0 + 32 * q + lane;
-      const bool row_ok = row < a.M;
-      const int j0 = int(cluster_rank()) * PER;
-      const uint32_t base = smem_u32(sm) + uint32_t((j0 * kBM + 32 * q + lane) * 4);
-      float pv[S][PER];
-#pragma unroll
-      for (int r = 0; r < S; r++) {
-        const uint32_t remote = mapa_cluster(base, uint32_t(r));
-#pragma unroll
-        for (int j = 0; j < PER; j++) pv[r][j] = ld_cluster(remote + uint32_t(j * kBM * 4));
-      }
-      float v[PER];
-#pragma unroll
-      for (int j = 0; j < PER; j++) {
-        v[j] = pv[0][j];
-#pragma unroll
-        for (int r = 1; r < S; r++) v[j] += pv[r][j];
-      }
-      // This CTA's reads of the cluster's tiles are done: it arrives now and
-      // waits only before exiting, so the barrier overlaps the epilogue (a
-      // release arrive after the epilogue's global stores would wait for them).
-      cluster_arrive();
-      epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + j0, v, pre, es);
-      if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + j0, v, lane);
-    } else {
-      cluster_arrive();
+    if (warp < 2) {
+      __syncwarp();
+      cluster_wait();  // pairs with the arrival at the start
     }
-    __syncwarp();
-    cluster_wait();  // no CTA leaves while another still reads its tile
   }
 
   tc_fence_before();
@@ -653,13 +685,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // ---- host side -----------------------------------------------------------------
 
+static_assert(kMaxSplitStages <= kMaxStages, "split plans fit the kernels' shared-memory attribute");
+
 std::mutex g_encode_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 template <int EPI, int S>
 cudaError_t set_attrs_one() {
   cudaError_t e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem_for(kMaxStages)));
+                                       int(smem_for(kMaxStages, false)));
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
@@ -679,7 +713,7 @@ void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = p.grid;
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = smem_for(p.stages);
+  cfg.dynamicSmemBytes = smem_for(p.stages, p.splits > 1);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
@@ -754,7 +788,7 @@ GemmPlan plan_gemm(int M, int K, int T, int sms, int max_cluster) {
   p.kb_per_split = (nkb + splits - 1) / splits;
   p.splits = splits;  // a power of two; a split past the end of K contributes zeros
   if (p.splits > 1) {
-    p.stages = std::min(kMaxStages, p.kb_per_split);
+    p.stages = std::min(kMaxSplitStages, p.kb_per_split);
     p.grid = dim3(unsigned(p.mtiles), unsigned(p.ntiles), unsigned(p.splits));
   } else {
     p.stages = kMaxStages;
@@ -777,7 +811,7 @@ int gemm_max_cluster() {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1, 1, n);
     cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = smem_for(kMaxStages);
+    cfg.dynamicSmemBytes = smem_for(kMaxSplitStages, true);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
