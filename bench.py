@@ -543,9 +543,21 @@ def profile_bs64(args):
     n, ctx = args.profile_seqs, args.profile_ctx
     bs = m.batch_state(n, ctx + BS64_GEN, kv="bf16")
     first = [m.forward_seq(bs, i, synth.prompt_tokens(ctx, V, seed=1000 + i), 0, logits=False) for i in range(n)]
+    m.decode_batch_enqueue(bs, first, [ctx] * n, 1)  # builds the step graph
+    dev.sync()
+    # Only the decode steps are profiled (ncu --profile-from-start off).
+    _profiler(True)
     m.decode_batch_enqueue(bs, first, [ctx] * n, args.launches)
     dev.sync()
+    _profiler(False)
     print(json.dumps({"profile_bs64": True, "seqs": n, "ctx": ctx, "steps": args.launches}))
+
+
+def _profiler(on):
+    """cudaProfilerStart / Stop (context-wide) through PyTorch's CUDA runtime."""
+    import torch
+    rt = torch.cuda.cudart()
+    (rt.cudaProfilerStart if on else rt.cudaProfilerStop)()
 
 
 GEMM_SHAPES = [(151936, 1024, 64), (6144, 1024, 64), (4096, 1024, 64), (1024, 2048, 64), (1024, 3072, 64),
@@ -565,8 +577,13 @@ def profile_gemm(args):
         x = dev.alloc(n * cols)
         dev.write(x, rng.standard_normal(n * cols, dtype=np.float32))
         out = dev.alloc(n * rows)
+        dev.matmul(out, w, x)  # first use: plans, tensor maps
+        dev.sync()
+        _profiler(True)
         for _ in range(args.launches):
             dev.matmul(out, w, x)
+        dev.sync()
+        _profiler(False)
     dev.sync()
     print(json.dumps({"profile_gemm": GEMM_SHAPES, "launches": args.launches}))
 

@@ -262,6 +262,14 @@ __device__ __forceinline__ void merge_splits(const float* part, int n, float* w,
 
 // 8 bf16 weights (one 16-byte word) dotted with 8 f32 activations, in the
 // order w0*x0 + ... accumulated into acc.
+// acc + the four products of bf16 pairs w0, w1 with a.
+__device__ __forceinline__ float dot4(uint32_t w0, uint32_t w1, float4 a, float acc) {
+  acc = fmaf(bf_lo(w0), a.x, acc);
+  acc = fmaf(bf_hi(w0), a.y, acc);
+  acc = fmaf(bf_lo(w1), a.z, acc);
+  acc = fmaf(bf_hi(w1), a.w, acc);
+  return acc;
+}
 __device__ __forceinline__ float dot8(uint4 w, float4 a, float4 b, float acc) {
   acc = fmaf(bf_lo(w.x), a.x, acc);
   acc = fmaf(bf_hi(w.x), a.y, acc);

@@ -248,23 +248,30 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     const int nr = max(0, min(CH, min(nrows, (st + 1) * stage_rows) - first));
     if (nr > 0) {
       const unsigned char* base = ring + size_t(s) * stage_bytes + size_t(warp * CH) * row_bytes;
-      float acc[CH];
+      // Two accumulators per row (the first and last four products of each
+      // eight) and every weight fragment of an iteration loaded before use:
+      // short dependency chains, many loads in flight.
+      float acc[CH], acc2[CH];
 #pragma unroll
-      for (int r = 0; r < CH; r++) acc[r] = 0.f;
+      for (int r = 0; r < CH; r++) acc[r] = acc2[r] = 0.f;
+#pragma unroll 4
       for (int col = lane * 8; col < cols; col += 256) {
         const float* xb0 = xs + (col - lane * 8) + lane * 4;
         const float4 xa = *reinterpret_cast<const float4*>(xb0);
         const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
+        uint4 wv[CH];
+#pragma unroll
+        for (int r = 0; r < CH; r++)
+          wv[r] = r < nr ? *reinterpret_cast<const uint4*>(base + size_t(r) * row_bytes + size_t(col) * 2)
+                         : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int r = 0; r < CH; r++) {
-          if (r < nr) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(base + size_t(r) * row_bytes + size_t(col) * 2);
-            acc[r] = dot8(wv, xa, xb, acc[r]);
-          }
+          acc[r] = dot4(wv[r].x, wv[r].y, xa, acc[r]);
+          acc2[r] = dot4(wv[r].z, wv[r].w, xb, acc2[r]);
         }
       }
 #pragma unroll
-      for (int r = 0; r < CH; r++) acc[r] = warp_sum(acc[r]) * scale;
+      for (int r = 0; r < CH; r++) acc[r] = warp_sum(acc[r] + acc2[r]) * scale;
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
 
