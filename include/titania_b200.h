@@ -54,6 +54,7 @@ typedef struct tb200_weight tb200_weight; /* Device::Weight, bf16 (model/device.
 typedef struct tb200_model tb200_model;   /* fused-path model (no trait counterpart) */
 typedef struct tb200_state tb200_state;   /* fused-path State (model/model.rs:156-172) */
 typedef struct tb200_tp tb200_tp;         /* a tensor-parallel group (one rank per process and GPU) */
+typedef struct tb200_sampler tb200_sampler; /* top-k / top-p / temperature sampling state on the device */
 
 /* Message for the last nonzero return on this thread. */
 TB200_API const char* tb200_last_error(void);
@@ -289,6 +290,24 @@ enum {
  * 1-5) on the device's stream, exactly as the step's graph runs it, without
  * waiting: for timing and testing kernels one at a time. */
 TB200_API int tb200_enqueue_op(tb200_model* model, tb200_state* state, int op, size_t layer);
+
+/* ---- sampling (model/sampler.rs) ------------------------------------------- */
+
+/* Sampler::new (model/sampler.rs:12-19) for `rows` rows of `vocab` logits:
+ * temperature, top_k (clamped to [1, vocab] as sampler.rs:29; at most 64 here)
+ * and top_p as the reference's; row i's xorshift64* state starts at
+ * max(seeds[i], 1) and lives in device memory. */
+TB200_API int tb200_sampler_new(tb200_device* dev, size_t rows, size_t vocab, float temperature, size_t top_k,
+                                float top_p, const uint64_t* seeds, tb200_sampler** out);
+TB200_API int tb200_sampler_free(tb200_sampler* sampler);
+/* Sampler::sample (model/sampler.rs:21-59) for every row of `logits`
+ * ([rows][vocab] f32, the buffer at least that long): one token per row into
+ * tokens[rows]; waits. Exact logit ties go to the lowest token id. */
+TB200_API int tb200_sample(tb200_sampler* sampler, const tb200_buffer* logits, uint32_t* tokens);
+/* The same without the copy back or the wait (tokens stay on the device). */
+TB200_API int tb200_sample_enqueue(tb200_sampler* sampler, const tb200_buffer* logits);
+/* The generator states, rows x u64 (sampler.rs:63-77's Rng). */
+TB200_API int tb200_sampler_state(tb200_sampler* sampler, uint64_t* out);
 
 /* ---- tracing ------------------------------------------------------------ */
 

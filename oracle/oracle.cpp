@@ -14,7 +14,8 @@
 //                           State buffers (f32 KV cache), rope_table
 //   model/weights.rs:35-81  safetensors reader (BF16 only)
 //   model/config.rs:10-35   config.json fields, head_dim default
-//   model/sampler.rs:21-33  greedy branch (temperature 0)
+//   model/sampler.rs:21-77  top-k / top-p / temperature sampling with
+//                           the xorshift64* generator (greedy at T = 0)
 // It is cross-checked bit-for-bit against an independent numpy restatement
 // (tests/golden/gen_golden.py) on the reference's own op-test shapes and
 // input generator (model/titania.rs:231-249, 319, 333, 346-359).
@@ -29,6 +30,7 @@
 //    attention heads); the partitions are independent, so results do not
 //    depend on the thread count.
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -652,6 +654,52 @@ uint32_t orc_sample_greedy(const float* logits, size_t n) {
   for (size_t i = 1; i < n; i++)
     if (total_key(logits[i]) > total_key(logits[best])) best = i;
   return uint32_t(best);
+}
+
+// sampler.rs:21-59 (Sampler::sample) with its xorshift64* generator
+// (sampler.rs:63-77), one call per token; *rng is the generator state (the
+// reference starts it at max(seed, 1)). The top-k candidates are the k
+// largest logits under total_cmp in descending order; exact ties (which the
+// reference leaves to an unstable selection) go to the lowest token id.
+// Every float step is the reference's, in its order: (logit - max) / T, expf,
+// a sequential f32 sum, p / sum, the running total while it is below top_p,
+// then r = next_f32() * total and r -= p until r <= 0.
+uint32_t orc_sample(const float* logits, size_t n, float temperature, size_t top_k, float top_p, uint64_t* rng) {
+  const size_t k = top_k < 1 ? 1 : (top_k > n ? n : top_k);
+  std::vector<uint32_t> idx(n);
+  for (size_t i = 0; i < n; i++) idx[i] = uint32_t(i);
+  auto better = [&](uint32_t a, uint32_t b) {
+    const int64_t ka = total_key(logits[a]), kb = total_key(logits[b]);
+    return ka != kb ? ka > kb : a < b;
+  };
+  std::partial_sort(idx.begin(), idx.begin() + k, idx.end(), better);
+  if (temperature == 0.0f) return idx[0];
+  const float max = logits[idx[0]];
+  std::vector<float> probs(k);
+  for (size_t i = 0; i < k; i++) probs[i] = expf((logits[idx[i]] - max) / temperature);
+  float sum = -0.0f;
+  for (size_t i = 0; i < k; i++) sum += probs[i];
+  float cumulative = 0.0f;
+  size_t m = 0;
+  for (size_t i = 0; i < k; i++) {
+    probs[i] /= sum;
+    if (cumulative < top_p) {
+      cumulative += probs[i];
+      m++;
+    }
+  }
+  uint64_t x = *rng;
+  x ^= x >> 12;
+  x ^= x << 25;
+  x ^= x >> 27;
+  *rng = x;
+  const float u = float((x * 0x2545F4914F6CDD1DULL) >> 40) / float(1u << 24);
+  float r = u * cumulative;
+  for (size_t i = 0; i < m; i++) {
+    r -= probs[i];
+    if (r <= 0.0f) return idx[i];
+  }
+  return idx[m > 0 ? m - 1 : 0];  // m == 0 (top_p <= 0) panics in the reference
 }
 
 void* orc_model_load(const char* dir) {

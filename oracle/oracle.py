@@ -59,6 +59,8 @@ def lib():
         L.orc_rope_table.argtypes = [f32p, sz, sz, ctypes.c_float]
         L.orc_sample_greedy.argtypes = [f32p, sz]
         L.orc_sample_greedy.restype = ctypes.c_uint32
+        L.orc_sample.argtypes = [f32p, sz, ctypes.c_float, sz, ctypes.c_float, ctypes.POINTER(ctypes.c_uint64)]
+        L.orc_sample.restype = ctypes.c_uint32
         L.orc_model_load.argtypes = [ctypes.c_char_p]
         L.orc_model_load.restype = ctypes.c_void_p
         L.orc_model_free.argtypes = [ctypes.c_void_p]
@@ -132,6 +134,20 @@ def rope_table(max_len, head_dim, theta):
     out = np.empty(max_len * head_dim, dtype=np.float32)
     _check(lib().orc_rope_table(_f32(out), max_len, head_dim, ctypes.c_float(theta)))
     return out
+
+
+class Sampler:
+    """model/sampler.rs:12-77 restated in C (oracle.cpp orc_sample): top-k,
+    top-p and temperature with the reference's xorshift64* state."""
+
+    def __init__(self, temperature: float, top_k: int, top_p: float, seed: int):
+        self.temperature, self.top_k, self.top_p = float(temperature), int(top_k), float(top_p)
+        self.state = ctypes.c_uint64(max(int(seed), 1) & 0xFFFFFFFFFFFFFFFF)
+
+    def sample(self, logits) -> int:
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        return int(lib().orc_sample(_f32(logits), logits.size, self.temperature, self.top_k, self.top_p,
+                                    ctypes.byref(self.state)))
 
 
 def sample_greedy(logits) -> int:

@@ -7,6 +7,7 @@ The package mirrors the reference's `model` crate interface:
 - `Model`, `State`: Model::load / Model::forward (model/model.rs) on the
   fused CUDA-graph decode path;
 - `OpModel`, `OpState`: the same forward pass issued one trait call at a time;
+- `DeviceSampler`: Sampler::sample (model/sampler.rs) on the device;
 - `Config`, `Weights`, `Tensor`, `Sampler`, `BATCH`.
 
 The CUDA library must be built (`python -m titania_b200.build`); there is no
@@ -15,7 +16,7 @@ CPU fallback.
 
 from ._lib import DeviceError
 from .device import B200, Buffer, Tensor, Weight
-from .model import BATCH, BatchState, Config, Model, OpModel, OpState, Sampler, State, Weights
+from .model import BATCH, BatchState, Config, DeviceSampler, Model, OpModel, OpState, Sampler, State, Weights
 
-__all__ = ["B200", "Buffer", "Tensor", "Weight", "DeviceError", "BATCH", "BatchState", "Config", "Model", "OpModel", "OpState",
-           "Sampler", "State", "Weights"]
+__all__ = ["B200", "Buffer", "Tensor", "Weight", "DeviceError", "BATCH", "BatchState", "Config", "DeviceSampler", "Model",
+           "OpModel", "OpState", "Sampler", "State", "Weights"]

@@ -73,6 +73,12 @@ SIGNATURES = {
     "tb200_free_weight": (ctypes.c_int, [P, P]),
     "tb200_argmax": (ctypes.c_int, [P, P, U32P]),
     "tb200_argmax_noalloc": (ctypes.c_int, [P, SZ, P, P]),
+    "tb200_sampler_new": (ctypes.c_int, [P, SZ, SZ, ctypes.c_float, SZ, ctypes.c_float,
+                                         ctypes.POINTER(ctypes.c_uint64), PP]),
+    "tb200_sampler_free": (ctypes.c_int, [P]),
+    "tb200_sample": (ctypes.c_int, [P, P, U32P]),
+    "tb200_sample_enqueue": (ctypes.c_int, [P, P]),
+    "tb200_sampler_state": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_uint64)]),
     "tb200_model_create": (ctypes.c_int, [P, ctypes.POINTER(Config), PP]),
     "tb200_model_bind": (ctypes.c_int, [P, ctypes.c_char_p, P]),
     "tb200_model_finalize": (ctypes.c_int, [P]),

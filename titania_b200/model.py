@@ -441,6 +441,42 @@ class BatchState:
         return out[out["ns"] != 0]
 
 
+class DeviceSampler:
+    """model/sampler.rs:12-77 on the B200 (tb200_sampler_*): top-k, top-p and
+    temperature over `rows` rows of `vocab` logits in a device buffer, with one
+    xorshift64* state per row kept in device memory (row i starts at
+    max(seeds[i], 1)). Exact logit ties go to the lowest token id."""
+
+    def __init__(self, dev: B200, rows: int, vocab: int, temperature: float, top_k: int, top_p: float, seeds):
+        seeds = [int(x) & 0xFFFFFFFFFFFFFFFF for x in seeds]
+        if len(seeds) != rows:
+            raise ValueError("one seed per row")
+        self._dev, self.rows, self.vocab = dev, int(rows), int(vocab)
+        arr = (ctypes.c_uint64 * rows)(*seeds)
+        h = ctypes.c_void_p()
+        call("tb200_sampler_new", dev._h, rows, vocab, float(temperature), int(top_k), float(top_p), arr,
+             ctypes.byref(h))
+        self._h = h.value
+
+    def sample(self, logits) -> np.ndarray:
+        """One token per row of `logits` (a device Buffer of rows x vocab f32)."""
+        out = np.zeros(self.rows, dtype=np.uint32)
+        call("tb200_sample", self._h, logits._h, out.ctypes.data_as(_lib.U32P))
+        return out
+
+    def states(self) -> np.ndarray:
+        out = (ctypes.c_uint64 * self.rows)()
+        call("tb200_sampler_state", self._h, out)
+        return np.array(list(out), dtype=np.uint64)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and not sys.is_finalizing():
+            _lib.lib().tb200_sampler_free(self._h)
+        self._h = None
+
+    __del__ = close
+
+
 class Sampler:
     """model/sampler.rs: top-k, then top-p, at a temperature; temperature 0 is
     greedy (ties to the lowest token id)."""
