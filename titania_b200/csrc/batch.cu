@@ -450,14 +450,16 @@ __global__ void __launch_bounds__(128) k_attn_rows(AttnRowsArgs a) {
 // Every product is exact (bf16 x bf16 in f32) and the planes make q and P
 // exact, so only the f32 accumulation order differs from k_attn_rows. Keys
 // and values arrive by TMA (128-byte swizzle, so ldmatrix is conflict-free)
-// in chunks of 64 positions; warp w owns positions 16w .. 16w+15 of every
-// chunk and keeps its own running max, sum and output, and the four warps
-// are combined once at the end.
+// in chunks of 32 positions; warps 2h and 2h + 1 take every other chunk
+// (h, h + 2, ...), positions 0..15 and 16..31 of it, each keeping its own
+// running max, sum and output; the four warps are combined once at the end.
 
-constexpr int kTcCh = 64;                         // positions per chunk
+constexpr int kTcCh = 32;                         // positions per chunk (two warps of 16)
 constexpr int kTcStages = 3;
-constexpr int kTcBox = kTcCh * 64 * 2;            // one 64-position x 64-dim box: 8 KB
-constexpr int kTcStage = 4 * kTcBox;              // K lo/hi dims, V lo/hi dims: 32 KB
+constexpr int kTcBox = kTcCh * 64 * 2;            // one 32-position x 64-dim box: 4 KB
+constexpr int kTcStage = 4 * kTcBox;              // K lo/hi dims, V lo/hi dims: 16 KB
+// 49 KB of staging: four CTAs fit on an SM, so 148 x 4 = 592 (token, kv group)
+// CTAs run at once (64 sequences x 8 kv heads = 512 in one wave).
 constexpr size_t kTcSmem = size_t(kTcStages) * kTcStage + 1024;
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -488,7 +490,8 @@ __device__ __forceinline__ uint16_t plane_of(float v, int j) {
 }
 
 template <int GRP>
-__global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CUtensorMap cache, AttnRowsArgs a) {
+__global__ void __launch_bounds__(128, GRP <= 2 ? 4 : 2)
+    k_attn_rows_tc(const __grid_constant__ CUtensorMap cache, AttnRowsArgs a) {
   constexpr int NC = 3 * GRP;        // live columns: plane j of head h at column GRP j + h
   constexpr int NB = (NC + 7) / 8;   // MMA column blocks of 8
   constexpr int HP = (GRP + 1) / 2;  // (position, head) pairs per lane: 16 positions x GRP heads / 32 lanes
@@ -501,7 +504,11 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   __shared__ float corr_w[4][GRP];
   __shared__ float wm[4][GRP], wl[4][GRP];
   __shared__ __align__(8) uint64_t bar[kTcStages];
-  __shared__ int consumed[kTcStages], issued_sh, is_last;
+  __shared__ int consumed[kTcStages], is_last;
+  // The chunk whose load was last issued into each stage. The two warp pairs
+  // walk different chunks, so a pair can be two phases of a stage's barrier
+  // ahead of its chunk; it waits for its own chunk's issue first.
+  __shared__ volatile int stage_chunk[kTcStages];
 
   pdl_launch_dependents();
   const int part = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
@@ -526,6 +533,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     unsigned char* st = sm + size_t(i % kTcStages) * kTcStage;
     uint64_t* b = &bar[i % kTcStages];
     const int c0 = p0 + i * kTcCh;
+    stage_chunk[i % kTcStages] = i;
     mbar_arrive_expect_tx(b, kTcStage);
     tma_load_2d(st, &cache, 0, krow + c0, b, pol);
     tma_load_2d(st + kTcBox, &cache, 64, krow + c0, b, pol);
@@ -538,6 +546,7 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
     for (int s = 0; s < kTcStages; s++) {
       mbar_init(&bar[s], 1);
       consumed[s] = 0;
+      stage_chunk[s] = -1;
     }
     fence_mbar_init();
     // Chunks wholly before the token's own position were written by earlier
@@ -553,7 +562,6 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   if (!active) return;
   if (tid == 0) {
     while (issued < kTcStages && issued < nchunks) issue(issued++);
-    issued_sh = issued;
   }
   for (int i = tid; i < GRP * kD; i += 128) qs[i / kD][i % kD] = a.q[size_t(t) * a.ldq + size_t(g) * GRP * kD + i];
   for (int i = tid; i < 4 * 8 * NB * 16; i += 128) (&pw[0][0][0])[i] = 0;  // pad columns stay zero
@@ -600,18 +608,30 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   // The warps go through the chunks independently: each waits for a chunk
   // itself, and the last warp done with a stage issues the chunk kTcStages
   // ahead into it (no block-wide barrier per chunk).
-  for (int i = 0; i < nchunks; i++) {
+  // Warps 2h and 2h + 1 take chunks h, h + 2, h + 4, ...: positions 0..15 and
+  // 16..31 of each.
+  for (int i = warp >> 1; i < nchunks; i += 2) {
     const int s = i % kTcStages;
     const int c0 = p0 + i * kTcCh;
     int got = 1;
-    if (lane == 0) got = mbar_wait(&bar[s], (i / kTcStages) & 1, a.err) ? 1 : 0;
+    if (lane == 0) {
+      // This chunk's load was issued (bounded wait), then it landed.
+      const uint64_t t0 = global_ns();
+      while (stage_chunk[s] != i)
+        if (global_ns() - t0 > kWaitNs) {
+          set_error(a.err, TB200_ERR_TIMEOUT);
+          got = 0;
+          break;
+        }
+      if (got) got = mbar_wait(&bar[s], (i / kTcStages) & 1, a.err) ? 1 : 0;
+    }
     if (!__shfl_sync(0xffffffffu, got, 0)) {
       failed = true;
       break;
     }
     mbar_wait(&bar[s], (i / kTcStages) & 1, nullptr);  // the phase is complete: returns at once
     const uint32_t kbase = smem_u32(sm + size_t(s) * kTcStage), vbase = kbase + 2 * kTcBox;
-    const int pw0 = 16 * warp;  // the warp's first position in the chunk
+    const int pw0 = 16 * (warp & 1);  // the warp's first position in the chunk
     {
       // All eight key fragments first, then two independent accumulation chains.
       const int ar = pw0 + (lane & 7) + 8 * ((lane >> 3) & 1), au = lane >> 4;
@@ -691,16 +711,14 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
         for (int nb = 0; nb < NB; nb++) mma16816(o[mb][nb], af[mb], pb[nb][0], pb[nb][1]);
     }
     // This warp is done with stage s (its fragments are in registers). The
-    // fourth warp to get here refills the stage.
+    // second warp of the chunk to get here refills the stage.
     __syncwarp();
     if (lane == 0) {
       __threadfence_block();
-      if (atomicAdd(&consumed[s], 1) == 3) {
+      if (atomicAdd(&consumed[s], 1) == 1) {  // both warps of the chunk are done
         consumed[s] = 0;
-        if (i + kTcStages < nchunks) {
-          issue(i + kTcStages);
-          atomicMax(&issued_sh, i + kTcStages + 1);
-        }
+        __threadfence_block();  // the reset is seen before the next chunk's issue
+        if (i + kTcStages < nchunks) issue(i + kTcStages);
       }
     }
   }
@@ -709,11 +727,11 @@ __global__ void __launch_bounds__(128) k_attn_rows_tc(const __grid_constant__ CU
   failed = __syncthreads_or(failed);
   if (failed) {
     // Let the copies in flight land (bounded) before the CTA's memory goes.
-    if (tid == 0) {
-      const int n_issued = issued_sh;
-      for (int i = max(0, n_issued - kTcStages); i < n_issued; i++)
-        mbar_wait(&bar[i % kTcStages], (i / kTcStages) & 1, nullptr);
-    }
+    if (tid == 0)
+      for (int s = 0; s < kTcStages; s++) {
+        const int c = stage_chunk[s];  // the last chunk issued into stage s
+        if (c >= 0) mbar_wait(&bar[s], (c / kTcStages) & 1, nullptr);
+      }
     return;
   }
   // The sums of the 16 lanes of each head.
@@ -1041,6 +1059,8 @@ cudaError_t init_batch_kernels() {
 bool batch_group_supported(int group) { return group == 1 || group == 2 || group == 4 || group == 8; }
 
 int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<false>::kCh; }
+
+int attn_cache_box_rows() { return kTcCh; }
 
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms) {
   // Enough CTAs for two per SM; never a part shorter than one chunk (the

@@ -113,7 +113,7 @@ int ensure_batch(tb200_state* st) {
   if (!st->kv_f32) {
     std::string why;
     const size_t rows = st->n_seqs * st->seq_stride / D;
-    if (int rc = tb::encode_tmap_bf16(&st->cache_map, st->kv, rows, D, 64, &why)) {
+    if (int rc = tb::encode_tmap_bf16(&st->cache_map, st->kv, rows, D, tb::attn_cache_box_rows(), &why)) {
       rt::free_batch(st);
       return fail(rc, "batch workspace: " + why);
     }

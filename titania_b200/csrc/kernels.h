@@ -291,6 +291,9 @@ bool attn_rows_tensor_cores(bool kv_f32, int group);
 // Context parts per (token, kv group) for launch_attn_rows: one when the
 // batch alone gives two CTAs per SM.
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms);
+// Rows (positions) of the boxes the tensor-core decode attention loads from
+// a bf16 cache: the cache_map of AttnRowsArgs uses this box height.
+int attn_cache_box_rows();
 void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int group, bool pdl);
 
 struct AttnPrefillArgs {
