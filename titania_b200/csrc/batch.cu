@@ -4,9 +4,9 @@
 //
 //   k_split_rows     x -> three bf16 planes, the operand form of gemm.cu
 //   k_norm_split     RMSNorm of each token row (cpu.rs:85-94), then the split
-//   k_qkv_post       per token: QK-norm of every q and k head, RoPE at the
-//                    token's position (cpu.rs:96-111), k and v appended to the
-//                    token's sequence cache (model.rs:119-120)
+//   k_embed_split    embedding rows -> the first RMSNorm's planes and sums of
+//                    squares (QK-norm, RoPE and the cache append run in the
+//                    q|k|v contraction's epilogue, gemm.cu)
 //   k_attn_rows      decode attention, one query token per sequence: a CTA per
 //                    (token, kv group[, part of the context]) streaming the
 //                    cache through a ring of bulk copies with an online
@@ -14,9 +14,10 @@
 //   k_attn_prefill   causal attention for a run of tokens of one sequence,
 //                    tiled: 64 query rows against 64-position key/value tiles
 //                    with an online softmax
-//   k_argmax_rows    greedy choice per row of logits (sampler.rs:21-33 at
-//                    temperature 0, ties to the lowest id), advancing each
-//                    sequence's position for the device-side token loop
+//   k_argmax_finish  greedy choice per row from the argmax keys the lm_head
+//                    contraction folded (sampler.rs:21-33 at temperature 0,
+//                    ties to the lowest id), advancing each sequence's
+//                    position for the device-side token loop
 //
 // The key/value cache of a batch is [sequence][layer][k|v][kv head][position]
 // [head_dim]; a sequence's block is the single-sequence layout, so the
@@ -129,80 +130,6 @@ __global__ void __launch_bounds__(256) k_embed_split(float* __restrict__ x, cons
     ssq[blockIdx.x] = tot;
     tr.at(blockIdx.x, TB200_TRACE_DONE);
   }
-}
-
-// ---- QK-norm, RoPE, cache append -------------------------------------------------
-
-// One CTA (4 warps) per token; a warp takes one head at a time, lane l
-// holding elements 4l .. 4l+3, so a head's RoPE partner (i, i + 64) sits in
-// lane l ^ 16.
-__global__ void __launch_bounds__(128) k_qkv_post(QkvPostArgs a) {
-  pdl_launch_dependents();
-  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_START);
-  pdl_wait();
-  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_WAITED);
-  const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos = a.pos[t], seq = a.seq[t];
-  if (pos < 0 || pos >= a.max_len || seq < 0 || seq >= a.n_seqs) {
-    if (threadIdx.x == 0) set_error(a.err, TB200_ERR_ARG);
-    return;
-  }
-  float* row = a.qkv + size_t(t) * a.ld;
-  const size_t cache_head = size_t(a.max_len) * kD;  // elements per kv head
-  const size_t v_off = size_t(a.n_kv_heads) * cache_head;
-  const size_t base = size_t(seq) * a.seq_stride + size_t(pos) * kD + 4 * lane;
-  // RoPE factors for this lane's four elements: pair index (4l + j) mod 64.
-  const int i0 = (4 * lane) & 63;
-  const float4 cs01 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kD + 2 * i0);
-  const float4 cs23 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kD + 2 * i0 + 4);
-  const float cs[4] = {cs01.x, cs01.z, cs23.x, cs23.z}, sn[4] = {cs01.y, cs01.w, cs23.y, cs23.w};
-  const bool first_half = lane < 16;
-  const int nq = a.n_heads, nk = a.n_kv_heads;
-  for (int h = warp; h < nq + 2 * nk; h += 4) {
-    float4 v = *reinterpret_cast<const float4*>(row + size_t(h) * kD + 4 * lane);
-    if (h >= nq + nk) {  // value head: into the cache as is
-      const size_t at = base + size_t(h - nq - nk) * cache_head + v_off;
-      if (a.kv_f32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(a.kv) + at) = v;
-      } else {
-        uint16_t* p = static_cast<uint16_t*>(a.kv) + at;
-        p[0] = f2bf(v.x); p[1] = f2bf(v.y); p[2] = f2bf(v.z); p[3] = f2bf(v.w);
-      }
-      continue;
-    }
-    const uint16_t* nw = h < nq ? a.q_norm : a.k_norm;
-    if (nw) {
-      const float s = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-      const float scale = 1.0f / sqrtf(s / float(kD) + a.eps);
-      const uint2 wb = *reinterpret_cast<const uint2*>(nw + 4 * lane);
-      v.x = __fmul_rn(v.x, __fmul_rn(scale, bf_lo(wb.x)));
-      v.y = __fmul_rn(v.y, __fmul_rn(scale, bf_hi(wb.x)));
-      v.z = __fmul_rn(v.z, __fmul_rn(scale, bf_lo(wb.y)));
-      v.w = __fmul_rn(v.w, __fmul_rn(scale, bf_hi(wb.y)));
-    }
-    float e[4] = {v.x, v.y, v.z, v.w}, r[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const float other = __shfl_xor_sync(0xffffffffu, e[j], 16);
-      r[j] = first_half ? __fsub_rn(__fmul_rn(e[j], cs[j]), __fmul_rn(other, sn[j]))
-                        : __fadd_rn(__fmul_rn(e[j], cs[j]), __fmul_rn(other, sn[j]));
-    }
-    const float4 o = make_float4(r[0], r[1], r[2], r[3]);
-    if (h < nq) {
-      *reinterpret_cast<float4*>(row + size_t(h) * kD + 4 * lane) = o;
-    } else {
-      const size_t at = base + size_t(h - nq) * cache_head;
-      if (a.kv_f32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(a.kv) + at) = o;
-      } else {
-        uint16_t* p = static_cast<uint16_t*>(a.kv) + at;
-        p[0] = f2bf(o.x); p[1] = f2bf(o.y); p[2] = f2bf(o.z); p[3] = f2bf(o.w);
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) a.trace.at(blockIdx.x, TB200_TRACE_DONE);
 }
 
 // ---- decode attention: one query token per sequence ------------------------------
@@ -955,45 +882,6 @@ __global__ void __launch_bounds__(256) k_attn_prefill(AttnPrefillArgs a) {
 
 // ---- greedy choice per row ----------------------------------------------------------
 
-__global__ void __launch_bounds__(1024) k_argmax_rows(ArgmaxRowsArgs a) {
-  __shared__ unsigned long long red[32];
-  __shared__ int step_s, is_last;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int r = blockIdx.x;
-  if (threadIdx.x == 0) step_s = a.step ? *a.step : 0;
-  const float* x = a.logits + size_t(r) * a.V;
-  unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < a.V; i += blockDim.x) {
-    const unsigned long long k = argmax_key(x[i], uint32_t(i));
-    best = k > best ? k : best;
-  }
-  best = warp_umax64(best);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    unsigned long long b = red[threadIdx.x];
-    b = warp_umax64(b);
-    if (threadIdx.x == 0) {
-      const int tok = int(argmax_index(b));
-      if (a.next) a.next[r] = tok;
-      if (a.tok) a.tok[r] = tok;
-      if (a.pos) a.pos[r] += 1;
-      if (a.out && step_s < a.out_cap) a.out[size_t(step_s) * gridDim.x + r] = tok;
-    }
-  }
-  if (!a.step) return;
-  // The last CTA advances the step counter, after every CTA has read it.
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (is_last && threadIdx.x == 0) {
-    *a.step = step_s + 1;
-    *a.ticket = 0u;
-  }
-}
-
 // One CTA: the token ids from the keys a contraction folded into best[],
 // which it zeroes for the next step.
 __global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigned long long* best, int rows) {
@@ -1091,9 +979,6 @@ void launch_embed_split(cudaStream_t s, float* x, const uint16_t* table, int dim
                tr);
 }
 
-void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl) {
-  if (tokens > 0) launch_pdl(s, dim3(tokens), dim3(128), 0, pdl, k_qkv_post, a);
-}
 
 bool attn_rows_tensor_cores(bool kv_f32, int group) {
   return !kv_f32 && (group == 1 || group == 2 || group == 4 || group == 8);
@@ -1143,8 +1028,5 @@ void launch_argmax_finish(cudaStream_t s, const ArgmaxRowsArgs& a, unsigned long
   if (rows > 0) launch_pdl(s, dim3(1), dim3(256), 0, pdl, k_argmax_finish, a, best, rows);
 }
 
-void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl) {
-  if (rows > 0) launch_pdl(s, dim3(rows), dim3(1024), 0, pdl, k_argmax_rows, a);
-}
 
 }  // namespace tb

@@ -188,7 +188,7 @@ struct GemmArgs {
   uint16_t* next_split;
   size_t next_plane;
   float* out_ssq;
-  // kGemmQkv (QkvPostArgs' meaning): norms, RoPE table, cache, token rows.
+  // kGemmQkv: QK-norm weights, RoPE table, cache, token rows.
   const uint16_t* q_norm;
   const uint16_t* k_norm;
   const float* rope;
@@ -246,22 +246,6 @@ void launch_embed_split(cudaStream_t s, float* x, const uint16_t* table, int dim
                         const uint16_t* w, uint16_t* out, size_t plane, float* ssq, int* err, int tokens, bool pdl,
                         const TraceAt& tr = TraceAt{});
 
-struct QkvPostArgs {
-  float* qkv;               // [T][ld]: q heads | k heads | v heads; q rewritten in place
-  int ld;
-  const uint16_t* q_norm;   // [head_dim] or null
-  const uint16_t* k_norm;
-  float eps;
-  const float* rope;        // [max_len][head_dim] (cos, sin) pairs
-  void* kv;                 // this layer's cache block of sequence 0
-  size_t seq_stride;        // cache elements between sequences
-  int kv_f32, max_len, n_heads, n_kv_heads, n_seqs;
-  const int* pos;           // [T] position of each token
-  const int* seq;           // [T] sequence of each token
-  int* err;
-  TraceAt trace;
-};
-void launch_qkv_post(cudaStream_t s, const QkvPostArgs& a, int tokens, bool pdl);
 
 struct AttnRowsArgs {
   const float* q;           // [T][ldq], query heads (normed, rotated) from column 0
@@ -309,8 +293,8 @@ struct AttnPrefillArgs {
 void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bool pdl);
 
 // The greedy choice after a contraction that folded argmax keys into
-// best[rows] (GemmArgs::best): writes the token ids as launch_argmax_rows
-// does and zeroes best.
+// best[rows] (GemmArgs::best): writes each row's token id (to next, tok and
+// the step's output row), advances positions and the step, zeroes best.
 void launch_argmax_finish(cudaStream_t s, const struct ArgmaxRowsArgs& a, unsigned long long* best, int rows,
                           bool pdl);
 
@@ -327,6 +311,5 @@ struct ArgmaxRowsArgs {
   int* err;                 // launch_argmax_finish: set when a row got no key
   TraceAt trace;
 };
-void launch_argmax_rows(cudaStream_t s, const ArgmaxRowsArgs& a, int rows, bool pdl);
 
 }  // namespace tb
