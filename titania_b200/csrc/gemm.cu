@@ -178,7 +178,8 @@ __device__ __forceinline__ float tile_token_sum(const float* tile, int e) {
 template <int N>
 struct EpiPre {
   float x[N];    // kGemmResid, kGemmResidNorm: the residual rows of the N tokens
-  float w;       // kGemmResidNorm: the next norm's weight; kGemmQkv: the QK-norm weight
+  float w;       // kGemmQkv: the QK-norm weight of this thread's row
+  uint2 w4;      // kGemmResidNorm: the next norm's weight, the 4 rows this lane stores
   float2 cs[N];  // kGemmQkv: RoPE cos / sin of each token's position
 };
 
@@ -202,7 +203,16 @@ __device__ __forceinline__ void epi_prefetch(const GemmArgs& a, int mt, int row,
   if (EPI == kGemmResid || EPI == kGemmResidNorm) {
 #pragma unroll
     for (int j = 0; j < N; j++) pre.x[j] = row_ok && t0 + j < a.T ? a.out[size_t(t0 + j) * a.ldo + row] : 0.f;
-    if (EPI == kGemmResidNorm) pre.w = row_ok ? bf16f(a.next_w[row]) : 0.f;
+    if (EPI == kGemmResidNorm) {
+      const int r4 = mt * kBM + 4 * lane;  // the rows this lane stores (epi_group's output pass)
+      if (r4 + 3 < a.M) {
+        pre.w4 = *reinterpret_cast<const uint2*>(a.next_w + r4);
+      } else {
+        uint16_t h[4];
+        for (int i = 0; i < 4; i++) h[i] = r4 + i < a.M ? a.next_w[r4 + i] : uint16_t(0);
+        pre.w4 = make_uint2(uint32_t(h[0]) | (uint32_t(h[1]) << 16), uint32_t(h[2]) | (uint32_t(h[3]) << 16));
+      }
+    }
   }
   if (EPI == kGemmQkv) {
     const int nq = a.n_heads, nk = a.n_kv_heads;
@@ -226,6 +236,52 @@ __device__ __forceinline__ void epi_prefetch(const GemmArgs& a, int mt, int row,
   }
 }
 
+// The epilogues' output pass: after the values go through shared memory
+// (tile[token][row], row stride kEpiLd), each warp writes whole token rows,
+// 4 consecutive rows per lane, as 16-byte (f32) or 8-byte (bf16) stores —
+// a quarter of the store instructions of one value per lane (the epilogue
+// time was measured per store instruction). Rows at or past `rows` are not
+// written; `vec` is false when the destination rows are not 16-byte aligned.
+constexpr int kEpiLd = 132;
+__device__ __forceinline__ void store_f32x4(float* dst, int r0, int rows, float4 v, bool vec) {
+  if (vec && r0 + 3 < rows) {
+    *reinterpret_cast<float4*>(dst + r0) = v;
+  } else {
+    const float w[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < 4; i++)
+      if (r0 + i < rows) dst[r0 + i] = w[i];
+  }
+}
+// Four values as three bf16 planes (store_split3's split), plane p at dst + p * plane.
+__device__ __forceinline__ void store_split3x4(uint16_t* dst, size_t plane, int r0, int rows, float4 v, bool vec) {
+  const float in[4] = {v.x, v.y, v.z, v.w};
+  uint16_t p0[4], p1[4], p2[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    p0[i] = f2bf(in[i]);
+    const float res = in[i] - bf16f(p0[i]);
+    p1[i] = f2bf(res);
+    p2[i] = f2bf(res - bf16f(p1[i]));
+  }
+  if (vec && r0 + 3 < rows) {
+    *reinterpret_cast<uint2*>(dst + r0) = make_uint2(p0[0] | (uint32_t(p0[1]) << 16), p0[2] | (uint32_t(p0[3]) << 16));
+    *reinterpret_cast<uint2*>(dst + plane + r0) =
+        make_uint2(p1[0] | (uint32_t(p1[1]) << 16), p1[2] | (uint32_t(p1[3]) << 16));
+    *reinterpret_cast<uint2*>(dst + 2 * plane + r0) =
+        make_uint2(p2[0] | (uint32_t(p2[1]) << 16), p2[2] | (uint32_t(p2[3]) << 16));
+  } else {
+    for (int i = 0; i < 4; i++)
+      if (r0 + i < rows) {
+        dst[r0 + i] = p0[i];
+        dst[plane + r0 + i] = p1[i];
+        dst[2 * plane + r0 + i] = p2[i];
+      }
+  }
+}
+__device__ __forceinline__ bool aligned16(const void* p, size_t ld_elems, size_t elem_bytes) {
+  return ((reinterpret_cast<uintptr_t>(p) | (ld_elems * elem_bytes)) & 15) == 0;
+}
+
 // The epilogue of N consecutive tokens t0 .. t0 + N - 1 (N <= 32) of row
 // `row` = m0 + 32 q + lane of row tile `mt`: v[j] is the accumulator of
 // token t0 + j, `pre` what epi_prefetch loaded for the same tokens. All 128
@@ -243,35 +299,50 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     for (int j = 0; j < N; j++) v[j] *= es.scale[j];
     named_sync(1, 128);
   }
+  const int r = 32 * q + lane;   // this thread's row of the tile
+  const int m0 = mt * kBM;       // the tile's first row
+  const int tw = e >> 5;         // output pass: this warp's token of each group of 4
+  const int rr = 4 * lane;       // output pass: this lane's 4 rows
+  static_assert(N % 4 == 0, "tokens in groups of 4");
   if (EPI == kGemmStore) {
 #pragma unroll
-    for (int j = 0; j < N; j++)
-      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = v[j];
+    for (int j = 0; j < N; j++) es.tile[j * kEpiLd + r] = v[j];
+    named_sync(1, 128);
+    const bool vec = aligned16(a.out, size_t(a.ldo), 4);
+#pragma unroll
+    for (int k = 0; k < N / 4; k++) {
+      const int j = 4 * k + tw, t = t0 + j;
+      if (t < a.T)
+        store_f32x4(a.out + size_t(t) * a.ldo, m0 + rr, a.M,
+                    *reinterpret_cast<const float4*>(&es.tile[j * kEpiLd + rr]), vec);
+    }
+    named_sync(1, 128);  // the tile is read before the next group writes it
   } else if (EPI == kGemmResid || EPI == kGemmResidNorm) {
-    float x[N];
 #pragma unroll
     for (int j = 0; j < N; j++) {
-      x[j] = __fadd_rn(pre.x[j], v[j]);
-      if (row_ok && t0 + j < a.T) a.out[size_t(t0 + j) * a.ldo + row] = x[j];
+      v[j] = __fadd_rn(pre.x[j], v[j]);  // x += W . input (rows past M are 0 + 0)
+      es.tile[j * kEpiLd + r] = v[j];
     }
-    if (EPI == kGemmResidNorm) {
-      // The next RMSNorm's input: x * w as planes, and this tile's sum of
-      // squares of x per token (its consumer divides by the row length).
-      constexpr int G = 128 / N, ST = 128 + G;
-      const float w = pre.w;
+    named_sync(1, 128);
+    const bool vec = aligned16(a.out, size_t(a.ldo), 4);
+    const bool vec_h = EPI == kGemmResidNorm && aligned16(a.next_split, size_t(a.ldo), 2) && (a.next_plane & 3) == 0;
 #pragma unroll
-      for (int j = 0; j < N; j++) {
-        es.tile[j * ST + e] = row_ok ? x[j] * x[j] : 0.f;
-        if (row_ok && t0 + j < a.T)
-          store_split3(a.next_split, a.next_plane, size_t(t0 + j) * a.ldo + row, __fmul_rn(x[j], w));
+    for (int k = 0; k < N / 4; k++) {
+      const int j = 4 * k + tw, t = t0 + j;
+      if (t >= a.T) continue;  // warp-uniform
+      const float4 x4 = *reinterpret_cast<const float4*>(&es.tile[j * kEpiLd + rr]);
+      store_f32x4(a.out + size_t(t) * a.ldo, m0 + rr, a.M, x4, vec);
+      if (EPI == kGemmResidNorm) {
+        // The next RMSNorm's input: x * w as planes, and this tile's sum of
+        // squares of x per token (its consumer divides by the row length).
+        const float ss = warp_sum(((x4.x * x4.x + x4.y * x4.y) + x4.z * x4.z) + x4.w * x4.w);
+        if (lane == 0) a.out_ssq[size_t(t) * a.mtiles + mt] = ss;
+        const float4 xw = make_float4(__fmul_rn(x4.x, bf_lo(pre.w4.x)), __fmul_rn(x4.y, bf_hi(pre.w4.x)),
+                                      __fmul_rn(x4.z, bf_lo(pre.w4.y)), __fmul_rn(x4.w, bf_hi(pre.w4.y)));
+        store_split3x4(a.next_split + size_t(t) * a.ldo, a.next_plane, m0 + rr, a.M, xw, vec_h);
       }
-      named_sync(1, 128);
-      const float ss = tile_token_sum<N>(es.tile, e);
-      if (e % G == 0 && t0 + e / G < a.T) a.out_ssq[size_t(t0 + e / G) * a.mtiles + mt] = ss;
-      named_sync(1, 128);  // the tile is read before the next group writes it
     }
-#pragma unroll
-    for (int j = 0; j < N; j++) v[j] = x[j];
+    named_sync(1, 128);  // the tile is read before the next group writes it
   } else if (EPI == kGemmSilu) {
     // Lanes 2i (gate) and 2i+1 (up) of hidden row i share tokens: the even
     // lane finishes token j, the odd lane token j + 1.
@@ -281,12 +352,23 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
     for (int j = 0; j < N; j += 2) {
       const float other = __shfl_xor_sync(0xffffffffu, even ? v[j + 1] : v[j], 1);
       const float g = even ? v[j] : other, u = even ? other : v[j + 1];
-      const int t = t0 + j + (even ? 0 : 1);
-      if (row_ok && t < a.T) store_split3(a.out_split, a.plane, size_t(t) * a.ldh + (row >> 1), silu_mul(g, u));
+      es.tile[(j + (even ? 0 : 1)) * kEpiLd + (r >> 1)] = silu_mul(g, u);
     }
+    named_sync(1, 128);
+    // 64 hidden rows per token: 16 lanes x 4 rows, 8 tokens per pass.
+    const int hq = 4 * (e & 15), hrows = a.M / 2;
+    const bool vec = aligned16(a.out_split, size_t(a.ldh), 2) && (a.plane & 3) == 0;
+#pragma unroll
+    for (int k = 0; k < (N + 7) / 8; k++) {
+      const int j = 8 * k + (e >> 4), t = t0 + j;
+      if (j < N && t < a.T)
+        store_split3x4(a.out_split + size_t(t) * a.ldh, a.plane, m0 / 2 + hq, hrows,
+                       *reinterpret_cast<const float4*>(&es.tile[j * kEpiLd + hq]), vec);
+    }
+    named_sync(1, 128);  // the tile is read before the next group writes it
   } else {  // kGemmQkv: tile mt is query head mt, key head mt - nq, or value head mt - nq - nk
     const int nq = a.n_heads, nk = a.n_kv_heads;
-    const int d = 32 * q + lane;  // the head dimension of this row (e is not: warp 2 reads lanes 64..95)
+    const int d = r;  // the head dimension of this row (e is not: warp 2 reads lanes 64..95)
     const bool is_v = mt >= nq + nk;
     if (!is_v) {
       const uint16_t* nw = mt < nq ? a.q_norm : a.k_norm;
@@ -315,27 +397,36 @@ __device__ __forceinline__ void epi_group(const GemmArgs& a, int mt, int row, bo
         v[j] = d < 64 ? __fsub_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y))
                       : __fadd_rn(__fmul_rn(v[j], cs.x), __fmul_rn(other, cs.y));
       }
-    } else {
-      named_sync(1, 128);  // es.pos / es.seq in place
     }
+    named_sync(1, 128);  // RoPE's reads are done; es.pos / es.seq in place
 #pragma unroll
-    for (int j = 0; j < N; j++) {
-      const int t = t0 + j;
-      if (t >= a.T) continue;
+    for (int j = 0; j < N; j++) es.tile[j * kEpiLd + d] = v[j];
+    named_sync(1, 128);
+    const bool vec = aligned16(a.out, size_t(a.ldo), 4);
+#pragma unroll
+    for (int k = 0; k < N / 4; k++) {
+      const int j = 4 * k + tw, t = t0 + j;
+      if (t >= a.T) continue;  // warp-uniform
+      const float4 v4 = *reinterpret_cast<const float4*>(&es.tile[j * kEpiLd + rr]);
       if (mt < nq) {
-        a.out[size_t(t) * a.ldo + row] = v[j];
+        store_f32x4(a.out + size_t(t) * a.ldo, m0 + rr, a.M, v4, vec);
         continue;
       }
       const int pos = es.pos[j], sq = es.seq[j];
       if (pos < 0 || pos >= a.max_len || sq < 0 || sq >= a.n_seqs) {
-        if (d == 0) set_error(a.err, TB200_ERR_ARG);
+        if (lane == 0) set_error(a.err, TB200_ERR_ARG);
         continue;
       }
       const int kh = is_v ? mt - nq - nk : mt - nq;
       const size_t at = size_t(sq) * a.seq_stride + (is_v ? size_t(nk) * a.max_len * 128 : 0) +
-                        (size_t(kh) * a.max_len + pos) * 128 + d;
-      if (a.kv_f32) static_cast<float*>(a.kv)[at] = v[j];
-      else static_cast<uint16_t*>(a.kv)[at] = f2bf(v[j]);
+                        (size_t(kh) * a.max_len + pos) * 128 + rr;  // 128 contiguous dims per (token, head)
+      if (a.kv_f32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(a.kv) + at) = v4;
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.kv) + at) =
+            make_uint2(uint32_t(f2bf(v4.x)) | (uint32_t(f2bf(v4.y)) << 16),
+                       uint32_t(f2bf(v4.z)) | (uint32_t(f2bf(v4.w)) << 16));
+      }
     }
     named_sync(1, 128);  // es.tile / es.pos / es.seq read before the next group writes them
   }
