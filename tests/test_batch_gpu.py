@@ -250,3 +250,30 @@ def test_qwen3_0_6b_long_prompt(b200, qwen06b):
     got = m.forward(st, prompt, 0)
     close(got, exp, REL, ABS)
     assert int(np.argmax(got)) == int(np.argmax(exp))
+
+
+@pytest.mark.parametrize("kv", ["bf16"])
+def test_tiny_batch_many_sequences_long_contexts(tiny, kv):
+    """Enough sequences that each (token, kv head) gets one CTA over its whole
+    context (148 x 2 kv heads >= two CTAs per SM), with contexts of 5 to 7
+    32-position chunks: the decode attention reuses its staging ring and its
+    two warp pairs walk alternate chunks. Every sequence against its own
+    oracle run."""
+    m, ref = tiny
+    rng = np.random.default_rng(31)
+    n = 148
+    lengths = [int(x) for x in rng.integers(140, 215, size=n)]
+    prompts = [synth.prompt_tokens(k, 1024, seed=4000 + i) for i, k in enumerate(lengths)]
+    steps = 3
+    max_len = max(lengths) + steps + 4
+    bs = m.batch_state(n, max_len, kv=kv)
+    first = [m.forward_seq(bs, i, p, 0, logits=False) for i, p in enumerate(prompts)]
+    expected = [orc.greedy_generate(ref, p, steps + 1, max_len=max_len) for p in prompts]
+    assert first == [e[0][0] for e in expected]
+    tokens, positions = list(first), list(lengths)
+    for step in range(steps):
+        logits, nxt = m.forward_batch(bs, tokens, positions)
+        for i in range(n):
+            close(logits[i], expected[i][1][step + 1], REL, 1.5e-2)
+            assert int(nxt[i]) == expected[i][0][step + 1], f"sequence {i} step {step}"
+        tokens, positions = nxt.tolist(), [p + 1 for p in positions]
