@@ -248,3 +248,48 @@ def test_tp2_qwen3_0_6b_against_oracle():
         for i in range(steps + 1):
             close(logits[i], ref_logits[i], REL, ABS)
         assert toks == ref_tokens and gen == ref_tokens, f"rank {r}"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_shard_rule_reassembles_at_4_and_8_ranks(tmp_path, world):
+    """The sharding rule at the tensor-parallel widths of the scaling run, on a
+    small model with 8 kv heads (as Qwen3-4B): every rank's slices put back
+    together are the whole tensor, and the per-rank shapes divide evenly."""
+    from titania_b200 import synth
+    from titania_b200.model import Config, Weights, tensor_names
+    from titania_b200.tp import shard_config, shard_tensor
+    cfg = dict(synth.TINY, num_attention_heads=16, num_key_value_heads=8, intermediate_size=1024)
+    d = str(tmp_path / "tiny-kv8")
+    synth.write_model(d, cfg, seed=9)
+    c = Config.load(os.path.join(d, "config.json"))
+    w = Weights.open(os.path.join(d, "model.safetensors"))
+    lc = shard_config(c, world)
+    assert lc.num_key_value_heads * world == 8 and lc.num_attention_heads * world == 16
+    assert lc.intermediate_size * world == 1024
+    for name, _ in tensor_names(c):
+        t = w.read(name)
+        full = t.data.reshape(t.shape)
+        arrs = [p[1].reshape(p[0]) for p in (shard_tensor(c, name, t.shape, t.data, r, world) for r in range(world))]
+        if name.endswith(("o_proj.weight", "down_proj.weight")):
+            back = np.concatenate(arrs, axis=1)
+        elif name.endswith(("q_proj.weight", "k_proj.weight", "v_proj.weight", "gate_proj.weight", "up_proj.weight")):
+            back = np.concatenate(arrs, axis=0)
+        else:
+            assert all(np.array_equal(a, full) for a in arrs), name
+            continue
+        assert np.array_equal(back, full), name
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_qwen3_4b_shards_fit_the_kernels(world):
+    """Config 4 at TP 1-8: per-rank widths are multiples of the kernels' 64-column
+    blocks and 16-row tiles, and a kv head keeps whole query groups."""
+    from titania_b200 import synth
+    from titania_b200.model import Config
+    from titania_b200.tp import shard_config
+    lc = shard_config(Config(**synth.QWEN3_4B), world)
+    hd = lc.head_dim()
+    widths = [lc.hidden_size, lc.intermediate_size, lc.num_attention_heads * hd, lc.num_key_value_heads * hd]
+    assert all(x % 64 == 0 for x in widths), widths
+    assert lc.num_attention_heads % lc.num_key_value_heads == 0
+    assert (lc.num_attention_heads // lc.num_key_value_heads) in (1, 2, 4, 8)
