@@ -112,7 +112,17 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
   // Consumers. Norm weights do not depend on the previous kernel either;
   // each thread stages exactly the elements it multiplies below, so no
   // barrier is needed between the two.
-  if (NORM)
+  // A 1024-column input that needs no summing or copying out skips shared
+  // memory: every warp loads the whole vector into registers, lane l holding
+  // the columns it multiplies (256k + 8l .. + 7, k = 0..3), and sums its own
+  // squares, so no barrier separates the input from the dot products.
+  constexpr int kXregCols = 1024;
+  const bool xreg = !KS && EPI != kMvResidual && cols == kXregCols && a.npartials == 0 && !a.x_out;
+  uint4 gw[kXregCols / 256];
+  if (NORM && xreg) {
+#pragma unroll
+    for (int k = 0; k < kXregCols / 256; k++) gw[k] = *reinterpret_cast<const uint4*>(a.norm_w + 256 * k + lane * 8);
+  } else if (NORM)
     for (int i = tid * 4; i < cols; i += kMvWarps * 32 * 4) {
       const uint2 g = *reinterpret_cast<const uint2*>(a.norm_w + i);
       *reinterpret_cast<float4*>(nw + i) = make_float4(bf_lo(g.x), bf_hi(g.x), bf_lo(g.y), bf_hi(g.y));
@@ -125,7 +135,15 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
   float rres = 0.f;
   if (EPI == kMvResidual && tid < nrows) rres = __ldcg((a.resid_src ? a.resid_src : a.out) + r0 + tid);
   float ss = 0.f;
-  for (int i = tid * 4; i < cols; i += kMvWarps * 32 * 4) {
+  float4 xr[kXregCols / 256][2];
+  if (xreg) {
+#pragma unroll
+    for (int k = 0; k < kXregCols / 256; k++) {
+      xr[k][0] = __ldcg(reinterpret_cast<const float4*>(a.x + 256 * k + lane * 8));
+      xr[k][1] = __ldcg(reinterpret_cast<const float4*>(a.x + 256 * k + lane * 8 + 4));
+    }
+  }
+  for (int i = tid * 4; !xreg && i < cols; i += kMvWarps * 32 * 4) {
     float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + i));
     if (a.npartials > 0) {
       // x + (p0 + p1 + ...): the o_proj output summed in group order, then
@@ -162,18 +180,44 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     // 8l+7) reads two runs of 512 contiguous bytes, free of bank conflicts.
     *reinterpret_cast<float4*>(xs + xperm(i)) = v;
   }
-  if (EPI == kMvResidual && tid < nrows) resid[tid] = rres;
-  if (NORM) {
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-  }
-  named_sync(1, kMvWarps * 32);
   float scale = 1.0f;
-  if (NORM) {
-    float tot = 0.f;
+  if (xreg) {
+    if (NORM) {
 #pragma unroll
-    for (int w = 0; w < kMvWarps; w++) tot += red[w];
-    scale = 1.0f / sqrtf(tot / float(cols) + a.eps);
+      for (int k = 0; k < kXregCols / 256; k++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const float4 v = xr[k][h];
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+      ss = warp_sum(ss);
+      scale = 1.0f / sqrtf(ss / float(cols) + a.eps);
+#pragma unroll
+      for (int k = 0; k < kXregCols / 256; k++) {
+        const uint4 g = gw[k];
+        xr[k][0].x *= bf_lo(g.x);
+        xr[k][0].y *= bf_hi(g.x);
+        xr[k][0].z *= bf_lo(g.y);
+        xr[k][0].w *= bf_hi(g.y);
+        xr[k][1].x *= bf_lo(g.z);
+        xr[k][1].y *= bf_hi(g.z);
+        xr[k][1].z *= bf_lo(g.w);
+        xr[k][1].w *= bf_hi(g.w);
+      }
+    }
+  } else {
+    if (EPI == kMvResidual && tid < nrows) resid[tid] = rres;
+    if (NORM) {
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+    }
+    named_sync(1, kMvWarps * 32);
+    if (NORM) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMvWarps; w++) tot += red[w];
+      scale = 1.0f / sqrtf(tot / float(cols) + a.eps);
+    }
   }
   if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_INPUT);
 
@@ -254,11 +298,8 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
       float acc[CH], acc2[CH];
 #pragma unroll
       for (int r = 0; r < CH; r++) acc[r] = acc2[r] = 0.f;
-#pragma unroll 4
-      for (int col = lane * 8; col < cols; col += 256) {
-        const float* xb0 = xs + (col - lane * 8) + lane * 4;
-        const float4 xa = *reinterpret_cast<const float4*>(xb0);
-        const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
+      // Columns col .. col + 7 of this warp's rows against x[col .. col + 7] = (xa, xb).
+      auto chunk = [&](int col, const float4& xa, const float4& xb) {
         uint4 wv[CH];
 #pragma unroll
         for (int r = 0; r < CH; r++)
@@ -268,6 +309,16 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
         for (int r = 0; r < CH; r++) {
           acc[r] = dot4(wv[r].x, wv[r].y, xa, acc[r]);
           acc2[r] = dot4(wv[r].z, wv[r].w, xb, acc2[r]);
+        }
+      };
+      if (xreg) {
+#pragma unroll
+        for (int k = 0; k < kXregCols / 256; k++) chunk(256 * k + lane * 8, xr[k][0], xr[k][1]);
+      } else {
+#pragma unroll 4
+        for (int col = lane * 8; col < cols; col += 256) {
+          const float* xb0 = xs + (col - lane * 8) + lane * 4;
+          chunk(col, *reinterpret_cast<const float4*>(xb0), *reinterpret_cast<const float4*>(xb0 + 128));
         }
       }
 #pragma unroll

@@ -65,6 +65,13 @@ constexpr int kStage = kStageA + kStageB;
 constexpr int kMaxStages = 5;
 constexpr int kMaxSplitStages = 4;               // split-K: room for the receive buffer
 constexpr size_t kRecvBytes = size_t(kBN) * kBM * 4;  // split-K: S slices of 64 / S tokens x 128 rows
+// Two splits send 16-byte pieces (4 tokens of a row) into rows padded to
+// kRecvLd2 floats ([source][row][token]: conflict-free on both sides); more
+// splits send 4-byte values into [source][token][row].
+constexpr int kRecvLd2 = kBN / 2 + 4;
+__host__ __device__ constexpr size_t recv_bytes_for(int splits) {
+  return splits == 2 ? size_t(2) * kBM * kRecvLd2 * 4 : (splits > 1 ? kRecvBytes : 0);
+}
 constexpr int kAccCols = 256;            // tensor-memory columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
 // Floor of the dynamic shared memory: more than half of an SM's 228 KB.
@@ -83,8 +90,8 @@ struct EpiScratch {
 // tensor-memory address and flags, the receive barrier (6 slots), then the
 // epilogue warps' argmax keys [4][kBN] and their EpiScratch; plus alignment
 // slack.
-size_t smem_for(int stages, bool split) {
-  const size_t need = size_t(stages) * kStage + (split ? kRecvBytes : 0) + (2 * size_t(stages) + 11) * 8 +
+size_t smem_for(int stages, int splits) {
+  const size_t need = size_t(stages) * kStage + recv_bytes_for(splits) + (2 * size_t(stages) + 11) * 8 +
                       4 * kBN * 8 + sizeof(EpiScratch) + 1024;
   return need > kMinSmem ? need : kMinSmem;
 }
@@ -461,6 +468,13 @@ __device__ __forceinline__ void st_async_f32(uint32_t remote, float x, uint32_t 
                "r"(__float_as_uint(x)), "r"(rbar)
                : "memory");
 }
+// The same for 16 bytes (the remote address 16-byte aligned).
+__device__ __forceinline__ void st_async_f32x4(uint32_t remote, float4 x, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(remote),
+               "r"(__float_as_uint(x.x)), "r"(__float_as_uint(x.y)), "r"(__float_as_uint(x.z)),
+               "r"(__float_as_uint(x.w)), "r"(rbar)
+               : "memory");
+}
 // mbar_wait with acquire at cluster scope: what other CTAs' st.async
 // delivered before the phase completed is visible afterwards.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
@@ -514,7 +528,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr bool split = S > 1;  // a.splits == S
   const int stages = a.stages;  // 1 .. kMaxStages (split-K: .. kMaxSplitStages)
   // Split-K: the receive buffer of the other CTAs' partial sums follows the stages.
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * kStage + (split ? kRecvBytes : 0));
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + size_t(stages) * kStage + recv_bytes_for(S));
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;  // [2] accumulator ready
   uint64_t* tempty = tfull + 2;      // [2] accumulator drained
@@ -681,6 +695,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (dst == R) recv[off / 4] = x;
         else st_async_f32(mapa_cluster(recv_s + off, uint32_t(dst)), x, mapa_cluster(rbar_s, uint32_t(dst)));
       };
+      auto push4 = [&](int jt, float4 x) {  // two splits: tokens jt .. jt + 3 of this row
+        const int dst = jt / PER;
+        const uint32_t off = uint32_t(((R * kBM + rl) * kRecvLd2 + jt % PER) * 4);
+        if (dst == R) *reinterpret_cast<float4*>(&recv[off / 4]) = x;
+        else st_async_f32x4(mapa_cluster(recv_s + off, uint32_t(dst)), x, mapa_cluster(rbar_s, uint32_t(dst)));
+      };
       bool ok = true;
       if (nk > 0) {
         ok = all_ok(mbar_wait(&tfull[0], 0, a.err));
@@ -692,24 +712,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int c = 0; c < kBN; c += 16) {
             float v[16];
             tmem_ld_tokens(taddr, c, v);
+            if constexpr (S == 2) {
 #pragma unroll
-            for (int j = 0; j < 16; j++) push(c + j, v[j]);
+              for (int j = 0; j < 16; j += 4) push4(c + j, make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; j++) push(c + j, v[j]);
+            }
           }
         }
       } else {
+        // A split past the end of K adds zeros.
+        if constexpr (S == 2) {
 #pragma unroll 1
-        for (int jt = 0; jt < kBN; jt++) push(jt, 0.f);  // a split past the end of K adds zeros
+          for (int jt = 0; jt < kBN; jt += 4) push4(jt, make_float4(0.f, 0.f, 0.f, 0.f));
+        } else {
+#pragma unroll 1
+          for (int jt = 0; jt < kBN; jt++) push(jt, 0.f);
+        }
       }
       // Every byte sent here lands before the CTA goes, whatever its verdict.
       const bool got = all_ok(mbar_wait_cluster(rbar, 0, a.err));
       if (ok && got) {
         if (threadIdx.x == 64) a.trace.at(cta, TB200_TRACE_REDUCE);
         float v[PER];
+        if constexpr (S == 2) {
 #pragma unroll
-        for (int j = 0; j < PER; j++) {
-          v[j] = recv[j * kBM + rl];
+          for (int j = 0; j < PER; j += 4) {
+            const float4 p0 = *reinterpret_cast<const float4*>(&recv[rl * kRecvLd2 + j]);
+            const float4 p1 = *reinterpret_cast<const float4*>(&recv[(kBM + rl) * kRecvLd2 + j]);
+            v[j] = p0.x + p1.x;
+            v[j + 1] = p0.y + p1.y;
+            v[j + 2] = p0.z + p1.z;
+            v[j + 3] = p0.w + p1.w;
+          }
+        } else {
 #pragma unroll
-          for (int r = 1; r < S; r++) v[j] += recv[(r * PER + j) * kBM + rl];
+          for (int j = 0; j < PER; j++) {
+            v[j] = recv[j * kBM + rl];
+#pragma unroll
+            for (int r = 1; r < S; r++) v[j] += recv[(r * PER + j) * kBM + rl];
+          }
         }
         epi_group<EPI, PER>(a, int(blockIdx.x), row, row_ok, q, lane, n0 + R * PER, v, pre, es);
         if (EPI == kGemmStore && a.best) argmax_tokens<PER>(a, row, row_ok, n0 + R * PER, v, lane);
@@ -777,6 +820,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---- host side -----------------------------------------------------------------
 
 static_assert(kMaxSplitStages <= kMaxStages, "split plans fit the kernels' shared-memory attribute");
+static_assert(size_t(kMaxSplitStages) * kStage + recv_bytes_for(2) <= size_t(kMaxStages) * kStage,
+              "the two-split receive buffer fits the kernels' shared-memory attribute");
 
 std::mutex g_encode_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -784,7 +829,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 template <int EPI, int S>
 cudaError_t set_attrs_one() {
   cudaError_t e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem_for(kMaxStages, false)));
+                                       int(smem_for(kMaxStages, 1)));
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_gemm<EPI, S>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
@@ -804,7 +849,7 @@ void launch_tile(cudaStream_t s, const GemmPlan& p, const CUtensorMap& tw, const
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = p.grid;
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = smem_for(p.stages, p.splits > 1);
+  cfg.dynamicSmemBytes = smem_for(p.stages, p.splits);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
@@ -902,7 +947,7 @@ int gemm_max_cluster() {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1, 1, n);
     cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = smem_for(kMaxSplitStages, true);
+    cfg.dynamicSmemBytes = smem_for(kMaxSplitStages, 2);  // the largest split layout
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
