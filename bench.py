@@ -337,6 +337,35 @@ def run_tp(args, rank, world, torch):
     return out
 
 
+def measure_load(dev, path, reps=2):
+    """Checkpoint load throughput, file already in the page cache: the
+    library's direct safetensors path (tb200_upload_safetensors, what
+    Model.load uses) against per-tensor Weights.read + upload (the
+    reference's Model::load shape, model/model.rs:251-254). Host wall clock
+    from the call to every byte on the device; best of `reps` after a first
+    call (reported as `first_seconds`: for the direct path it also page-locks
+    the device's staging buffers, which later loads reuse)."""
+    from titania_b200.model import Config, Weights, load_weights, tensor_names, upload_checkpoint
+    c = Config.load(os.path.join(path, "config.json"))
+    f = os.path.join(path, "model.safetensors")
+    w = Weights.open(f)
+    nbytes = sum(w.entries[n]["data_offsets"][1] - w.entries[n]["data_offsets"][0]
+                 for n, _ in tensor_names(c) if w.contains(n))
+    out = {"bytes": nbytes, "page_cache": "warm"}
+    for kind, fn in (("direct", lambda: upload_checkpoint(dev, c, f)),
+                     ("per_tensor", lambda: load_weights(dev, c, Weights.open(f)))):
+        times = []
+        for i in range(reps + 1):
+            t0 = time.perf_counter()
+            ws = fn()
+            dev.sync()
+            times.append(time.perf_counter() - t0)
+            del ws
+        best = min(times[1:])
+        out[kind] = {"seconds": best, "gbs": nbytes / best / 1e9, "first_seconds": times[0]}
+    return out
+
+
 def run_ours(args, rank, world, torch):
     import titania_b200 as tb
     from titania_b200 import synth
@@ -346,6 +375,7 @@ def run_ours(args, rank, world, torch):
     cfg = dict(synth.QWEN3_0_6B)
     path = cached_model_all_ranks("qwen3-0.6b", rank, world, torch)
     m = tb.Model.load(path, dev)
+    load = measure_load(dev, path) if world == 1 else None
     prompt = synth.prompt_tokens(PROMPT, cfg["vocab_size"], seed=1)
     st = m.state(PROMPT + GEN + 1)
     first = m.forward(st, prompt, 0, logits=False)  # prefill: K/V for positions 0..15
@@ -445,6 +475,8 @@ def run_ours(args, rank, world, torch):
                               "frac": d["gbs"] / peak, "peak_kind": peak_kind, "traffic": traffic,
                               "algorithmic_bytes_per_launch": d["bytes"], "avg_launch_us": d["avg_us"]}
         result["kernels"] = kern
+    if load is not None:
+        result["load"] = load
     if rank == 0 and world == 1 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline(path, prompt, budget_s=args.cpu_seconds)
     if args.tp4b or (world > 1 and not args.no_tp):

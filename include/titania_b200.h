@@ -46,6 +46,8 @@ enum {
   TB200_ERR_ARG = 1,     /* an argument violates the op's contract (a reference panic) */
   TB200_ERR_CUDA = 2,    /* a CUDA runtime error */
   TB200_ERR_TIMEOUT = 3, /* a bounded wait inside a kernel gave up */
+  TB200_ERR_IO = 4,      /* a file could not be opened or read (Weights' io::Error) */
+  TB200_ERR_FORMAT = 5,  /* a file is not a valid safetensors checkpoint of bf16 tensors */
 };
 
 typedef struct tb200_device tb200_device; /* a Device on one GPU */
@@ -81,6 +83,34 @@ TB200_API int tb200_rope_table(size_t max_len, size_t head_dim, float theta, flo
 /* device.rs:18 `upload(&self, tensor: Tensor) -> Weight`; `data` holds the
  * product of `shape` bf16 values, row-major (model/weights.rs:14-17). */
 TB200_API int tb200_upload(tb200_device* dev, const uint16_t* data, const size_t* shape, size_t ndim, tb200_weight** out);
+/* Weights::open + Weights::read + Device::upload for many tensors at once
+ * (model/weights.rs:35-81, model/device.rs:18; the reads Model::load makes,
+ * model/model.rs:42,251-254), with no host-side conversion: the safetensors
+ * file at `path` is parsed once and the `n` tensors `names` go from the file
+ * to device memory through pinned staging buffers on `threads` host threads
+ * (0: up to 8), reading overlapped with copying. The staging buffers (two of
+ * 8 MB per thread) are page-locked on first use and kept by the device until
+ * tb200_device_close, so later loads skip that cost. out[i] is NULL where the file
+ * has no tensor names[i] (Weights::contains is false; the caller decides
+ * whether it was required). A tensor that is not BF16 fails as Weights::read
+ * does ("tensor 'x' is F32, expected BF16", TB200_ERR_FORMAT); so does one
+ * whose byte range lies outside the file or does not hold two bytes per
+ * element of its shape. An unreadable file is TB200_ERR_IO. On any error no
+ * weight stays allocated and every out[i] is NULL. Returns once every byte
+ * is on the device. */
+TB200_API int tb200_upload_safetensors(tb200_device* dev, const char* path, const char* const* names, size_t n,
+                                       int threads, tb200_weight** out);
+/* The header entry of tensor `name` in the safetensors file at `path`
+ * (model/weights.rs:35-57), parsed as tb200_upload_safetensors parses it:
+ * *found = 0 when there is none; otherwise its dtype (NUL-terminated, at
+ * most dtype_cap bytes), its shape (*ndim <= max_ndim values in `shape`)
+ * and its bytes in the file (*offset from the file's start, *bytes long).
+ * Host only. */
+/* The shape of a weight as uploaded: *ndim <= max_ndim values in `shape`.
+ * Host only. */
+TB200_API int tb200_weight_shape(const tb200_weight* w, size_t* shape, size_t max_ndim, size_t* ndim);
+TB200_API int tb200_safetensors_entry(const char* path, const char* name, int* found, char* dtype, size_t dtype_cap,
+                                      size_t* shape, size_t max_ndim, size_t* ndim, uint64_t* offset, uint64_t* bytes);
 /* device.rs:21 `alloc(&self, len) -> Buffer`: a zeroed buffer. */
 TB200_API int tb200_alloc(tb200_device* dev, size_t len, tb200_buffer** out);
 /* device.rs:26 `resize(&self, &mut Buffer, len)`: len <= allocated length. */

@@ -1,0 +1,246 @@
+"""The safetensors fast path (tb200_upload_safetensors, tb200_safetensors_entry)
+against model/weights.rs:35-81 read as Python does it.
+
+CPU: the library's header parser against `json` on the same files (the
+checkpoint the other tests use and hand-written headers with every JSON form a
+header may hold), and its errors. GPU: the bytes on the device are the file's,
+for tensors spanning several staging pieces and at file offsets that are not
+16-byte aligned, with 1..16 host threads; a model loaded this way computes
+bit-identical logits to one loaded tensor by tensor.
+"""
+
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+from titania_b200 import _lib
+from titania_b200.device import safetensors_entry
+
+PIECE = 16 << 20  # the loader's staging piece (bytes)
+
+
+def write_raw(path, header: bytes, data: bytes = b"", pad: int = 0):
+    """A file with an 8-byte header length, `header` (+ `pad` spaces) and `data`."""
+    h = header + b" " * pad
+    with open(path, "wb") as fh:
+        fh.write(struct.pack("<Q", len(h)) + h + data)
+    return str(path)
+
+
+def write_tensors(path, tensors, metadata=None):
+    """tensors: list of (name, dtype, shape, raw bytes), laid out back to back
+    in the given order with no alignment padding."""
+    header, blobs, off = {}, [], 0
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for name, dtype, shape, raw in tensors:
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    return write_raw(path, json.dumps(header).encode(), b"".join(blobs))
+
+
+def bf16_bits(rng, shape):
+    return rng.integers(0, 1 << 16, size=shape, dtype=np.uint16) & np.uint16(0x7F7F)  # finite values
+
+
+# ---- CPU: the header parser --------------------------------------------------
+
+def test_entries_match_json(tiny_model_dir):
+    f = os.path.join(tiny_model_dir, "model.safetensors")
+    with open(f, "rb") as fh:
+        n = struct.unpack("<Q", fh.read(8))[0]
+        header = json.loads(fh.read(n))
+    names = [k for k in header if k != "__metadata__"]
+    assert len(names) > 10
+    for name in names:
+        e = header[name]
+        dtype, shape, off, nbytes = safetensors_entry(f, name)
+        assert (dtype, shape) == (e["dtype"], e["shape"]), name
+        assert off == 8 + n + e["data_offsets"][0], name
+        assert nbytes == e["data_offsets"][1] - e["data_offsets"][0], name
+    assert safetensors_entry(f, "model.layers.99.mlp.up_proj.weight") is None
+
+
+def test_header_forms(tmp_path):
+    """Field order, unknown fields of every JSON type, escapes, metadata
+    anywhere, whitespace and the spaces safetensors pads the header with."""
+    header = (b'{\n  "a\\"b\\\\c" : {"shape": [2, 3], "extra": {"x": [1, -2.5e+3, true, false, null, "s"]},'
+              b' "data_offsets": [0, 12], "dtype": "BF16"},\r\n'
+              b' "__metadata__": {"format": "pt", "nested": {"k": [0.5, {}]}},\t'
+              b'"caf\\u00e9\\ud83d\\ude00/\\n" :{"dtype":"F32","data_offsets":[12,20],"shape":[2]},'
+              b'"scalar": {"dtype": "BF16", "shape": [], "data_offsets": [20, 22]}}')
+    f = write_raw(tmp_path / "forms.safetensors", header, bytes(22), pad=5)
+    start = 8 + len(header) + 5
+    assert safetensors_entry(f, 'a"b\\c') == ("BF16", [2, 3], start, 12)
+    assert safetensors_entry(f, "café\U0001F600/\n") == ("F32", [2], start + 12, 8)
+    assert safetensors_entry(f, "scalar") == ("BF16", [], start + 20, 2)
+    assert safetensors_entry(f, "__metadata__") is None
+    assert safetensors_entry(f, "a") is None
+
+
+def test_empty_header_object(tmp_path):
+    f = write_raw(tmp_path / "empty.safetensors", b"{}", pad=6)
+    assert safetensors_entry(f, "x") is None
+
+
+@pytest.mark.parametrize("header", [
+    b"[]",                                                              # not an object
+    b'{"t": {"shape": [1], "data_offsets": [0, 2]}}',                    # missing dtype
+    b'{"t": {"dtype": "BF16", "data_offsets": [0, 2]}}',                 # missing shape
+    b'{"t": {"dtype": "BF16", "shape": [1]}}',                           # missing data_offsets
+    b'{"t": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2, 4]}}',  # three offsets
+    b'{"t": {"dtype": "BF16", "shape": [-1], "data_offsets": [0, 2]}}',  # negative dimension
+    b'{"t": {"dtype": "BF16", "shape": [1.0], "data_offsets": [0, 2]}}',  # fractional dimension
+    b'{"t": {"dtype": "BF16", "shape": [01], "data_offsets": [0, 2]}}',  # leading zero
+    b'{"t": {"dtype": "BF16", "shape": [99999999999999999999], "data_offsets": [0, 2]}}',  # > u64
+    b'{"t": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}} x',  # bytes after the object
+    b'{"t": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}',    # unterminated object
+    b'{"t": {"dtype": "BF16, "shape": [1], "data_offsets": [0, 2]}}',    # broken string
+    b'{"t\\ud800": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}}',  # unpaired surrogate
+    b'{"t": {"dtype": "BF16", "shape": [1], "data_offsets": [0, 2]}, "u": tru}',  # bad literal
+])
+def test_header_errors(tmp_path, header):
+    f = write_raw(tmp_path / "bad.safetensors", header, bytes(4))
+    with pytest.raises(_lib.DeviceError) as e:
+        safetensors_entry(f, "t")
+    assert e.value.code == _lib.TB200_ERR_FORMAT, str(e.value)
+
+
+def test_header_longer_than_file(tmp_path):
+    f = tmp_path / "short.safetensors"
+    f.write_bytes(struct.pack("<Q", 1000) + b"{}")
+    with pytest.raises(_lib.DeviceError) as e:
+        safetensors_entry(str(f), "t")
+    assert e.value.code == _lib.TB200_ERR_FORMAT and "header length 1000" in str(e.value)
+
+
+def test_unreadable_files(tmp_path):
+    with pytest.raises(_lib.DeviceError) as e:
+        safetensors_entry(str(tmp_path / "nonexistent.safetensors"), "t")
+    assert e.value.code == _lib.TB200_ERR_IO
+    f = tmp_path / "tiny.safetensors"
+    f.write_bytes(b"\x02\x00\x00")  # shorter than the length field: read_exact fails
+    with pytest.raises(_lib.DeviceError) as e:
+        safetensors_entry(str(f), "t")
+    assert e.value.code == _lib.TB200_ERR_IO and "end of file" in str(e.value)
+
+
+# ---- GPU: the bytes on the device ------------------------------------------
+
+def device_bits(dev, w):
+    """The bf16 bits of a 2-D weight, read back exactly through Device::embed
+    (bf16 -> f32 is a shift)."""
+    import titania_b200 as tb
+
+    rows, cols = w.shape
+    out = dev.alloc(rows * cols)
+    dev.embed(out, w, np.arange(rows, dtype=np.uint32))
+    return (dev.read(out).view(np.uint32) >> 16).astype(np.uint16).reshape(rows, cols)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("threads", [0, 1, 3, 16])
+def test_pieces_and_unaligned_offsets(b200, tmp_path, threads):
+    rng = np.random.default_rng(5)
+    odd = bf16_bits(rng, (3, 5))          # 30 bytes: everything after it starts off 16-byte alignment
+    big = bf16_bits(rng, (4200, 2048))    # 17.2 MB: two staging pieces
+    mid = bf16_bits(rng, (7, 9))
+    f = write_tensors(tmp_path / "t.safetensors", [
+        ("odd", "BF16", odd.shape, odd.tobytes()),
+        ("skip", "F32", (3,), np.arange(3, dtype=np.float32).tobytes()),
+        ("big", "BF16", big.shape, big.tobytes()),
+        ("empty", "BF16", (0, 8), b""),
+        ("mid", "BF16", mid.shape, mid.tobytes()),
+    ], metadata={"format": "pt"})
+    assert big.nbytes > PIECE and safetensors_entry(f, "big")[2] % 16 != 0
+    ws = b200.upload_safetensors(f, ["big", "nope", "odd", "empty", "mid"], threads=threads)
+    assert ws[1] is None
+    assert ws[3].shape == [0, 8]
+    for w, ref in ((ws[0], big), (ws[2], odd), (ws[4], mid)):
+        assert w.shape == list(ref.shape)
+        np.testing.assert_array_equal(device_bits(b200, w), ref)
+
+
+@pytest.mark.gpu
+def test_norm_vectors_match_per_tensor_upload(b200, tiny_model_dir):
+    """1-D tensors (norm weights): rmsnorm with the fast-path weight equals,
+    bit for bit, rmsnorm with the same tensor uploaded by Device::upload."""
+    from titania_b200.model import Weights
+
+    f = os.path.join(tiny_model_dir, "model.safetensors")
+    w = Weights.open(f)
+    names = [n for n, e in w.entries.items() if len(e["shape"]) == 1]
+    assert names
+    fast = b200.upload_safetensors(f, names)
+    rng = np.random.default_rng(3)
+    for name, wf in zip(names, fast):
+        ws = b200.upload(w.read(name))
+        dim = wf.shape[0]
+        x = rng.standard_normal(4 * dim).astype(np.float32)
+        a, b = b200.alloc(x.size), b200.alloc(x.size)
+        b200.write(a, x)
+        b200.write(b, x)
+        b200.rmsnorm(a, wf, 1e-6)
+        b200.rmsnorm(b, ws, 1e-6)
+        np.testing.assert_array_equal(b200.read(a), b200.read(b), err_msg=name)
+
+
+@pytest.mark.gpu
+def test_matrices_match_file(b200, tiny_model_dir):
+    from titania_b200.model import Weights
+
+    f = os.path.join(tiny_model_dir, "model.safetensors")
+    w = Weights.open(f)
+    names = [n for n, e in w.entries.items() if len(e["shape"]) == 2]
+    for name, wf in zip(names, b200.upload_safetensors(f, names, threads=4)):
+        np.testing.assert_array_equal(device_bits(b200, wf), w.read(name).data.reshape(wf.shape), err_msg=name)
+
+
+@pytest.mark.gpu
+def test_upload_errors(b200, tmp_path):
+    rng = np.random.default_rng(1)
+    ok = bf16_bits(rng, (4, 4))
+    f = write_tensors(tmp_path / "e.safetensors", [("ok", "BF16", ok.shape, ok.tobytes()),
+                                                   ("f", "F32", (2,), bytes(8))])
+    with pytest.raises(_lib.DeviceError) as e:  # Weights::read's dtype check
+        b200.upload_safetensors(f, ["ok", "f"])
+    assert e.value.code == _lib.TB200_ERR_FORMAT and "tensor 'f' is F32, expected BF16" in str(e.value)
+    bad = write_raw(tmp_path / "o.safetensors",  # offsets past the end of the data
+                    b'{"t": {"dtype": "BF16", "shape": [4], "data_offsets": [0, 8]}}', bytes(6))
+    with pytest.raises(_lib.DeviceError) as e:
+        b200.upload_safetensors(bad, ["t"])
+    assert e.value.code == _lib.TB200_ERR_FORMAT and "outside" in str(e.value)
+    size = write_raw(tmp_path / "s.safetensors",  # 6 bytes for a shape of 4 elements
+                     b'{"t": {"dtype": "BF16", "shape": [4], "data_offsets": [0, 6]}}', bytes(6))
+    with pytest.raises(_lib.DeviceError) as e:
+        b200.upload_safetensors(size, ["t"])
+    assert e.value.code == _lib.TB200_ERR_FORMAT
+    with pytest.raises(_lib.DeviceError) as e:
+        b200.upload_safetensors(str(tmp_path / "missing.safetensors"), ["t"])
+    assert e.value.code == _lib.TB200_ERR_IO
+    with pytest.raises(_lib.DeviceError) as e:
+        b200.upload_safetensors(f, ["ok"], threads=17)
+    assert e.value.code == _lib.TB200_ERR_ARG
+    # the device is still usable and the good tensor loads
+    (w,) = b200.upload_safetensors(f, ["ok"])
+    np.testing.assert_array_equal(device_bits(b200, w), ok)
+
+
+@pytest.mark.gpu
+def test_model_load_direct_equals_per_tensor(b200, tiny_model_dir):
+    import titania_b200 as tb
+    from titania_b200 import synth
+    from titania_b200.model import Config, Weights, load_weights, upload_checkpoint
+
+    c = Config.load(os.path.join(tiny_model_dir, "config.json"))
+    f = os.path.join(tiny_model_dir, "model.safetensors")
+    fast = tb.Model(c, b200, upload_checkpoint(b200, c, f))
+    slow = tb.Model(c, b200, load_weights(b200, c, Weights.open(f)))
+    prompt = synth.prompt_tokens(6, synth.TINY["vocab_size"], seed=4)
+    la = fast.forward(fast.state(16), prompt, 0)
+    lb = slow.forward(slow.state(16), prompt, 0)
+    np.testing.assert_array_equal(la, lb)

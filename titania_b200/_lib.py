@@ -11,7 +11,7 @@ import os
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtitania_b200.so")
 
-TB200_OK, TB200_ERR_ARG, TB200_ERR_CUDA, TB200_ERR_TIMEOUT = 0, 1, 2, 3
+TB200_OK, TB200_ERR_ARG, TB200_ERR_CUDA, TB200_ERR_TIMEOUT, TB200_ERR_IO, TB200_ERR_FORMAT = 0, 1, 2, 3, 4, 5
 
 
 class DeviceError(RuntimeError):
@@ -56,6 +56,12 @@ SIGNATURES = {
     "tb200_device_sms": (ctypes.c_int, [P]),
     "tb200_rope_table": (ctypes.c_int, [SZ, SZ, ctypes.c_float, F32P]),
     "tb200_upload": (ctypes.c_int, [P, U16P, SZP, SZ, PP]),
+    "tb200_upload_safetensors": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), SZ, ctypes.c_int,
+                                                PP]),
+    "tb200_weight_shape": (ctypes.c_int, [P, SZP, SZ, SZP]),
+    "tb200_safetensors_entry": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int),
+                                               ctypes.c_char_p, SZ, SZP, SZ, SZP, ctypes.POINTER(ctypes.c_uint64),
+                                               ctypes.POINTER(ctypes.c_uint64)]),
     "tb200_alloc": (ctypes.c_int, [P, SZ, PP]),
     "tb200_resize": (ctypes.c_int, [P, P, SZ]),
     "tb200_buffer_len": (ctypes.c_size_t, [P]),

@@ -175,6 +175,7 @@ int tb200_device_close(tb200_device* d) {
   cudaFree(d->best);
   cudaFree(d->split);
   cudaFree(d->err);
+  for (void* p : d->stage) cudaFreeHost(p);
   cudaStreamDestroy(d->stream);
   delete d;
   return TB200_OK;

@@ -27,6 +27,10 @@ struct tb200_device {
   size_t split_cap = 0;
   int max_cluster = 1;        // largest split-K cluster (gemm_max_cluster, at most 8)
   int* err = nullptr;         // device error word of the trait ops
+  // Pinned staging buffers of the safetensors loader (loader.cu), two per
+  // worker thread, allocated on first use and kept until the device closes:
+  // page-locking costs about as much as the copies it serves.
+  std::vector<void*> stage;
 };
 
 struct tb200_buffer {

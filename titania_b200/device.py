@@ -10,6 +10,7 @@ contract raises `DeviceError` where the reference panics.
 from __future__ import annotations
 
 import ctypes
+import os
 import sys
 
 import numpy as np
@@ -62,6 +63,22 @@ class Buffer:
         self._h = None
 
 
+def safetensors_entry(path: str, name: str):
+    """(dtype, shape, file offset, bytes) of tensor `name` in the safetensors
+    file at `path` as the library parses its header, or None when the file
+    has no such tensor. Host only: needs no GPU."""
+    found = ctypes.c_int()
+    dtype = ctypes.create_string_buffer(64)
+    shape = (ctypes.c_size_t * 16)()
+    ndim = ctypes.c_size_t()
+    off, nbytes = ctypes.c_uint64(), ctypes.c_uint64()
+    call("tb200_safetensors_entry", os.fsencode(path), name.encode(), ctypes.byref(found), dtype, len(dtype), shape,
+         16, ctypes.byref(ndim), ctypes.byref(off), ctypes.byref(nbytes))
+    if not found.value:
+        return None
+    return dtype.value.decode(), [int(shape[i]) for i in range(ndim.value)], int(off.value), int(nbytes.value)
+
+
 def _f32(a):
     a = np.ascontiguousarray(a, dtype=np.float32)
     return a, a.ctypes.data_as(_lib.F32P)
@@ -107,6 +124,27 @@ class B200:
         call("tb200_upload", self._h, tensor.data.ctypes.data_as(_lib.U16P), shape, len(tensor.shape),
              ctypes.byref(h))
         return Weight(h.value, tensor.shape, self)
+
+    def upload_safetensors(self, path: str, names, threads: int = 0) -> list:
+        """Weights::read + upload for every name in `names` at once, straight
+        from the safetensors file at `path` to device memory (no host-side
+        conversion; reads overlapped with copies on `threads` host threads,
+        0 = automatic). Returns one Weight per name, or None where the file
+        has no such tensor; a tensor that is not BF16 raises as
+        Weights::read fails (model/weights.rs:61-81)."""
+        names = [str(n) for n in names]
+        arr = (ctypes.c_char_p * max(1, len(names)))(*[n.encode() for n in names])
+        out = (ctypes.c_void_p * max(1, len(names)))()
+        call("tb200_upload_safetensors", self._h, os.fsencode(path), arr, len(names), int(threads), out)
+        res = []
+        shape, ndim = (ctypes.c_size_t * 16)(), ctypes.c_size_t()
+        for i in range(len(names)):
+            if out[i]:
+                call("tb200_weight_shape", out[i], shape, 16, ctypes.byref(ndim))
+                res.append(Weight(out[i], shape[:ndim.value], self))
+            else:
+                res.append(None)
+        return res
 
     def alloc(self, length: int) -> Buffer:
         h = ctypes.c_void_p()

@@ -124,6 +124,22 @@ def load_weights(device, c: Config, w: Weights) -> dict:
     return up
 
 
+def upload_checkpoint(device: B200, c: Config, path: str) -> dict:
+    """Model::load's reads and uploads (model/model.rs:42-72, 251-254) in one
+    library call: every tensor goes from the safetensors file at `path` to
+    device memory with no host-side conversion (tb200_upload_safetensors).
+    A missing required tensor raises KeyError as Weights::read fails."""
+    names = tensor_names(c)
+    ws = device.upload_safetensors(path, [n for n, _ in names])
+    up = {}
+    for (name, required), w in zip(names, ws):
+        if w is not None:
+            up[name] = w
+        elif required:
+            raise KeyError(f"missing tensor '{name}'")
+    return up
+
+
 def rope_table(max_len: int, head_dim: int, theta: float) -> np.ndarray:
     """model/model.rs:239-250, computed by the library on the host with the
     platform libm, as the reference computes it."""
@@ -245,7 +261,7 @@ class Model:
     def load(cls, path: str, device: B200) -> "Model":
         """Model::load (model/model.rs:40-77)."""
         c = Config.load(os.path.join(path, "config.json"))
-        return cls(c, device, load_weights(device, c, Weights.open(os.path.join(path, "model.safetensors"))))
+        return cls(c, device, upload_checkpoint(device, c, os.path.join(path, "model.safetensors")))
 
     def __del__(self):
         if getattr(self, "_h", None) and not sys.is_finalizing():
