@@ -19,7 +19,7 @@ import pytest
 from titania_b200 import _lib
 from titania_b200.device import safetensors_entry
 
-PIECE = 16 << 20  # the loader's staging piece (bytes)
+PIECE = 8 << 20  # the loader's staging piece (bytes)
 
 
 def write_raw(path, header: bytes, data: bytes = b"", pad: int = 0):
@@ -129,6 +129,49 @@ def test_unreadable_files(tmp_path):
     assert e.value.code == _lib.TB200_ERR_IO and "end of file" in str(e.value)
 
 
+class _StubDevice:
+    """Answers upload_safetensors from a set of present names (no GPU)."""
+
+    def __init__(self, present):
+        self.present, self.asked = set(present), None
+
+    def upload_safetensors(self, path, names, threads=0):
+        self.asked = list(names)
+        return [f"w:{n}" if n in self.present else None for n in names]
+
+
+def test_upload_checkpoint_names_and_optional_tensors():
+    """Model::load's tensor list (model/model.rs:46-72): q_norm / k_norm are
+    optional, everything else is required; a tied model reads no lm_head."""
+    from titania_b200.model import Config, tensor_names, upload_checkpoint
+
+    c = Config(**dict(synth_cfg(), tie_word_embeddings=True))
+    names = [n for n, _ in tensor_names(c)]
+    optional = {n for n, req in tensor_names(c) if not req}
+    assert "lm_head.weight" not in names
+    assert optional == {f"model.layers.{i}.self_attn.{k}_norm.weight" for i in range(2) for k in "qk"}
+    dev = _StubDevice(set(names) - optional)
+    up = upload_checkpoint(dev, c, "unused")
+    assert dev.asked == names and set(up) == set(names) - optional
+    untied = Config(**dict(synth_cfg(), tie_word_embeddings=False))
+    assert "lm_head.weight" in [n for n, _ in tensor_names(untied)]
+
+
+def test_upload_checkpoint_missing_required_tensor():
+    from titania_b200.model import Config, tensor_names, upload_checkpoint
+
+    c = Config(**dict(synth_cfg(), tie_word_embeddings=True))
+    names = [n for n, _ in tensor_names(c)]
+    with pytest.raises(KeyError, match="missing tensor 'model.layers.1.mlp.down_proj.weight'"):
+        upload_checkpoint(_StubDevice(set(names) - {"model.layers.1.mlp.down_proj.weight"}), c, "unused")
+
+
+def synth_cfg():
+    from titania_b200 import synth
+
+    return dict(synth.TINY, num_hidden_layers=2)
+
+
 # ---- GPU: the bytes on the device ------------------------------------------
 
 def device_bits(dev, w):
@@ -147,7 +190,7 @@ def device_bits(dev, w):
 def test_pieces_and_unaligned_offsets(b200, tmp_path, threads):
     rng = np.random.default_rng(5)
     odd = bf16_bits(rng, (3, 5))          # 30 bytes: everything after it starts off 16-byte alignment
-    big = bf16_bits(rng, (4200, 2048))    # 17.2 MB: two staging pieces
+    big = bf16_bits(rng, (4200, 2048))    # 17.2 MB: three staging pieces
     mid = bf16_bits(rng, (7, 9))
     f = write_tensors(tmp_path / "t.safetensors", [
         ("odd", "BF16", odd.shape, odd.tobytes()),
