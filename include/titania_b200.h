@@ -106,6 +106,21 @@ TB200_API int tb200_upload_safetensors(tb200_device* dev, const char* path, cons
  * most dtype_cap bytes), its shape (*ndim <= max_ndim values in `shape`)
  * and its bytes in the file (*offset from the file's start, *bytes long).
  * Host only. */
+/* A window of a 2-D checkpoint tensor: rows [row0, row0 + rows) and columns
+ * [col0, col0 + cols); rows = cols = 0 takes the tensor whole (any rank). */
+typedef struct tb200_window {
+  size_t row0, rows, col0, cols;
+} tb200_window;
+/* tb200_upload_safetensors for one window of each tensor (no counterpart in
+ * the reference: a tensor-parallel rank's share of a checkpoint, e.g. the
+ * q/k/v/gate/up rows and o/down columns it holds). out[i] has shape
+ * [rows, cols], packed, or the tensor's own shape for a whole window. A
+ * window of whole rows is read as one run; a column window reads whole rows
+ * and copies their middle out (rows up to 4M elements). A window outside
+ * its tensor, or one on a tensor that is not a matrix, is TB200_ERR_ARG. */
+TB200_API int tb200_upload_safetensors_windows(tb200_device* dev, const char* path, const char* const* names,
+                                               const tb200_window* windows, size_t n, int threads,
+                                               tb200_weight** out);
 /* The shape of a weight as uploaded: *ndim <= max_ndim values in `shape`.
  * Host only. */
 TB200_API int tb200_weight_shape(const tb200_weight* w, size_t* shape, size_t max_ndim, size_t* ndim);

@@ -287,3 +287,90 @@ def test_model_load_direct_equals_per_tensor(b200, tiny_model_dir):
     la = fast.forward(fast.state(16), prompt, 0)
     lb = slow.forward(slow.state(16), prompt, 0)
     np.testing.assert_array_equal(la, lb)
+
+
+# ---- windows: a tensor-parallel rank's share -------------------------------
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [1, 2])
+def test_windows_match_the_shard_rule(b200, tiny_model_dir, world):
+    """Every rank's windows hold exactly the bytes titania_b200.tp.shard_tensor
+    cuts from the file: row blocks (q/k/v/gate/up), column blocks (o/down),
+    and whole tensors (norms, embedding)."""
+    from titania_b200.model import Config, Weights, tensor_names
+    from titania_b200.tp import shard_tensor, shard_window
+
+    c = Config.load(os.path.join(tiny_model_dir, "config.json"))
+    f = os.path.join(tiny_model_dir, "model.safetensors")
+    w = Weights.open(f)
+    names = [n for n, _ in tensor_names(c) if w.contains(n)]
+    for rank in range(world):
+        wins = [shard_window(c, n, w.entries[n]["shape"], rank, world) for n in names]
+        assert any(x is not None and x[3] < w.entries[n]["shape"][1] for x, n in zip(wins, names)) == (world > 1)
+        for name, wt in zip(names, b200.upload_safetensors(f, names, windows=wins)):
+            t = w.read(name)
+            shape, data = shard_tensor(c, name, t.shape, t.data, rank, world)
+            assert wt.shape == shape, name
+            if len(shape) == 2:
+                np.testing.assert_array_equal(device_bits(b200, wt), data.reshape(shape), err_msg=f"{name} rank {rank}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("threads", [1, 4])
+def test_windows_across_staging_pieces(b200, tmp_path, threads):
+    rng = np.random.default_rng(9)
+    head = bf16_bits(rng, (1, 7))                 # 14 bytes: the matrix starts off 16-byte alignment
+    m = bf16_bits(rng, (1200, 4000))              # 9.6 MB: more than one staging piece
+    f = write_tensors(tmp_path / "w.safetensors", [("head", "BF16", head.shape, head.tobytes()),
+                                                   ("m", "BF16", m.shape, m.tobytes())])
+    cases = [(5, 1190, 1000, 2000),   # column window, rows in two pieces
+             (3, 1100, 0, 4000),      # whole rows: one run
+             (0, 1200, 3999, 1),      # the last column
+             (1199, 1, 0, 1),         # one element
+             (0, 0, 0, 0)]            # whole
+    ws = b200.upload_safetensors(f, ["m"] * len(cases), threads=threads,
+                                 windows=[None if x == (0, 0, 0, 0) else x for x in cases])
+    for (r0, nr, c0, nc), wt in zip(cases, ws):
+        ref = m if nr == 0 else m[r0:r0 + nr, c0:c0 + nc]
+        np.testing.assert_array_equal(device_bits(b200, wt), ref, err_msg=str((r0, nr, c0, nc)))
+
+
+@pytest.mark.gpu
+def test_window_errors(b200, tmp_path):
+    rng = np.random.default_rng(2)
+    m = bf16_bits(rng, (6, 10))
+    v = bf16_bits(rng, (10,))
+    f = write_tensors(tmp_path / "we.safetensors", [("m", "BF16", m.shape, m.tobytes()),
+                                                    ("v", "BF16", v.shape, v.tobytes())])
+    for names, wins, what in ((["m"], [(4, 3, 0, 10)], "outside"), (["m"], [(0, 6, 8, 3)], "outside"),
+                              (["m"], [(0, 0, 0, 5)], "empty window"), (["v"], [(0, 1, 0, 5)], "needs a matrix")):
+        with pytest.raises(_lib.DeviceError) as e:
+            b200.upload_safetensors(f, names, windows=wins)
+        assert e.value.code == _lib.TB200_ERR_ARG and what in str(e.value), str(e.value)
+    with pytest.raises(ValueError):
+        b200.upload_safetensors(f, ["m", "v"], windows=[None])
+    (wv,) = b200.upload_safetensors(f, ["v"], windows=[None])  # a vector whole is fine
+    assert wv.shape == [10]
+
+
+def test_shard_window_agrees_with_shard_tensor(tiny_model_dir):
+    """The window rule and the numpy slicing are one rule (CPU)."""
+    from titania_b200.model import Config, Weights, tensor_names
+    from titania_b200.tp import shard_tensor, shard_window
+
+    c = Config.load(os.path.join(tiny_model_dir, "config.json"))
+    w = Weights.open(os.path.join(tiny_model_dir, "model.safetensors"))
+    for world in (1, 2):
+        for rank in range(world):
+            for name, _ in tensor_names(c):
+                if not w.contains(name):
+                    continue
+                t = w.read(name)
+                shape, data = shard_tensor(c, name, t.shape, t.data, rank, world)
+                win = shard_window(c, name, t.shape, rank, world)
+                full = t.data.reshape(t.shape)
+                if win is None:
+                    assert shape == t.shape
+                else:
+                    r0, nr, c0, nc = win
+                    np.testing.assert_array_equal(full[r0:r0 + nr, c0:c0 + nc].reshape(-1), data)

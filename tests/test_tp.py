@@ -215,6 +215,30 @@ def _two_gpus():
 
 
 @pytest.mark.gpu
+def test_tp1_group_load_against_oracle(tiny_model_dir):
+    """load_tp_model (checkpoint windows straight to the device) with a
+    one-rank group, on one GPU: the logits after a prompt match the oracle
+    and the greedy token is the oracle's."""
+    import titania_b200 as tb
+    from oracle import oracle as orc
+    from titania_b200 import synth
+    from titania_b200.tp import TPGroup, load_tp_model
+    prompt = synth.prompt_tokens(9, 1024, seed=3)
+    ref_tokens, ref_logits = orc.greedy_generate(orc.Model(tiny_model_dir), prompt, 2)
+    dev = tb.B200(0)
+    group = TPGroup(dev, 0, 1, TPGroup.unique_id())
+    try:
+        m = load_tp_model(tiny_model_dir, dev, group)
+        st = m.state(32)
+        logits = m.forward(st, prompt, 0)
+        close(logits, ref_logits[0], REL, ABS)
+        assert int(np.argmax(logits)) == ref_tokens[0]
+        del st, m
+    finally:
+        group.close()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
 def test_tp2_tiny_against_oracle(tiny_model_dir, kv):
     if not _two_gpus():

@@ -23,6 +23,13 @@ class DeviceError(RuntimeError):
         self.code = code
 
 
+class Window(ctypes.Structure):
+    """tb200_window: rows [row0, row0 + rows) x columns [col0, col0 + cols)."""
+
+    _fields_ = [("row0", ctypes.c_size_t), ("rows", ctypes.c_size_t), ("col0", ctypes.c_size_t),
+                ("cols", ctypes.c_size_t)]
+
+
 class Config(ctypes.Structure):
     _fields_ = [
         ("hidden_size", ctypes.c_size_t),
@@ -59,6 +66,8 @@ SIGNATURES = {
     "tb200_upload_safetensors": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p), SZ, ctypes.c_int,
                                                 PP]),
     "tb200_weight_shape": (ctypes.c_int, [P, SZP, SZ, SZP]),
+    "tb200_upload_safetensors_windows": (ctypes.c_int, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p),
+                                                        ctypes.POINTER(Window), SZ, ctypes.c_int, PP]),
     "tb200_safetensors_entry": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int),
                                                ctypes.c_char_p, SZ, SZP, SZ, SZP, ctypes.POINTER(ctypes.c_uint64),
                                                ctypes.POINTER(ctypes.c_uint64)]),

@@ -371,10 +371,15 @@ int check_bf16(const File& f, const std::string& name, const Entry& e, size_t* n
   return TB200_OK;
 }
 
+// One read into a staging buffer and the copy out of it: `len` bytes at
+// `file_off`, to `dst` whole (rows == 0) or, for a column window, `rows`
+// rows of `width` bytes taken at `src_off` + r * `pitch` of the staged bytes
+// and packed at dst + r * width.
 struct Piece {
   uint64_t file_off;
   unsigned char* dst;
   size_t len;
+  size_t rows = 0, src_off = 0, pitch = 0, width = 0;
 };
 
 }  // namespace
@@ -409,8 +414,11 @@ int tb200_safetensors_entry(const char* path, const char* name, int* found, char
   return TB200_OK;
 }
 
-int tb200_upload_safetensors(tb200_device* d, const char* path, const char* const* names, size_t n, int threads,
-                             tb200_weight** out) {
+namespace {
+
+// tb200_upload_safetensors with optional windows (null: every tensor whole).
+int upload_impl(tb200_device* d, const char* path, const char* const* names, const tb200_window* win, size_t n,
+                int threads, tb200_weight** out) {
   if (int rc = rt::use(d)) return rc;
   ARG_CHECK(out && (names || n == 0), "null argument");
   ARG_CHECK(threads >= 0 && threads <= kMaxThreads, "threads must be 0 (automatic) .. " + std::to_string(kMaxThreads));
@@ -427,6 +435,19 @@ int tb200_upload_safetensors(tb200_device* d, const char* path, const char* cons
     if (it == f.entries.end()) continue;  // Weights::contains is false: the caller decides
     ent[i] = &it->second;
     if (int rc = check_bf16(f, it->first, it->second, &numel[i])) return rc;
+    if (!win || (win[i].rows == 0 && win[i].cols == 0)) continue;
+    const tb200_window& wi = win[i];
+    const std::vector<size_t>& sh = it->second.shape;
+    const std::string nm = "tensor '" + it->first + "': ";
+    ARG_CHECK(sh.size() == 2, nm + "a window needs a matrix");
+    ARG_CHECK(wi.rows > 0 && wi.cols > 0, nm + "an empty window");
+    ARG_CHECK(wi.row0 <= sh[0] && wi.rows <= sh[0] - wi.row0 && wi.col0 <= sh[1] && wi.cols <= sh[1] - wi.col0,
+              nm + "window rows " + std::to_string(wi.row0) + "+" + std::to_string(wi.rows) + ", columns " +
+                  std::to_string(wi.col0) + "+" + std::to_string(wi.cols) + " outside its " + std::to_string(sh[0]) +
+                  " x " + std::to_string(sh[1]));
+    ARG_CHECK(wi.cols == sh[1] || sh[1] * 2 <= kPiece,
+              nm + "rows wider than " + std::to_string(kPiece / 2) + " elements take no column window");
+    numel[i] = wi.rows * wi.cols;
   }
 
   std::vector<tb200_weight*> made;
@@ -442,7 +463,8 @@ int tb200_upload_safetensors(tb200_device* d, const char* path, const char* cons
   for (size_t i = 0; i < n; i++) {
     if (!ent[i]) continue;
     auto* w = new tb200_weight;
-    w->shape = ent[i]->shape;
+    const bool whole = !win || (win[i].rows == 0 && win[i].cols == 0);
+    w->shape = whole ? ent[i]->shape : std::vector<size_t>{win[i].rows, win[i].cols};
     w->numel = numel[i];
     made.push_back(w);
     out[i] = w;
@@ -452,10 +474,26 @@ int tb200_upload_safetensors(tb200_device* d, const char* path, const char* cons
       w->ptr = nullptr;
       return undo(rt::fail(TB200_ERR_CUDA, std::string("upload_safetensors: ") + cudaGetErrorString(e)));
     }
-    const uint64_t base = f.data_start + ent[i]->start;
+    unsigned char* dst = reinterpret_cast<unsigned char*>(w->ptr);
+    uint64_t base = f.data_start + ent[i]->start;
+    if (!whole && win[i].cols == ent[i]->shape[1]) {  // whole rows: one contiguous run
+      base += uint64_t(win[i].row0) * win[i].cols * 2;
+    } else if (!whole) {  // a column window: stage whole rows, copy their middle out
+      const size_t pitch = ent[i]->shape[1] * 2, width = win[i].cols * 2;
+      const size_t per = std::max<size_t>(1, kPiece / pitch);  // rows per piece
+      for (size_t r = 0; r < win[i].rows; r += per) {
+        const size_t nr = std::min(per, win[i].rows - r);
+        Piece pc{base + uint64_t(win[i].row0 + r) * pitch, dst + r * width, nr * pitch};
+        pc.rows = nr;
+        pc.src_off = win[i].col0 * 2;
+        pc.pitch = pitch;
+        pc.width = width;
+        pieces.push_back(pc);
+      }
+      continue;
+    }
     for (size_t off = 0; off < w->numel * 2; off += kPiece)
-      pieces.push_back({base + off, reinterpret_cast<unsigned char*>(w->ptr) + off,
-                        std::min(kPiece, w->numel * 2 - off)});
+      pieces.push_back({base + off, dst + off, std::min(kPiece, w->numel * 2 - off)});
   }
   if (pieces.empty()) return TB200_OK;
 
@@ -504,7 +542,10 @@ int tb200_upload_safetensors(tb200_device* d, const char* path, const char* cons
         record(TB200_ERR_IO, std::string(path) + ": " + err);
         break;
       }
-      e = cudaMemcpyAsync(pieces[i].dst, buf[b], pieces[i].len, cudaMemcpyHostToDevice, s);
+      const Piece& pc = pieces[i];
+      e = pc.rows ? cudaMemcpy2DAsync(pc.dst, pc.width, static_cast<unsigned char*>(buf[b]) + pc.src_off, pc.pitch,
+                                      pc.width, pc.rows, cudaMemcpyHostToDevice, s)
+                  : cudaMemcpyAsync(pc.dst, buf[b], pc.len, cudaMemcpyHostToDevice, s);
       if (e == cudaSuccess) e = cudaEventRecord(ev[b], s);
       pending[b] = true;
     }
@@ -523,4 +564,21 @@ int tb200_upload_safetensors(tb200_device* d, const char* path, const char* cons
   for (auto& t : pool) t.join();
   if (first_code != TB200_OK) return undo(rt::fail(first_code, first_err));
   return TB200_OK;
+}
+
+}  // namespace
+
+int tb200_upload_safetensors(tb200_device* d, const char* path, const char* const* names, size_t n, int threads,
+                             tb200_weight** out) {
+  return upload_impl(d, path, names, nullptr, n, threads, out);
+}
+
+int tb200_upload_safetensors_windows(tb200_device* d, const char* path, const char* const* names,
+                                     const tb200_window* windows, size_t n, int threads, tb200_weight** out) {
+  if (!windows && n) {
+    if (out)
+      for (size_t i = 0; i < n; i++) out[i] = nullptr;
+    return rt::fail(TB200_ERR_ARG, "null windows");
+  }
+  return upload_impl(d, path, names, windows, n, threads, out);
 }

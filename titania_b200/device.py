@@ -125,17 +125,26 @@ class B200:
              ctypes.byref(h))
         return Weight(h.value, tensor.shape, self)
 
-    def upload_safetensors(self, path: str, names, threads: int = 0) -> list:
+    def upload_safetensors(self, path: str, names, threads: int = 0, windows=None) -> list:
         """Weights::read + upload for every name in `names` at once, straight
         from the safetensors file at `path` to device memory (no host-side
         conversion; reads overlapped with copies on `threads` host threads,
         0 = automatic). Returns one Weight per name, or None where the file
         has no such tensor; a tensor that is not BF16 raises as
-        Weights::read fails (model/weights.rs:61-81)."""
+        Weights::read fails (model/weights.rs:61-81). `windows`, if given,
+        holds per name None (the tensor whole) or (row0, rows, col0, cols):
+        that block of a matrix, packed (a tensor-parallel rank's share)."""
         names = [str(n) for n in names]
         arr = (ctypes.c_char_p * max(1, len(names)))(*[n.encode() for n in names])
         out = (ctypes.c_void_p * max(1, len(names)))()
-        call("tb200_upload_safetensors", self._h, os.fsencode(path), arr, len(names), int(threads), out)
+        if windows is None:
+            call("tb200_upload_safetensors", self._h, os.fsencode(path), arr, len(names), int(threads), out)
+        else:
+            if len(windows) != len(names):
+                raise ValueError(f"{len(windows)} windows for {len(names)} tensors")
+            win = (_lib.Window * max(1, len(names)))(*[_lib.Window(*(w or (0, 0, 0, 0))) for w in windows])
+            call("tb200_upload_safetensors_windows", self._h, os.fsencode(path), arr, win, len(names),
+                 int(threads), out)
         res = []
         shape, ndim = (ctypes.c_size_t * 16)(), ctypes.c_size_t()
         for i in range(len(names)):

@@ -24,7 +24,6 @@ import numpy as np
 
 from . import _lib
 from ._lib import call
-from .device import Tensor
 
 ID_BYTES = 128
 
@@ -51,26 +50,49 @@ def shard_config(c, world: int):
     return Config(**d)
 
 
-def shard_tensor(c, name: str, shape, data: np.ndarray, rank: int, world: int):
-    """Rank `rank`'s part of checkpoint tensor `name` (shape, bf16 bits)."""
-    shape = list(shape)
-    a = np.asarray(data).reshape(shape)
+def shard_window(c, name: str, shape, rank: int, world: int):
+    """Rank `rank`'s block of checkpoint tensor `name` of `shape`, as
+    (row0, rows, col0, cols), or None when every rank holds it whole."""
     d = c.head_dim()
     q_rows = c.num_attention_heads // world * d
     kv_rows = c.num_key_value_heads // world * d
     f = c.intermediate_size // world
     if name.endswith(("q_proj.weight",)):
-        a = a[rank * q_rows:(rank + 1) * q_rows]
-    elif name.endswith(("k_proj.weight", "v_proj.weight")):
-        a = a[rank * kv_rows:(rank + 1) * kv_rows]
-    elif name.endswith("o_proj.weight"):
-        a = a[:, rank * q_rows:(rank + 1) * q_rows]
-    elif name.endswith(("gate_proj.weight", "up_proj.weight")):
-        a = a[rank * f:(rank + 1) * f]
-    elif name.endswith("down_proj.weight"):
-        a = a[:, rank * f:(rank + 1) * f]
+        return rank * q_rows, q_rows, 0, shape[1]
+    if name.endswith(("k_proj.weight", "v_proj.weight")):
+        return rank * kv_rows, kv_rows, 0, shape[1]
+    if name.endswith("o_proj.weight"):
+        return 0, shape[0], rank * q_rows, q_rows
+    if name.endswith(("gate_proj.weight", "up_proj.weight")):
+        return rank * f, f, 0, shape[1]
+    if name.endswith("down_proj.weight"):
+        return 0, shape[0], rank * f, f
+    return None
+
+
+def shard_tensor(c, name: str, shape, data: np.ndarray, rank: int, world: int):
+    """Rank `rank`'s part of checkpoint tensor `name` (shape, bf16 bits)."""
+    shape = list(shape)
+    a = np.asarray(data).reshape(shape)
+    w = shard_window(c, name, shape, rank, world)
+    if w is not None:
+        r0, nr, c0, nc = w
+        a = a[r0:r0 + nr, c0:c0 + nc]
     a = np.ascontiguousarray(a)
     return list(a.shape), a.reshape(-1)
+
+
+def _nccl_after_torch() -> None:
+    """The library opens NCCL as libnccl.so.2 the first time a group needs
+    it. PyTorch links its own (newer) libnccl.so.2, and the dynamic linker
+    resolves a library by that name to whichever copy the process loaded
+    first: if the system's older NCCL came first, `import torch` afterwards
+    fails on a missing NCCL symbol. Importing torch (when installed) before
+    the first NCCL call makes both use PyTorch's copy."""
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
 
 
 class TPGroup:
@@ -80,6 +102,7 @@ class TPGroup:
     def __init__(self, device, rank: int, world: int, uid: bytes):
         if len(uid) != ID_BYTES:
             raise ValueError(f"group id is {ID_BYTES} bytes")
+        _nccl_after_torch()
         h = ctypes.c_void_p()
         call("tb200_tp_init", device._h, int(rank), int(world), uid, ID_BYTES, ctypes.byref(h))
         self._h = h.value
@@ -87,6 +110,7 @@ class TPGroup:
 
     @staticmethod
     def unique_id() -> bytes:
+        _nccl_after_torch()
         buf = ctypes.create_string_buffer(ID_BYTES)
         call("tb200_tp_unique_id", buf, ID_BYTES)
         return buf.raw
@@ -107,14 +131,12 @@ def load_tp_model(path: str, device, group: TPGroup):
     from .model import Config, Model, Weights, tensor_names
     c = Config.load(os.path.join(path, "config.json"))
     local = shard_config(c, group.world)
-    w = Weights.open(os.path.join(path, "model.safetensors"))
-    up = {}
-    for name, required in tensor_names(c):
-        if not w.contains(name):
-            if required:
-                raise KeyError(f"missing tensor '{name}'")
-            continue
-        t = w.read(name)
-        shape, data = shard_tensor(c, name, t.shape, t.data, group.rank, group.world)
-        up[name] = device.upload(Tensor(shape, data))
-    return Model(local, device, up, tp=group)
+    f = os.path.join(path, "model.safetensors")
+    w = Weights.open(f)  # the header, for the shapes the windows are cut from
+    names = [(n, req) for n, req in tensor_names(c) if w.contains(n) or req]
+    for n, req in names:
+        if not w.contains(n):
+            raise KeyError(f"missing tensor '{n}'")
+    wins = [shard_window(c, n, w.entries[n]["shape"], group.rank, group.world) for n, _ in names]
+    ws = device.upload_safetensors(f, [n for n, _ in names], windows=wins)
+    return Model(local, device, dict(zip([n for n, _ in names], ws)), tp=group)
