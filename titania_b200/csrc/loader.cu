@@ -560,7 +560,14 @@ int upload_impl(tb200_device* d, const char* path, const char* const* names, con
   };
   std::vector<std::thread> pool;
   pool.reserve(size_t(nt));
-  for (int t = 0; t < nt; t++) pool.emplace_back(worker, t);
+  for (int t = 0; t < nt; t++) {
+    try {
+      pool.emplace_back(worker, t);
+    } catch (const std::exception& ex) {  // no thread: stop the others, report (nothing crosses the C ABI)
+      record(TB200_ERR_IO, std::string("upload_safetensors: cannot start a worker thread: ") + ex.what());
+      break;
+    }
+  }
   for (auto& t : pool) t.join();
   if (first_code != TB200_OK) return undo(rt::fail(first_code, first_err));
   return TB200_OK;
