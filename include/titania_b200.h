@@ -307,6 +307,17 @@ TB200_API int tb200_batch_read_kv(tb200_state* state, size_t seq, size_t layer, 
  * times; writes the `steps` chosen tokens to `out` (host memory). */
 TB200_API int tb200_generate(tb200_model* model, tb200_state* state, uint32_t token, size_t pos, size_t steps,
                    uint32_t* out);
+/* tb200_generate as one persistent kernel per step (opt-in; no counterpart
+ * in the reference: Model::forward + the greedy choice, model/model.rs:83-149
+ * and model/sampler.rs:31-33, for `steps` tokens from `token` at `pos`).
+ * One CTA per SM runs every phase of the step, the phases exchanging tagged
+ * vectors instead of ending kernels. Same tokens as tb200_generate; logits
+ * (optional, [steps][vocab]) for checking. Needs an f32-cache state, head_dim
+ * 128, hidden / FFN / query widths up to 3072, at most 4 query heads per kv
+ * head, at most 64 layers and contexts up to 64 positions (TB200_ERR_ARG
+ * otherwise). Allocates its scratch per call. */
+TB200_API int tb200_decode_persistent(tb200_model* model, tb200_state* state, uint32_t token, size_t pos,
+                                      size_t steps, uint32_t* tokens_out, float* logits_out);
 
 /* Enqueues greedy decode steps on the device's stream without waiting or
  * copying anything back: feeds `token` at `pos`, then each chosen token,

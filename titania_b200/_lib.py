@@ -116,6 +116,7 @@ SIGNATURES = {
     "tb200_decode_batch_enqueue": (ctypes.c_int, [P, P, U32P, SZP, SZ]),
     "tb200_batch_read_kv": (ctypes.c_int, [P, SZ, SZ, ctypes.c_int, SZ, F32P]),
     "tb200_generate": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P]),
+    "tb200_decode_persistent": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P, F32P]),
     "tb200_decode_enqueue": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ]),
     "tb200_enqueue_op": (ctypes.c_int, [P, P, ctypes.c_int, SZ]),
     "tb200_trace_start": (ctypes.c_int, [P, SZ]),

@@ -293,6 +293,16 @@ class Model:
         call("tb200_generate", self._h, state._h, int(token), int(pos), int(steps), out.ctypes.data_as(_lib.U32P))
         return out.tolist()
 
+    def decode_persistent(self, state: "State", token: int, pos: int, steps: int, logits: bool = False):
+        """`generate` with one persistent kernel per step (f32 cache states):
+        the `steps` chosen tokens, and with logits=True also their
+        [steps][vocab] logits."""
+        out = np.empty(steps, dtype=np.uint32)
+        lg = np.empty((steps, self.config.vocab_size), dtype=np.float32) if logits else None
+        call("tb200_decode_persistent", self._h, state._h, int(token), int(pos), int(steps),
+             out.ctypes.data_as(_lib.U32P), lg.ctypes.data_as(_lib.F32P) if logits else None)
+        return (out.tolist(), lg) if logits else out.tolist()
+
     def decode_enqueue(self, state: "State", token: int, pos: int, steps: int) -> None:
         """Enqueues `steps` greedy steps from `token` at `pos` without waiting
         or copying back (for timing)."""
