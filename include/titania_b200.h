@@ -307,15 +307,33 @@ TB200_API int tb200_batch_read_kv(tb200_state* state, size_t seq, size_t layer, 
  * times; writes the `steps` chosen tokens to `out` (host memory). */
 TB200_API int tb200_generate(tb200_model* model, tb200_state* state, uint32_t token, size_t pos, size_t steps,
                    uint32_t* out);
-/* tb200_generate as one persistent kernel per step (opt-in; no counterpart
- * in the reference: Model::forward + the greedy choice, model/model.rs:83-149
- * and model/sampler.rs:31-33, for `steps` tokens from `token` at `pos`).
- * One CTA per SM runs every phase of the step, the phases exchanging tagged
- * vectors instead of ending kernels. Same tokens as tb200_generate; logits
- * (optional, [steps][vocab]) for checking. Needs an f32-cache state, head_dim
- * 128, hidden / FFN / query widths up to 3072, at most 4 query heads per kv
- * head, at most 64 layers and contexts up to 64 positions (TB200_ERR_ARG
- * otherwise). Allocates its scratch per call. */
+/* What a one-sequence state's single-token steps run (tb200_forward with one
+ * token, tb200_generate, tb200_decode_enqueue; no counterpart in the
+ * reference, whose Model::forward is one path, model/model.rs:83-149):
+ *  - TB200_DECODE_FUSED: 2 + 5 * layers fused kernels per step, replayed from
+ *    a CUDA graph (every model this library runs, tensor-parallel included);
+ *  - TB200_DECODE_PERSISTENT: one persistent kernel (one CTA per SM) runs all
+ *    of a step's phases, the phases exchanging tagged vectors instead of
+ *    ending kernels, and tb200_generate / tb200_decode_enqueue run all their
+ *    steps in one launch. Needs an unsharded model with head_dim 128, hidden
+ *    / FFN / query widths up to 3072, at most 4 query heads per kv head, at
+ *    most 8 kv heads and 64 layers (Qwen3-0.6B fits; Qwen3-4B does not).
+ * tb200_state_new picks PERSISTENT where the model allows it, else FUSED.
+ * Both give the same tokens and logits within the tolerance of their
+ * different summation orders. */
+enum { TB200_DECODE_FUSED = 0, TB200_DECODE_PERSISTENT = 1 };
+/* Selects the single-token path of a one-sequence state; TB200_ERR_ARG (with
+ * the reason) when the state's model cannot run it. */
+TB200_API int tb200_state_set_decode(tb200_state* state, int mode);
+/* The state's single-token path (TB200_DECODE_*), -1 for a null state. */
+TB200_API int tb200_state_decode(const tb200_state* state);
+
+/* tb200_generate through the persistent kernel whatever the state's decode
+ * mode (see TB200_DECODE_PERSISTENT; TB200_ERR_ARG with the reason where the
+ * model cannot run it): `steps` greedy tokens from `token` at `pos` into
+ * tokens_out (host). With logits_out ([steps][vocab] floats, host; may be
+ * NULL) every step is its own launch and its logits are copied back, for
+ * checking. */
 TB200_API int tb200_decode_persistent(tb200_model* model, tb200_state* state, uint32_t token, size_t pos,
                                       size_t steps, uint32_t* tokens_out, float* logits_out);
 
@@ -394,6 +412,19 @@ enum {
   TB200_TRACE_OP_FINAL_NORM = 25, /* (tensor parallel) */
   TB200_TRACE_OP_LM_HEAD = 26,  /* lm_head contraction (+ argmax keys) */
   TB200_TRACE_OP_ARGMAX = 27,
+};
+
+/* Phases of the persistent single-token step (TB200_DECODE_PERSISTENT), as
+ * the op half of their trace tags. A traced CTA records INPUT when its input
+ * vector is complete and DONE when it has written its rows. */
+enum {
+  TB200_TRACE_OP_P_QKV = 32,   /* q|k|v = W_qkv . rmsnorm(x)                         */
+  TB200_TRACE_OP_P_ATTO = 33,  /* QK-norm, RoPE, append, attention, o_proj partial   */
+  TB200_TRACE_OP_P_GU = 34,    /* x' = x + partials; h = silu(gate) * up             */
+  TB200_TRACE_OP_P_DOWN = 35,  /* x = x' + W_d . h                                   */
+  TB200_TRACE_OP_P_LM = 36,    /* lm_head rows and their greedy choice              */
+  TB200_TRACE_OP_P_START = 37, /* the CTA began (START)                              */
+  TB200_TRACE_OP_P_TOKEN = 38, /* the last CTA published the step's token (DONE)     */
 };
 
 /* One trace record: tag = op << 16 | layer (TB200_OP_* for the single-token

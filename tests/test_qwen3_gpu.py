@@ -31,13 +31,14 @@ def golden_tiny():
     return dict(np.load(os.path.join(ROOT, "tests", "golden", "tiny_model.npz")))
 
 
+@pytest.mark.parametrize("decode", ["fused", "persistent"])
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
-def test_tiny_fused_against_golden(b200, tiny_model_dir, golden_tiny, kv):
+def test_tiny_fused_against_golden(b200, tiny_model_dir, golden_tiny, kv, decode):
     g = golden_tiny
     m = tb.Model.load(tiny_model_dir, b200)
     prompt = g["prompt"].tolist()
     steps = len(g["tokens"])
-    st = m.state(len(prompt) + steps + 1, kv=kv)
+    st = m.state(len(prompt) + steps + 1, kv=kv, decode=decode)
     logits = m.forward(st, prompt, 0)
     pos = len(prompt)
     for i in range(steps):
@@ -57,11 +58,12 @@ def test_tiny_fused_against_golden(b200, tiny_model_dir, golden_tiny, kv):
         close(st.read_kv(1, 1, p), v_ref[p], tol, tol)
 
 
-def test_tiny_generate_matches_forward_loop(b200, tiny_model_dir, golden_tiny):
+@pytest.mark.parametrize("decode", ["fused", "persistent"])
+def test_tiny_generate_matches_forward_loop(b200, tiny_model_dir, golden_tiny, decode):
     g = golden_tiny
     m = tb.Model.load(tiny_model_dir, b200)
     prompt = g["prompt"].tolist()
-    st = m.state(64)
+    st = m.state(64, decode=decode)
     first = m.forward(st, prompt, 0, logits=False)
     assert first == int(g["tokens"][0])
     toks = m.generate(st, first, len(prompt), len(g["tokens"]) - 1)
@@ -94,7 +96,7 @@ def test_tiny_crosses_from_short_to_long_context_graph(b200, tiny_model_dir, kv)
     ref = orc.Model(tiny_model_dir)
     ref_tokens, ref_logits = orc.greedy_generate(ref, prompt, 10, max_len=80)
     m = tb.Model.load(tiny_model_dir, b200)
-    st = m.state(80, kv=kv)
+    st = m.state(80, kv=kv, decode="fused")
     logits = m.forward(st, prompt, 0)
     pos = len(prompt)
     tol = (1e-3, 1e-3) if kv == "f32" else (REL, ABS)
@@ -104,7 +106,7 @@ def test_tiny_crosses_from_short_to_long_context_graph(b200, tiny_model_dir, kv)
         assert t == ref_tokens[i]
         logits = m.forward(st, [t], pos)
         pos += 1
-    st2 = m.state(80, kv=kv)
+    st2 = m.state(80, kv=kv, decode="fused")
     first = m.forward(st2, prompt, 0, logits=False)
     assert [first] + m.generate(st2, first, 60, 9) == ref_tokens
 
@@ -133,12 +135,14 @@ def qwen06b_oracle(qwen06b):
     return prompt, tokens, logits
 
 
+@pytest.mark.parametrize("decode", ["fused", "persistent"])
 @pytest.mark.parametrize("kv,rel,abs_", [("f32", REL, ABS), ("bf16", REL, 1.5e-2)])
-def test_qwen3_0_6b_greedy_32_steps(b200, qwen06b, qwen06b_oracle, kv, rel, abs_):
-    """16-token prompt, 32 greedy steps, batch 1."""
+def test_qwen3_0_6b_greedy_32_steps(b200, qwen06b, qwen06b_oracle, kv, rel, abs_, decode):
+    """16-token prompt, 32 greedy steps, batch 1, on both
+    single-token paths."""
     prompt, ref_tokens, ref_logits = qwen06b_oracle
     m = tb.Model.load(qwen06b, b200)
-    st = m.state(64, kv=kv)
+    st = m.state(64, kv=kv, decode=decode)
     logits = m.forward(st, prompt, 0)
     pos = len(prompt)
     margins = []
@@ -151,7 +155,7 @@ def test_qwen3_0_6b_greedy_32_steps(b200, qwen06b, qwen06b_oracle, kv, rel, abs_
         logits = m.forward(st, [t], pos)
         pos += 1
     # and the on-device loop makes the same choices
-    st2 = m.state(64, kv=kv)
+    st2 = m.state(64, kv=kv, decode=decode)
     first = m.forward(st2, prompt, 0, logits=False)
     assert [first] + m.generate(st2, first, 16, 31) == ref_tokens
 

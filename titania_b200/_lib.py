@@ -118,6 +118,8 @@ SIGNATURES = {
     "tb200_generate": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P]),
     "tb200_decode_persistent": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ, U32P, F32P]),
     "tb200_decode_enqueue": (ctypes.c_int, [P, P, ctypes.c_uint32, SZ, SZ]),
+    "tb200_state_set_decode": (ctypes.c_int, [P, ctypes.c_int]),
+    "tb200_state_decode": (ctypes.c_int, [P]),
     "tb200_enqueue_op": (ctypes.c_int, [P, P, ctypes.c_int, SZ]),
     "tb200_trace_start": (ctypes.c_int, [P, SZ]),
     "tb200_trace_stop": (ctypes.c_int, [P, P, SZ, SZP]),

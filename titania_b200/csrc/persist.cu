@@ -1,15 +1,31 @@
-// persist.cu — batch-1 greedy decode with one persistent kernel per step
-// (model/model.rs:83-149 for one token, then the greedy choice of
-// model/sampler.rs:31-33), an opt-in alternative to the fused path's chain of
-// 2 + 5 * layers kernels.
+// persist.cu — batch-1 greedy decode as one persistent kernel per launch:
+// Model::forward for one token (model/model.rs:93-149) followed by the greedy
+// choice (model/sampler.rs:31-33), repeated for `steps` tokens inside the
+// launch.
 //
-// One CTA per SM for the whole step (a cooperative launch, so CTAs may wait
-// on one another); phases exchange vectors as 64-bit (tag << 32 | value bits)
-// words, so data and synchronisation cost one L2 round trip together; one
-// producer warp streams this CTA's weight rows for every phase of the step
-// through a shared-memory ring without draining it at phase boundaries.
-// Every wait is bounded, and no control flow depends on a wait's outcome: the
-// first wait that gives up sets the CTA's abort flag and the error word,
+// One CTA per SM (a cooperative launch, so CTAs may wait on one another).
+// A step has four phases per layer and the lm_head:
+//   QKV    qkv   = W_qkv · rmsnorm(x)                      rows split over CTAs
+//   ATT_O  CTA (kv group g, member s): QK-norm, RoPE and K/V append of group
+//          g, its attention, then rows of part_o[g] = W_o[:, cols of g] · att_g
+//   GU     x' = x + Σ_g part_o[g] (g in order);  h = silu(W_g·n(x')) * (W_u·n(x'))
+//   DOWN   x  = x' + W_d · h                               rows owned by CTAs
+//   LM     logits = W_lm · rmsnorm(x); greedy token over the grid
+// Phases exchange vectors as 64-bit (tag << 32 | value bits) words in global
+// memory: a reader polls the words it needs until each carries the tag of
+// the current (step, layer, phase), so data and synchronisation cost one L2
+// round trip together and no grid barrier exists. Attention over a context
+// of up to kRedundantCtx positions is computed by every member of the kv
+// group (no exchange); past it, member s attends to its share of the
+// positions and the members exchange and merge their partial results.
+//
+// One producer warp streams this CTA's weight rows of every phase of every
+// step through a shared-memory ring with cp.async.bulk, never draining at a
+// phase boundary: while the consumers wait for a vector, the next phases'
+// weights keep arriving.
+//
+// Every wait is bounded, and no control flow depends on a wait's outcome:
+// the first wait that gives up sets the CTA's abort flag and the error word,
 // every later wait returns at once, and all threads still reach every
 // barrier, so the kernel ends promptly and drains its copies in flight.
 #include <cuda_runtime.h>
@@ -22,85 +38,119 @@
 
 namespace tb::persist {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kWarps = 8;                 // consumer warps
+constexpr int kConsumers = kWarps * 32;
+constexpr int kThreads = kConsumers + 32;  // + the producer warp
 constexpr int kSlotBytes = 64 * 1024;
 constexpr int kSlots = 3;
 constexpr int kMaxLayers = 64;
 constexpr int kHd = 128;
-constexpr int kMaxCols = 3072;  // widest input vector
-constexpr int kKsplitRows = 8;
-constexpr int kMaxGrp = 4;      // query heads per kv head
-constexpr int kAttnPer = 8;     // cached positions per warp held in registers at a time
-// Longest context the entry point accepts: one register chunk of cached
-// positions per warp (the chunk loop beyond it is written, not yet checked).
-constexpr int kMaxCtx = kWarps * kAttnPer;
+constexpr int kMaxCols = 3072;       // widest input vector
+constexpr int kKsplitRows = 8;       // a slice of at most this many rows splits K over all warps
+constexpr int kMaxRowsPerWarp = 8;
+constexpr int kMaxGrp = 4;           // query heads per kv head
+constexpr int kMaxKv = 8;            // kv heads (o_proj partial vectors summed by GU)
+constexpr int kMaxOwn = 32;          // residual rows a CTA owns
+constexpr int kAttnPer = 8;          // cached positions per warp held in registers at a time
+constexpr int kRedundantCtx = 256;   // contexts up to this: every group member attends over all of it
+constexpr int kPartWords = 132;      // a member's partial per head: acc[128], max, sum, 2 pad
 constexpr size_t kSmemBytes = size_t(2) * kMaxCols * 4 + size_t(kSlots) * kSlotBytes + 2 * kSlots * 8;
 
 using TW = unsigned long long;  // a tagged word
 
 struct Layer {
-  const uint16_t *wqkv, *wo, *wgu, *wd;  // [Q+2KV][H], [H][Q], [2F][H] (gate/up rows interleaved), [H][F]
+  const uint16_t *wqkv, *wo_g, *wgu, *wd;  // [Q+2KV][H], [Hkv][H][grp*128], [2F][H] (gate/up interleaved), [H][F]
   const uint16_t *attn_norm, *mlp_norm, *q_norm, *k_norm;
-  float *kc, *vc;  // [Hkv][max_len][kHd] f32
+  void *kc, *vc;  // [Hkv][max_len][128], f32 or bf16
 };
 
 struct Args {
   Layer layer[kMaxLayers];
-  int L, H, Q, KV, F, V, Hq, Hkv;
+  int L, H, Q, KV, F, V, Hq, Hkv, grp;
   float eps;
   const uint16_t *embed, *lm_head, *norm;
-  const float* rope;  // [max_len][kHd] (cos, sin) pairs
-  int max_len;
-  TW *x, *qkv, *att, *h;  // [H], [Q+2KV], [Q], [F]
-  int* token;
-  int* pos;
-  uint32_t* epoch;          // tag base of this step (advanced by the last CTA)
-  unsigned long long* best;
-  unsigned* ticket;
-  int* err;
-  float* logits;  // [V] or null: the lm_head rows as well as their argmax
-  int* tokens;    // [steps]: token of the step at position p goes to tokens[p - pos0]
-  int pos0;
+  const float* rope;  // [max_len][128] (cos, sin) pairs
+  int max_len, kv_f32;
+  TW *x, *qkv, *h, *part_o, *part_att, *tokw;  // [H], [Q+2KV], [F], [Hkv][H], [Hkv][nsplit][grp][kPartWords], [4]
+  int nsplit;  // most members of a kv group (ceil(CTAs / Hkv))
+  int* io;            // [0] token, [1] position, [2] generated-token counter, [3] error word
+  int* tokens_out;    // [tokens_cap]: generated tokens by counter
+  int tokens_cap;
+  unsigned long long* best;  // argmax key, zero between steps
+  unsigned* ticket;          // zero between steps
+  float* logits;             // [V] of the last step, or null
+  uint32_t epoch;            // tag base of the first step (tags never repeat: the host advances it)
+  int steps;
+  Trace trace;
 };
 
-enum { P_QKV = 0, P_ATT = 1, P_O = 2, P_GU = 3, P_DOWN = 4, kPerLayer = 5 };
-// Tag offset of a phase's output (0 is the embedding).
-__host__ __device__ constexpr uint32_t phase_index(int layer, int p) { return 1u + uint32_t(layer) * kPerLayer + p; }
+enum { P_QKV = 0, P_ATTO = 1, P_GU = 2, P_DOWN = 3, kPhases = 4 };
+
+// Tags of one step, relative to its base: 0 the embedded token's x, then
+// 1 + 4 layer + phase, then the chosen token.
+__host__ __device__ constexpr uint32_t tags_per_step(int L) { return 2u + 4u * uint32_t(L); }
+__device__ __forceinline__ uint32_t phase_tag(uint32_t base, int layer, int p) {
+  return base + 1u + 4u * uint32_t(layer) + uint32_t(p);
+}
+// Trace slot group of a phase: 0 the step's start, 1 + 4 layer + phase, then the lm_head.
+__device__ __forceinline__ uint32_t trace_base(int layer, int p, int G) {
+  return (1u + 4u * uint32_t(layer) + uint32_t(p)) * uint32_t(G) * kTraceEvents;
+}
 
 struct Slice {
-  const uint16_t* w;
-  int r0, n, cols;
+  const uint16_t* w;  // first row of the slice
+  int r0, n, cols;    // output rows [r0, r0 + n) of the phase's vector
 };
 
-// Rows [r0, r0 + n) of a matrix phase for CTA `cta` of G (layer == L: lm_head).
-__device__ __forceinline__ Slice slice_of(const Args& a, int layer, int p, int cta, int G) {
+// The kv group and member of CTA c in ATT_O, and the group's member count.
+__device__ __forceinline__ void group_of(const Args& a, int c, int G, int& g, int& s, int& ng) {
+  g = c % a.Hkv;
+  s = c / a.Hkv;
+  ng = (G - g + a.Hkv - 1) / a.Hkv;
+}
+
+// This CTA's rows of a matrix phase (layer == L: the lm_head).
+__device__ __forceinline__ Slice slice_of(const Args& a, int layer, int p, int c, int G) {
   const Layer& Ly = a.layer[layer < a.L ? layer : 0];
+  if (layer == a.L) {
+    const int r0 = int((long long)c * a.V / G), r1 = int((long long)(c + 1) * a.V / G);
+    return Slice{a.lm_head + size_t(r0) * a.H, r0, r1 - r0, a.H};
+  }
+  if (p == P_ATTO) {
+    int g, s, ng;
+    group_of(a, c, G, g, s, ng);
+    const int cols = a.grp * kHd;
+    const int r0 = s * a.H / ng, r1 = (s + 1) * a.H / ng;
+    return Slice{Ly.wo_g + (size_t(g) * a.H + r0) * cols, r0, r1 - r0, cols};
+  }
   int rows, cols, align;
   const uint16_t* w;
-  if (layer == a.L) {
-    w = a.lm_head, rows = a.V, cols = a.H, align = 1;
-  } else if (p == P_QKV) {
+  if (p == P_QKV) {
     w = Ly.wqkv, rows = a.Q + 2 * a.KV, cols = a.H, align = 1;
-  } else if (p == P_O) {
-    w = Ly.wo, rows = a.H, cols = a.Q, align = 1;
   } else if (p == P_GU) {
     w = Ly.wgu, rows = 2 * a.F, cols = a.H, align = 2;
   } else {
     w = Ly.wd, rows = a.H, cols = a.F, align = 1;
   }
   const int units = rows / align;
-  const int r0 = int((long long)cta * units / G) * align;
-  const int r1 = int((long long)(cta + 1) * units / G) * align;
-  return Slice{w, r0, r1 - r0, cols};
+  const int r0 = int((long long)c * units / G) * align;
+  const int r1 = int((long long)(c + 1) * units / G) * align;
+  return Slice{w + size_t(r0) * cols, r0, r1 - r0, cols};
 }
 
-// Rows per stage: a slice of <= kKsplitRows rows is one K-split stage; else
-// up to 4 rows per consumer warp, within one slot.
+// Rows per ring stage: a slice of <= kKsplitRows rows splits K over all
+// warps; longer slices give each warp up to kMaxRowsPerWarp rows. Even, so
+// that a gate/up pair never straddles two stages.
 __device__ __forceinline__ int stage_rows(const Slice& s) {
-  if (s.n <= kKsplitRows) return s.n;
-  const int fit = kSlotBytes / (s.cols * 2);
-  return min(fit, kWarps * 4) & ~1;
+  const int fit = (kSlotBytes / (s.cols * 2)) & ~1;
+  if (s.n <= kKsplitRows) return min(s.n, fit);
+  return min(fit, kWarps * kMaxRowsPerWarp);
+}
+
+// Residual rows CTA c owns (its embedding, down_proj rows and lm_head-free).
+__device__ __forceinline__ void own_rows(const Args& a, int c, int G, int& r0, int& r1) {
+  r0 = int((long long)c * a.H / G);
+  r1 = int((long long)(c + 1) * a.H / G);
 }
 
 __device__ __forceinline__ void st_tagged(TW* p, float v, uint32_t tag) {
@@ -112,24 +162,28 @@ __device__ __forceinline__ TW ld_tagged(const TW* p) {
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
-// Two tagged words; each 64-bit element is read atomically.
-__device__ __forceinline__ void ld_tagged2(const TW* p, TW& a, TW& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+// Four tagged words (32 bytes); each 64-bit element is read atomically.
+__device__ __forceinline__ void ld_tagged4(const TW* p, TW (&w)[4]) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w[0]), "=l"(w[1]) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w[2]), "=l"(w[3]) : "l"(p + 2) : "memory");
 }
 __device__ __forceinline__ float tval(TW w) { return __uint_as_float(uint32_t(w)); }
 __device__ __forceinline__ uint32_t ttag(TW w) { return uint32_t(w >> 32); }
+__device__ __forceinline__ bool tags4(const TW (&w)[4], uint32_t tag) {
+  return ttag(w[0]) == tag && ttag(w[1]) == tag && ttag(w[2]) == tag && ttag(w[3]) == tag;
+}
 
-// Polls *p until it carries `tag`; bounded (see the abort rule above).
-__device__ __forceinline__ float wait_word(const TW* p, uint32_t tag, uint64_t t0, int* err, volatile int* abort) {
-  for (;;) {
-    const TW w = ld_tagged(p);
-    if (ttag(w) == tag || *abort) return tval(w);
-    if (global_ns() - t0 > kWaitNs) {
-      set_error(err, TB200_ERR_TIMEOUT);
-      *abort = 1;
-      return tval(w);
-    }
-  }
+// Shared-memory position of input element i (i a multiple of 4): columns
+// 256k + 8l .. 8l+3 at 256k + 4l and 8l+4 .. 8l+7 at 256k + 128 + 4l, so
+// that lane l reads its eight columns of a 256-column block as two float4.
+__device__ __forceinline__ int xperm(int i) { return (i & ~255) + ((i >> 2) & 1) * 128 + ((i >> 3) & 31) * 4; }
+
+// Records a timeout: the error word, and this CTA's abort flag.
+__device__ __forceinline__ bool timed_out(uint64_t t0, int* err, volatile int* abort) {
+  if (global_ns() - t0 <= kWaitNs) return false;
+  set_error(err, TB200_ERR_TIMEOUT);
+  *abort = 1;
+  return true;
 }
 
 // mbar_wait under the abort rule.
@@ -138,181 +192,330 @@ __device__ __forceinline__ void wait_full(uint64_t* bar, uint32_t parity, int* e
   if (!mbar_wait(bar, parity, err)) *abort = 1;
 }
 
-// Consumer thread `tid` polls its groups of 4 words of vec[0, n) until every
-// word carries `tag` and stores the values to xs, permuted as the library's
-// matrix-vector kernel stores its input (column 256k + 8l + 4h at
-// 256k + 128h + 4l). Bounded.
-__device__ void poll_vector(const TW* vec, int n, uint32_t tag, float* xs, int tid, int* err, volatile int* abort) {
+// Polls vec[0, n) (n a multiple of 4, at most 4 kConsumers) until every word
+// carries `tag`; with np > 0, also np partial vectors parts[j * pstride ...]
+// carrying ptag, which are added to the vector in order j = 0, 1, ... The
+// sums go to xs at xperm positions; elements [own0, own1) also to own[].
+// All of a thread's loads are issued before any is checked. Bounded.
+__device__ void poll_vector(const TW* vec, int n, uint32_t tag, const TW* parts, int np, int pstride, uint32_t ptag,
+                            float* xs, float* own, int own0, int own1, int tid, int* err, volatile int* abort) {
+  constexpr int kG = 3;  // groups of 4 words per thread (n <= 3072)
+  bool done[kG];
+#pragma unroll
+  for (int k = 0; k < kG; k++) done[k] = tid * 4 + k * kConsumers * 4 >= n;
   const uint64_t t0 = global_ns();
-  for (int i = tid * 4; i < n; i += kWarps * 32 * 4) {
-    TW w0, w1, w2, w3;
-    for (;;) {
-      ld_tagged2(vec + i, w0, w1);
-      ld_tagged2(vec + i + 2, w2, w3);
-      if ((ttag(w0) == tag && ttag(w1) == tag && ttag(w2) == tag && ttag(w3) == tag) || *abort) break;
-      if (global_ns() - t0 > kWaitNs) {
-        set_error(err, TB200_ERR_TIMEOUT);
-        *abort = 1;
-        break;
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int k = 0; k < kG; k++) {
+      if (done[k]) continue;
+      const int i = tid * 4 + k * kConsumers * 4;
+      TW w[4];
+      ld_tagged4(vec + i, w);
+      bool ok = tags4(w, tag);
+      float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
+      for (int j = 0; j < np; j++) {
+        TW u[4];
+        ld_tagged4(parts + size_t(j) * pstride + i, u);
+        ok = ok && tags4(u, ptag);
+        v.x = __fadd_rn(v.x, tval(u[0]));
+        v.y = __fadd_rn(v.y, tval(u[1]));
+        v.z = __fadd_rn(v.z, tval(u[2]));
+        v.w = __fadd_rn(v.w, tval(u[3]));
+      }
+      if (ok || *abort) {
+        *reinterpret_cast<float4*>(xs + xperm(i)) = v;
+        if (own) {
+          const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; q++)
+            if (i + q >= own0 && i + q < own1) own[i + q - own0] = e[q];
+        }
+        done[k] = true;
+      } else {
+        all = false;
       }
     }
-    const int at = (i & ~255) + ((i >> 2) & 1) * 128 + ((i >> 3) & 31) * 4;
-    *reinterpret_cast<float4*>(xs + at) = make_float4(tval(w0), tval(w1), tval(w2), tval(w3));
+    if (all || timed_out(t0, err, abort)) break;
   }
 }
 
-// Attention for kv head g at position pos (model.rs:107-124 for one token):
-// QK-norm of the group's query heads and the key, RoPE, K/V append, then the
-// softmax-weighted sum of values over positions 0..pos, warps taking
-// positions w, w + 8, ... with their own online softmax, merged at the end.
-// `sm` holds at least 5000 floats. Run by the 256 consumer threads.
-__device__ void attention_phase(const Args& a, const Layer& Ly, int g, int pos, uint32_t in_tag, uint32_t out_tag,
-                                float* sm, int tid, volatile int* abort) {
-  const int grp = a.Hq / a.Hkv;
-  const int warp = tid >> 5, lane = tid & 31;
-  float* qs = sm;                           // [grp][kHd]
-  float* kn = qs + kMaxGrp * kHd;           // [kHd]
-  float* vn = kn + kHd;                     // [kHd]
-  float* wm = vn + kHd;                     // [kWarps][kMaxGrp]
-  float* wl = wm + kWarps * kMaxGrp;        // [kWarps][kMaxGrp]
-  float* wacc = wl + kWarps * kMaxGrp;      // [kWarps][kMaxGrp][kHd]
+// ---- attention ----------------------------------------------------------------
 
-  // Cached keys and values (positions < pos) do not depend on this step:
-  // the first chunk (positions warp + 8 i) is requested before the wait.
+__device__ __forceinline__ float4 ld_kv(const void* base, size_t at, bool f32) {
+  if (f32) return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(base) + at));
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + at));
+  return make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y));
+}
+__device__ __forceinline__ void st_kv(void* base, size_t at, float4 v, bool f32) {
+  if (f32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(base) + at) = v;
+  } else {
+    const uint32_t lo = uint32_t(f2bf(v.x)) | (uint32_t(f2bf(v.y)) << 16);
+    const uint32_t hi = uint32_t(f2bf(v.z)) | (uint32_t(f2bf(v.w)) << 16);
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + at) = make_uint2(lo, hi);
+  }
+}
+// What the cache holds for v: v itself (f32) or its bf16 rounding.
+__device__ __forceinline__ float4 as_cached(float4 v, bool f32) {
+  if (f32) return v;
+  return make_float4(bf16f(f2bf(v.x)), bf16f(f2bf(v.y)), bf16f(f2bf(v.z)), bf16f(f2bf(v.w)));
+}
+
+// Attention of kv group g at position `pos` (model.rs:107-124 for one
+// token; cpu.rs:113-149), run by the consumer warps of member s of the
+// group's ng members. Warp w < grp + 2 polls head w of q (w < grp), k, v
+// from the q|k|v vector, applies QK-norm (model.rs:111-116) and RoPE
+// (cpu.rs:96-111) in registers; member 0 appends k and v to the cache. The
+// context [lo, hi) this member attends to is all of 0..pos when pos < the
+// redundant limit, else its share; warps take positions lo + w, lo + w + 8,
+// ... with their own online softmax, merged at the end. In split mode the
+// members then exchange partials (tag `ptag`) and every member merges all of
+// them in member order. The result, grp heads of 128, goes to xs at xperm
+// positions (the o_proj partial's input). `sc` is shared scratch of at least
+// 4928 floats.
+template <int GRP>
+__device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, int ng, int pos, uint32_t qtag,
+                                uint32_t ptag, float* xs, float* sc, int tid, volatile int* abort, const TraceAt& tr) {
+  constexpr int grp = GRP;
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool f32 = a.kv_f32 != 0;
+  float* qs = sc;                        // [grp][128]
+  float* kn = qs + kMaxGrp * kHd;        // [128]
+  float* vn = kn + kHd;                  // [128]
+  float* wm = vn + kHd;                  // [kWarps][kMaxGrp]
+  float* wl = wm + kWarps * kMaxGrp;     // [kWarps][kMaxGrp]
+  float* wacc = wl + kWarps * kMaxGrp;   // [kWarps][kMaxGrp][128]
+
+  const int ctx = pos + 1;
+  const bool split = ctx > kRedundantCtx;
+  const int lo = split ? int((long long)s * ctx / ng) : 0;
+  const int hi = split ? int((long long)(s + 1) * ctx / ng) : ctx;
+  const size_t head0 = size_t(g) * a.max_len * kHd;
+
+  // Cached positions (< pos) do not depend on this step: the first chunk is
+  // requested before the wait.
   float4 kr[kAttnPer], vr[kAttnPer];
+#pragma unroll
+  for (int i = 0; i < kAttnPer; i++) kr[i] = vr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   auto load_chunk = [&](int base) {
 #pragma unroll
     for (int i = 0; i < kAttnPer; i++) {
       const int j = base + warp + kWarps * i;
-      if (j < pos) {
-        const size_t at = (size_t(g) * a.max_len + j) * kHd + 4 * lane;
-        kr[i] = __ldcg(reinterpret_cast<const float4*>(Ly.kc + at));
-        vr[i] = __ldcg(reinterpret_cast<const float4*>(Ly.vc + at));
+      if (j < hi && j < pos) {
+        const size_t at = head0 + size_t(j) * kHd + 4 * lane;
+        kr[i] = ld_kv(Ly.kc, at, f32);
+        vr[i] = ld_kv(Ly.vc, at, f32);
       }
     }
   };
-  load_chunk(0);
+  load_chunk(lo);
 
-  // q (grp heads), k, v of this group from the tagged q|k|v vector.
-  const uint64_t t0 = global_ns();
-  for (int i = tid; i < (grp + 2) * kHd; i += kWarps * 32) {
-    const int h = i / kHd, d = i % kHd;
-    const int at = h < grp ? (g * grp + h) * kHd + d : h == grp ? a.Q + g * kHd + d : a.Q + a.KV + g * kHd + d;
-    (h < grp ? qs + h * kHd : h == grp ? kn : vn)[d] = wait_word(a.qkv + at, in_tag, t0, a.err, abort);
-  }
-  named_sync(1, kWarps * 32);
-
-  // QK-norm (rmsnorm over each head with q_norm / k_norm): warp h takes head h.
-  if (warp < grp + 1) {
-    float* x = warp < grp ? qs + warp * kHd : kn;
-    const uint16_t* nw = warp < grp ? Ly.q_norm : Ly.k_norm;
-    if (nw) {
-      float4 v = *reinterpret_cast<float4*>(x + 4 * lane);
-      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
-      const float scale = 1.0f / sqrtf(ss / float(kHd) + a.eps);
-      v.x = __fmul_rn(v.x, __fmul_rn(scale, bf16f(nw[4 * lane + 0])));
-      v.y = __fmul_rn(v.y, __fmul_rn(scale, bf16f(nw[4 * lane + 1])));
-      v.z = __fmul_rn(v.z, __fmul_rn(scale, bf16f(nw[4 * lane + 2])));
-      v.w = __fmul_rn(v.w, __fmul_rn(scale, bf16f(nw[4 * lane + 3])));
-      *reinterpret_cast<float4*>(x + 4 * lane) = v;
+  // Warp w < grp + 2: head w of q, then k, then v, polled and prepared in registers.
+  if (warp < grp + 2) {
+    const int at = warp < grp ? (g * grp + warp) * kHd : warp == grp ? a.Q + g * kHd : a.Q + a.KV + g * kHd;
+    TW w[4];
+    const uint64_t t0 = global_ns();
+    for (;;) {
+      ld_tagged4(a.qkv + at + 4 * lane, w);
+      if (tags4(w, qtag) || *abort || timed_out(t0, a.io + 3, abort)) break;
     }
-  }
-  named_sync(1, kWarps * 32);
-  // RoPE at pos: element i pairs with i + 64.
-  if (tid < kHd / 2) {
-    const float c = a.rope[size_t(pos) * kHd + 2 * tid], s = a.rope[size_t(pos) * kHd + 2 * tid + 1];
-    for (int h = 0; h < grp + 1; h++) {
-      float* x = h < grp ? qs + h * kHd : kn;
-      const float u = x[tid], w = x[tid + kHd / 2];
-      x[tid] = __fsub_rn(__fmul_rn(u, c), __fmul_rn(w, s));
-      x[tid + kHd / 2] = __fadd_rn(__fmul_rn(w, c), __fmul_rn(u, s));
-    }
-  }
-  named_sync(1, kWarps * 32);
-  if (tid < kHd) {  // append this position's key and value
-    const size_t at = (size_t(g) * a.max_len + pos) * kHd + tid;
-    Ly.kc[at] = kn[tid];
-    Ly.vc[at] = vn[tid];
-  }
-
-  // Online softmax per warp over positions warp, warp + 8, ...
-  const float sc = 1.0f / sqrtf(float(kHd));
-  float m[kMaxGrp], l[kMaxGrp];
-  float4 acc[kMaxGrp];
+    float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
+    if (warp <= grp) {
+      const uint16_t* nw = warp < grp ? Ly.q_norm : Ly.k_norm;
+      if (nw) {  // rmsnorm over the head (cpu.rs:85-94 with dim 128)
+        const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        const float scale = 1.0f / sqrtf(ss / float(kHd) + a.eps);
+        const uint2 gw = *reinterpret_cast<const uint2*>(nw + 4 * lane);
+        v.x = __fmul_rn(v.x, __fmul_rn(scale, bf_lo(gw.x)));
+        v.y = __fmul_rn(v.y, __fmul_rn(scale, bf_hi(gw.x)));
+        v.z = __fmul_rn(v.z, __fmul_rn(scale, bf_lo(gw.y)));
+        v.w = __fmul_rn(v.w, __fmul_rn(scale, bf_hi(gw.y)));
+      }
+      // RoPE: element i pairs with i + 64, held by lane ^ 16.
+      const float4 o = make_float4(__shfl_xor_sync(0xffffffffu, v.x, 16), __shfl_xor_sync(0xffffffffu, v.y, 16),
+                                   __shfl_xor_sync(0xffffffffu, v.z, 16), __shfl_xor_sync(0xffffffffu, v.w, 16));
+      const int i0 = (4 * lane) & 63;
+      const float4 cs0 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kHd + 2 * i0);
+      const float4 cs1 = *reinterpret_cast<const float4*>(a.rope + size_t(pos) * kHd + 2 * i0 + 4);
+      const float c[4] = {cs0.x, cs0.z, cs1.x, cs1.z}, sn[4] = {cs0.y, cs0.w, cs1.y, cs1.w};
+      float e[4] = {v.x, v.y, v.z, v.w};
+      const float f[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
-  for (int h = 0; h < kMaxGrp; h++) {
+      for (int q = 0; q < 4; q++)
+        e[q] = lane < 16 ? __fsub_rn(__fmul_rn(e[q], c[q]), __fmul_rn(f[q], sn[q]))
+                         : __fadd_rn(__fmul_rn(e[q], c[q]), __fmul_rn(f[q], sn[q]));
+      v = make_float4(e[0], e[1], e[2], e[3]);
+    }
+    if (warp >= grp) {
+      if (s == 0) {  // member 0 appends this position's key and value
+        st_kv(warp == grp ? Ly.kc : Ly.vc, head0 + size_t(pos) * kHd + 4 * lane, v, f32);
+        __threadfence();  // a later step of this launch reads it from another CTA
+      }
+      v = as_cached(v, f32);
+    }
+    *reinterpret_cast<float4*>((warp < grp ? qs + warp * kHd : warp == grp ? kn : vn) + 4 * lane) = v;
+  }
+  named_sync(1, kConsumers);
+  if (tid == 0) tr.at(blockIdx.x, TB200_TRACE_WAITED);
+
+  // Online softmax per warp over its positions of [lo, hi), eight at a time.
+  const float scale = 1.0f / sqrtf(float(kHd));
+  float m[GRP], l[GRP];
+  float4 acc[GRP], q[GRP];
+#pragma unroll
+  for (int h = 0; h < GRP; h++) {
     m[h] = -INFINITY;
     l[h] = 0.f;
     acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    q[h] = *reinterpret_cast<const float4*>(qs + h * kHd + 4 * lane);
   }
-  for (int base = 0; base <= pos; base += kWarps * kAttnPer) {
-    if (base > 0) load_chunk(base);
+  const float4 kcur = *reinterpret_cast<const float4*>(kn + 4 * lane);
+  const float4 vcur = *reinterpret_cast<const float4*>(vn + 4 * lane);
+  for (int base = lo; base < hi; base += kWarps * kAttnPer) {
+    if (base > lo) load_chunk(base);
+    float sco[GRP][kAttnPer];
 #pragma unroll
     for (int i = 0; i < kAttnPer; i++) {
-    const int j = base + warp + kWarps * i;
-    if (j > pos) break;
-    const float4 kj = j == pos ? *reinterpret_cast<const float4*>(kn + 4 * lane) : kr[i];
-    const float4 vj = j == pos ? *reinterpret_cast<const float4*>(vn + 4 * lane) : vr[i];
+      const int j = base + warp + kWarps * i;
+      if (j == pos) kr[i] = kcur, vr[i] = vcur;
 #pragma unroll
-    for (int h = 0; h < kMaxGrp; h++) {
-      if (h >= grp) break;
-      const float4 q = *reinterpret_cast<const float4*>(qs + h * kHd + 4 * lane);
-      const float s = warp_sum(q.x * kj.x + q.y * kj.y + q.z * kj.z + q.w * kj.w) * sc;
-      const float mn = fmaxf(m[h], s);
-      const float corr = expf(m[h] - mn), p = expf(s - mn);
-      l[h] = l[h] * corr + p;
-      acc[h].x = acc[h].x * corr + p * vj.x;
-      acc[h].y = acc[h].y * corr + p * vj.y;
-      acc[h].z = acc[h].z * corr + p * vj.z;
-      acc[h].w = acc[h].w * corr + p * vj.w;
-      m[h] = mn;
+      for (int h = 0; h < GRP; h++)
+        sco[h][i] = q[h].x * kr[i].x + q[h].y * kr[i].y + q[h].z * kr[i].z + q[h].w * kr[i].w;
     }
+    // All GRP x kAttnPer dot products reduced across the warp at once.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < GRP; h++)
+#pragma unroll
+        for (int i = 0; i < kAttnPer; i++) sco[h][i] += __shfl_xor_sync(0xffffffffu, sco[h][i], o);
+#pragma unroll
+    for (int h = 0; h < GRP; h++) {
+      float mx = m[h];
+#pragma unroll
+      for (int i = 0; i < kAttnPer; i++)
+        if (base + warp + kWarps * i < hi) mx = fmaxf(mx, sco[h][i] * scale);
+      const float corr = expf(m[h] - mx);
+      float4 ac = make_float4(acc[h].x * corr, acc[h].y * corr, acc[h].z * corr, acc[h].w * corr);
+      float lsum = l[h] * corr;
+#pragma unroll
+      for (int i = 0; i < kAttnPer; i++) {
+        if (base + warp + kWarps * i >= hi) break;
+        const float p = expf(sco[h][i] * scale - mx);
+        lsum += p;
+        ac.x += p * vr[i].x;
+        ac.y += p * vr[i].y;
+        ac.z += p * vr[i].z;
+        ac.w += p * vr[i].w;
+      }
+      if (mx != -INFINITY) {
+        m[h] = mx;
+        l[h] = lsum;
+        acc[h] = ac;
+      }
     }
   }
 #pragma unroll
-  for (int h = 0; h < kMaxGrp; h++) {
-    if (h >= grp) break;
+  for (int h = 0; h < GRP; h++) {
     if (lane == 0) {
       wm[warp * kMaxGrp + h] = m[h];
       wl[warp * kMaxGrp + h] = l[h];
     }
     *reinterpret_cast<float4*>(wacc + (warp * kMaxGrp + h) * kHd + 4 * lane) = acc[h];
   }
-  named_sync(1, kWarps * 32);
-  for (int i = tid; i < grp * kHd; i += kWarps * 32) {
-    const int h = i / kHd, d = i % kHd;
-    float M = -INFINITY;
-    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * kMaxGrp + h]);
-    float L = 0.f, O = 0.f;
+  named_sync(1, kConsumers);
+  if (tid == 0) tr.at(blockIdx.x, TB200_TRACE_REDUCE);
+  // Merge the warps: thread (h, 4 dims) of the grp * 32 threads.
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = -INFINITY, Ls = 0.f;
+  const int mh = tid >> 5, d4 = tid & 31;
+  if (tid < grp * 32) {
+    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * kMaxGrp + mh]);
     for (int w = 0; w < kWarps; w++) {
-      const float e = wl[w * kMaxGrp + h] > 0.f ? expf(wm[w * kMaxGrp + h] - M) : 0.f;
-      L += wl[w * kMaxGrp + h] * e;
-      O += wacc[(w * kMaxGrp + h) * kHd + d] * e;
+      const float lw = wl[w * kMaxGrp + mh];
+      if (lw > 0.f) {
+        const float e = expf(wm[w * kMaxGrp + mh] - M);
+        const float4 aw = *reinterpret_cast<const float4*>(wacc + (w * kMaxGrp + mh) * kHd + 4 * d4);
+        Ls += lw * e;
+        o.x += aw.x * e;
+        o.y += aw.y * e;
+        o.z += aw.z * e;
+        o.w += aw.w * e;
+      }
     }
-    st_tagged(a.att + (g * grp + h) * kHd + d, O / L, out_tag);
   }
-  named_sync(1, kWarps * 32);  // the scratch is reused by the next phase
+  if (split) {
+    // Publish this member's partial, then merge every member's in order.
+    TW* mine = a.part_att + (size_t(g * a.nsplit + s) * grp) * kPartWords;
+    if (tid < grp * 32) {
+      TW* p = mine + mh * kPartWords;
+      st_tagged(p + 4 * d4 + 0, o.x, ptag);
+      st_tagged(p + 4 * d4 + 1, o.y, ptag);
+      st_tagged(p + 4 * d4 + 2, o.z, ptag);
+      st_tagged(p + 4 * d4 + 3, o.w, ptag);
+      if (d4 == 0) {
+        st_tagged(p + 128, M, ptag);
+        st_tagged(p + 129, Ls, ptag);
+        st_tagged(p + 130, 0.f, ptag);
+        st_tagged(p + 131, 0.f, ptag);
+      }
+    }
+    o = make_float4(0.f, 0.f, 0.f, 0.f);
+    M = -INFINITY;
+    Ls = 0.f;
+    if (tid < grp * 32) {
+      const uint64_t t0 = global_ns();
+      for (int sp = 0; sp < ng; sp++) {
+        const TW* p = a.part_att + (size_t(g * a.nsplit + sp) * grp + mh) * kPartWords;
+        TW w[4], ml[4];
+        for (;;) {
+          ld_tagged4(p + 4 * d4, w);
+          ld_tagged4(p + 128, ml);
+          if ((tags4(w, ptag) && tags4(ml, ptag)) || *abort || timed_out(t0, a.io + 3, abort)) break;
+        }
+        const float ms = tval(ml[0]), ls = tval(ml[1]);
+        if (ls > 0.f) {
+          const float Mn = fmaxf(M, ms);
+          const float cold = expf(M - Mn), cnew = expf(ms - Mn);
+          o.x = o.x * cold + tval(w[0]) * cnew;
+          o.y = o.y * cold + tval(w[1]) * cnew;
+          o.z = o.z * cold + tval(w[2]) * cnew;
+          o.w = o.w * cold + tval(w[3]) * cnew;
+          Ls = Ls * cold + ls * cnew;
+          M = Mn;
+        }
+      }
+    }
+  }
+  if (tid < grp * 32) {
+    const float inv = 1.0f / Ls;
+    *reinterpret_cast<float4*>(xs + xperm(mh * kHd + 4 * d4)) = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  }
 }
 
+// ---- the kernel -----------------------------------------------------------------
+
+template <int GRP>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  float* xs = reinterpret_cast<float*>(smem);  // [kMaxCols] permuted input
+  float* xs = reinterpret_cast<float*>(smem);  // [kMaxCols] input, xperm layout
   float* nw = xs + kMaxCols;                   // [kMaxCols] norm weight (f32)
   unsigned char* ring = reinterpret_cast<unsigned char*>(nw + kMaxCols);
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(kSlots) * kSlotBytes);
   uint64_t* empty = full + kSlots;
   __shared__ float red[kWarps];
   __shared__ float ksum[kWarps][kKsplitRows];
+  __shared__ float own[kMaxOwn];  // x' (after attention) on this CTA's residual rows
   __shared__ unsigned long long best_sm[kWarps];
   __shared__ volatile int abort_sm;  // a wait gave up (or the arguments are bad): wait no more
   __shared__ volatile int issued_sm;
-  __shared__ int is_last;
-  __shared__ int pos_ok;
+  __shared__ int tok_sm;
 
   const int c = blockIdx.x, G = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t epoch = *a.epoch;
-  const int pos = *a.pos;
+  const int pos0 = a.io[1], tok0 = a.io[0], count0 = a.io[2];
+  const uint32_t per_step = tags_per_step(a.L);
 
   if (tid == 0) {
     for (int s = 0; s < kSlots; s++) {
@@ -320,189 +523,258 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
       mbar_init(&empty[s], kWarps);
     }
     fence_mbar_init();
-    pos_ok = (pos >= 0 && pos < a.max_len && a.Hq / a.Hkv <= kMaxGrp) ? 1 : 0;
-    abort_sm = pos_ok ? 0 : 1;
+    const bool ok = pos0 >= 0 && pos0 + a.steps <= a.max_len && count0 >= 0 && count0 + a.steps <= a.tokens_cap &&
+                    tok0 >= 0 && tok0 < a.V;
+    abort_sm = ok ? 0 : 1;
     issued_sm = 0;
-    if (!pos_ok && c == 0) set_error(a.err, TB200_ERR_ARG);
+    tok_sm = tok0;
+    if (!ok && c == 0) set_error(a.io + 3, TB200_ERR_ARG);
+    trace_at(a.trace, 0, uint32_t(TB200_TRACE_OP_P_START) << 16, c, TB200_TRACE_START);
   }
   __syncthreads();
+  const bool valid = !abort_sm;  // uniform: nothing is written for invalid arguments
 
-  unsigned long long best = 0ull;
   if (warp == kWarps) {
     // ---- producer: every matrix phase's rows of this CTA, in phase order ----
-    if (lane == 0 && !abort_sm) {
+    if (lane == 0 && valid) {
       const uint64_t pol = l2_evict_first();
       int k = 0;
-      for (int layer = 0; layer <= a.L && !abort_sm; layer++)
-        for (int p = 0; p < kPerLayer && !abort_sm; p++) {
-          if (p == P_ATT) continue;
-          if (layer == a.L && p != P_QKV) break;  // the lm_head
+      for (int step = 0; step < a.steps && !abort_sm; step++)
+        for (int layer = 0; layer <= a.L && !abort_sm; layer++)
+          for (int p = 0; p < kPhases && !abort_sm; p++) {
+            if (layer == a.L && p != 0) break;  // the lm_head
+            const Slice s = slice_of(a, layer, p, c, G);
+            const int sr = stage_rows(s);
+            for (int r = 0; r < s.n && !abort_sm; r += sr, k++) {
+              const int slot = k % kSlots;
+              if (k >= kSlots && !mbar_wait(&empty[slot], ((k / kSlots) - 1) & 1, a.io + 3)) {
+                abort_sm = 1;
+                break;
+              }
+              const uint32_t bytes = uint32_t(min(sr, s.n - r)) * uint32_t(s.cols) * 2;
+              mbar_arrive_expect_tx(&full[slot], bytes);
+              bulk_g2s(ring + size_t(slot) * kSlotBytes, s.w + size_t(r) * s.cols, bytes, &full[slot], pol);
+              issued_sm = k + 1;
+            }
+          }
+    }
+  } else if (valid) {
+    // ---- consumers: the same control flow whatever the waits return ----
+    int own0, own1;
+    own_rows(a, c, G, own0, own1);
+    int ag, as, ang;
+    group_of(a, c, G, ag, as, ang);
+    int k = 0;
+    for (int step = 0; step < a.steps; step++) {
+      const uint32_t T = a.epoch + uint32_t(step) * per_step;
+      const int pos = pos0 + step;
+      // The token: the launch's input, or the previous step's choice.
+      if (step > 0) {
+        if (tid == 0) {
+          const uint64_t t0 = global_ns();
+          TW w = 0;
+          for (;;) {
+            w = ld_tagged(a.tokw);
+            if (ttag(w) == T - 1u || abort_sm || timed_out(t0, a.io + 3, &abort_sm)) break;
+          }
+          const int t = int(uint32_t(w));
+          tok_sm = t >= 0 && t < a.V ? t : 0;
+          // Acquire: the cache entries other CTAs appended in earlier steps
+          // of this launch are read after this point.
+          __threadfence();
+        }
+        named_sync(1, kConsumers);
+      }
+      const int tok = tok_sm;
+      for (int r = own0 + tid; r < own1; r += kConsumers)
+        st_tagged(a.x + r, bf16f(a.embed[size_t(tok) * a.H + r]), T);
+      uint32_t x_tag = T;  // tag of the residual stream's current version
+
+      unsigned long long best = 0ull;
+      for (int layer = 0; layer <= a.L; layer++) {
+        const Layer& Ly = a.layer[layer < a.L ? layer : 0];
+        const bool head = layer == a.L;
+        for (int p = 0; p < kPhases; p++) {
+          if (head && p != 0) break;
+          const uint32_t out_tag = phase_tag(T, layer, p);
+          const TraceAt tr{a.trace, head ? trace_base(a.L, 0, G) : trace_base(layer, p, G),
+                           (uint32_t(TB200_TRACE_OP_P_QKV + (head ? 4 : p)) << 16) | uint32_t(layer)};
+          float scale = 1.0f;
+          if (p == P_ATTO) {
+            attention_phase<GRP>(a, Ly, ag, as, ang, pos, phase_tag(T, layer, P_QKV), out_tag, xs, xs + 1024, tid,
+                                 &abort_sm, tr);
+            named_sync(1, kConsumers);
+          } else {
+            const TW* in;
+            int n_in, np = 0;
+            uint32_t in_tag;
+            const uint16_t* norm = nullptr;
+            if (p == P_QKV) {
+              in = a.x, n_in = a.H, in_tag = x_tag, norm = head ? a.norm : Ly.attn_norm;
+            } else if (p == P_GU) {
+              in = a.x, n_in = a.H, in_tag = x_tag, norm = Ly.mlp_norm, np = a.Hkv;
+            } else {
+              in = a.h, n_in = a.F, in_tag = phase_tag(T, layer, P_GU);
+            }
+            if (norm)
+              for (int i = tid * 4; i < n_in; i += kConsumers * 4) {
+                const uint2 gw = *reinterpret_cast<const uint2*>(norm + i);
+                *reinterpret_cast<float4*>(nw + i) = make_float4(bf_lo(gw.x), bf_hi(gw.x), bf_lo(gw.y), bf_hi(gw.y));
+              }
+            poll_vector(in, n_in, in_tag, a.part_o, np, a.H, phase_tag(T, layer, P_ATTO), xs,
+                        p == P_GU ? own : nullptr, own0, own1, tid, a.io + 3, &abort_sm);
+            named_sync(1, kConsumers);
+            if (tid == 0) tr.at(c, TB200_TRACE_WAITED);
+            if (norm) {  // rmsnorm (cpu.rs:85-94): x * w in place, the 1/rms scale applied to each dot
+              float ss = 0.f;
+              for (int i = tid * 4; i < n_in; i += kConsumers * 4) {
+                float4 v = *reinterpret_cast<float4*>(xs + xperm(i));
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                const float4 gw = *reinterpret_cast<const float4*>(nw + i);
+                v.x *= gw.x, v.y *= gw.y, v.z *= gw.z, v.w *= gw.w;
+                *reinterpret_cast<float4*>(xs + xperm(i)) = v;  // the float4 this thread stored
+              }
+              ss = warp_sum(ss);
+              if (lane == 0) red[warp] = ss;
+              named_sync(1, kConsumers);
+              float tot = 0.f;
+              for (int w = 0; w < kWarps; w++) tot += red[w];
+              scale = 1.0f / sqrtf(tot / float(n_in) + a.eps);
+            }
+          }
+          if (tid == 0) tr.at(c, TB200_TRACE_INPUT);
+          // One output row of a matrix phase.
+          auto emit = [&](int row, float v) {
+            if (head) {
+              if (a.logits) a.logits[row] = v;
+              const unsigned long long key = argmax_key(v, uint32_t(row));
+              best = key > best ? key : best;
+            } else if (p == P_QKV) {
+              st_tagged(a.qkv + row, v, out_tag);
+            } else if (p == P_ATTO) {
+              st_tagged(a.part_o + size_t(ag) * a.H + row, v, out_tag);
+            } else {  // down_proj: the residual add on a row this CTA owns
+              const float x1 = __fadd_rn(own[row - own0], v);
+              st_tagged(a.x + row, x1, out_tag);
+            }
+          };
+          auto emit_h = [&](int row, float gt, float up) {  // rows 2i (gate), 2i + 1 (up) -> h[i]
+            st_tagged(a.h + row / 2, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), out_tag);
+          };
           const Slice s = slice_of(a, layer, p, c, G);
           const int sr = stage_rows(s);
-          for (int r = 0; r < s.n && !abort_sm; r += sr, k++) {
+          const size_t rb = size_t(s.cols) * 2;
+          for (int r = 0; r < s.n; r += sr, k++) {
             const int slot = k % kSlots;
-            if (k >= kSlots && !mbar_wait(&empty[slot], ((k / kSlots) - 1) & 1, a.err)) {
-              abort_sm = 1;
-              break;
-            }
-            const uint32_t bytes = uint32_t(min(sr, s.n - r)) * uint32_t(s.cols) * 2;
-            mbar_arrive_expect_tx(&full[slot], bytes);
-            bulk_g2s(ring + size_t(slot) * kSlotBytes, s.w + size_t(s.r0 + r) * s.cols, bytes, &full[slot], pol);
-            issued_sm = k + 1;
-          }
-        }
-    }
-  } else {
-    // ---- consumers: the same control flow whatever the waits return ----
-    {  // embedding rows of this CTA (the same rows it owns in o and down)
-      const int tok = *a.token;
-      const int r0 = int((long long)c * a.H / G), r1 = int((long long)(c + 1) * a.H / G);
-      for (int r = r0 + tid; r < r1; r += kWarps * 32) st_tagged(a.x + r, bf16f(a.embed[size_t(tok) * a.H + r]), epoch);
-    }
-    int k = 0;
-    uint32_t x_tag = epoch;  // tag of the residual stream's current version
-    for (int layer = 0; layer <= a.L; layer++) {
-      const Layer& Ly = a.layer[layer < a.L ? layer : 0];
-      const bool head = layer == a.L;
-      for (int p = 0; p < kPerLayer; p++) {
-        if (head && p != P_QKV) break;
-        const uint32_t out_tag = epoch + phase_index(layer, p);
-        if (p == P_ATT) {
-          // pos_ok is uniform: an invalid position never reaches the cache.
-          if (c < a.Hkv && pos_ok)
-            attention_phase(a, Ly, c, pos, epoch + phase_index(layer, P_QKV), out_tag, xs, tid, &abort_sm);
-          continue;
-        }
-        const TW* in;
-        int n_in;
-        uint32_t in_tag;
-        const uint16_t* norm = nullptr;
-        if (p == P_QKV) {
-          in = a.x, n_in = a.H, in_tag = x_tag, norm = head ? a.norm : Ly.attn_norm;
-        } else if (p == P_O) {
-          in = a.att, n_in = a.Q, in_tag = epoch + phase_index(layer, P_ATT);
-        } else if (p == P_GU) {
-          in = a.x, n_in = a.H, in_tag = x_tag, norm = Ly.mlp_norm;
-        } else {
-          in = a.h, n_in = a.F, in_tag = epoch + phase_index(layer, P_GU);
-        }
-        if (norm)
-          for (int i = tid * 4; i < n_in; i += kWarps * 32 * 4) {
-            const uint2 g = *reinterpret_cast<const uint2*>(norm + i);
-            *reinterpret_cast<float4*>(nw + i) = make_float4(bf_lo(g.x), bf_hi(g.x), bf_lo(g.y), bf_hi(g.y));
-          }
-        poll_vector(in, n_in, in_tag, xs, tid, a.err, &abort_sm);
-        named_sync(1, kWarps * 32);
-        float scale = 1.0f;
-        if (norm) {
-          float ss = 0.f;
-          for (int i = tid * 4; i < n_in; i += kWarps * 32 * 4) {
-            const int at = (i & ~255) + ((i >> 2) & 1) * 128 + ((i >> 3) & 31) * 4;
-            float4 v = *reinterpret_cast<float4*>(xs + at);
-            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            const float4 g = *reinterpret_cast<const float4*>(nw + i);
-            v.x *= g.x, v.y *= g.y, v.z *= g.z, v.w *= g.w;
-            *reinterpret_cast<float4*>(xs + at) = v;  // the same thread wrote this float4 above
-          }
-          ss = warp_sum(ss);
-          if (lane == 0) red[warp] = ss;
-          named_sync(1, kWarps * 32);
-          float tot = 0.f;
-          for (int w = 0; w < kWarps; w++) tot += red[w];
-          scale = 1.0f / sqrtf(tot / float(n_in) + a.eps);
-        }
-        // One output row of a matrix phase.
-        auto emit = [&](int row, float v) {
-          if (head) {
-            if (a.logits) a.logits[row] = v;
-            const unsigned long long key = argmax_key(v, uint32_t(row));
-            best = key > best ? key : best;
-          } else if (p == P_QKV) {
-            st_tagged(a.qkv + row, v, out_tag);
-          } else {  // o_proj and down_proj: the residual add, on rows this CTA owns
-            st_tagged(a.x + row, __fadd_rn(tval(ld_tagged(a.x + row)), v), out_tag);
-          }
-        };
-        const Slice s = slice_of(a, layer, p, c, G);
-        const int sr = stage_rows(s);
-        const size_t rb = size_t(s.cols) * 2;
-        for (int r = 0; r < s.n; r += sr, k++) {
-          const int slot = k % kSlots;
-          wait_full(&full[slot], (k / kSlots) & 1, a.err, &abort_sm);
-          const unsigned char* base = ring + size_t(slot) * kSlotBytes;
-          const int nrs = min(sr, s.n - r);
-          if (s.n <= kKsplitRows) {  // all warps on every row, K split
-            float acc[kKsplitRows];
+            wait_full(&full[slot], (k / kSlots) & 1, a.io + 3, &abort_sm);
+            if (tid == 0) tr.at(c, r == 0 ? TB200_TRACE_WEIGHTS : TB200_TRACE_LAST_WEIGHTS);
+            const unsigned char* base = ring + size_t(slot) * kSlotBytes;
+            const int nrs = min(sr, s.n - r);
+            if (s.n <= kKsplitRows) {  // all warps on every row, K split
+              float acc[kKsplitRows];
 #pragma unroll
-            for (int j = 0; j < kKsplitRows; j++) acc[j] = 0.f;
-            for (int u = tid; u < s.cols / 8; u += kWarps * 32) {
-              const float* xb0 = xs + (u >> 5) * 256 + (u & 31) * 4;
-              const float4 xa = *reinterpret_cast<const float4*>(xb0);
-              const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
+              for (int j = 0; j < kKsplitRows; j++) acc[j] = 0.f;
+              for (int u = tid; u < s.cols / 8; u += kConsumers) {
+                const float* xb0 = xs + (u >> 5) * 256 + (u & 31) * 4;
+                const float4 xa = *reinterpret_cast<const float4*>(xb0);
+                const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
 #pragma unroll
-              for (int j = 0; j < kKsplitRows; j++)
-                if (j < nrs) acc[j] = dot8(*reinterpret_cast<const uint4*>(base + j * rb + size_t(u) * 16), xa, xb, acc[j]);
-            }
+                for (int j = 0; j < kKsplitRows; j++)
+                  if (j < nrs) acc[j] = dot8(*reinterpret_cast<const uint4*>(base + j * rb + size_t(u) * 16), xa, xb, acc[j]);
+              }
 #pragma unroll
-            for (int j = 0; j < kKsplitRows; j++) {
-              const float v = warp_sum(acc[j]);
-              if (lane == 0) ksum[warp][j] = v;
+              for (int j = 0; j < kKsplitRows; j++) {
+                const float v = warp_sum(acc[j]);
+                if (lane == 0) ksum[warp][j] = v;
+              }
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&empty[slot]);
+              named_sync(1, kConsumers);
+              if (warp == 0) {
+                float v = 0.f;
+                if (lane < nrs) {
+                  for (int w = 0; w < kWarps; w++) v += ksum[w][lane];
+                  v *= scale;
+                }
+                const float up = __shfl_down_sync(0xffffffffu, v, 1);
+                if (p == P_GU && !head) {
+                  if ((lane & 1) == 0 && lane < nrs) emit_h(s.r0 + r + lane, v, up);
+                } else if (lane < nrs) {
+                  emit(s.r0 + r + lane, v);
+                }
+              }
+              named_sync(1, kConsumers);  // ksum is reused
+              continue;
             }
+            // Row branch: warp w takes rows [w rpw, w rpw + nr) of the stage.
+            const int rpw = ((nrs + 2 * kWarps - 1) / (2 * kWarps)) * 2;
+            const int first = warp * rpw;
+            const int nr = max(0, min(rpw, nrs - first));
+            float acc[kMaxRowsPerWarp], acc2[kMaxRowsPerWarp];
+#pragma unroll
+            for (int j = 0; j < kMaxRowsPerWarp; j++) acc[j] = acc2[j] = 0.f;
+            if (nr > 0)
+              for (int col = lane * 8; col < s.cols; col += 256) {
+                const float* xb0 = xs + (col - lane * 8) + lane * 4;
+                const float4 xa = *reinterpret_cast<const float4*>(xb0);
+                const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
+#pragma unroll
+                for (int j = 0; j < kMaxRowsPerWarp; j++)
+                  if (j < nr) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(base + (first + j) * rb + size_t(col) * 2);
+                    acc[j] = dot4(wv.x, wv.y, xa, acc[j]);
+                    acc2[j] = dot4(wv.z, wv.w, xb, acc2[j]);
+                  }
+              }
+#pragma unroll
+            for (int j = 0; j < kMaxRowsPerWarp; j++) acc[j] = warp_sum(acc[j] + acc2[j]) * scale;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            named_sync(1, kWarps * 32);
-            if (warp == 0) {
-              float v = 0.f;
-              if (lane < nrs) {
-                for (int w = 0; w < kWarps; w++) v += ksum[w][lane];
-                v *= scale;
+            const int row0 = s.r0 + r + first;
+            if (p == P_GU && !head) {
+              if (lane < nr / 2) {
+                float gt = acc[0], up = acc[1];
+#pragma unroll
+                for (int j = 1; j < kMaxRowsPerWarp / 2; j++)
+                  if (lane == j) gt = acc[2 * j], up = acc[2 * j + 1];
+                emit_h(row0 + 2 * lane, gt, up);
               }
-              if (p == P_GU && !head) {  // rows 2i (gate), 2i + 1 (up) -> h[i]; stages hold even row counts
-                const float up = __shfl_down_sync(0xffffffffu, v, 1);
-                if ((lane & 1) == 0 && lane < nrs)
-                  st_tagged(a.h + (s.r0 + r + lane) / 2, __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), up), out_tag);
-              } else if (lane < nrs) {
-                emit(s.r0 + r + lane, v);
-              }
+            } else if (lane < nr) {
+              float v = acc[0];
+#pragma unroll
+              for (int j = 1; j < kMaxRowsPerWarp; j++)
+                if (lane == j) v = acc[j];
+              emit(row0 + lane, v);
             }
-            named_sync(1, kWarps * 32);  // ksum is reused
-            continue;
           }
-          const int first = warp * 4;
-          const int nr = max(0, min(4, nrs - first));
-          float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int col = lane * 8; col < s.cols; col += 256) {
-            const float* xb0 = xs + (col - lane * 8) + lane * 4;
-            const float4 xa = *reinterpret_cast<const float4*>(xb0);
-            const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-              if (j < nr) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(base + (first + j) * rb + size_t(col) * 2);
-                acc[j] = dot4(wv.x, wv.y, xa, acc[j]);
-                acc2[j] = dot4(wv.z, wv.w, xb, acc2[j]);
-              }
-          }
-#pragma unroll
-          for (int j = 0; j < 4; j++) acc[j] = warp_sum(acc[j] + acc2[j]) * scale;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[slot]);
-          const int row0 = s.r0 + r + first;
-          if (p == P_GU && !head) {  // rows 2i (gate), 2i + 1 (up) -> h[i]
-            if (lane < nr / 2) {
-              const float gt = lane == 0 ? acc[0] : acc[2], up = lane == 0 ? acc[1] : acc[3];
-              st_tagged(a.h + row0 / 2 + lane, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), out_tag);
-            }
-          } else if (lane < nr) {
-            float v = acc[0];
-#pragma unroll
-            for (int j = 1; j < 4; j++)
-              if (lane == j) v = acc[j];
-            emit(row0 + lane, v);
-          }
+          if (p == P_DOWN) x_tag = out_tag;
+          if (tid == 0) tr.at(c, TB200_TRACE_DONE);
+          named_sync(1, kConsumers);  // xs, nw and own are rewritten by the next phase
         }
-        if (p == P_O || p == P_DOWN) x_tag = out_tag;
-        named_sync(1, kWarps * 32);  // xs / nw are rewritten by the next phase
+      }
+
+      // The greedy token over the grid; the last CTA to arrive publishes it.
+      best = warp_umax64(best);
+      if (lane == 0) best_sm[warp] = best;
+      named_sync(1, kConsumers);
+      if (tid == 0) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kWarps; w++) b = best_sm[w] > b ? best_sm[w] : b;
+        atomicMax(a.best, b);
+        __threadfence();
+        if (atomicAdd(a.ticket, 1u) == unsigned(G - 1)) {
+          __threadfence();
+          const unsigned long long bb = atomicExch(a.best, 0ull);
+          *a.ticket = 0u;
+          const int t = int(argmax_index(bb));
+          a.io[0] = t;
+          a.io[1] = pos + 1;
+          a.io[2] = count0 + step + 1;
+          a.tokens_out[count0 + step] = t;
+          __threadfence();
+          st_tagged(a.tokw, __int_as_float(t), T + per_step - 1u);
+          trace_at(a.trace, trace_base(a.L, 1, G), uint32_t(TB200_TRACE_OP_P_TOKEN) << 16, c, TB200_TRACE_DONE);
+        }
       }
     }
   }
@@ -519,46 +791,22 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
       if (last >= 0) mbar_wait(&full[s], (last / kSlots) & 1, nullptr);
     }
   }
-
-  // lm_head argmax across the grid; the last CTA advances token, position
-  // and the tag base.
-  if (warp < kWarps) {
-    best = warp_umax64(best);
-    if (lane == 0) best_sm[warp] = best;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long b = 0ull;
-    for (int w = 0; w < kWarps; w++) b = best_sm[w] > b ? best_sm[w] : b;
-    atomicMax(a.best, b);
-    __threadfence();
-    is_last = atomicAdd(a.ticket, 1u) == unsigned(G - 1);
-  }
-  __syncthreads();
-  if (is_last && tid == 0) {
-    __threadfence();
-    const unsigned long long b = atomicExch(a.best, 0ull);
-    if (pos_ok) {  // an invalid position advances nothing (the error word says why)
-      *a.token = int(argmax_index(b));
-      *a.pos = pos + 1;
-      if (pos - a.pos0 >= 0) a.tokens[pos - a.pos0] = int(argmax_index(b));
-    }
-    *a.ticket = 0u;
-    *a.epoch = epoch + phase_index(a.L, 0) + 1u;
-  }
 }
 
-// One step on `sms` CTAs, all resident (the kernel's shared memory allows
+// One launch on `sms` CTAs, all resident (the kernel's shared memory allows
 // one per SM), as a cooperative launch.
-cudaError_t launch_step(const Args& a, int sms, cudaStream_t s) {
+cudaError_t launch(const Args& a, int sms, cudaStream_t s) {
   static bool init[64] = {};  // per device ordinal
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  void (*kern)(Args) = a.grp == 1 ? step_kernel<1> : a.grp == 2 ? step_kernel<2> : step_kernel<4>;
   if (!init[dev]) {
-    e = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
-    if (e != cudaSuccess) return e;
+    for (void (*k)(Args) : {step_kernel<1>, step_kernel<2>, step_kernel<4>}) {
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmemBytes));
+      if (e != cudaSuccess) return e;
+    }
     init[dev] = true;
   }
   cudaLaunchConfig_t cfg{};
@@ -571,109 +819,120 @@ cudaError_t launch_step(const Args& a, int sms, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, step_kernel, a);
-}
-
-// The arguments for model m and state st (sequence 0, f32 cache).
-// `tagged` holds 2 * H + 2 * Q + 2 * KV + F words (zeroed once); `ctl` 6
-// words: [0] tag base, which must start at 1 (a zeroed word carries tag 0,
-// so a first step at tag base 0 would take the zeros for its embedding),
-// [2..3] argmax key and [4] ticket, zeroed once.
-bool make_args(const tb200_model* m, const tb200_state* st, TW* tagged, uint32_t* ctl, float* logits, Args* out) {
-  const tb200_config& c = m->c;
-  if (!st->kv_f32 || c.num_hidden_layers > size_t(kMaxLayers) || c.head_dim != size_t(kHd) ||
-      c.intermediate_size > size_t(kMaxCols) || m->q_dim > size_t(kMaxCols) || c.hidden_size > size_t(kMaxCols) ||
-      c.num_attention_heads / c.num_key_value_heads > size_t(kMaxGrp))
-    return false;  // unsupported shape or cache type
-  Args a{};
-  const size_t per = c.num_key_value_heads * st->max_len * kHd;  // one cache tensor of one layer
-  for (size_t l = 0; l < c.num_hidden_layers; l++) {
-    const FusedLayer& L = m->layers[l];
-    float* base = reinterpret_cast<float*>(st->kv) + l * 2 * per;
-    a.layer[l] = Layer{L.wqkv, L.wo, L.wgu, L.wd, L.attn_norm, L.mlp_norm, L.q_norm, L.k_norm, base, base + per};
-  }
-  a.L = int(c.num_hidden_layers), a.H = int(c.hidden_size), a.Q = int(m->q_dim), a.KV = int(m->kv_dim);
-  a.F = int(c.intermediate_size), a.V = int(c.vocab_size);
-  a.Hq = int(c.num_attention_heads), a.Hkv = int(c.num_key_value_heads);
-  a.eps = c.rms_norm_eps;
-  a.embed = m->embed, a.lm_head = m->lm_head, a.norm = m->norm;
-  a.rope = st->rope, a.max_len = int(st->max_len);
-  a.x = tagged, a.qkv = a.x + a.H, a.att = a.qkv + a.Q + 2 * a.KV, a.h = a.att + a.Q;
-  a.token = st->io + 0, a.pos = st->io + 1, a.err = st->io + 3;
-  a.epoch = ctl, a.best = reinterpret_cast<unsigned long long*>(ctl + 2), a.ticket = ctl + 4;
-  a.logits = logits;
-  *out = a;
-  return true;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 }  // namespace tb::persist
 
-int tb200_decode_persistent(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, size_t steps,
-                            uint32_t* tokens_out, float* logits_out) {
-  namespace P = tb::persist;
-  ARG_CHECK(m && st && st->m == m, "bad model/state");
-  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
-  ARG_CHECK(tokens_out || steps == 0, "null output");
-  ARG_CHECK(pos + steps <= st->max_len, "tokens past the end of the cache");
-  ARG_CHECK(token < m->c.vocab_size, "token past the vocabulary");
-  ARG_CHECK(pos + steps <= size_t(P::kMaxCtx), "persistent decode runs contexts up to " + std::to_string(P::kMaxCtx) +
-                                                   " positions");
-  if (int rc = rt::use(m->dev)) return rc;
-  P::Args probe;
-  ARG_CHECK(P::make_args(m, st, nullptr, nullptr, nullptr, &probe),
-            "persistent decode needs an f32 cache, head_dim 128, widths up to 3072, at most 4 query heads per "
-            "kv head and at most 64 layers");
+namespace rt {
+
+namespace P = tb::persist;
+
+// Why model m and state st cannot run the persistent step ("" when they can).
+std::string persist_unsupported(const tb200_model* m, const tb200_state* st) {
+  const tb200_config& c = m->c;
+  const int sms = m->dev->sms;
+  if (m->tp) return "persistent decode runs unsharded models (no tensor parallelism)";
+  if (st->n_seqs != 1) return "persistent decode runs one-sequence states";
+  if (c.num_hidden_layers > size_t(P::kMaxLayers)) return "persistent decode runs at most 64 layers";
+  if (c.head_dim != size_t(P::kHd)) return "persistent decode needs head_dim 128";
+  if (c.intermediate_size > size_t(P::kMaxCols) || m->q_dim > size_t(P::kMaxCols) ||
+      c.hidden_size > size_t(P::kMaxCols))
+    return "persistent decode needs hidden, FFN and query widths up to 3072";
+  const size_t grp = c.num_attention_heads / c.num_key_value_heads;
+  if (grp > size_t(P::kMaxGrp) || c.num_key_value_heads > size_t(P::kMaxKv))
+    return "persistent decode needs at most 4 query heads per kv head and at most 8 kv heads";
+  const size_t G = std::min<size_t>({size_t(sms), c.hidden_size, c.intermediate_size, m->q_dim + 2 * m->kv_dim,
+                                     c.vocab_size});
+  if (G < c.num_key_value_heads || (c.hidden_size + G - 1) / G > size_t(P::kMaxOwn))
+    return "persistent decode: this GPU's SM count does not fit the model's kv groups and residual rows";
+  return "";
+}
+
+// The state's persistent-step scratch, allocated on first use: tagged words
+// (zeroed once; tags only grow, so stale words never match) and the argmax
+// key and ticket.
+static size_t persist_grid(const tb200_model* m) {
+  const tb200_config& c = m->c;
+  return std::min<size_t>({size_t(m->dev->sms), c.hidden_size, c.intermediate_size, m->q_dim + 2 * m->kv_dim,
+                           c.vocab_size});
+}
+
+static int persist_prepare(tb200_state* st) {
+  if (st->ps_words) return TB200_OK;
+  const tb200_model* m = st->m;
+  const tb200_config& c = m->c;
+  const size_t grp = c.num_attention_heads / c.num_key_value_heads;
+  const size_t nsplit = (persist_grid(m) + c.num_key_value_heads - 1) / c.num_key_value_heads;
+  const size_t words = c.hidden_size + m->q_dim + 2 * m->kv_dim + c.intermediate_size +
+                       c.num_key_value_heads * c.hidden_size + c.num_key_value_heads * nsplit * grp * P::kPartWords + 4;
+  cudaStream_t s = m->dev->stream;
+  CUDA_TRY(cudaMalloc(&st->ps_words, words * 8));
+  CUDA_TRY(cudaMemsetAsync(st->ps_words, 0, words * 8, s));
+  CUDA_TRY(cudaMalloc(&st->ps_ctl, 16));
+  CUDA_TRY(cudaMemsetAsync(st->ps_ctl, 0, 16, s));
+  st->ps_nwords = words;
+  st->ps_epoch = 1;  // a zeroed word carries tag 0
+  return TB200_OK;
+}
+
+// Enqueues `steps` greedy steps from the token and position in st->io as
+// one launch (io[2] counts generated tokens into st->tokens_out); the last
+// step's logits go to st->logits when `logits`.
+int persist_enqueue(tb200_state* st, size_t steps, bool logits) {
   if (!steps) return TB200_OK;
+  if (int rc = persist_prepare(st)) return rc;
+  const tb200_model* m = st->m;
   const tb200_config& c = m->c;
   cudaStream_t s = m->dev->stream;
-  const size_t words = 2 * c.hidden_size + 2 * m->q_dim + 2 * m->kv_dim + c.intermediate_size;
-  P::TW* tagged = nullptr;
-  uint32_t* ctl = nullptr;
-  int* toks = nullptr;
-  float* logits = nullptr;
-  auto release = [&](int rc) {
-    cudaStreamSynchronize(s);
-    cudaFree(tagged);
-    cudaFree(ctl);
-    cudaFree(toks);
-    cudaFree(logits);
-    return rc;
-  };
-  cudaError_t e = cudaMalloc(&tagged, words * sizeof(P::TW));
-  if (e == cudaSuccess) e = cudaMalloc(&ctl, 6 * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMalloc(&toks, steps * sizeof(int));
-  if (e == cudaSuccess && logits_out) e = cudaMalloc(&logits, c.vocab_size * sizeof(float));
-  if (e == cudaSuccess) e = cudaMemsetAsync(tagged, 0, words * sizeof(P::TW), s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(ctl, 0, 6 * sizeof(uint32_t), s);
-  int* stage = st->io_host + 2 * st->max_len;  // pinned
-  stage[0] = int(token);
-  stage[1] = int(pos);
-  stage[2] = 0;
-  stage[3] = 0;
-  if (e == cudaSuccess) e = cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s);
-  static const uint32_t one = 1u;  // the first tag base (a zeroed word carries tag 0)
-  if (e == cudaSuccess) e = cudaMemcpyAsync(ctl, &one, sizeof(one), cudaMemcpyHostToDevice, s);
-  if (e != cudaSuccess) return release(rt::fail(TB200_ERR_CUDA, std::string("persistent decode: ") + cudaGetErrorString(e)));
-  P::Args a;
-  P::make_args(m, st, tagged, ctl, logits, &a);
-  a.tokens = toks;
-  a.pos0 = int(pos);
-  // Every CTA owns rows of every matrix phase (no CTA can run a phase ahead
-  // of a vector it has yet to read; see the kernel's exchange rule).
-  const int grid = int(std::min<size_t>({size_t(m->dev->sms), c.hidden_size, c.intermediate_size,
-                                         m->q_dim + 2 * m->kv_dim, c.vocab_size}));
-  for (size_t i = 0; i < steps && e == cudaSuccess; i++) {
-    e = P::launch_step(a, grid, s);
-    if (e == cudaSuccess && logits_out)
-      e = cudaMemcpyAsync(logits_out + i * c.vocab_size, logits, c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost,
-                          s);
+  const uint32_t per = P::tags_per_step(int(c.num_hidden_layers));
+  if (st->ps_dirty) {  // a launch that gave up may have left the grid's argmax half done
+    CUDA_TRY(cudaMemsetAsync(st->ps_ctl, 0, 16, s));
+    st->ps_dirty = false;
   }
-  if (e == cudaSuccess) e = cudaMemcpyAsync(tokens_out, toks, steps * sizeof(int), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(stage, st->io, 4 * sizeof(int), cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return release(rt::fail(TB200_ERR_CUDA, std::string("persistent decode: ") + cudaGetErrorString(e)));
-  if (stage[3] == TB200_ERR_TIMEOUT) return release(rt::fail(TB200_ERR_TIMEOUT, "a kernel's bounded wait timed out"));
-  if (stage[3] != 0) return release(rt::fail(TB200_ERR_ARG, "persistent decode: the kernel rejected its input"));
-  st->host_pos = pos + steps;
-  return release(TB200_OK);
+  if (uint64_t(st->ps_epoch) + uint64_t(per) * steps >= 0xFFFF0000ull) {  // tags would wrap: start over
+    CUDA_TRY(cudaMemsetAsync(st->ps_words, 0, st->ps_nwords * 8, s));
+    st->ps_epoch = 1;
+  }
+  P::Args a{};
+  const size_t eb = st->kv_f32 ? 4 : 2;
+  const size_t per_layer = 2 * c.num_key_value_heads * st->max_len * c.head_dim;  // elements
+  for (size_t l = 0; l < c.num_hidden_layers; l++) {
+    const FusedLayer& L = m->layers[l];
+    unsigned char* kb = st->kv + l * per_layer * eb;
+    a.layer[l] = P::Layer{L.wqkv, L.wo_packed, L.wgu, L.wd, L.attn_norm, L.mlp_norm, L.q_norm, L.k_norm, kb,
+                          kb + per_layer / 2 * eb};
+  }
+  a.L = int(c.num_hidden_layers), a.H = int(c.hidden_size), a.Q = int(m->q_dim), a.KV = int(m->kv_dim);
+  a.F = int(c.intermediate_size), a.V = int(c.vocab_size);
+  a.Hq = int(c.num_attention_heads), a.Hkv = int(c.num_key_value_heads), a.grp = a.Hq / a.Hkv;
+  a.eps = c.rms_norm_eps;
+  a.embed = m->embed, a.lm_head = m->lm_head, a.norm = m->norm;
+  a.rope = st->rope, a.max_len = int(st->max_len), a.kv_f32 = st->kv_f32;
+  P::TW* w = static_cast<P::TW*>(st->ps_words);
+  a.x = w, a.qkv = a.x + a.H, a.h = a.qkv + a.Q + 2 * a.KV, a.part_o = a.h + a.F;
+  const int grid = int(persist_grid(m));
+  a.nsplit = (grid + a.Hkv - 1) / a.Hkv;
+  a.part_att = a.part_o + size_t(a.Hkv) * a.H;
+  a.tokw = a.part_att + size_t(a.Hkv) * a.nsplit * a.grp * P::kPartWords;
+  a.io = st->io, a.tokens_out = st->tokens_out, a.tokens_cap = int(st->max_len);
+  a.best = reinterpret_cast<unsigned long long*>(st->ps_ctl);
+  a.ticket = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(st->ps_ctl) + 8);
+  a.logits = logits ? st->logits : nullptr;
+  a.epoch = st->ps_epoch;
+  a.steps = int(steps);
+  a.trace = st->trace;
+  st->ps_epoch += per * uint32_t(steps);
+  st->ps_grid = grid;
+  if (st->trace.rec) st->ps_traced = true;
+  cudaError_t e = P::launch(a, grid, s);
+  if (e != cudaSuccess) return fail(TB200_ERR_CUDA, std::string("persistent decode: ") + cudaGetErrorString(e));
+  return TB200_OK;
 }
+
+// Trace slots one persistent step uses.
+size_t persist_trace_slots(const tb200_state* st) {
+  return (3 + 4 * st->m->c.num_hidden_layers) * size_t(std::max(st->ps_grid, st->m->dev->sms)) * tb::kTraceEvents;
+}
+
+}  // namespace rt

@@ -826,6 +826,7 @@ int finish(tb200_state* st) {
   int* back = st->io_host + 2 * st->max_len;
   CUDA_TRY(cudaMemcpyAsync(back, st->io, 4 * sizeof(int), cudaMemcpyDeviceToHost, s));
   CUDA_TRY(cudaStreamSynchronize(s));
+  if (back[3] != 0) st->ps_dirty = true;
   if (back[3] == TB200_ERR_TIMEOUT) return fail(TB200_ERR_TIMEOUT, "a kernel's bounded wait timed out");
   if (back[3] != 0) return fail(TB200_ERR_ARG, "a kernel rejected its input (token or position out of range)");
   return TB200_OK;
@@ -914,6 +915,7 @@ int state_create(tb200_model* m, size_t n_seqs, size_t max_len, int kv_dtype, tb
       tb200_state_free(st);
       return rc;
     }
+    if (rt::persist_unsupported(m, st).empty()) st->decode_mode = TB200_DECODE_PERSISTENT;
   }
   *out = st;
   return TB200_OK;
@@ -940,7 +942,7 @@ int tb200_state_free(tb200_state* st) {
   rt::free_batch(st);
   void* ptrs[] = {st->kv, st->rope, st->x, st->qkv, st->att, st->h, st->logits, st->part, st->attn_ticket,
                   st->mv_partial, st->mv_ticket, st->io, st->tokens_out, st->x2, st->part_o, st->part_tp,
-                  st->part_tp2};
+                  st->part_tp2, st->ps_words, st->ps_ctl};
   for (void* p : ptrs) cudaFree(p);
   if (st->io_host) cudaFreeHost(st->io_host);
   tb200_model* m = st->m;
@@ -972,7 +974,11 @@ int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_
     stage[0] = int(tokens[i]);
     stage[1] = int(pos + i);
     CUDA_TRY(cudaMemcpyAsync(st->io, stage, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-    CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
+    if (st->decode_mode == TB200_DECODE_PERSISTENT) {
+      if (int rc = rt::persist_enqueue(st, 1, logits != nullptr)) return rc;
+    } else {
+      CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
+    }
   }
   if (logits) CUDA_TRY(cudaMemcpyAsync(logits, st->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
@@ -996,7 +1002,11 @@ int tb200_generate(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, 
   stage[2] = 0;
   stage[3] = 0;
   CUDA_TRY(cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s));
-  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
+  if (st->decode_mode == TB200_DECODE_PERSISTENT) {
+    if (int rc = rt::persist_enqueue(st, steps, false)) return rc;
+  } else {
+    for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
+  }
   static_assert(sizeof(uint32_t) == sizeof(int), "token width");
   CUDA_TRY(cudaMemcpyAsync(out, st->tokens_out, steps * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
@@ -1012,7 +1022,60 @@ int tb200_decode_enqueue(tb200_model* m, tb200_state* st, uint32_t token, size_t
   if (int rc = use(m->dev)) return rc;
   tb::launch_set_io(m->dev->stream, st->io, int(token), int(pos));
   if (int rc = launched("set_io")) return rc;
-  for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), m->dev->stream));
+  if (st->decode_mode == TB200_DECODE_PERSISTENT) {
+    if (int rc = rt::persist_enqueue(st, steps, false)) return rc;
+  } else {
+    for (size_t i = 0; i < steps; i++) CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), m->dev->stream));
+  }
+  st->host_pos = pos + steps;
+  return TB200_OK;
+}
+
+int tb200_state_set_decode(tb200_state* st, int mode) {
+  ARG_CHECK(st, "null state");
+  ARG_CHECK(mode == TB200_DECODE_FUSED || mode == TB200_DECODE_PERSISTENT, "unknown decode mode");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
+  if (mode == TB200_DECODE_PERSISTENT) {
+    const std::string why = rt::persist_unsupported(st->m, st);
+    ARG_CHECK(why.empty(), why);
+  }
+  st->decode_mode = mode;
+  return TB200_OK;
+}
+
+int tb200_state_decode(const tb200_state* st) { return st ? st->decode_mode : -1; }
+
+int tb200_decode_persistent(tb200_model* m, tb200_state* st, uint32_t token, size_t pos, size_t steps,
+                            uint32_t* tokens_out, float* logits_out) {
+  ARG_CHECK(m && st && st->m == m, "bad model/state");
+  ARG_CHECK(st->n_seqs == 1, "the single-token path runs one-sequence states");
+  ARG_CHECK(tokens_out || steps == 0, "null output");
+  ARG_CHECK(pos + steps <= st->max_len, "tokens past the end of the cache");
+  ARG_CHECK(token < m->c.vocab_size, "token past the vocabulary");
+  {
+    const std::string why = rt::persist_unsupported(m, st);
+    ARG_CHECK(why.empty(), why);
+  }
+  if (int rc = use(m->dev)) return rc;
+  if (!steps) return TB200_OK;
+  cudaStream_t s = m->dev->stream;
+  int* stage = st->io_host + 2 * st->max_len;
+  stage[0] = int(token);
+  stage[1] = int(pos);
+  stage[2] = 0;
+  stage[3] = 0;
+  CUDA_TRY(cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s));
+  if (!logits_out) {
+    if (int rc = rt::persist_enqueue(st, steps, false)) return rc;
+  } else {
+    for (size_t i = 0; i < steps; i++) {
+      if (int rc = rt::persist_enqueue(st, 1, true)) return rc;
+      CUDA_TRY(cudaMemcpyAsync(logits_out + i * m->c.vocab_size, st->logits, m->c.vocab_size * 4,
+                               cudaMemcpyDeviceToHost, s));
+    }
+  }
+  CUDA_TRY(cudaMemcpyAsync(tokens_out, st->tokens_out, steps * 4, cudaMemcpyDeviceToHost, s));
+  if (int rc = finish(st)) return rc;
   st->host_pos = pos + steps;
   return TB200_OK;
 }
@@ -1035,6 +1098,7 @@ int tb200_trace_start(tb200_state* st, size_t capacity) {
   CUDA_TRY(cudaMalloc(&st->trace.rec, capacity * sizeof(tb::TraceRec)));
   CUDA_TRY(cudaMemset(st->trace.rec, 0, capacity * sizeof(tb::TraceRec)));
   st->trace.cap = unsigned(capacity);
+  st->ps_traced = false;
   rt::drop_batch_graph(st);  // recaptured with the buffer on next use
   return st->n_seqs == 1 ? build_graph(st) : TB200_OK;
 }
@@ -1045,7 +1109,7 @@ int tb200_trace_stop(tb200_state* st, tb200_trace_record* out, size_t cap, size_
   static_assert(sizeof(tb200_trace_record) == sizeof(tb::TraceRec), "trace record layout");
   if (int rc = use(st->dev)) return rc;
   CUDA_TRY(cudaStreamSynchronize(st->dev->stream));
-  *n = st->trace_next;
+  *n = st->ps_traced ? rt::persist_trace_slots(st) : st->trace_next;
   const size_t k = std::min<size_t>(st->trace.cap, cap);
   if (k) CUDA_TRY(cudaMemcpy(out, st->trace.rec, k * sizeof(tb::TraceRec), cudaMemcpyDeviceToHost));
   cudaFree(st->trace.rec);

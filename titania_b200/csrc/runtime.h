@@ -101,6 +101,15 @@ struct tb200_state {
   uint32_t trace_next = 0;  // next free record slot while capturing
   cudaGraphExec_t graph = nullptr;        // positions >= kAttnOMaxCtx
   cudaGraphExec_t graph_short = nullptr;  // positions < kAttnOMaxCtx (fused attention + o_proj)
+  // ---- single-token path as one persistent kernel (persist.cu)
+  int decode_mode = TB200_DECODE_FUSED;  // TB200_DECODE_*: what single-token steps run
+  void* ps_words = nullptr;   // tagged words the phases exchange, zeroed once
+  size_t ps_nwords = 0;
+  void* ps_ctl = nullptr;     // argmax key, ticket
+  uint32_t ps_epoch = 0;      // tag base of the next launch
+  int ps_grid = 0;            // CTAs of the last launch
+  bool ps_traced = false;     // a persistent launch ran while tracing
+  bool ps_dirty = false;      // a launch may have stopped mid-step: reset the argmax key and ticket first
 
   // ---- many-token / many-sequence path (forward.cu), allocated on first use
   int cap = 0;                 // tokens per pass
@@ -142,6 +151,14 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
                    uint32_t* next);
 // Sums `n` floats at `buf` over the tensor-parallel group, on stream `s`.
 int tp_allreduce(tb200_tp* tp, float* buf, size_t n, cudaStream_t s);
+
+// persist.cu: why the persistent single-token step cannot run model m with
+// state st ("" when it can); enqueues `steps` greedy steps from st->io as
+// one launch (the last step's logits to st->logits when `logits`); the trace
+// slots one step uses.
+std::string persist_unsupported(const tb200_model* m, const tb200_state* st);
+int persist_enqueue(tb200_state* st, size_t steps, bool logits);
+size_t persist_trace_slots(const tb200_state* st);
 
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);

@@ -268,8 +268,8 @@ class Model:
             _lib.lib().tb200_model_free(self._h)
         self._h = None
 
-    def state(self, max_len: int, kv: str = "f32") -> "State":
-        return State(self, max_len, kv)
+    def state(self, max_len: int, kv: str = "f32", decode: str | None = None) -> "State":
+        return State(self, max_len, kv, decode)
 
     def forward(self, state: "State", tokens, pos: int, logits: bool = True, out=None):
         """Model::forward (model/model.rs:83-91): the logits for the token after
@@ -294,9 +294,9 @@ class Model:
         return out.tolist()
 
     def decode_persistent(self, state: "State", token: int, pos: int, steps: int, logits: bool = False):
-        """`generate` with one persistent kernel per step (f32 cache states):
-        the `steps` chosen tokens, and with logits=True also their
-        [steps][vocab] logits."""
+        """`generate` through the persistent kernel whatever the state's
+        decode mode: the `steps` chosen tokens, and with logits=True also
+        their [steps][vocab] logits (one launch per step then)."""
         out = np.empty(steps, dtype=np.uint32)
         lg = np.empty((steps, self.config.vocab_size), dtype=np.float32) if logits else None
         call("tb200_decode_persistent", self._h, state._h, int(token), int(pos), int(steps),
@@ -359,6 +359,7 @@ class Model:
 
 
 KV_TYPES = {"bf16": 0, "f32": 1}
+DECODE_MODES = {"fused": 0, "persistent": 1}
 
 
 class State:
@@ -366,7 +367,7 @@ class State:
     holds f32 like the reference (default) or bf16, which halves the bytes
     attention reads at long contexts at the cost of rounding K and V."""
 
-    def __init__(self, model: Model, max_len: int, kv: str = "f32"):
+    def __init__(self, model: Model, max_len: int, kv: str = "f32", decode: str | None = None):
         if kv not in KV_TYPES:
             raise ValueError(f"kv must be one of {sorted(KV_TYPES)}")
         h = ctypes.c_void_p()
@@ -375,6 +376,21 @@ class State:
         self.model = model
         self.max_len = max_len
         self.kv = kv
+        if decode is not None:
+            self.decode = decode
+
+    @property
+    def decode(self) -> str:
+        """What single-token steps run: "persistent" (one kernel per launch,
+        the default where the model allows it) or "fused" (2 + 5 * layers
+        kernels per step from a CUDA graph)."""
+        return {v: k for k, v in DECODE_MODES.items()}[_lib.lib().tb200_state_decode(self._h)]
+
+    @decode.setter
+    def decode(self, mode: str) -> None:
+        if mode not in DECODE_MODES:
+            raise ValueError(f"decode must be one of {sorted(DECODE_MODES)}")
+        call("tb200_state_set_decode", self._h, DECODE_MODES[mode])
 
     def __del__(self):
         if getattr(self, "_h", None) and not sys.is_finalizing():

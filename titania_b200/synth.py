@@ -38,7 +38,19 @@ TINY = dict(
     num_key_value_heads=2, head_dim=128, rms_norm_eps=1e-06, rope_theta=1000000.0,
     vocab_size=1024, tie_word_embeddings=True,
 )
-CONFIGS = {"qwen3-0.6b": QWEN3_0_6B, "qwen3-4b": QWEN3_4B, "tiny": TINY}
+# Two layers of Qwen3-0.6B (every matrix its real shape, lm_head included):
+# the single-token kernels see the real per-CTA row counts at a fraction of
+# the oracle's time.
+QWEN3_0_6B_2L = dict(QWEN3_0_6B, num_hidden_layers=2)
+# Two layers with four query heads per kv head (Qwen3-4B's grouping) and a
+# hidden size that gives every CTA more than eight residual rows.
+WIDE_GQA4 = dict(
+    hidden_size=1536, intermediate_size=2048, num_hidden_layers=2, num_attention_heads=16,
+    num_key_value_heads=4, head_dim=128, rms_norm_eps=1e-06, rope_theta=1000000.0,
+    vocab_size=4096, tie_word_embeddings=True,
+)
+CONFIGS = {"qwen3-0.6b": QWEN3_0_6B, "qwen3-4b": QWEN3_4B, "tiny": TINY, "qwen3-0.6b-2l": QWEN3_0_6B_2L,
+           "wide-gqa4": WIDE_GQA4}
 
 
 def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
