@@ -7,22 +7,27 @@
 // A step has four phases per layer and the lm_head:
 //   QKV    qkv   = W_qkv · rmsnorm(x)                      rows split over CTAs
 //   ATT_O  CTA (kv group g, member s): QK-norm, RoPE and K/V append of group
-//          g, its attention, then rows of part_o[g] = W_o[:, cols of g] · att_g
-//   GU     x' = x + Σ_g part_o[g] (g in order);  h = silu(W_g·n(x')) * (W_u·n(x'))
+//          g, its attention, then rows of part_o[g] = W_o[:, cols of g] · att_g;
+//          then each CTA sums x' = x + Σ_g part_o[g] (g in order) on its own
+//          residual rows
+//   GU     h = silu(W_g · rmsnorm(x')) * (W_u · rmsnorm(x'))
 //   DOWN   x  = x' + W_d · h                               rows owned by CTAs
 //   LM     logits = W_lm · rmsnorm(x); greedy token over the grid
 // Phases exchange vectors as 64-bit (tag << 32 | value bits) words in global
 // memory: a reader polls the words it needs until each carries the tag of
 // the current (step, layer, phase), so data and synchronisation cost one L2
-// round trip together and no grid barrier exists. Attention over a context
-// of up to kRedundantCtx positions is computed by every member of the kv
-// group (no exchange); past it, member s attends to its share of the
-// positions and the members exchange and merge their partial results.
+// round trip together and no grid barrier exists. The vectors every CTA
+// reads (x, h) are written in kRep copies, CTA c reading copy c % kRep, which
+// spreads the polling over more L2 lines. Attention over a context of up to
+// kRedundantCtx positions is computed by every member of the kv group (no
+// exchange); past it, member s attends to its share of the positions and
+// the members exchange and merge their partial results.
 //
 // One producer warp streams this CTA's weight rows of every phase of every
 // step through a shared-memory ring with cp.async.bulk, never draining at a
 // phase boundary: while the consumers wait for a vector, the next phases'
-// weights keep arriving.
+// weights keep arriving. What each CTA computes (its rows of every phase,
+// their ring stages) is planned once per launch.
 //
 // Every wait is bounded, and no control flow depends on a wait's outcome:
 // the first wait that gives up sets the CTA's abort flag and the error word,
@@ -46,15 +51,15 @@ constexpr int kSlots = 3;
 constexpr int kMaxLayers = 64;
 constexpr int kHd = 128;
 constexpr int kMaxCols = 3072;       // widest input vector
-constexpr int kKsplitRows = 8;       // a slice of at most this many rows splits K over all warps
-constexpr int kMaxRowsPerWarp = 8;
+constexpr int kMaxRowsPerWarp = 8;   // rows a warp takes in one ring stage
 constexpr int kMaxGrp = 4;           // query heads per kv head
-constexpr int kMaxKv = 8;            // kv heads (o_proj partial vectors summed by GU)
+constexpr int kMaxKv = 8;            // kv heads (o_proj partial vectors summed per residual row)
 constexpr int kMaxOwn = 32;          // residual rows a CTA owns
 constexpr int kAttnPer = 8;          // cached positions per warp held in registers at a time
 constexpr int kRedundantCtx = 256;   // contexts up to this: every group member attends over all of it
 constexpr int kPartWords = 132;      // a member's partial per head: acc[128], max, sum, 2 pad
-constexpr size_t kSmemBytes = size_t(2) * kMaxCols * 4 + size_t(kSlots) * kSlotBytes + 2 * kSlots * 8;
+constexpr int kRep = 4;              // copies of the vectors every CTA reads (x, h): CTA c reads copy c % kRep
+constexpr size_t kSmemBytes = size_t(kMaxCols) * 2 * 4 + size_t(kSlots) * kSlotBytes + 2 * kSlots * 8;
 
 using TW = unsigned long long;  // a tagged word
 
@@ -71,8 +76,9 @@ struct Args {
   const uint16_t *embed, *lm_head, *norm;
   const float* rope;  // [max_len][128] (cos, sin) pairs
   int max_len, kv_f32;
-  TW *x, *qkv, *h, *part_o, *part_att, *tokw;  // [H], [Q+2KV], [F], [Hkv][H], [Hkv][nsplit][grp][kPartWords], [4]
-  int nsplit;  // most members of a kv group (ceil(CTAs / Hkv))
+  // x [kRep][H], qkv [Q+2KV], h [kRep][F], part_o [Hkv][H], part_att [Hkv][nsplit][grp][kPartWords], tokw [4]
+  TW *x, *qkv, *h, *part_o, *part_att, *tokw;
+  int nsplit;         // most members of a kv group (ceil(CTAs / Hkv))
   int* io;            // [0] token, [1] position, [2] generated-token counter, [3] error word
   int* tokens_out;    // [tokens_cap]: generated tokens by counter
   int tokens_cap;
@@ -84,7 +90,8 @@ struct Args {
   Trace trace;
 };
 
-enum { P_QKV = 0, P_ATTO = 1, P_GU = 2, P_DOWN = 3, kPhases = 4 };
+// Matrix phases; K_LM is the lm_head, after the last layer.
+enum { K_QKV = 0, K_ATTO = 1, K_GU = 2, K_DOWN = 3, K_LM = 4, kKinds = 5, kPhases = 4 };
 
 // Tags of one step, relative to its base: 0 the embedded token's x, then
 // 1 + 4 layer + phase, then the chosen token.
@@ -92,14 +99,18 @@ __host__ __device__ constexpr uint32_t tags_per_step(int L) { return 2u + 4u * u
 __device__ __forceinline__ uint32_t phase_tag(uint32_t base, int layer, int p) {
   return base + 1u + 4u * uint32_t(layer) + uint32_t(p);
 }
-// Trace slot group of a phase: 0 the step's start, 1 + 4 layer + phase, then the lm_head.
+// Trace slot group of a phase: 0 the step's start, 1 + 4 layer + phase, then
+// the lm_head and the token.
 __device__ __forceinline__ uint32_t trace_base(int layer, int p, int G) {
   return (1u + 4u * uint32_t(layer) + uint32_t(p)) * uint32_t(G) * kTraceEvents;
 }
 
-struct Slice {
-  const uint16_t* w;  // first row of the slice
-  int r0, n, cols;    // output rows [r0, r0 + n) of the phase's vector
+// One CTA's share of a matrix phase: output rows [r0, r0 + n) of `cols`
+// columns, the first at row `w0` of the phase's matrix, in `nst` ring stages
+// of `sr` rows (the last may hold fewer).
+struct Plan {
+  int r0, n, cols, sr, nst;
+  long long w0;
 };
 
 // The kv group and member of CTA c in ATT_O, and the group's member count.
@@ -109,48 +120,45 @@ __device__ __forceinline__ void group_of(const Args& a, int c, int G, int& g, in
   ng = (G - g + a.Hkv - 1) / a.Hkv;
 }
 
-// This CTA's rows of a matrix phase (layer == L: the lm_head).
-__device__ __forceinline__ Slice slice_of(const Args& a, int layer, int p, int c, int G) {
-  const Layer& Ly = a.layer[layer < a.L ? layer : 0];
-  if (layer == a.L) {
-    const int r0 = int((long long)c * a.V / G), r1 = int((long long)(c + 1) * a.V / G);
-    return Slice{a.lm_head + size_t(r0) * a.H, r0, r1 - r0, a.H};
-  }
-  if (p == P_ATTO) {
-    int g, s, ng;
-    group_of(a, c, G, g, s, ng);
-    const int cols = a.grp * kHd;
-    const int r0 = s * a.H / ng, r1 = (s + 1) * a.H / ng;
-    return Slice{Ly.wo_g + (size_t(g) * a.H + r0) * cols, r0, r1 - r0, cols};
-  }
-  int rows, cols, align;
-  const uint16_t* w;
-  if (p == P_QKV) {
-    w = Ly.wqkv, rows = a.Q + 2 * a.KV, cols = a.H, align = 1;
-  } else if (p == P_GU) {
-    w = Ly.wgu, rows = 2 * a.F, cols = a.H, align = 2;
-  } else {
-    w = Ly.wd, rows = a.H, cols = a.F, align = 1;
-  }
-  const int units = rows / align;
-  const int r0 = int((long long)c * units / G) * align;
-  const int r1 = int((long long)(c + 1) * units / G) * align;
-  return Slice{w + size_t(r0) * cols, r0, r1 - r0, cols};
-}
-
-// Rows per ring stage: a slice of <= kKsplitRows rows splits K over all
-// warps; longer slices give each warp up to kMaxRowsPerWarp rows. Even, so
-// that a gate/up pair never straddles two stages.
-__device__ __forceinline__ int stage_rows(const Slice& s) {
-  const int fit = (kSlotBytes / (s.cols * 2)) & ~1;
-  if (s.n <= kKsplitRows) return min(s.n, fit);
-  return min(fit, kWarps * kMaxRowsPerWarp);
-}
-
-// Residual rows CTA c owns (its embedding, down_proj rows and lm_head-free).
+// Residual rows CTA c owns (its embedding, x' and down_proj rows).
 __device__ __forceinline__ void own_rows(const Args& a, int c, int G, int& r0, int& r1) {
   r0 = int((long long)c * a.H / G);
   r1 = int((long long)(c + 1) * a.H / G);
+}
+
+__device__ Plan plan_of(const Args& a, int kind, int c, int G) {
+  Plan p{};
+  int rows, align = 1;
+  if (kind == K_ATTO) {
+    int g, s, ng;
+    group_of(a, c, G, g, s, ng);
+    p.cols = a.grp * kHd;
+    p.r0 = s * a.H / ng;
+    p.n = (s + 1) * a.H / ng - p.r0;
+    p.w0 = (long long)g * a.H + p.r0;
+  } else {
+    if (kind == K_QKV) rows = a.Q + 2 * a.KV, p.cols = a.H;
+    else if (kind == K_GU) rows = 2 * a.F, p.cols = a.H, align = 2;
+    else if (kind == K_DOWN) rows = a.H, p.cols = a.F;
+    else rows = a.V, p.cols = a.H;
+    const int units = rows / align;
+    p.r0 = int((long long)c * units / G) * align;
+    p.n = int((long long)(c + 1) * units / G) * align - p.r0;
+    p.w0 = p.r0;
+  }
+  // Stages of equal size (even, so that a gate/up pair never straddles two),
+  // each at most one slot and kWarps * kMaxRowsPerWarp rows.
+  const int maxrows = min((kSlotBytes / (p.cols * 2)) & ~1, kWarps * kMaxRowsPerWarp);
+  p.nst = (p.n + maxrows - 1) / maxrows;
+  p.sr = p.nst ? (((p.n + p.nst - 1) / p.nst) + 1) & ~1 : 0;
+  if (p.sr > maxrows) p.sr = maxrows;
+  return p;
+}
+
+// The phase's matrix in layer `Ly` (or the lm_head).
+__device__ __forceinline__ const uint16_t* matrix_of(const Args& a, const Layer& Ly, int kind) {
+  return kind == K_QKV ? Ly.wqkv : kind == K_ATTO ? Ly.wo_g : kind == K_GU ? Ly.wgu : kind == K_DOWN ? Ly.wd
+                                                                                                      : a.lm_head;
 }
 
 __device__ __forceinline__ void st_tagged(TW* p, float v, uint32_t tag) {
@@ -192,17 +200,106 @@ __device__ __forceinline__ void wait_full(uint64_t* bar, uint32_t parity, int* e
   if (!mbar_wait(bar, parity, err)) *abort = 1;
 }
 
+// ---- cross-lane reductions ------------------------------------------------------
+
+// Sums each of the PR values of every lane over the warp, PR - 1 + 5 -
+// log2(PR) shuffles in all (a reduce-scatter, then a butterfly over the lanes
+// that hold the same value): lane l ends with the sum of value
+// row_of_lane<PR>(l). v is clobbered.
+template <int PR>
+__device__ __forceinline__ float reduce_rows(float (&v)[PR], int lane) {
+#pragma unroll
+  for (int h = PR / 2, o = 16; h >= 1; h /= 2, o /= 2) {
+    const bool upper = lane & o;
+#pragma unroll
+    for (int i = 0; i < h; i++) {
+      const float send = upper ? v[i] : v[i + h];
+      const float keep = upper ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  float r = v[0];
+#pragma unroll
+  for (int o = 16 / PR; o >= 1; o /= 2) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+// Which of the PR values lane l holds after reduce_rows (lanes l and
+// l ^ m, m < 32 / PR, hold the same one).
+template <int PR>
+__device__ __forceinline__ int row_of_lane(int lane) {
+  int r = 0;
+#pragma unroll
+  for (int h = PR / 2, o = 16; h >= 1; h /= 2, o /= 2)
+    if (lane & o) r += h;
+  return r;
+}
+// The lowest lane that holds value r after reduce_rows.
+template <int PR>
+__device__ __forceinline__ int lane_of_row(int r) {
+  int l = 0;
+#pragma unroll
+  for (int h = PR / 2, o = 16; h >= 1; h /= 2, o /= 2)
+    if (r & h) l += o;
+  return l;
+}
+
+// ---- the matrix-vector product of one warp's rows -------------------------------
+
+struct WarpRows {
+  float v;     // this lane's row's dot product (unscaled)
+  int row;     // which of the warp's rows (>= nr: none)
+  int stride;  // lanes between consecutive rows' holders
+};
+
+// Rows w[0 .. NR) (rb bytes apart, shared memory) dotted with the input in
+// xs (xperm layout, cols columns): lane l takes columns 8l .. 8l+7 of every
+// 256-column block.
+template <int NR>
+__device__ __forceinline__ WarpRows dot_rows(const unsigned char* w, int rb, int cols, const float* xs, int lane) {
+  constexpr int PR = NR == 1 ? 1 : NR == 2 ? 2 : NR <= 4 ? 4 : 8;
+  float acc[PR], acc2[NR];
+#pragma unroll
+  for (int j = 0; j < PR; j++) acc[j] = 0.f;
+#pragma unroll
+  for (int j = 0; j < NR; j++) acc2[j] = 0.f;
+  const unsigned char* wl = w + lane * 16;
+  const float* xl = xs + lane * 4;
+  auto block = [&](int col) {
+    const float4 xa = *reinterpret_cast<const float4*>(xl + col);
+    const float4 xb = *reinterpret_cast<const float4*>(xl + col + 128);
+#pragma unroll
+    for (int j = 0; j < NR; j++) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(wl + j * rb + col * 2);
+      acc[j] = dot4(wv.x, wv.y, xa, acc[j]);
+      acc2[j] = dot4(wv.z, wv.w, xb, acc2[j]);
+    }
+  };
+  const int whole = cols & ~255;
+#pragma unroll 2
+  for (int col = 0; col < whole; col += 256) block(col);
+  if (whole + lane * 8 < cols) block(whole);  // a last block of fewer than 256 columns
+#pragma unroll
+  for (int j = 0; j < NR; j++) acc[j] += acc2[j];
+  WarpRows r;
+  r.v = reduce_rows<PR>(acc, lane);
+  r.row = (lane & (32 / PR - 1)) == 0 ? row_of_lane<PR>(lane) : 1 << 20;
+  r.stride = 32 / PR;
+  return r;
+}
+
 // Polls vec[0, n) (n a multiple of 4, at most 4 kConsumers) until every word
-// carries `tag`; with np > 0, also np partial vectors parts[j * pstride ...]
-// carrying ptag, which are added to the vector in order j = 0, 1, ... The
-// sums go to xs at xperm positions; elements [own0, own1) also to own[].
-// All of a thread's loads are issued before any is checked. Bounded.
-__device__ void poll_vector(const TW* vec, int n, uint32_t tag, const TW* parts, int np, int pstride, uint32_t ptag,
-                            float* xs, float* own, int own0, int own1, int tid, int* err, volatile int* abort) {
+// carries `tag`. With a norm weight, the values times the weight go to xs
+// (xperm positions) and the thread's sum of squares of the values is
+// returned (the RMSNorm's, cpu.rs:85-94); without one, the values
+// themselves. All of a thread's loads are issued before any is checked.
+// Bounded.
+__device__ float poll_vector(const TW* vec, int n, uint32_t tag, const uint16_t* norm, float* xs, int tid, int* err,
+                             volatile int* abort) {
   constexpr int kG = 3;  // groups of 4 words per thread (n <= 3072)
   bool done[kG];
 #pragma unroll
   for (int k = 0; k < kG; k++) done[k] = tid * 4 + k * kConsumers * 4 >= n;
+  float ss = 0.f;
   const uint64_t t0 = global_ns();
   for (;;) {
     bool all = true;
@@ -212,25 +309,14 @@ __device__ void poll_vector(const TW* vec, int n, uint32_t tag, const TW* parts,
       const int i = tid * 4 + k * kConsumers * 4;
       TW w[4];
       ld_tagged4(vec + i, w);
-      bool ok = tags4(w, tag);
-      float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
-      for (int j = 0; j < np; j++) {
-        TW u[4];
-        ld_tagged4(parts + size_t(j) * pstride + i, u);
-        ok = ok && tags4(u, ptag);
-        v.x = __fadd_rn(v.x, tval(u[0]));
-        v.y = __fadd_rn(v.y, tval(u[1]));
-        v.z = __fadd_rn(v.z, tval(u[2]));
-        v.w = __fadd_rn(v.w, tval(u[3]));
-      }
-      if (ok || *abort) {
-        *reinterpret_cast<float4*>(xs + xperm(i)) = v;
-        if (own) {
-          const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int q = 0; q < 4; q++)
-            if (i + q >= own0 && i + q < own1) own[i + q - own0] = e[q];
+      if (tags4(w, tag) || *abort) {
+        float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
+        if (norm) {
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+          const uint2 g = *reinterpret_cast<const uint2*>(norm + i);
+          v.x *= bf_lo(g.x), v.y *= bf_hi(g.x), v.z *= bf_lo(g.y), v.w *= bf_hi(g.y);
         }
+        *reinterpret_cast<float4*>(xs + xperm(i)) = v;
         done[k] = true;
       } else {
         all = false;
@@ -238,6 +324,7 @@ __device__ void poll_vector(const TW* vec, int n, uint32_t tag, const TW* parts,
     }
     if (all || timed_out(t0, err, abort)) break;
   }
+  return ss;
 }
 
 // ---- attention ----------------------------------------------------------------
@@ -264,20 +351,24 @@ __device__ __forceinline__ float4 as_cached(float4 v, bool f32) {
 
 // Attention of kv group g at position `pos` (model.rs:107-124 for one
 // token; cpu.rs:113-149), run by the consumer warps of member s of the
-// group's ng members. Warp w < grp + 2 polls head w of q (w < grp), k, v
+// group's ng members. Warp w < GRP + 2 polls head w of q (w < GRP), k, v
 // from the q|k|v vector, applies QK-norm (model.rs:111-116) and RoPE
 // (cpu.rs:96-111) in registers; member 0 appends k and v to the cache. The
 // context [lo, hi) this member attends to is all of 0..pos when pos < the
 // redundant limit, else its share; warps take positions lo + w, lo + w + 8,
-// ... with their own online softmax, merged at the end. In split mode the
-// members then exchange partials (tag `ptag`) and every member merges all of
-// them in member order. The result, grp heads of 128, goes to xs at xperm
-// positions (the o_proj partial's input). `sc` is shared scratch of at least
-// 4928 floats.
+// ... eight at a time: the GRP x 8 dot products of a chunk are reduced
+// together (reduce_rows), each lane then owns one (head, position) score for
+// the online softmax, and the probabilities are broadcast for the weighted
+// sum of values, each lane holding 4 of the 128 dimensions. The warps are
+// merged at the end. In split mode the members then exchange partials (tag
+// `ptag`) and every member merges all of them in member order. The result,
+// GRP heads of 128, goes to xs at xperm positions (the o_proj partial's
+// input). `sc` is shared scratch of at least 4960 floats.
 template <int GRP>
 __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, int ng, int pos, uint32_t qtag,
-                                uint32_t ptag, float* xs, float* sc, int tid, volatile int* abort, const TraceAt& tr) {
+                                uint32_t ptag, float* xs, float* sc, int tid, volatile int* abort) {
   constexpr int grp = GRP;
+  constexpr int PR = GRP * kAttnPer;  // (head, slot) scores of a chunk
   const int warp = tid >> 5, lane = tid & 31;
   const bool f32 = a.kv_f32 != 0;
   float* qs = sc;                        // [grp][128]
@@ -286,6 +377,7 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
   float* wm = vn + kHd;                  // [kWarps][kMaxGrp]
   float* wl = wm + kWarps * kMaxGrp;     // [kWarps][kMaxGrp]
   float* wacc = wl + kWarps * kMaxGrp;   // [kWarps][kMaxGrp][128]
+  float* we = wacc + kWarps * kMaxGrp * kHd;  // [kMaxGrp][kWarps] merge weights
 
   const int ctx = pos + 1;
   const bool split = ctx > kRedundantCtx;
@@ -357,10 +449,11 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
     *reinterpret_cast<float4*>((warp < grp ? qs + warp * kHd : warp == grp ? kn : vn) + 4 * lane) = v;
   }
   named_sync(1, kConsumers);
-  if (tid == 0) tr.at(blockIdx.x, TB200_TRACE_WAITED);
 
   // Online softmax per warp over its positions of [lo, hi), eight at a time.
   const float scale = 1.0f / sqrtf(float(kHd));
+  const int myr = row_of_lane<PR>(lane);  // this lane's (head, slot) after the reduction
+  const int myh = myr / kAttnPer, myi = myr % kAttnPer;
   float m[GRP], l[GRP];
   float4 acc[GRP], q[GRP];
 #pragma unroll
@@ -374,46 +467,50 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
   const float4 vcur = *reinterpret_cast<const float4*>(vn + 4 * lane);
   for (int base = lo; base < hi; base += kWarps * kAttnPer) {
     if (base > lo) load_chunk(base);
-    float sco[GRP][kAttnPer];
+    const int nvalid = min(kAttnPer, (hi - base - warp + kWarps - 1) / kWarps);  // slots of this warp in [lo, hi)
+    float sco[PR];
 #pragma unroll
     for (int i = 0; i < kAttnPer; i++) {
-      const int j = base + warp + kWarps * i;
-      if (j == pos) kr[i] = kcur, vr[i] = vcur;
+      if (base + warp + kWarps * i == pos) kr[i] = kcur, vr[i] = vcur;
 #pragma unroll
       for (int h = 0; h < GRP; h++)
-        sco[h][i] = q[h].x * kr[i].x + q[h].y * kr[i].y + q[h].z * kr[i].z + q[h].w * kr[i].w;
+        sco[h * kAttnPer + i] = q[h].x * kr[i].x + q[h].y * kr[i].y + q[h].z * kr[i].z + q[h].w * kr[i].w;
     }
-    // All GRP x kAttnPer dot products reduced across the warp at once.
+    float sv = reduce_rows<PR>(sco, lane);
+    sv = myi < nvalid ? sv * scale : -INFINITY;
+    // The chunk's maximum and probability sum per head: over the lanes
+    // holding that head's slots.
+    float cm = sv;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int h = 0; h < GRP; h++)
-#pragma unroll
-        for (int i = 0; i < kAttnPer; i++) sco[h][i] += __shfl_xor_sync(0xffffffffu, sco[h][i], o);
+    for (int b = 0; b < 3; b++) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, (32 / PR) << b));
+    float Mn[GRP], corr[GRP];
 #pragma unroll
     for (int h = 0; h < GRP; h++) {
-      float mx = m[h];
+      Mn[h] = fmaxf(m[h], __shfl_sync(0xffffffffu, cm, lane_of_row<PR>(h * kAttnPer)));
+      corr[h] = Mn[h] == -INFINITY ? 1.f : expf(m[h] - Mn[h]);
+    }
+    float mine = Mn[0];
 #pragma unroll
-      for (int i = 0; i < kAttnPer; i++)
-        if (base + warp + kWarps * i < hi) mx = fmaxf(mx, sco[h][i] * scale);
-      const float corr = expf(m[h] - mx);
-      float4 ac = make_float4(acc[h].x * corr, acc[h].y * corr, acc[h].z * corr, acc[h].w * corr);
-      float lsum = l[h] * corr;
+    for (int h = 1; h < GRP; h++)
+      if (myh == h) mine = Mn[h];
+    const float p = sv == -INFINITY ? 0.f : expf(sv - mine);
+    float ps = p;
+#pragma unroll
+    for (int b = 0; b < 3; b++) ps += __shfl_xor_sync(0xffffffffu, ps, (32 / PR) << b);
+#pragma unroll
+    for (int h = 0; h < GRP; h++) {
+      l[h] = l[h] * corr[h] + __shfl_sync(0xffffffffu, ps, lane_of_row<PR>(h * kAttnPer));
+      m[h] = Mn[h];
+      float4 ac = make_float4(acc[h].x * corr[h], acc[h].y * corr[h], acc[h].z * corr[h], acc[h].w * corr[h]);
 #pragma unroll
       for (int i = 0; i < kAttnPer; i++) {
-        if (base + warp + kWarps * i >= hi) break;
-        const float p = expf(sco[h][i] * scale - mx);
-        lsum += p;
-        ac.x += p * vr[i].x;
-        ac.y += p * vr[i].y;
-        ac.z += p * vr[i].z;
-        ac.w += p * vr[i].w;
+        const float pi = __shfl_sync(0xffffffffu, p, lane_of_row<PR>(h * kAttnPer + i));
+        ac.x += pi * vr[i].x;
+        ac.y += pi * vr[i].y;
+        ac.z += pi * vr[i].z;
+        ac.w += pi * vr[i].w;
       }
-      if (mx != -INFINITY) {
-        m[h] = mx;
-        l[h] = lsum;
-        acc[h] = ac;
-      }
+      acc[h] = ac;
     }
   }
 #pragma unroll
@@ -425,24 +522,31 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
     *reinterpret_cast<float4*>(wacc + (warp * kMaxGrp + h) * kHd + 4 * lane) = acc[h];
   }
   named_sync(1, kConsumers);
-  if (tid == 0) tr.at(blockIdx.x, TB200_TRACE_REDUCE);
-  // Merge the warps: thread (h, 4 dims) of the grp * 32 threads.
+  // Merge weights of the warps, one thread per (head, warp).
+  if (tid < grp * kWarps) {
+    const int h = tid / kWarps, w = tid % kWarps;
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kWarps; u++) M = fmaxf(M, wm[u * kMaxGrp + h]);
+    const float lw = wl[w * kMaxGrp + h];
+    we[h * kWarps + w] = lw > 0.f ? expf(wm[w * kMaxGrp + h] - M) : 0.f;
+  }
+  named_sync(1, kConsumers);
+  // Merge: thread (h, 4 dims) of the grp * 32 threads.
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
   float M = -INFINITY, Ls = 0.f;
   const int mh = tid >> 5, d4 = tid & 31;
   if (tid < grp * 32) {
-    for (int w = 0; w < kWarps; w++) M = fmaxf(M, wm[w * kMaxGrp + mh]);
+#pragma unroll
     for (int w = 0; w < kWarps; w++) {
-      const float lw = wl[w * kMaxGrp + mh];
-      if (lw > 0.f) {
-        const float e = expf(wm[w * kMaxGrp + mh] - M);
-        const float4 aw = *reinterpret_cast<const float4*>(wacc + (w * kMaxGrp + mh) * kHd + 4 * d4);
-        Ls += lw * e;
-        o.x += aw.x * e;
-        o.y += aw.y * e;
-        o.z += aw.z * e;
-        o.w += aw.w * e;
-      }
+      const float e = we[mh * kWarps + w];
+      const float4 aw = *reinterpret_cast<const float4*>(wacc + (w * kMaxGrp + mh) * kHd + 4 * d4);
+      Ls += wl[w * kMaxGrp + mh] * e;
+      o.x += aw.x * e;
+      o.y += aw.y * e;
+      o.z += aw.z * e;
+      o.w += aw.w * e;
+      M = fmaxf(M, wm[w * kMaxGrp + mh]);
     }
   }
   if (split) {
@@ -499,15 +603,14 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
 template <int GRP>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  float* xs = reinterpret_cast<float*>(smem);  // [kMaxCols] input, xperm layout
-  float* nw = xs + kMaxCols;                   // [kMaxCols] norm weight (f32)
-  unsigned char* ring = reinterpret_cast<unsigned char*>(nw + kMaxCols);
+  float* xs = reinterpret_cast<float*>(smem);  // [kMaxCols] input, xperm layout; attention scratch after 1024
+  unsigned char* ring = smem + size_t(kMaxCols) * 2 * 4;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(kSlots) * kSlotBytes);
   uint64_t* empty = full + kSlots;
   __shared__ float red[kWarps];
-  __shared__ float ksum[kWarps][kKsplitRows];
-  __shared__ float own[kMaxOwn];  // x' (after attention) on this CTA's residual rows
+  __shared__ float own[kMaxOwn];  // the residual stream x on this CTA's rows, as this CTA last wrote it
   __shared__ unsigned long long best_sm[kWarps];
+  __shared__ Plan plan[kKinds];
   __shared__ volatile int abort_sm;  // a wait gave up (or the arguments are bad): wait no more
   __shared__ volatile int issued_sm;
   __shared__ int tok_sm;
@@ -517,7 +620,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
   const int pos0 = a.io[1], tok0 = a.io[0], count0 = a.io[2];
   const uint32_t per_step = tags_per_step(a.L);
 
-  if (tid == 0) {
+  if (tid < kKinds) plan[tid] = plan_of(a, tid, c, G);
+  if (tid == 32) {
     for (int s = 0; s < kSlots; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kWarps);
@@ -542,18 +646,20 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
       for (int step = 0; step < a.steps && !abort_sm; step++)
         for (int layer = 0; layer <= a.L && !abort_sm; layer++)
           for (int p = 0; p < kPhases && !abort_sm; p++) {
-            if (layer == a.L && p != 0) break;  // the lm_head
-            const Slice s = slice_of(a, layer, p, c, G);
-            const int sr = stage_rows(s);
-            for (int r = 0; r < s.n && !abort_sm; r += sr, k++) {
+            if (layer == a.L && p != 0) break;
+            const int kind = layer == a.L ? K_LM : p;
+            const Plan& pl = plan[kind];
+            const uint16_t* w = matrix_of(a, a.layer[layer < a.L ? layer : 0], kind) + pl.w0 * pl.cols;
+            for (int b = 0; b < pl.nst && !abort_sm; b++, k++) {
               const int slot = k % kSlots;
               if (k >= kSlots && !mbar_wait(&empty[slot], ((k / kSlots) - 1) & 1, a.io + 3)) {
                 abort_sm = 1;
                 break;
               }
-              const uint32_t bytes = uint32_t(min(sr, s.n - r)) * uint32_t(s.cols) * 2;
+              const int r = b * pl.sr;
+              const uint32_t bytes = uint32_t(min(pl.sr, pl.n - r)) * uint32_t(pl.cols) * 2;
               mbar_arrive_expect_tx(&full[slot], bytes);
-              bulk_g2s(ring + size_t(slot) * kSlotBytes, s.w + size_t(r) * s.cols, bytes, &full[slot], pol);
+              bulk_g2s(ring + size_t(slot) * kSlotBytes, w + size_t(r) * pl.cols, bytes, &full[slot], pol);
               issued_sm = k + 1;
             }
           }
@@ -586,8 +692,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
         named_sync(1, kConsumers);
       }
       const int tok = tok_sm;
-      for (int r = own0 + tid; r < own1; r += kConsumers)
-        st_tagged(a.x + r, bf16f(a.embed[size_t(tok) * a.H + r]), T);
+      for (int r = own0 + tid; r < own1; r += kConsumers) {
+        const float e = bf16f(a.embed[size_t(tok) * a.H + r]);
+        own[r - own0] = e;
+#pragma unroll
+        for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + r, e, T);
+      }
       uint32_t x_tag = T;  // tag of the residual stream's current version
 
       unsigned long long best = 0ull;
@@ -596,160 +706,115 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
         const bool head = layer == a.L;
         for (int p = 0; p < kPhases; p++) {
           if (head && p != 0) break;
+          const int kind = head ? K_LM : p;
           const uint32_t out_tag = phase_tag(T, layer, p);
           const TraceAt tr{a.trace, head ? trace_base(a.L, 0, G) : trace_base(layer, p, G),
-                           (uint32_t(TB200_TRACE_OP_P_QKV + (head ? 4 : p)) << 16) | uint32_t(layer)};
+                           (uint32_t(TB200_TRACE_OP_P_QKV + kind) << 16) | uint32_t(layer)};
           float scale = 1.0f;
-          if (p == P_ATTO) {
-            attention_phase<GRP>(a, Ly, ag, as, ang, pos, phase_tag(T, layer, P_QKV), out_tag, xs, xs + 1024, tid,
-                                 &abort_sm, tr);
+          if (kind == K_ATTO) {
+            attention_phase<GRP>(a, Ly, ag, as, ang, pos, phase_tag(T, layer, K_QKV), out_tag, xs, xs + 1024, tid,
+                                 &abort_sm);
             named_sync(1, kConsumers);
           } else {
-            const TW* in;
-            int n_in, np = 0;
-            uint32_t in_tag;
-            const uint16_t* norm = nullptr;
-            if (p == P_QKV) {
-              in = a.x, n_in = a.H, in_tag = x_tag, norm = head ? a.norm : Ly.attn_norm;
-            } else if (p == P_GU) {
-              in = a.x, n_in = a.H, in_tag = x_tag, norm = Ly.mlp_norm, np = a.Hkv;
-            } else {
-              in = a.h, n_in = a.F, in_tag = phase_tag(T, layer, P_GU);
-            }
-            if (norm)
-              for (int i = tid * 4; i < n_in; i += kConsumers * 4) {
-                const uint2 gw = *reinterpret_cast<const uint2*>(norm + i);
-                *reinterpret_cast<float4*>(nw + i) = make_float4(bf_lo(gw.x), bf_hi(gw.x), bf_lo(gw.y), bf_hi(gw.y));
-              }
-            poll_vector(in, n_in, in_tag, a.part_o, np, a.H, phase_tag(T, layer, P_ATTO), xs,
-                        p == P_GU ? own : nullptr, own0, own1, tid, a.io + 3, &abort_sm);
-            named_sync(1, kConsumers);
-            if (tid == 0) tr.at(c, TB200_TRACE_WAITED);
-            if (norm) {  // rmsnorm (cpu.rs:85-94): x * w in place, the 1/rms scale applied to each dot
-              float ss = 0.f;
-              for (int i = tid * 4; i < n_in; i += kConsumers * 4) {
-                float4 v = *reinterpret_cast<float4*>(xs + xperm(i));
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                const float4 gw = *reinterpret_cast<const float4*>(nw + i);
-                v.x *= gw.x, v.y *= gw.y, v.z *= gw.z, v.w *= gw.w;
-                *reinterpret_cast<float4*>(xs + xperm(i)) = v;  // the float4 this thread stored
-              }
+            const int n_in = kind == K_DOWN ? a.F : a.H;
+            const TW* in = (kind == K_DOWN ? a.h : a.x) + (c % kRep) * n_in;
+            const uint32_t in_tag = kind == K_DOWN ? phase_tag(T, layer, K_GU)
+                                    : kind == K_GU ? phase_tag(T, layer, K_ATTO)
+                                                   : x_tag;
+            const uint16_t* norm = kind == K_QKV ? Ly.attn_norm : kind == K_GU ? Ly.mlp_norm : kind == K_LM ? a.norm
+                                                                                                             : nullptr;
+            float ss = poll_vector(in, n_in, in_tag, norm, xs, tid, a.io + 3, &abort_sm);
+            if (norm) {  // rmsnorm (cpu.rs:85-94): x * w stored, the 1/rms scale applied to each dot
               ss = warp_sum(ss);
               if (lane == 0) red[warp] = ss;
-              named_sync(1, kConsumers);
+            }
+            named_sync(1, kConsumers);
+            if (norm) {
               float tot = 0.f;
+#pragma unroll
               for (int w = 0; w < kWarps; w++) tot += red[w];
               scale = 1.0f / sqrtf(tot / float(n_in) + a.eps);
             }
           }
           if (tid == 0) tr.at(c, TB200_TRACE_INPUT);
-          // One output row of a matrix phase.
-          auto emit = [&](int row, float v) {
-            if (head) {
-              if (a.logits) a.logits[row] = v;
-              const unsigned long long key = argmax_key(v, uint32_t(row));
-              best = key > best ? key : best;
-            } else if (p == P_QKV) {
-              st_tagged(a.qkv + row, v, out_tag);
-            } else if (p == P_ATTO) {
-              st_tagged(a.part_o + size_t(ag) * a.H + row, v, out_tag);
-            } else {  // down_proj: the residual add on a row this CTA owns
-              const float x1 = __fadd_rn(own[row - own0], v);
-              st_tagged(a.x + row, x1, out_tag);
-            }
-          };
-          auto emit_h = [&](int row, float gt, float up) {  // rows 2i (gate), 2i + 1 (up) -> h[i]
-            st_tagged(a.h + row / 2, __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up), out_tag);
-          };
-          const Slice s = slice_of(a, layer, p, c, G);
-          const int sr = stage_rows(s);
-          const size_t rb = size_t(s.cols) * 2;
-          for (int r = 0; r < s.n; r += sr, k++) {
+          const Plan pl = plan[kind];
+          const int rb = pl.cols * 2;
+          for (int b = 0; b < pl.nst; b++, k++) {
             const int slot = k % kSlots;
+            const int rs0 = b * pl.sr, nrs = min(pl.sr, pl.n - rs0);
+            int rpw = (nrs + kWarps - 1) / kWarps;
+            if (kind == K_GU) rpw = (rpw + 1) & ~1;
+            const int first = warp * rpw, nr = max(0, min(rpw, nrs - first));
             wait_full(&full[slot], (k / kSlots) & 1, a.io + 3, &abort_sm);
-            if (tid == 0) tr.at(c, r == 0 ? TB200_TRACE_WEIGHTS : TB200_TRACE_LAST_WEIGHTS);
-            const unsigned char* base = ring + size_t(slot) * kSlotBytes;
-            const int nrs = min(sr, s.n - r);
-            if (s.n <= kKsplitRows) {  // all warps on every row, K split
-              float acc[kKsplitRows];
-#pragma unroll
-              for (int j = 0; j < kKsplitRows; j++) acc[j] = 0.f;
-              for (int u = tid; u < s.cols / 8; u += kConsumers) {
-                const float* xb0 = xs + (u >> 5) * 256 + (u & 31) * 4;
-                const float4 xa = *reinterpret_cast<const float4*>(xb0);
-                const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
-#pragma unroll
-                for (int j = 0; j < kKsplitRows; j++)
-                  if (j < nrs) acc[j] = dot8(*reinterpret_cast<const uint4*>(base + j * rb + size_t(u) * 16), xa, xb, acc[j]);
-              }
-#pragma unroll
-              for (int j = 0; j < kKsplitRows; j++) {
-                const float v = warp_sum(acc[j]);
-                if (lane == 0) ksum[warp][j] = v;
-              }
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&empty[slot]);
-              named_sync(1, kConsumers);
-              if (warp == 0) {
-                float v = 0.f;
-                if (lane < nrs) {
-                  for (int w = 0; w < kWarps; w++) v += ksum[w][lane];
-                  v *= scale;
-                }
-                const float up = __shfl_down_sync(0xffffffffu, v, 1);
-                if (p == P_GU && !head) {
-                  if ((lane & 1) == 0 && lane < nrs) emit_h(s.r0 + r + lane, v, up);
-                } else if (lane < nrs) {
-                  emit(s.r0 + r + lane, v);
-                }
-              }
-              named_sync(1, kConsumers);  // ksum is reused
-              continue;
+            const unsigned char* wbase = ring + size_t(slot) * kSlotBytes + size_t(first) * rb;
+            WarpRows d{0.f, 1 << 20, 32};
+            switch (nr) {
+              case 1: d = dot_rows<1>(wbase, rb, pl.cols, xs, lane); break;
+              case 2: d = dot_rows<2>(wbase, rb, pl.cols, xs, lane); break;
+              case 3: d = dot_rows<3>(wbase, rb, pl.cols, xs, lane); break;
+              case 4: d = dot_rows<4>(wbase, rb, pl.cols, xs, lane); break;
+              case 5: d = dot_rows<5>(wbase, rb, pl.cols, xs, lane); break;
+              case 6: d = dot_rows<6>(wbase, rb, pl.cols, xs, lane); break;
+              case 7: d = dot_rows<7>(wbase, rb, pl.cols, xs, lane); break;
+              case 8: d = dot_rows<8>(wbase, rb, pl.cols, xs, lane); break;
+              default: break;
             }
-            // Row branch: warp w takes rows [w rpw, w rpw + nr) of the stage.
-            const int rpw = ((nrs + 2 * kWarps - 1) / (2 * kWarps)) * 2;
-            const int first = warp * rpw;
-            const int nr = max(0, min(rpw, nrs - first));
-            float acc[kMaxRowsPerWarp], acc2[kMaxRowsPerWarp];
-#pragma unroll
-            for (int j = 0; j < kMaxRowsPerWarp; j++) acc[j] = acc2[j] = 0.f;
-            if (nr > 0)
-              for (int col = lane * 8; col < s.cols; col += 256) {
-                const float* xb0 = xs + (col - lane * 8) + lane * 4;
-                const float4 xa = *reinterpret_cast<const float4*>(xb0);
-                const float4 xb = *reinterpret_cast<const float4*>(xb0 + 128);
-#pragma unroll
-                for (int j = 0; j < kMaxRowsPerWarp; j++)
-                  if (j < nr) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(base + (first + j) * rb + size_t(col) * 2);
-                    acc[j] = dot4(wv.x, wv.y, xa, acc[j]);
-                    acc2[j] = dot4(wv.z, wv.w, xb, acc2[j]);
-                  }
-              }
-#pragma unroll
-            for (int j = 0; j < kMaxRowsPerWarp; j++) acc[j] = warp_sum(acc[j] + acc2[j]) * scale;
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
-            const int row0 = s.r0 + r + first;
-            if (p == P_GU && !head) {
-              if (lane < nr / 2) {
-                float gt = acc[0], up = acc[1];
+            const int row = pl.r0 + rs0 + first + d.row;  // output row of this lane's value
+            const float v = d.v * scale;
+            if (kind == K_GU) {  // rows 2i (gate), 2i + 1 (up) -> h[i]
+              const float up = __shfl_down_sync(0xffffffffu, v, d.stride);
+              if (d.row < nr && (d.row & 1) == 0) {
+                const float hv = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), up);
 #pragma unroll
-                for (int j = 1; j < kMaxRowsPerWarp / 2; j++)
-                  if (lane == j) gt = acc[2 * j], up = acc[2 * j + 1];
-                emit_h(row0 + 2 * lane, gt, up);
+                for (int q = 0; q < kRep; q++) st_tagged(a.h + q * a.F + row / 2, hv, out_tag);
               }
-            } else if (lane < nr) {
-              float v = acc[0];
+            } else if (d.row < nr) {
+              if (kind == K_QKV) {
+                st_tagged(a.qkv + row, v, out_tag);
+              } else if (kind == K_ATTO) {
+                st_tagged(a.part_o + size_t(ag) * a.H + row, v, out_tag);
+              } else if (kind == K_DOWN) {  // the residual add on a row this CTA owns
+                const float x1 = __fadd_rn(own[row - own0], v);
+                own[row - own0] = x1;
 #pragma unroll
-              for (int j = 1; j < kMaxRowsPerWarp; j++)
-                if (lane == j) v = acc[j];
-              emit(row0 + lane, v);
+                for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + row, x1, out_tag);
+              } else {
+                if (a.logits) a.logits[row] = v;
+                const unsigned long long key = argmax_key(v, uint32_t(row));
+                best = key > best ? key : best;
+              }
             }
           }
-          if (p == P_DOWN) x_tag = out_tag;
+          if (kind == K_ATTO && tid < own1 - own0) {
+            // x' = x + the o_proj partials of every kv group, in group order
+            // (model.rs:131-132), on this CTA's residual rows: a poll of
+            // Hkv words per row, so that the next phase reads x' alone.
+            const int r = own0 + tid;
+            float xv = own[tid];
+            TW w[kMaxKv];
+            const uint64_t t0 = global_ns();
+            for (;;) {
+              bool ok = true;
+#pragma unroll
+              for (int g = 0; g < kMaxKv; g++)
+                if (g < a.Hkv) {
+                  w[g] = ld_tagged(a.part_o + size_t(g) * a.H + r);
+                  ok = ok && ttag(w[g]) == out_tag;
+                }
+              if (ok || abort_sm || timed_out(t0, a.io + 3, &abort_sm)) break;
+            }
+#pragma unroll
+            for (int g = 0; g < kMaxKv; g++)
+              if (g < a.Hkv) xv = __fadd_rn(xv, tval(w[g]));
+            own[tid] = xv;
+#pragma unroll
+            for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + r, xv, out_tag);
+          }
+          if (kind == K_DOWN) x_tag = out_tag;
           if (tid == 0) tr.at(c, TB200_TRACE_DONE);
-          named_sync(1, kConsumers);  // xs, nw and own are rewritten by the next phase
+          named_sync(1, kConsumers);  // xs and own are rewritten by the next phase
         }
       }
 
@@ -864,7 +929,7 @@ static int persist_prepare(tb200_state* st) {
   const tb200_config& c = m->c;
   const size_t grp = c.num_attention_heads / c.num_key_value_heads;
   const size_t nsplit = (persist_grid(m) + c.num_key_value_heads - 1) / c.num_key_value_heads;
-  const size_t words = c.hidden_size + m->q_dim + 2 * m->kv_dim + c.intermediate_size +
+  const size_t words = P::kRep * c.hidden_size + m->q_dim + 2 * m->kv_dim + P::kRep * c.intermediate_size +
                        c.num_key_value_heads * c.hidden_size + c.num_key_value_heads * nsplit * grp * P::kPartWords + 4;
   cudaStream_t s = m->dev->stream;
   CUDA_TRY(cudaMalloc(&st->ps_words, words * 8));
@@ -910,7 +975,7 @@ int persist_enqueue(tb200_state* st, size_t steps, bool logits) {
   a.embed = m->embed, a.lm_head = m->lm_head, a.norm = m->norm;
   a.rope = st->rope, a.max_len = int(st->max_len), a.kv_f32 = st->kv_f32;
   P::TW* w = static_cast<P::TW*>(st->ps_words);
-  a.x = w, a.qkv = a.x + a.H, a.h = a.qkv + a.Q + 2 * a.KV, a.part_o = a.h + a.F;
+  a.x = w, a.qkv = a.x + P::kRep * a.H, a.h = a.qkv + a.Q + 2 * a.KV, a.part_o = a.h + P::kRep * a.F;
   const int grid = int(persist_grid(m));
   a.nsplit = (grid + a.Hkv - 1) / a.Hkv;
   a.part_att = a.part_o + size_t(a.Hkv) * a.H;
