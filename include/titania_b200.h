@@ -156,6 +156,17 @@ TB200_API int tb200_rope(tb200_device* dev, tb200_buffer* x, const tb200_buffer*
  * head_dim, n_kv_heads)`; caches laid out [position][kv head][head_dim]. */
 TB200_API int tb200_attention(tb200_device* dev, tb200_buffer* out, const tb200_buffer* q, const tb200_buffer* k_cache,
                     const tb200_buffer* v_cache, size_t pos, size_t n_heads, size_t head_dim, size_t n_kv_heads);
+/* Device::attention (device.rs:75-85, model/cpu.rs:113-149) for one query
+ * token in each of `batch` sequences, over a bf16 key/value cache in the
+ * layout the model path keeps (no trait counterpart: the trait's caches are
+ * f32, [position][kv head][head_dim]): `cache` has shape
+ * [batch, 2 (K, V), n_kv_heads, max_len, 128]; q[b] (n_heads x 128 f32,
+ * after QK-norm and RoPE) at positions[b] attends to cached positions
+ * 0..positions[b] of sequence b; out[b] receives n_heads x 128 f32. q and out
+ * hold batch * n_heads * 128 values; 1, 2, 4 or 8 query heads per kv head.
+ * Runs the batched decode step's tensor-core attention kernel. */
+TB200_API int tb200_attention_cache(tb200_device* dev, tb200_buffer* out, const tb200_buffer* q,
+                                    const tb200_weight* cache, const size_t* positions, size_t batch, size_t n_heads);
 /* device.rs:88 `silu_mul(&self, gate, up)`. */
 TB200_API int tb200_silu_mul(tb200_device* dev, tb200_buffer* gate, const tb200_buffer* up);
 

@@ -83,6 +83,7 @@ SIGNATURES = {
     "tb200_rmsnorm": (ctypes.c_int, [P, P, P, ctypes.c_float]),
     "tb200_rope": (ctypes.c_int, [P, P, P, SZ, SZ, SZ]),
     "tb200_attention": (ctypes.c_int, [P, P, P, P, P, SZ, SZ, SZ, SZ]),
+    "tb200_attention_cache": (ctypes.c_int, [P, P, P, P, SZP, SZ, SZ]),
     "tb200_silu_mul": (ctypes.c_int, [P, P, P]),
     "tb200_free_buffer": (ctypes.c_int, [P, P]),
     "tb200_free_weight": (ctypes.c_int, [P, P]),

@@ -175,6 +175,10 @@ int tb200_device_close(tb200_device* d) {
   cudaFree(d->best);
   cudaFree(d->split);
   cudaFree(d->err);
+  cudaFree(d->ao_part);
+  cudaFree(d->ao_ticket);
+  cudaFree(d->ao_meta);
+  cudaFree(d->ao_planes);
   for (void* p : d->stage) cudaFreeHost(p);
   cudaStreamDestroy(d->stream);
   delete d;

@@ -31,6 +31,20 @@ struct tb200_device {
   // worker thread, allocated on first use and kept until the device closes:
   // page-locking costs about as much as the copies it serves.
   std::vector<void*> stage;
+  // Workspace of the standalone decode attention (attn_op.cu), grown on
+  // demand and kept until the device closes.
+  float* ao_part = nullptr;        // split-context partials
+  size_t ao_part_cap = 0;          // floats
+  unsigned* ao_ticket = nullptr;   // one per (sequence, kv head), zero between launches
+  size_t ao_ticket_cap = 0;
+  int* ao_meta = nullptr;          // [2][cap]: position, sequence of each query row
+  size_t ao_meta_cap = 0;
+  std::vector<int> ao_meta_host;   // what ao_meta holds
+  uint16_t* ao_planes = nullptr;   // [3][rows][q_dim] attention output planes
+  size_t ao_planes_cap = 0;        // elements
+  const void* ao_map_base = nullptr;  // the cache the tensor map describes
+  size_t ao_map_rows = 0;
+  CUtensorMap ao_map{};
 };
 
 struct tb200_buffer {

@@ -207,5 +207,15 @@ class B200:
         call("tb200_argmax", self._h, logits._h, ctypes.byref(out))
         return int(out.value)
 
+    def attention_cache(self, out: Buffer, q: Buffer, cache: Weight, positions, n_heads: int) -> None:
+        """Decode attention over a bf16 cache in the model path's layout
+        (`cache` of shape [batch, 2, n_kv_heads, max_len, 128]): for each
+        sequence b, the query q[b] (n_heads x 128, after QK-norm and RoPE) at
+        positions[b] attends to cached positions 0..positions[b]
+        (Device::attention, model/cpu.rs:113-149, one token per sequence)."""
+        pos = np.ascontiguousarray(positions, dtype=np.uint64)
+        call("tb200_attention_cache", self._h, out._h, q._h, cache._h, pos.ctypes.data_as(_lib.SZP), pos.size,
+             int(n_heads))
+
 
 __all__ = ["B200", "Buffer", "Weight", "Tensor", "DeviceError"]
