@@ -78,7 +78,19 @@ class Clocks:
         self.index = index
         self.proc = None
 
+    def _query(self):
+        try:
+            r = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=20)
+            return [ln for ln in r.stdout.splitlines() if ln.strip()]
+        except (OSError, subprocess.SubprocessError):
+            return []
+
     def __enter__(self):
+        # One sample just before the region and one just after it (a timed
+        # region shorter than the sampling period would otherwise have none),
+        # and a 100 ms stream in between.
+        self.before = self._query()
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -93,6 +105,7 @@ class Clocks:
             self.proc.terminate()
             out, _ = self.proc.communicate(timeout=10)
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self.lines = self.before + self.lines + self._query()
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -113,48 +126,238 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def time_kernels(tb, m, dev, cfg, torch):
-    """Times each fused kernel alone (CUDA events on the library's stream),
-    cycling through every layer's weights and writing a 256 MB buffer
-    between launches so that no launch finds its weights in L2."""
-    from titania_b200.model import OP_ATTENTION, OP_DOWN, OP_GATE_UP, OP_LM_HEAD, OP_O, OP_QKV
-    H, F, L, V = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["vocab_size"]
-    q_dim, kv_dim = cfg["num_attention_heads"] * 128, cfg["num_key_value_heads"] * 128
-    shapes = {  # rows, cols, extra f32 bytes read (residual)
-        OP_QKV: ("q|k|v matvec (+rmsnorm)", q_dim + 2 * kv_dim, H, 0),
-        OP_O: ("o_proj matvec (+residual)", H, q_dim, H * 4),
-        OP_GATE_UP: ("gate|up matvec (+rmsnorm, silu)", 2 * F, H, 0),
-        OP_DOWN: ("down matvec (+residual)", H, F, H * 4),
-        OP_LM_HEAD: ("lm_head matvec (+rmsnorm, argmax)", V, H, 0),
-    }
+def busy(torch, us=300):
+    """Keeps the GPU busy for about `us` microseconds (a spin kernel on the
+    current stream), so that the host has enqueued the next timed work before
+    the GPU reaches it and the events time the device alone."""
+    torch.cuda._sleep(int(us * 2000))
+
+
+def timed_calls(torch, stream, fn, reps, flush=None):
+    """Device durations (s) of `fn` (which only enqueues work on `stream`),
+    one per repetition; `flush` (a buffer larger than L2) is rewritten before
+    each, so no repetition finds its inputs in L2."""
+    ts = []
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            busy(torch)
+            if flush is not None:
+                flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            ts.append((e0, e1))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) * 1e-3 for a, b in ts]
+
+
+def timeline(tr, names, end_tag=None):
+    """Splits a traced decode step into consecutive segments, one per launch
+    (or phase of the persistent kernel), ordered by when its last CTA
+    finished: a segment runs from the previous unit's last DONE to this
+    one's, the first from the step's earliest record. The segments add up to
+    the step; per op they are summed over layers (us). Also the median over
+    CTAs of each unit's own INPUT -> DONE time, averaged over its layers."""
+    tr = tr[tr["ns"] > 0]
+    t0 = int(tr["ns"].min())
+    done = {}
+    work = {}
+    for tag in np.unique(tr["tag"]):
+        r = tr[tr["tag"] == tag]
+        d = r[r["event"] == 4]
+        if not d.size:
+            continue
+        done[int(tag)] = int(d["ns"].max())
+        i = r[r["event"] == 2]
+        if i.size:
+            by = {int(x["cta"]): int(x["ns"]) for x in i}
+            w = [int(x["ns"]) - by[int(x["cta"])] for x in d if int(x["cta"]) in by]
+            if w:
+                work[int(tag)] = float(np.median(w))
+    seg, comp, cnt = {}, {}, {}
+    prev = t0
+    for tag, t in sorted(done.items(), key=lambda kv: kv[1]):
+        name = names.get(tag >> 16, str(tag >> 16))
+        seg[name] = seg.get(name, 0.0) + (t - prev) / 1e3
+        if tag in work:
+            comp[name] = comp.get(name, 0.0) + work[tag] / 1e3
+            cnt[name] = cnt.get(name, 0) + 1
+        prev = t
+    return {"step_us": (prev - t0) / 1e3,
+            "segments_us": {k: round(v, 2) for k, v in seg.items()},
+            "own_work_us_per_launch": {k: round(comp[k] / cnt[k], 3) for k in comp}}
+
+
+PERSIST_NAMES = {32: "q|k|v", 33: "attention + o_proj partials + residual", 34: "gate|up + silu", 35: "down + residual",
+                 36: "lm_head + argmax", 38: "token"}
+FUSED_NAMES = {0: "embed", 1: "q|k|v", 2: "attention", 3: "o_proj", 4: "gate|up", 5: "down", 6: "lm_head",
+               7: "attention + o_proj", 8: "gate|up (+o partials)"}
+
+
+def step_trace(m, st, first, decode):
+    """One traced single-token step at position PROMPT + 16 (the middle of
+    config 0's contexts) on the given path."""
+    prev = st.decode
+    st.decode = decode
+    m.decode_enqueue(st, first, PROMPT, 16)
+    st.trace_start(1 << 22)
+    m.decode_enqueue(st, first, PROMPT + 16, 1)
+    tr = st.trace_stop()
+    st.decode = prev
+    return timeline(tr, PERSIST_NAMES if decode == "persistent" else FUSED_NAMES)
+
+
+def run_attn_sweep(tb, dev, torch, peak):
+    """GQA decode attention (16 query / 8 kv heads,
+    head_dim 128) over a bf16 cache, contexts 512 / 4096 / 32768 at batch 1
+    and 64, through tb200_attention_cache. Each call is timed alone on the
+    device with L2 flushed before it; bytes = the K and V read."""
     stream = torch.cuda.ExternalStream(dev.stream)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    st = m.state(512)
-    m.forward(st, [1] * PROMPT, 0)
-    out = {}
-    for op, (name, rows, cols, extra) in shapes.items():
-        layers = [0] if op == OP_LM_HEAD else list(range(L))
-        reps = 8 if op == OP_LM_HEAD else 2
-        times = []
-        with torch.cuda.stream(stream):
-            for r in range(reps):
-                for layer in layers:
-                    flush.zero_()
-                    if op == OP_LM_HEAD:  # argmax advances the position: rewind it
-                        m.decode_enqueue(st, 1, PROMPT, 0)
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record(stream)
-                    m.enqueue_op(st, op, layer)
-                    e1.record(stream)
-                    times.append((e0, e1))
-        torch.cuda.synchronize()
-        dur = [a.elapsed_time(b) * 1e-3 for a, b in times[len(layers):]]  # drop the first pass
-        avg = sum(dur) / len(dur)
-        nbytes = rows * cols * 2 + cols * 4 + rows * 4 + extra
-        out[name] = {"op": op, "launches_per_step": len(layers) if op != OP_LM_HEAD else 1, "avg_us": avg * 1e6,
-                     "bytes": nbytes, "gbs": nbytes / avg / 1e9}
+    rng = np.random.default_rng(0)
+    from titania_b200.synth import f32_to_bf16_bits
+    block = f32_to_bf16_bits(rng.standard_normal(1 << 24, dtype=np.float32))
+    out = []
+    for batch in (1, 64):
+        shape = (batch, 2, 8, 32768, 128)
+        bits = np.resize(block, int(np.prod(shape))).reshape(shape)  # K, V ~ N(0, 1) in bf16 (a 16M-value block tiled)
+        cache = dev.upload(tb.Tensor(list(shape), bits))
+        del bits
+        q, o = dev.alloc(batch * 2048), dev.alloc(batch * 2048)
+        dev.write(q, rng.standard_normal(batch * 2048, dtype=np.float32))
+        for ctx in (512, 4096, 32768):
+            pos = [ctx - 1] * batch
+            for _ in range(3):
+                dev.attention_cache(o, q, cache, pos, 16)
+            dev.sync()
+            t = statistics.median(timed_calls(torch, stream, lambda: dev.attention_cache(o, q, cache, pos, 16), 20,
+                                              flush))
+            nbytes = batch * ctx * 8 * 128 * 2 * 2 + 2 * batch * 2048 * 4
+            out.append({"ctx": ctx, "batch": batch, "us": t * 1e6, "gbs": nbytes / t / 1e9,
+                        "frac_of_measured": nbytes / t / 1e9 / peak})
+        del cache, q, o
     dev.sync()
-    return out
+    return {"workload": "config 2: GQA decode attention, 16 q / 8 kv heads, head_dim 128, bf16 K/V ~N(0,1)",
+            "op": "tb200_attention_cache (tensor-core decode attention + planes -> f32)",
+            "l2": "256 MB written before every timed call", "timing": "median of 20 calls, CUDA events",
+            "peak_gbs": peak, "points": out}
+
+
+def run_op_sweep(tb, dev, torch):
+    """BASELINE config 1, the ops besides the fused matvecs, one trait call
+    each (model/cpu.rs:85-111, 151-155): RMSNorm over 1024 and per head over
+    128 (16 + 8 heads), RoPE on 16 + 8 heads x 128 at position 4095, SiLU-mul
+    over 3072; and the matvecs of Qwen3-0.6B's shapes through the trait's
+    matmul at batch 1. Each timed alone on the device after an L2 flush."""
+    from titania_b200 import synth
+    stream = torch.cuda.ExternalStream(dev.stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    rng = np.random.default_rng(1)
+
+    def buf(n, std=1.0):
+        b = dev.alloc(n)
+        dev.write(b, (rng.standard_normal(n, dtype=np.float32) * std).astype(np.float32))
+        return b
+
+    def weight(shape, std=0.02):
+        return dev.upload(tb.Tensor(list(shape), synth.f32_to_bf16_bits(
+            rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(std))))
+
+    ones1024 = dev.upload(tb.Tensor([1024], np.full(1024, 0x3F80, dtype=np.uint16)))
+    ones128 = dev.upload(tb.Tensor([128], np.full(128, 0x3F80, dtype=np.uint16)))
+    x = buf(1024)
+    heads = buf(24 * 128)
+    table = dev.alloc(4096 * 128)
+    tab = np.empty(4096 * 128, dtype=np.float32)
+    _lib_call = tb._lib.call
+    _lib_call("tb200_rope_table", 4096, 128, np.float32(1e6).item(), tab.ctypes.data_as(tb._lib.F32P))
+    dev.write(table, tab)
+    g, u = buf(3072), buf(3072)
+    ops = {
+        "rmsnorm 1024": (lambda: dev.rmsnorm(x, ones1024, 1e-6), 1024 * 4 * 2 + 1024 * 2),
+        "rmsnorm per head 24 x 128": (lambda: dev.rmsnorm(heads, ones128, 1e-6), 24 * 128 * 4 * 2 + 128 * 2),
+        "rope 24 heads x 128 at 4095": (lambda: dev.rope(heads, table, 4095, 24, 128), 24 * 128 * 4 * 2 + 128 * 4),
+        "silu_mul 3072": (lambda: dev.silu_mul(g, u), 3072 * 4 * 3),
+    }
+    for name, (rows, cols) in (("q", (2048, 1024)), ("k", (1024, 1024)), ("v", (1024, 1024)), ("o", (1024, 2048)),
+                               ("gate", (3072, 1024)), ("up", (3072, 1024)), ("down", (1024, 3072)),
+                               ("lm_head", (151936, 1024))):
+        w = weight((rows, cols))
+        xin, xo = buf(cols), dev.alloc(rows)
+        ops[f"matmul {name} {rows}x{cols}"] = ((lambda w=w, xin=xin, xo=xo: dev.matmul(xo, w, xin)),
+                                               rows * cols * 2 + cols * 4 + rows * 4)
+    res = {}
+    for name, (fn, nbytes) in ops.items():
+        fn()
+        dev.sync()
+        t = statistics.median(timed_calls(torch, stream, fn, 20, flush))
+        res[name] = {"us": t * 1e6, "gbs": nbytes / t / 1e9, "bytes": nbytes}
+    dev.sync()
+    return {"workload": "config 1: per-op sweep on Qwen3-0.6B shapes (trait ops, batch 1)",
+            "l2": "256 MB written before every timed call", "timing": "median of 20 calls, CUDA events",
+            "ops": res}
+
+
+def run_prefill(tb, m, dev, cfg, torch):
+    """BASELINE config 3's prompt: 2048 uniform token ids at batch 1 through
+    Model::forward (the tensor-core path, passes of up to 1024 tokens).
+    FLOPs: 2 x the linear parameters x tokens (the lm_head only for the last
+    token) + causal attention 2 x 2 x head_dim x T^2 / 2 per head and layer."""
+    from titania_b200 import synth
+    T = 2048
+    prompt = synth.prompt_tokens(T, cfg["vocab_size"], seed=3)
+    st = m.state(T + 1, kv="bf16")
+    stream = torch.cuda.ExternalStream(dev.stream)
+    m.forward(st, prompt, 0, logits=False)
+    times = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        m.forward(st, prompt, 0, logits=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e-3)
+    t = min(times)
+    H, F, L, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["head_dim"]
+    q_dim, kv_dim = cfg["num_attention_heads"] * D, cfg["num_key_value_heads"] * D
+    linear = L * (H * (q_dim + 2 * kv_dim) + q_dim * H + 3 * H * F)
+    flops = 2.0 * linear * T + 2.0 * H * cfg["vocab_size"] + L * cfg["num_attention_heads"] * 2.0 * D * T * T
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            pk = json.load(fh)
+        peak_tf, kind = float(pk["bf16_tflops_sustained"]), "measured sustained"
+    except Exception:
+        peak_tf, kind = 1400.0, "fallback sustained"
+    del st
+    return {"workload": "config 3 prefill: 2048 uniform ids, batch 1, bf16 cache", "seconds": t,
+            "tok_s": T / t, "tflops": flops / t / 1e12, "flops": flops, "peak_tflops": peak_tf, "peak_kind": kind,
+            "frac_of_peak": flops / t / 1e12 / peak_tf,
+            "timing": "CUDA events around Model::forward (host orchestration included), best of 3"}
+
+
+def run_trait_path(tb, dev, path, cfg, torch):
+    """The literal drop-in: Model::forward_batch issued one Device-trait call
+    at a time (titania_b200.OpModel, about 594 calls per token), greedy
+    decode of config 0 after the 16-token prompt, host wall clock."""
+    from titania_b200 import synth
+    om = tb.OpModel.load(path, dev)
+    prompt = synth.prompt_tokens(PROMPT, cfg["vocab_size"], seed=1)
+    st = om.state(PROMPT + GEN + 1)
+    logits = om.forward(st, prompt, 0)
+    tok, pos = int(np.argmax(logits)), PROMPT
+    n = 0
+    for _ in range(2):  # warm-up
+        logits = om.forward(st, [tok], pos)
+        tok, pos = int(np.argmax(logits)), pos + 1
+    t0 = time.perf_counter()
+    while n < 12:
+        logits = om.forward(st, [tok], pos)
+        tok, pos, n = int(np.argmax(logits)), pos + 1, n + 1
+    secs = time.perf_counter() - t0
+    del om, st
+    return {"value": n / secs, "unit": "tok/s", "steps": n,
+            "path": "OpModel: one C-ABI Device call per op (model/model.rs:93-149), logits read every step"}
 
 
 BS64_SEQS, BS64_CTX, BS64_GEN = 64, 1024, 128  # config 3's batched decode
@@ -377,28 +580,43 @@ def run_ours(args, rank, world, torch):
     m = tb.Model.load(path, dev)
     load = measure_load(dev, path) if world == 1 else None
     prompt = synth.prompt_tokens(PROMPT, cfg["vocab_size"], seed=1)
-    st = m.state(PROMPT + GEN + 1)
+    st = m.state(PROMPT + GEN + 1)  # the default single-token path: the persistent kernel where the model allows it
+    decode = st.decode
     first = m.forward(st, prompt, 0, logits=False)  # prefill: K/V for positions 0..15
 
     K, W = args.steps, args.warmup
     gens = lambda k: [(GEN if i + GEN <= k else k - i) for i in range(0, k, GEN)]
     stream = torch.cuda.ExternalStream(dev.stream)
+    weights, kv_per_pos = model_bytes(cfg)
+    ctx_of = lambda i: PROMPT + 1 + (i % GEN)  # context of step i of a generation
 
-    for g in gens(W):
-        m.decode_enqueue(st, first, PROMPT, g)
-    dev.sync()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(dev.ordinal) as clk:
-        e0.record(stream)
-        for g in gens(K):
-            m.decode_enqueue(st, first, PROMPT, g)
-        e1.record(stream)
+    def device_rate(state, k):
+        """K greedy steps (config 0's generation replayed) on `state`'s path,
+        device time; also each launch's own events (one launch is one
+        generation on the persistent path)."""
+        for g in gens(W):
+            m.decode_enqueue(state, first, PROMPT, g)
         dev.sync()
+        if world > 1:
+            torch.distributed.barrier()
         torch.cuda.synchronize()
-    secs = e0.elapsed_time(e1) * 1e-3
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        per = []
+        with Clocks(dev.ordinal) as clk:
+            e0.record(stream)
+            for g in gens(k):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                m.decode_enqueue(state, first, PROMPT, g)
+                b.record(stream)
+                per.append((a, b, g))
+            e1.record(stream)
+            dev.sync()
+            torch.cuda.synchronize()
+        launches = [(a.elapsed_time(b) * 1e-3, g) for a, b, g in per]
+        return e0.elapsed_time(e1) * 1e-3, launches, clk.summary()
+
+    secs, launches, clocks = device_rate(st, K)
     if world > 1:
         torch.distributed.barrier()
 
@@ -427,10 +645,9 @@ def run_ours(args, rank, world, torch):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         secs, e2e_secs = t.tolist()
 
-    weights, kv_per_pos = model_bytes(cfg)
-    ctxs = [PROMPT + 1 + (i % GEN) for i in range(K)]
-    step_bytes = weights + kv_per_pos * (sum(ctxs) / K)
+    step_bytes = weights + kv_per_pos * (sum(ctx_of(i) for i in range(K)) / K)
     peak, peak_kind = peaks()
+    persistent = decode == "persistent"
     result = {
         "metric": METRIC,
         "value": world * K / secs,
@@ -450,31 +667,68 @@ def run_ours(args, rank, world, torch):
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "weights": "bf16", "activations": "f32", "kv_cache": "f32 (the reference's; bf16 optional)",
                    "l2": "no flush needed: each step streams 1.19 GB of weights, > 126 MB L2",
-                   "launch": "one CUDA graph per step, programmatic dependent launch between kernels"},
+                   "decode": decode,
+                   "launch": ("one persistent cooperative kernel (one CTA per SM) per 32-step generation"
+                              if persistent else "one CUDA graph per step, programmatic dependent launch")},
         "hbm": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes * K / secs / 1e9,
                 "frac_of_8tbs": step_bytes * K / secs / 1e9 / NOMINAL_HBM_GBS,
                 "frac_of_measured": step_bytes * K / secs / 1e9 / peak, "peak_gbs": peak, "peak_kind": peak_kind},
         "e2e": {"value": world * K / e2e_secs, "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 16},
-        "gpu_launches": K * (2 + 5 * cfg["num_hidden_layers"]) + len(gens(K)),
-        "clocks": clk.summary(),
+        "gpu_launches": (2 * len(gens(K)) if persistent
+                         else K * (2 + 5 * cfg["num_hidden_layers"]) + len(gens(K))),
+        "clocks": clocks,
     }
-    if not args.no_bs64:
-        result["bs64"] = run_bs64(args, tb, m, dev, cfg, torch, world)
-    if rank == 0 and world == 1 and not args.no_kernels:
-        kern = time_kernels(tb, m, dev, cfg, torch)
-        dom = max(kern.items(), key=lambda kv: kv[1]["avg_us"] * kv[1]["launches_per_step"])
-        name, d = dom
+    if rank == 0 and world == 1:
+        # The dominant kernel of the step: on the persistent path the step
+        # kernel itself (each launch runs a whole generation), timed by its own
+        # events inside the timed region; bytes = every step's weights + K/V.
+        lt = sum(t for t, _ in launches)
+        lbytes, i = 0.0, 0
+        for _, g in launches:
+            lbytes += sum(weights + kv_per_pos * ctx_of(j) for j in range(g))
         traffic = None
         try:
             with open(os.path.join(ROOT, "profiles", "traffic.json")) as fh:
-                traffic = json.load(fh).get(name)
+                tj = json.load(fh)
+            if persistent and tj.get("persistent step"):
+                # captured on a one-step launch; a timed launch runs its generation's steps
+                traffic = tj["persistent step"] * sum(g for _, g in launches) / len(launches)
         except Exception:
             pass
-        result["roofline"] = {"bound": "hbm", "kernel": name, "achieved": d["gbs"], "peak": peak, "unit": "GB/s",
-                              "frac": d["gbs"] / peak, "peak_kind": peak_kind, "traffic": traffic,
-                              "algorithmic_bytes_per_launch": d["bytes"], "avg_launch_us": d["avg_us"]}
-        result["kernels"] = kern
+        result["roofline"] = {
+            "bound": "hbm", "kernel": ("tb::persist::step_kernel (the whole decode step)" if persistent
+                                       else "the fused step's kernels (one graph)"),
+            "achieved": lbytes / lt / 1e9, "peak": peak, "unit": "GB/s", "frac": lbytes / lt / 1e9 / peak,
+            "peak_kind": peak_kind, "traffic": traffic,
+            "algorithmic_bytes_per_launch": lbytes / len(launches), "avg_launch_us": lt / len(launches) * 1e6,
+            "launches": len(launches), "steps_per_launch": sum(g for _, g in launches) / len(launches),
+            "traffic_note": "ncu dram read+write of a one-step launch (profiles/traffic.json), times the steps "
+                            "per timed launch"}
+        # Where a step goes: the traced step cut into consecutive segments
+        # (they add up to the step), on both single-token paths.
+        try:
+            result["step_timeline"] = step_trace(m, st, first, decode)
+            if persistent:
+                fst = m.state(PROMPT + GEN + 1, decode="fused")
+                fsecs, _, _ = device_rate(fst, min(K, 256))
+                result["fused"] = {"value": min(K, 256) / fsecs, "unit": "tok/s",
+                                   "ms_per_step": fsecs / min(K, 256) * 1e3,
+                                   "step_timeline": step_trace(m, fst, first, "fused")}
+                del fst
+        except Exception as e:
+            result["step_timeline"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    if not args.no_bs64:
+        result["bs64"] = run_bs64(args, tb, m, dev, cfg, torch, world)
+    if rank == 0 and world == 1 and not args.no_sweeps:
+        for key, fn in (("attn_sweep", lambda: run_attn_sweep(tb, dev, torch, peak)),
+                        ("op_sweep", lambda: run_op_sweep(tb, dev, torch)),
+                        ("prefill", lambda: run_prefill(tb, m, dev, cfg, torch)),
+                        ("trait_path", lambda: run_trait_path(tb, dev, path, cfg, torch))):
+            try:
+                result[key] = fn()
+            except Exception as e:  # secondary sections: report, keep the headline line
+                result[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if load is not None:
         result["load"] = load
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -565,6 +819,22 @@ def profile_op(args):
     print(json.dumps({"profile_op": args.profile_op, "launches": args.launches}))
 
 
+def profile_persistent(args):
+    """For ncu: the persistent single-token step on Qwen3-0.6B (f32 cache):
+    the 16-token prompt, then `--launches` one-step launches at context 17
+    (capture the last with `-k regex:step_kernel -s <launches - 1> -c 1`)."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    dev = tb.B200(0)
+    m = tb.Model.load(synth.cached_model("qwen3-0.6b", seed=0), dev)
+    st = m.state(PROMPT + GEN + 1)
+    first = m.forward(st, synth.prompt_tokens(PROMPT, synth.QWEN3_0_6B["vocab_size"], seed=1), 0, logits=False)
+    for _ in range(args.launches):
+        m.decode_enqueue(st, first, PROMPT, 1)
+    dev.sync()
+    print(json.dumps({"profile_persistent": st.decode, "launches": args.launches}))
+
+
 def profile_bs64(args):
     """For ncu: config 3's prefill (`--profile-seqs` sequences x
     `--profile-ctx` tokens, one pass of 228 kernels each at the defaults), then
@@ -629,7 +899,8 @@ def main():
     ap.add_argument("--steps", type=int, default=4096)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timing")
+    ap.add_argument("--no-sweeps", action="store_true",
+                    help="skip the config 1/2/3 sections (op sweep, attention sweep, prefill) and the trait path")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-bs64", action="store_true", help="skip the batch-64 decode (config 3)")
@@ -646,11 +917,16 @@ def main():
                     help="small case for ncu: the bs64 prefill, then --launches batched decode steps")
     ap.add_argument("--profile-seqs", type=int, default=BS64_SEQS)
     ap.add_argument("--profile-ctx", type=int, default=BS64_CTX)
+    ap.add_argument("--profile-persistent", action="store_true",
+                    help="small case for ncu: --launches one-step launches of the persistent decode kernel")
     ap.add_argument("--profile-gemm", action="store_true",
                     help="small case for ncu: the tensor-core contraction at the batched shapes")
     args = ap.parse_args()
     if args.profile_gemm:
         profile_gemm(args)
+        return
+    if args.profile_persistent:
+        profile_persistent(args)
         return
     if args.profile_op:
         profile_op(args)

@@ -58,3 +58,27 @@ def test_clock_summary_median_and_reasons():
     s = _clocks([ok, hot, "garbage line", ""])
     assert s["reasons"] == ["sw_thermal_slowdown"] and s["samples"] == 2
     assert _clocks([])["sm_mhz"] is None
+
+
+def test_step_timeline_segments_add_up_to_the_step():
+    """bench.timeline: consecutive segments ordered by each unit's last DONE
+    sum to the traced step, per op summed over layers."""
+    import numpy as np
+
+    import bench
+
+    dt = np.dtype([("tag", "<u4"), ("cta", "<u4"), ("event", "<u4"), ("sm", "<u4"), ("ns", "<u8")])
+    recs = []
+    t = 1000
+    for layer in range(3):
+        for op in (32, 33, 34, 35):
+            for cta in range(4):
+                recs.append(((op << 16) | layer, cta, 2, 0, t + 10 * cta))        # INPUT
+                recs.append(((op << 16) | layer, cta, 4, 0, t + 100 + 10 * cta))  # DONE
+            t += 200
+    recs.append((37 << 16, 0, 0, 0, 900))  # START, the step's first record
+    tr = np.array(recs, dtype=dt)
+    tl = bench.timeline(tr, bench.PERSIST_NAMES)
+    assert abs(sum(tl["segments_us"].values()) - tl["step_us"]) < 1e-6
+    assert tl["step_us"] == (t - 200 + 130 - 900) / 1e3
+    assert tl["own_work_us_per_launch"]["q|k|v"] == 0.1

@@ -951,10 +951,13 @@ int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<
 int attn_cache_box_rows() { return kTcCh; }
 
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms) {
-  // Enough CTAs for two per SM; never a part shorter than one chunk (the
-  // tensor-core kernel's chunk is at least as long as the other's).
+  // Enough CTAs for two per SM (four when the (token, kv head) pairs are
+  // fewer than the SMs: a few long contexts need more loads in flight); never
+  // a part shorter than one chunk (the tensor-core kernel's chunk is at least
+  // as long as the other's).
   const int units = std::max(1, tokens * n_kv_heads);
-  const int want = (2 * sms + units - 1) / units;
+  const int per_sm = units < sms ? 4 : 2;
+  const int want = (per_sm * sms + units - 1) / units;
   const int chunk = std::max(attn_rows_chunk(kv_f32), kTcCh);
   const int chunks = (max_len + chunk - 1) / chunk;
   return std::max(1, std::min(want, chunks));
