@@ -835,6 +835,21 @@ def profile_persistent(args):
     print(json.dumps({"profile_persistent": st.decode, "launches": args.launches}))
 
 
+def profile_prefill(args):
+    """For ncu: config 3's 2048-token prompt at batch 1 (bf16 cache),
+    `--launches` times."""
+    import titania_b200 as tb
+    from titania_b200 import synth
+    dev = tb.B200(0)
+    m = tb.Model.load(synth.cached_model("qwen3-0.6b", seed=0), dev)
+    st = m.state(2049, kv="bf16")
+    prompt = synth.prompt_tokens(2048, synth.QWEN3_0_6B["vocab_size"], seed=3)
+    for _ in range(args.launches):
+        m.forward(st, prompt, 0, logits=False)
+    dev.sync()
+    print(json.dumps({"profile_prefill": 2048, "launches": args.launches}))
+
+
 def profile_bs64(args):
     """For ncu: config 3's prefill (`--profile-seqs` sequences x
     `--profile-ctx` tokens, one pass of 228 kernels each at the defaults), then
@@ -919,6 +934,8 @@ def main():
     ap.add_argument("--profile-ctx", type=int, default=BS64_CTX)
     ap.add_argument("--profile-persistent", action="store_true",
                     help="small case for ncu: --launches one-step launches of the persistent decode kernel")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="small case for ncu: --launches passes of config 3's 2048-token prompt")
     ap.add_argument("--profile-gemm", action="store_true",
                     help="small case for ncu: the tensor-core contraction at the batched shapes")
     args = ap.parse_args()
@@ -927,6 +944,9 @@ def main():
         return
     if args.profile_persistent:
         profile_persistent(args)
+        return
+    if args.profile_prefill:
+        profile_prefill(args)
         return
     if args.profile_op:
         profile_op(args)

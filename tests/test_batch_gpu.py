@@ -277,3 +277,26 @@ def test_tiny_batch_many_sequences_long_contexts(tiny, kv):
             close(logits[i], expected[i][1][step + 1], REL, 1.5e-2)
             assert int(nxt[i]) == expected[i][0][step + 1], f"sequence {i} step {step}"
         tokens, positions = nxt.tolist(), [p + 1 for p in positions]
+
+
+@pytest.mark.slow
+def test_config3_prompt_2048_two_layers(b200):
+    """BASELINE config 3's prompt length: 2048 uniform ids in two passes of the
+    tensor-core path, causal attention on the tensor cores over a bf16 cache,
+    on two layers of Qwen3-0.6B (every matrix its real shape) against the
+    oracle; then one single-token step over the 2048 cached positions."""
+    path = synth.cached_model("qwen3-0.6b-2l", seed=0)
+    m = tb.Model.load(path, b200)
+    ref = orc.Model(path)
+    prompt = synth.prompt_tokens(2048, 151936, seed=12)
+    rs = ref.state(2050)
+    exp = ref.forward(rs, prompt, 0)
+    st = m.state(2050, kv="bf16")
+    got = m.forward(st, prompt, 0)
+    close(got, exp, REL, 1.5e-2)
+    t = int(np.argmax(exp))
+    assert int(np.argmax(got)) == t
+    exp = ref.forward(rs, [t], 2048)
+    got = m.forward(st, [t], 2048)
+    close(got, exp, REL, 1.5e-2)
+    assert int(np.argmax(got)) == int(np.argmax(exp))

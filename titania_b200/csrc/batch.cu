@@ -910,6 +910,221 @@ __global__ void __launch_bounds__(256) k_argmax_finish(ArgmaxRowsArgs a, unsigne
   if (threadIdx.x == 0) a.trace.at(0, TB200_TRACE_DONE);
 }
 
+// ---- causal prompt attention on the tensor cores (bf16 cache) -------------------
+//
+// CTA (query block, kv group g) of 4 warps; warp w owns query rows 16w ..
+// 16w+15 of the block (row r = token r / GRP, head r % GRP of the group).
+// For every 64-position tile of keys and values (double-buffered in shared
+// memory with cp.async, rows padded to 272 bytes so that ldmatrix reads
+// distinct banks): scores S = Q K^T with mma.sync m16n8k16 (Q as two bf16
+// planes, q = q0 + q1 to 2^-17, K exact), a base-2 online softmax per row
+// (the four lanes of a quad share a row), then O += P V with P as two bf16
+// planes taken straight from the score accumulators. The result leaves as
+// the three bf16 planes of O / l, the next contraction's operand.
+constexpr int kPQR = 64;            // query rows per CTA
+constexpr int kPKT = 64;            // cache positions per tile
+constexpr int kPRow = kD + 8;       // shared-memory row of a tile, in bf16 elements (272 bytes)
+constexpr size_t kPTile = size_t(kPKT) * kPRow * 2;
+constexpr size_t kPrefillTcSmem = 4 * kPTile;  // K and V, two stages
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
+}
+__device__ __forceinline__ float bf_round(float v) { return bf16f(f2bf(v)); }
+
+template <int GRP>
+__global__ void __launch_bounds__(128) k_attn_prefill_tc(AttnPrefillArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_pf[];
+  uint16_t* tiles = reinterpret_cast<uint16_t*>(smem_pf);  // [stage][K | V][kPKT][kPRow]
+  constexpr int QT = kPQR / GRP;  // tokens per CTA
+  pdl_launch_dependents();
+  pdl_wait();
+  const int nqb = (a.T + QT - 1) / QT;
+  const int qb = nqb - 1 - int(blockIdx.x);  // longest rows first
+  const int g = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
+  const int tok0 = qb * QT;
+  const int qtok = min(QT, a.T - tok0);
+  const int kend = a.pos0 + tok0 + qtok;  // keys [0, kend) cover every row's causal window
+  const uint16_t* kc = static_cast<const uint16_t*>(a.kv) + size_t(g) * a.max_len * kD;
+  const uint16_t* vc = kc + size_t(a.n_kv_heads) * a.max_len * kD;
+
+  // This lane's two rows and their positions (the causal limits).
+  int rtok[2], rqp[2];
+  bool rok[2];
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int r = 16 * warp + gq + 8 * i;
+    rtok[i] = r / GRP;
+    rok[i] = rtok[i] < qtok;
+    rqp[i] = a.pos0 + tok0 + rtok[i];
+  }
+  auto qval = [&](int i, int d) -> float {
+    const int r = 16 * warp + gq + 8 * i;
+    return rok[i] ? a.q[size_t(tok0 + rtok[i]) * a.ldq + size_t(g * GRP + r % GRP) * kD + d] : 0.f;
+  };
+  // Q as A fragments, two planes: a0 = (row gq, dims 2tq, 2tq+1), a1 = row
+  // gq + 8, a2 / a3 the same at dims + 8, per 16-dim k-block.
+  uint32_t qa[2][8][4];
+#pragma unroll
+  for (int kb = 0; kb < 8; kb++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int i = j & 1, d = 16 * kb + 2 * tq + 8 * (j >> 1);
+      const float x0 = qval(i, d), x1 = qval(i, d + 1);
+      qa[0][kb][j] = pack2(x0, x1);
+      qa[1][kb][j] = pack2(x0 - bf_round(x0), x1 - bf_round(x1));
+    }
+
+  auto load_tile = [&](int kt, int stage) {
+    uint16_t* ks = tiles + size_t(stage) * 2 * kPKT * kPRow;
+    uint16_t* vs = ks + kPKT * kPRow;
+    for (int i = tid; i < kPKT * (kD / 8); i += 128) {
+      const int r = i / (kD / 8), c = (i % (kD / 8)) * 8;
+      const int p = kt * kPKT + r;
+      const bool ok = p < a.max_len;
+      const size_t at = size_t(ok ? p : 0) * kD + c;
+      cp_async16(ks + r * kPRow + c, kc + at, ok);
+      cp_async16(vs + r * kPRow + c, vc + at, ok);
+    }
+    cp_async_commit();
+  };
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  const float scale2 = 1.4426950408889634f / sqrtf(float(kD));
+  const int ntiles = (kend + kPKT - 1) / kPKT;
+  load_tile(0, 0);
+  for (int kt = 0; kt < ntiles; kt++) {
+    if (kt + 1 < ntiles) {
+      load_tile(kt + 1, (kt + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint16_t* ks = tiles + size_t(kt & 1) * 2 * kPKT * kPRow;
+    const uint16_t* vs = ks + kPKT * kPRow;
+    // S = Q K^T over the tile's 64 positions: n-block nb = positions 8nb .. 8nb+7.
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+      for (int kbp = 0; kbp < 4; kbp++) {
+        uint32_t b[4];
+        ldsm_x4(smem_u32(ks + (nb * 8 + (lane & 7)) * kPRow + 32 * kbp + (lane >> 3) * 8), b);
+#pragma unroll
+        for (int pl = 0; pl < 2; pl++) {
+          mma16816(s[nb], qa[pl][2 * kbp], b[0], b[1]);
+          mma16816(s[nb], qa[pl][2 * kbp + 1], b[2], b[3]);
+        }
+      }
+    }
+    // Online softmax, base 2: lane holds rows (gq, gq + 8) at positions
+    // 8nb + 2tq + {0, 1}; a row's four lanes are a quad.
+    float mx[2] = {m[0], m[1]};
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = j >> 1, p = kt * kPKT + 8 * nb + 2 * tq + (j & 1);
+        const float v = (rok[i] && p <= rqp[i]) ? s[nb][j] * scale2 : -INFINITY;
+        s[nb][j] = v;
+        mx[i] = fmaxf(mx[i], v);
+      }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+    }
+    float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 2; i++) corr[i] = mx[i] == -INFINITY ? 1.f : exp2f(m[i] - mx[i]);
+#pragma unroll
+    for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = j >> 1;
+        const float p = s[nb][j] == -INFINITY ? 0.f : exp2f(s[nb][j] - mx[i]);
+        s[nb][j] = p;
+        rs[i] += p;
+      }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      l[i] = l[i] * corr[i] + rs[i];  // this lane's share; the quad sums at the end
+      m[i] = mx[i];
+    }
+#pragma unroll
+    for (int n = 0; n < 16; n++) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+    // O += P V: k-block kb = positions 16kb .. 16kb+15 (score n-blocks 2kb, 2kb+1).
+#pragma unroll
+    for (int kb = 0; kb < 4; kb++) {
+      uint32_t pa[2][4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int nb = 2 * kb + (j >> 1), c = (j & 1) * 2;
+        const float x0 = s[nb][c], x1 = s[nb][c + 1];
+        pa[0][j] = pack2(x0, x1);
+        pa[1][j] = pack2(x0 - bf_round(x0), x1 - bf_round(x1));
+      }
+#pragma unroll
+      for (int nbp = 0; nbp < 8; nbp++) {
+        uint32_t b[4];
+        const int mi = lane >> 3;  // matrix: (positions +0 / +8, dims +0 / +8)
+        ldsm_x4_t(smem_u32(vs + (16 * kb + (mi & 1) * 8 + (lane & 7)) * kPRow + 16 * nbp + (mi >> 1) * 8), b);
+#pragma unroll
+        for (int pl = 0; pl < 2; pl++) {
+          mma16816(o[2 * nbp], pa[pl], b[0], b[1]);
+          mma16816(o[2 * nbp + 1], pa[pl], b[2], b[3]);
+        }
+      }
+    }
+    __syncthreads();  // the stage is reloaded two tiles later
+  }
+  // Normalise and store the three planes of each output value.
+  float inv[2];
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    float L = l[i];
+    L += __shfl_xor_sync(0xffffffffu, L, 1);
+    L += __shfl_xor_sync(0xffffffffu, L, 2);
+    inv[i] = L > 0.f ? 1.0f / L : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    if (!rok[i]) continue;
+    const int r = 16 * warp + gq + 8 * i;
+    const size_t row = size_t(tok0 + rtok[i]) * a.ldo + size_t(g * GRP + r % GRP) * kD;
+#pragma unroll
+    for (int n = 0; n < 16; n++)
+#pragma unroll
+      for (int j = 0; j < 2; j++) store_split3(a.out, a.plane, row + 8 * n + 2 * tq + j, o[n][2 * i + j] * inv[i]);
+  }
+}
+
+template <int G>
+cudaError_t prefill_tc_attr() {
+  return cudaFuncSetAttribute(k_attn_prefill_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(kPrefillTcSmem));
+}
+
 template <int G>
 cudaError_t tc_attr() {
   return cudaFuncSetAttribute(k_attn_rows_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
@@ -941,6 +1156,10 @@ cudaError_t init_batch_kernels() {
   if (e == cudaSuccess) e = tc_attr<2>();
   if (e == cudaSuccess) e = tc_attr<4>();
   if (e == cudaSuccess) e = tc_attr<8>();
+  if (e == cudaSuccess) e = prefill_tc_attr<1>();
+  if (e == cudaSuccess) e = prefill_tc_attr<2>();
+  if (e == cudaSuccess) e = prefill_tc_attr<4>();
+  if (e == cudaSuccess) e = prefill_tc_attr<8>();
   return e;
 }
 
@@ -951,13 +1170,11 @@ int attn_rows_chunk(bool kv_f32) { return kv_f32 ? RowsCfg<true>::kCh : RowsCfg<
 int attn_cache_box_rows() { return kTcCh; }
 
 int attn_rows_parts(int tokens, int n_kv_heads, int max_len, bool kv_f32, int sms) {
-  // Enough CTAs for two per SM (four when the (token, kv head) pairs are
-  // fewer than the SMs: a few long contexts need more loads in flight); never
-  // a part shorter than one chunk (the tensor-core kernel's chunk is at least
-  // as long as the other's).
+  // Enough CTAs for two per SM; never a part shorter than one chunk (the
+  // tensor-core kernel's chunk is at least as long as the other's). Four per
+  // SM measured slower at batch 1 (the last CTA merges twice the partials).
   const int units = std::max(1, tokens * n_kv_heads);
-  const int per_sm = units < sms ? 4 : 2;
-  const int want = (per_sm * sms + units - 1) / units;
+  const int want = (2 * sms + units - 1) / units;
   const int chunk = std::max(attn_rows_chunk(kv_f32), kTcCh);
   const int chunks = (max_len + chunk - 1) / chunk;
   return std::max(1, std::min(want, chunks));
@@ -1012,6 +1229,15 @@ void launch_attn_rows(cudaStream_t s, const AttnRowsArgs& a, int tokens, int gro
 
 void launch_attn_prefill(cudaStream_t s, const AttnPrefillArgs& a, int group, bool pdl) {
   if (a.T <= 0) return;
+  if (!a.kv_f32) {  // bf16 cache: the tensor cores
+    const int qt = kPQR / group;
+    const dim3 grid(unsigned((a.T + qt - 1) / qt), unsigned(a.n_kv_heads));
+    if (group == 1) launch_pdl(s, grid, dim3(128), kPrefillTcSmem, pdl, k_attn_prefill_tc<1>, a);
+    if (group == 2) launch_pdl(s, grid, dim3(128), kPrefillTcSmem, pdl, k_attn_prefill_tc<2>, a);
+    if (group == 4) launch_pdl(s, grid, dim3(128), kPrefillTcSmem, pdl, k_attn_prefill_tc<4>, a);
+    if (group == 8) launch_pdl(s, grid, dim3(128), kPrefillTcSmem, pdl, k_attn_prefill_tc<8>, a);
+    return;
+  }
   const int qt = kPR / group;
   const dim3 grid(unsigned((a.T + qt - 1) / qt), unsigned(a.n_kv_heads));
 #define TB_PRE(G)                                                                                          \
