@@ -193,9 +193,11 @@ TB200_API int tb200_argmax(tb200_device* dev, const tb200_buffer* logits, uint32
  * library (about 16 KB per GPU, held until the process exits), which limits
  * `n` to 8,388,608; larger inputs return TB200_ERR_ARG. The first call on a
  * GPU looks the array up on that GPU (set-up, once per device); make that
- * first call before any stream capture. Calls share the array, so calls
- * whose work overlaps on the GPU (other streams, other threads) race and
- * must be ordered by the caller. */
+ * first call before any stream capture. The looked-up address is kept for
+ * the life of the process: after a cudaDeviceReset of a GPU (a new primary
+ * context), do not call this entry point on that GPU again. Calls share the
+ * array, so calls whose work overlaps on the GPU (other streams, other
+ * threads) race and must be ordered by the caller. */
 TB200_API int tb200_argmax_noalloc(const float* logits, size_t n, uint32_t* out, void* stream);
 
 /* ---- Fused model path --------------------------------------------------- */

@@ -49,10 +49,10 @@
 namespace {
 
 // ---------------------------------------------------------------------------
-// Numerics helpers (model/cpu.rs:247-282)
+// Numerics helpers (model/cpu.rs:159-193)
 // ---------------------------------------------------------------------------
 
-// cpu.rs:248-250 — bf16 is the top half of an f32.
+// cpu.rs:159-161 — bf16 is the top half of an f32.
 inline float bf16(uint16_t bits) {
   uint32_t u = uint32_t(bits) << 16;
   float f;
@@ -60,7 +60,7 @@ inline float bf16(uint16_t bits) {
   return f;
 }
 
-// cpu.rs:256-266 — eight running sums over chunks of eight, summed in order,
+// cpu.rs:167-177 — eight running sums over chunks of eight, summed in order,
 // plus the (sequential) sum of a ragged tail.
 float dot(const uint16_t* w, const float* x, size_t n) {
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -74,14 +74,14 @@ float dot(const uint16_t* w, const float* x, size_t n) {
   return s + rest;
 }
 
-// cpu.rs:268-270
+// cpu.rs:179-181
 float dot_f32(const float* a, const float* b, size_t n) {
   float s = -0.0f;
   for (size_t i = 0; i < n; i++) s += a[i] * b[i];
   return s;
 }
 
-// cpu.rs:272-282 — f32::max ignores NaN like fmaxf.
+// cpu.rs:183-193 — f32::max ignores NaN like fmaxf.
 void softmax(float* x, size_t n) {
   float mx = -INFINITY;
   for (size_t i = 0; i < n; i++) mx = fmaxf(mx, x[i]);

@@ -77,7 +77,7 @@ def bf16(bits):
 # --- numpy restatement of model/cpu.rs ---------------------------------------
 
 def dot_rows(w, x):
-    """cpu.rs:256-266 for every row of w at once: eight running sums in
+    """cpu.rs:167-177 for every row of w at once: eight running sums in
     order, summed in order, plus the ragged tail."""
     wf = bf16(w)
     rows, cols = wf.shape

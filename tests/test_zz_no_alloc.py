@@ -38,6 +38,10 @@ def test_noalloc_argmax_matches_argmax_on_consecutive_calls():
         if tie:  # equal maxima: both entry points take the lowest index
             x[n // 3] = x[2 * n // 3] = np.float32(9.5)
         cases.append(x)
+    # the maximum in the last, partial tile (151936 is not a multiple of the tile)
+    last = rng.standard_normal(151936).astype(np.float32)
+    last[-1] = np.float32(12.0)
+    cases.append(last)
     out = torch.zeros(1, dtype=torch.int32, device="cuda")
     for x in cases:  # consecutive calls share and reuse the scratch
         logits = torch.from_numpy(x).to("cuda")
@@ -45,7 +49,9 @@ def test_noalloc_argmax_matches_argmax_on_consecutive_calls():
         torch.cuda.synchronize()
         buf = dev.alloc(x.size)
         dev.write(buf, x)
-        assert int(out.item()) == dev.argmax(buf)
+        got = int(out.item())
+        assert got == dev.argmax(buf)
+        assert got == int(np.argmax(x))  # numpy: the first index of the maximum
 
 
 def test_noalloc_argmax_rejects_inputs_beyond_its_scratch():

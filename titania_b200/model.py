@@ -519,6 +519,19 @@ class DeviceSampler:
     __del__ = close
 
 
+def _libm_expf():
+    """The platform libm's expf, which Rust's f32::exp calls on Linux."""
+    import ctypes.util
+    libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+    f = libm.expf
+    f.restype = ctypes.c_float
+    f.argtypes = [ctypes.c_float]
+    return f
+
+
+_expf = _libm_expf()
+
+
 class Sampler:
     """model/sampler.rs: top-k, then top-p, at a temperature; temperature 0 is
     greedy (ties to the lowest token id)."""
@@ -544,17 +557,25 @@ class Sampler:
         order = np.lexsort((np.arange(logits.size), -key))[:k]
         if self.temperature == 0:
             return int(order[0])
+        # sampler.rs:35-50 in its order, in f32: exp through the platform libm
+        # (as Rust's f32::exp), the sum of the probabilities accumulated
+        # sequentially, then each divided by it while the running total is
+        # below top_p.
         cand = logits[order]
-        probs = np.exp((cand - cand[0]) / self.temperature).astype(np.float32)
-        probs /= probs.sum(dtype=np.float32)
-        cum, n = np.float32(0), 0
+        mx = np.float32(cand[0])
+        probs = [np.float32(_expf(float((np.float32(c) - mx) / self.temperature))) for c in cand]
+        total = np.float32(0)
         for p in probs:
+            total = np.float32(total + p)
+        cum, n = np.float32(0), 0
+        for i in range(len(probs)):
+            probs[i] = np.float32(probs[i] / total)
             if cum < self.top_p:
-                cum += p
+                cum = np.float32(cum + probs[i])
                 n += 1
-        r = self._next_f32() * cum
+        r = np.float32(self._next_f32() * cum)
         for tok, p in zip(order[:n], probs[:n]):
-            r -= p
+            r = np.float32(r - p)
             if r <= 0:
                 return int(tok)
         return int(order[n - 1])
