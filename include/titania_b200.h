@@ -273,6 +273,17 @@ TB200_API int tb200_tp_world(const tb200_tp* tp);
 TB200_API int tb200_tp_allreduce(tb200_tp* tp, tb200_buffer* buf);
 /* Attaches the group to a model before tb200_model_finalize. */
 TB200_API int tb200_model_set_tp(tb200_model* model, tb200_tp* tp);
+/* 1 when a finalized tensor-parallel model adds the single-token step's
+ * o_proj and down_proj partial sums by peer stores instead of NCCL: each
+ * rank's kernel stores its rows into every rank's receive buffer (CUDA IPC
+ * over NVLink, plain stores) and raises a per-step flag there; the next
+ * kernel waits (bounded: TB200_ERR_TIMEOUT after a second) for every rank's
+ * flag and sums the slots in rank order, so every rank computes the same
+ * values. tb200_model_finalize sets it up when every rank has its own GPU
+ * and can map the others' memory (all ranks agree, else all keep NCCL;
+ * TB200_TP_ALLREDUCE=nccl in the environment keeps NCCL). Prompts and the
+ * batched path keep NCCL. 0 otherwise. */
+TB200_API int tb200_model_tp_peer_exchange(const tb200_model* model);
 
 /* ---- many sequences ------------------------------------------------------- */
 

@@ -141,7 +141,7 @@ def test_tp_data_flow_gloo(tiny_model_dir):
 
 # ---- on two GPUs -------------------------------------------------------------
 
-def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q):
+def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0):
     # No NVLink multicast (NVLS) in tests: a rank that dies bound to a
     # multicast object can fault the other ranks' GPUs.
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -157,8 +157,27 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q):
         dist.broadcast_object_list(uid, src=0)
         group = TPGroup(dev, rank, world, uid[0])
         m = load_tp_model(model_dir, dev, group)
+        peer = m.tp_peer_exchange
         st = m.state(len(prompt) + steps + 2, kv=kv)
         logits = [m.forward(st, prompt, 0)]
+        if late:
+            # The last rank starts its first single-token step `late` seconds
+            # after the others: their kernels wait a bounded second for its
+            # partial sums and report TB200_ERR_TIMEOUT; no rank hangs.
+            import time
+            if rank == world - 1:
+                time.sleep(late)
+            tok = int(np.argmax(logits[-1]))
+            code = 0
+            try:
+                m.forward(st, [tok], len(prompt))
+            except tb.DeviceError as e:
+                code = e.code
+            q.put((rank, (peer, code)))
+            del st, m
+            group.close()
+            dist.destroy_process_group()
+            return
         toks = [int(np.argmax(logits[-1]))]
         pos = len(prompt)
         for _ in range(steps):
@@ -172,7 +191,7 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q):
         bs = m.batch_state(2, len(prompt) + steps + 2, kv=kv)
         bfirst = [m.forward_seq(bs, i, prompt, 0, logits=False) for i in range(2)]
         bgen = m.generate_batch(bs, bfirst, [len(prompt)] * 2, steps)
-        q.put((rank, (np.stack(logits), toks, gen, [bfirst] + bgen.tolist())))
+        q.put((rank, (np.stack(logits), toks, gen, [bfirst] + bgen.tolist(), peer)))
         del st, st2, bs, m
         group.close()
         dist.destroy_process_group()
@@ -181,7 +200,7 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q):
         q.put((rank, traceback.format_exc()))
 
 
-def _run_tp(model_dir, prompt, steps, kv, world=2):
+def _run_tp(model_dir, prompt, steps, kv, world=2, late=0.0):
     import multiprocessing as mp
     import socket
     with socket.socket() as s:
@@ -189,7 +208,7 @@ def _run_tp(model_dir, prompt, steps, kv, world=2):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_tp_rank, args=(r, world, port, model_dir, prompt, steps, kv, q))
+    procs = [ctx.Process(target=_gpu_tp_rank, args=(r, world, port, model_dir, prompt, steps, kv, q, late))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -240,16 +259,22 @@ def test_tp1_group_load_against_oracle(tiny_model_dir):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
-def test_tp2_tiny_against_oracle(tiny_model_dir, kv):
+@pytest.mark.parametrize("plen", [9, 70])
+def test_tp2_tiny_against_oracle(tiny_model_dir, kv, plen):
+    """Two ranks against the oracle. With a 9-token prompt the steps run the
+    short-context graph (attention + o_proj per kv group, NCCL for those
+    partials, peer stores for down_proj); past 64 positions every partial sum
+    goes by peer stores."""
     if not _two_gpus():
         pytest.skip("needs two GPUs")
     from oracle import oracle as orc
     from titania_b200 import synth
-    prompt = synth.prompt_tokens(9, 1024, seed=3)
+    prompt = synth.prompt_tokens(plen, 1024, seed=3)
     steps = 6
-    ref_tokens, ref_logits = orc.greedy_generate(orc.Model(tiny_model_dir), prompt, steps + 1)
+    ref_tokens, ref_logits = orc.greedy_generate(orc.Model(tiny_model_dir), prompt, steps + 1, max_len=plen + 16)
     out = _run_tp(tiny_model_dir, prompt, steps, kv)
-    for r, (logits, toks, gen, bgen) in out.items():
+    for r, (logits, toks, gen, bgen, peer) in out.items():
+        assert peer, f"rank {r}: the partial sums should go by peer stores on distinct GPUs"
         for i in range(steps + 1):
             close(logits[i], ref_logits[i], REL, ABS)
         assert toks == ref_tokens, f"rank {r}"
@@ -268,10 +293,25 @@ def test_tp2_qwen3_0_6b_against_oracle():
     steps = 8
     ref_tokens, ref_logits = orc.greedy_generate(orc.Model(d), prompt, steps + 1, max_len=64)
     out = _run_tp(d, prompt, steps, "f32")
-    for r, (logits, toks, gen, bgen) in out.items():
+    for r, (logits, toks, gen, bgen, peer) in out.items():
         for i in range(steps + 1):
             close(logits[i], ref_logits[i], REL, ABS)
         assert toks == ref_tokens and gen == ref_tokens, f"rank {r}"
+
+
+@pytest.mark.gpu
+def test_tp2_late_rank_times_out_without_hanging(tiny_model_dir):
+    """A rank that starts its step three seconds late: the other rank's
+    kernels give up their bounded wait for its partial sums after a second
+    and the call reports TB200_ERR_TIMEOUT; the late rank then finds the
+    other's flags set and finishes; both processes end normally."""
+    if not _two_gpus():
+        pytest.skip("needs two GPUs")
+    from titania_b200 import _lib, synth
+    prompt = synth.prompt_tokens(70, 1024, seed=4)  # past 64 positions: no NCCL in the step
+    out = _run_tp(tiny_model_dir, prompt, 1, "f32", late=3.0)
+    assert out[0] == (True, _lib.TB200_ERR_TIMEOUT), out
+    assert out[1][0] is True
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])

@@ -110,6 +110,7 @@ SIGNATURES = {
     "tb200_tp_world": (ctypes.c_int, [P]),
     "tb200_tp_allreduce": (ctypes.c_int, [P, P]),
     "tb200_model_set_tp": (ctypes.c_int, [P, P]),
+    "tb200_model_tp_peer_exchange": (ctypes.c_int, [P]),
     "tb200_state_seqs": (SZ, [P]),
     "tb200_forward_seq": (ctypes.c_int, [P, P, SZ, U32P, SZ, SZ, F32P, U32P]),
     "tb200_forward_batch": (ctypes.c_int, [P, P, U32P, SZP, F32P, U32P]),

@@ -129,6 +129,30 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     }
 
   pdl_wait();  // everything below may read what the previous kernel wrote
+  unsigned epoch = 0;
+  if (a.epoch) epoch = *reinterpret_cast<volatile unsigned*>(a.epoch);
+  if (a.nwait > 0) {
+    // Every rank's partial sum of this input has landed in our receive
+    // buffer once each rank's flag holds this step's epoch. Bounded; after a
+    // timeout (or an earlier one, recorded in the error word) the kernel
+    // goes on without waiting, and the host reports TB200_ERR_TIMEOUT.
+    if (tid == 0) {
+      const volatile unsigned* f = a.wait_flags;
+      const volatile int* err = a.err;
+      const uint64_t t0 = global_ns();
+      bool ok = *err != 0;
+      while (!ok) {
+        ok = true;
+        for (int p = 0; p < a.nwait; p++) ok = ok && f[p] == epoch;
+        if (!ok && global_ns() - t0 > kWaitNs) {
+          set_error(a.err, TB200_ERR_TIMEOUT);
+          break;
+        }
+      }
+      __threadfence_system();  // acquire: the peers' stores before their flags
+    }
+    named_sync(1, kMvWarps * 32);
+  }
   if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_WAITED);
   // The residual rows, the input and the partials are all requested before
   // any is used, so staging costs one round trip to L2.
@@ -276,6 +300,8 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
           const int row = r0 + row0 + lane;
           if (EPI == kMvResidual) {
             a.out[row] = __fadd_rn(resid[row - r0], v);
+          } else if (EPI == kMvStore && a.npeers > 0) {
+            for (int p = 0; p < a.npeers; p++) a.peer_out[p][row] = v;
           } else {
             a.out[row] = v;
             if (EPI == kMvArgmax) {
@@ -345,6 +371,8 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
           const int row = rb + lane;
           if (EPI == kMvResidual) {
             a.out[row] = __fadd_rn(resid[row - r0], v);
+          } else if (EPI == kMvStore && a.npeers > 0) {
+            for (int p = 0; p < a.npeers; p++) a.peer_out[p][row] = v;
           } else {
             a.out[row] = v;
             if (EPI == kMvArgmax) {
@@ -360,6 +388,20 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     }
   }
 
+  if (EPI == kMvStore && a.npeers > 0) {
+    // Release: every CTA's peer stores, then the last CTA to arrive writes
+    // this step's epoch into each rank's flag word for this rank.
+    __shared__ int last_p2p;
+    __threadfence_system();
+    named_sync(1, kMvWarps * 32);
+    if (tid == 0) last_p2p = atomicAdd(a.p2p_ticket, 1u) == unsigned(G - 1);
+    named_sync(1, kMvWarps * 32);
+    if (last_p2p && tid == 0) {
+      __threadfence_system();
+      *a.p2p_ticket = 0u;
+      for (int p = 0; p < a.npeers; p++) *reinterpret_cast<volatile unsigned*>(a.peer_flag[p]) = epoch;
+    }
+  }
   if (a.trace.rec) {
     named_sync(1, kMvWarps * 32);
     if (tid == 0) trace_at(a.trace, a.trace_base, a.tag, c, TB200_TRACE_DONE);
@@ -394,6 +436,7 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
         *a.step = stp + 1;
         *a.pos = *a.pos + 1;
         *a.ticket = 0u;
+        if (a.epoch) *a.epoch = epoch + 1u;  // the next step's tag for the ranks' flags
       }
     }
   }

@@ -65,6 +65,21 @@ struct MvArgs {
   Trace trace;
   uint32_t trace_base;  // first record slot of this launch
   uint32_t tag;
+  // Tensor parallelism without NCCL (the o_proj / down_proj partial sums,
+  // see P2P below): a kMvStore launch with npeers > 0 stores row r of its
+  // output at peer_out[p][r] for every rank p instead of out[r] (peer_out[p]
+  // is this rank's slot of rank p's receive buffer), and its last CTA then
+  // writes *epoch into peer_flag[p] (this rank's flag word at rank p). A
+  // launch with nwait > 0 first waits, bounded, until wait_flags[0 .. nwait)
+  // all hold *epoch (every rank's slots of its input are written). A kMvArgmax
+  // launch with epoch set advances *epoch once its step is done.
+  float* peer_out[8];
+  unsigned* peer_flag[8];
+  int npeers;
+  unsigned* p2p_ticket;  // with npeers: zero between launches
+  const unsigned* wait_flags;
+  int nwait;
+  unsigned* epoch;
 };
 
 // Rows a CTA of a residual-epilogue launch may own (staged in shared memory).

@@ -543,6 +543,8 @@ int tb200_model_finalize(tb200_model* m) {
     if (int rc = tb::encode_tmap_bf16(&m->m_lm, m->lm_head, V, H, 128, &why)) return fail(rc, "model: " + why);
   }
   CUDA_TRY(cudaStreamSynchronize(s));
+  if (m->tp)
+    if (int rc = rt::tp_p2p_setup(m)) return rc;
   m->finalized = true;
   return TB200_OK;
 }
@@ -550,6 +552,7 @@ int tb200_model_finalize(tb200_model* m) {
 static void delete_model(tb200_model* m) {
   cudaSetDevice(m->dev->ordinal);
   cudaStreamSynchronize(m->dev->stream);
+  rt::tp_p2p_free(m);
   for (auto& L : m->layers) {
     cudaFree(L.wqkv);
     cudaFree(L.wgu);
@@ -598,6 +601,27 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
   };
   a.eps = c.rms_norm_eps;
   a.row_align = 1;
+  // Tensor parallelism by peer stores: slot 0 of a layer is the o_proj
+  // partial sums, slot 1 the down_proj ones.
+  const TpP2p& pp = m->p2p;
+  auto publish = [&](size_t layer, int slot) {
+    for (int r = 0; r < pp.world; r++) {
+      unsigned char* base = static_cast<unsigned char*>(pp.peer[r]);
+      a.peer_out[r] = reinterpret_cast<float*>(base + (slot ? pp.off_d : 0)) + size_t(pp.rank) * H;
+      a.peer_flag[r] = reinterpret_cast<unsigned*>(base + pp.off_flags) + (2 * layer + slot) * pp.world + pp.rank;
+    }
+    a.npeers = pp.world;
+    a.p2p_ticket = pp.tickets + 2 * layer + slot;
+    a.epoch = pp.epoch;
+  };
+  auto receive = [&](size_t layer, int slot) {
+    unsigned char* base = static_cast<unsigned char*>(pp.region);
+    a.partials = reinterpret_cast<const float*>(base + (slot ? pp.off_d : 0));
+    a.npartials = pp.world;
+    a.wait_flags = reinterpret_cast<const unsigned*>(base + pp.off_flags) + (2 * layer + slot) * pp.world;
+    a.nwait = pp.world;
+    a.epoch = pp.epoch;
+  };
   switch (op) {
     case TB200_OP_EMBED:
       tb::launch_embed_token(s, st->x, m->embed, H, st->io + 0, int(c.vocab_size), err, pdl);
@@ -613,6 +637,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
         a.partials = st->part_tp2;
         a.npartials = 1;
         a.x_out = st->x;
+        if (pp.on) receive(l - 1, 1);  // ... summed here from every rank's slot
       }
       a.norm_w = L.attn_norm;
       a.out = st->qkv;
@@ -684,6 +709,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       a.trace_base = slots_for(st->p_o.grid);
       if (m->tp) {  // this rank's partial sum; reduced over the group next
         a.out = st->part_tp;
+        if (pp.on) publish(l, 0);
         tb::launch_mv(s, st->p_o, tb::kMvStore, a, pdl);
         return;
       }
@@ -704,6 +730,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       } else if (m->tp) {  // x + the reduced o_proj partial
         a.partials = st->part_tp;
         a.npartials = 1;
+        if (pp.on) receive(l, 0);
       }
       a.norm_w = m->layers[l].mlp_norm;
       a.out = st->h;
@@ -722,6 +749,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
       if (m->tp) {  // this rank's partial sum; the next kernel adds it to x2 once reduced
         a.out = st->part_tp2;
         a.resid_src = nullptr;
+        if (pp.on) publish(l, 1);
         tb::launch_mv(s, st->p_down, tb::kMvStore, a, pdl);
         return;
       }
@@ -737,6 +765,7 @@ void enqueue_op(tb200_state* st, int op, size_t l, bool pdl) {
         a.x = st->x2;
         a.partials = st->part_tp2;
         a.npartials = 1;
+        if (pp.on) receive(c.num_hidden_layers - 1, 1);
       }
       a.norm_w = m->norm;
       a.out = st->logits;
@@ -776,12 +805,12 @@ int enqueue_step(tb200_state* st, bool short_ctx) {
     } else {
       enqueue_op(st, TB200_OP_ATTENTION, l, pdl);
       enqueue_op(st, TB200_OP_O, l, pdl);
-      if (m->tp)
+      if (m->tp && !m->p2p.on)
         if (int rc = rt::tp_allreduce(m->tp, st->part_tp, H, s)) return rc;
       enqueue_op(st, TB200_OP_GATE_UP, l, pdl);
     }
     enqueue_op(st, TB200_OP_DOWN, l, pdl);
-    if (m->tp)
+    if (m->tp && !m->p2p.on)
       if (int rc = rt::tp_allreduce(m->tp, st->part_tp2, H, s)) return rc;
   }
   enqueue_op(st, TB200_OP_LM_HEAD, 0, pdl);

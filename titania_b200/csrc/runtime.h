@@ -70,6 +70,20 @@ struct FusedLayer {
   CUtensorMap m_qkv{}, m_o{}, m_gu{}, m_down{};
 };
 
+// Tensor parallelism without NCCL on the single-token path: each rank's
+// receive buffers for the o_proj and down_proj partial sums of every rank,
+// the flag words that say a rank's slot is written, and the other ranks'
+// buffers mapped into this process (CUDA IPC over NVLink).
+struct TpP2p {
+  bool on = false;
+  int world = 1, rank = 0;
+  void* region = nullptr;               // this rank's: recv_o [world][H], recv_d [world][H] f32, flags [2L][world]
+  void* peer[8] = {};                   // every rank's region as mapped here (this rank's: region)
+  size_t off_d = 0, off_flags = 0;      // byte offsets of recv_d and the flags in a region
+  unsigned* tickets = nullptr;          // [2L] arrival counters of the publishing launches
+  unsigned* epoch = nullptr;            // this step's flag value; advanced by the lm_head
+};
+
 struct tb200_model {
   tb200_device* dev = nullptr;
   int live_states = 0;          // states built on this model
@@ -81,6 +95,7 @@ struct tb200_model {
   const uint16_t *embed = nullptr, *norm = nullptr, *lm_head = nullptr;
   CUtensorMap m_lm{};
   tb200_tp* tp = nullptr;  // tensor-parallel group: this model holds one rank's heads and FFN columns
+  TpP2p p2p;               // single-token partial sums by peer stores (tp.cu), when every rank can
   size_t q_dim = 0, kv_dim = 0;
   int attn_o_slices = 0;  // output slices per kv group of the fused attention + o_proj
 };
@@ -165,6 +180,10 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
                    uint32_t* next);
 // Sums `n` floats at `buf` over the tensor-parallel group, on stream `s`.
 int tp_allreduce(tb200_tp* tp, float* buf, size_t n, cudaStream_t s);
+// Sets up m->p2p (every rank calls it at finalize; all ranks agree whether
+// to use it, else they keep NCCL) and releases it.
+int tp_p2p_setup(tb200_model* m);
+void tp_p2p_free(tb200_model* m);
 
 // persist.cu: why the persistent single-token step cannot run model m with
 // state st ("" when it can); enqueues `steps` greedy steps from st->io as

@@ -268,6 +268,12 @@ class Model:
             _lib.lib().tb200_model_free(self._h)
         self._h = None
 
+    @property
+    def tp_peer_exchange(self) -> bool:
+        """Whether this tensor-parallel rank's single-token step adds the
+        o_proj / down_proj partial sums by peer stores (else NCCL)."""
+        return bool(_lib.lib().tb200_model_tp_peer_exchange(self._h))
+
     def state(self, max_len: int, kv: str = "f32", decode: str | None = None) -> "State":
         return State(self, max_len, kv, decode)
 
