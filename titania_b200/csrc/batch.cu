@@ -543,9 +543,9 @@ __global__ void __launch_bounds__(128, GRP <= 2 ? 4 : 2)
     int got = 1;
     if (lane == 0) {
       // This chunk's load was issued (bounded wait), then it landed.
-      const uint64_t t0 = global_ns();
+      const long long t0 = clock64();
       while (stage_chunk[s] != i)
-        if (global_ns() - t0 > kWaitNs) {
+        if (clock64() - t0 > kWaitCycles) {
           set_error(a.err, TB200_ERR_TIMEOUT);
           got = 0;
           break;

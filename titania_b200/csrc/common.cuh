@@ -1,7 +1,7 @@
 // common.cuh — device helpers shared by the kernels: bf16 unpacking, warp
 // reductions, and thin wrappers over sm_90+/sm_100a PTX (mbarrier,
 // cp.async.bulk, programmatic dependent launch). Every wait on an mbarrier
-// is bounded in wall time; on expiry it records TB200_ERR_TIMEOUT in the
+// is bounded (kWaitCycles, about a second); on expiry it records TB200_ERR_TIMEOUT in the
 // device's error word and the kernel returns.
 #pragma once
 
@@ -13,8 +13,11 @@
 
 namespace tb {
 
-// One second: the longest any in-kernel wait may take before it gives up.
-constexpr unsigned long long kWaitNs = 1000000000ull;
+// The longest any in-kernel wait may take before it gives up: 2e9 SM cycles,
+// one second at 2 GHz (longer at lower clocks). Waits count cycles because
+// %clock64 reads in a few cycles while a %globaltimer read takes ~100 ns,
+// which a spin loop would add to every poll.
+constexpr long long kWaitCycles = 2000000000ll;
 
 __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
 // The two bf16 values packed in a 32-bit word, low half first.
@@ -156,12 +159,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with `parity` to complete, at most kWaitNs.
+// Waits for the phase with `parity` to complete, at most kWaitCycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_ns();
+  long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitNs) {
+    if (clock64() - t0 > kWaitCycles) {
       set_error(err, TB200_ERR_TIMEOUT);
       return false;
     }
@@ -179,6 +182,11 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
 
 // Bulk copy global -> this CTA's shared memory, completing on `bar`.
 // dst and src 16-byte aligned, bytes a multiple of 16.
+// Asks L2 to fetch [src, src + bytes) from memory; nothing waits for it.
+// src and bytes multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
   asm volatile(

@@ -139,12 +139,12 @@ __global__ void __launch_bounds__(kMvThreads) mv_kernel(MvArgs a, int stage_rows
     if (tid == 0) {
       const volatile unsigned* f = a.wait_flags;
       const volatile int* err = a.err;
-      const uint64_t t0 = global_ns();
+      const long long t0 = clock64();
       bool ok = *err != 0;
       while (!ok) {
         ok = true;
         for (int p = 0; p < a.nwait; p++) ok = ok && f[p] == epoch;
-        if (!ok && global_ns() - t0 > kWaitNs) {
+        if (!ok && clock64() - t0 > kWaitCycles) {
           set_error(a.err, TB200_ERR_TIMEOUT);
           break;
         }

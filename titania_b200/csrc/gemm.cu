@@ -35,7 +35,7 @@
 // Every CTA takes more than half an SM's shared memory, so no two share an
 // SM and the 512-column allocation never waits.
 //
-// Every mbarrier wait is bounded (kWaitNs); on expiry the kernel records
+// Every mbarrier wait is bounded (kWaitCycles); on expiry the kernel records
 // TB200_ERR_TIMEOUT, lets what it issued drain (bounded), frees its tensor
 // memory on every path, and returns.
 
@@ -490,9 +490,9 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
+  const long long t0 = clock64();
   while (!mbar_try_wait_cluster(bar, parity)) {
-    if (global_ns() - t0 > kWaitNs) {
+    if (clock64() - t0 > kWaitCycles) {
       set_error(err, TB200_ERR_TIMEOUT);
       return false;
     }

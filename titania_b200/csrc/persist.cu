@@ -45,7 +45,7 @@ namespace tb::persist {
 
 constexpr int kWarps = 8;                 // consumer warps
 constexpr int kConsumers = kWarps * 32;
-constexpr int kThreads = kConsumers + 32;  // + the producer warp
+constexpr int kThreads = kConsumers + 64;  // + the producer warp and the prefetch warp
 constexpr int kSlotBytes = 64 * 1024;
 constexpr int kSlots = 3;
 constexpr int kMaxLayers = 64;
@@ -185,6 +185,9 @@ __device__ __forceinline__ void ld_tagged4(const TW* p, TW (&w)[4]) {
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w[0]), "=l"(w[1]) : "l"(p) : "memory");
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w[2]), "=l"(w[3]) : "l"(p + 2) : "memory");
 }
+__device__ __forceinline__ void ld_tagged2(const TW* p, TW (&w)[2]) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w[0]), "=l"(w[1]) : "l"(p) : "memory");
+}
 __device__ __forceinline__ float tval(TW w) { return __uint_as_float(uint32_t(w)); }
 __device__ __forceinline__ uint32_t ttag(TW w) { return uint32_t(w >> 32); }
 __device__ __forceinline__ bool tags4(const TW (&w)[4], uint32_t tag) {
@@ -197,8 +200,8 @@ __device__ __forceinline__ bool tags4(const TW (&w)[4], uint32_t tag) {
 __device__ __forceinline__ int xperm(int i) { return (i & ~255) + ((i >> 2) & 1) * 128 + ((i >> 3) & 31) * 4; }
 
 // Records a timeout: the error word, and this CTA's abort flag.
-__device__ __forceinline__ bool timed_out(uint64_t t0, int* err, volatile int* abort) {
-  if (global_ns() - t0 <= kWaitNs) return false;
+__device__ __forceinline__ bool timed_out(long long t0, int* err, volatile int* abort) {
+  if (clock64() - t0 <= kWaitCycles) return false;
   set_error(err, TB200_ERR_TIMEOUT);
   *abort = 1;
   return true;
@@ -310,7 +313,7 @@ __device__ float poll_vector(const TW* vec, int n, uint32_t tag, const uint16_t*
 #pragma unroll
   for (int k = 0; k < kG; k++) done[k] = tid * 4 + k * kConsumers * 4 >= n;
   float ss = 0.f;
-  const uint64_t t0 = global_ns();
+  const long long t0 = clock64();
   for (;;) {
     bool all = true;
 #pragma unroll
@@ -371,12 +374,13 @@ __device__ __forceinline__ float4 as_cached(float4 v, bool f32) {
 // the online softmax, and the probabilities are broadcast for the weighted
 // sum of values, each lane holding 4 of the 128 dimensions. The warps are
 // merged at the end. In split mode the members then exchange partials (tag
-// `ptag`) and every member merges all of them in member order. The result,
+// `ptag`) and every member merges all of them in one fixed order. The result,
 // GRP heads of 128, goes to xs at xperm positions (the o_proj partial's
 // input). `sc` is shared scratch of at least 4960 floats.
 template <int GRP>
 __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, int ng, int pos, uint32_t qtag,
-                                uint32_t ptag, float* xs, float* sc, int tid, volatile int* abort) {
+                                uint32_t ptag, float* xs, float* sc, int tid, volatile int* abort, const TraceAt& tr,
+                                int cta) {
   constexpr int grp = GRP;
   constexpr int PR = GRP * kAttnPer;  // (head, slot) scores of a chunk
   const int warp = tid >> 5, lane = tid & 31;
@@ -417,7 +421,7 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
   if (warp < grp + 2) {
     const int at = warp < grp ? (g * grp + warp) * kHd : warp == grp ? a.Q + g * kHd : a.Q + a.KV + g * kHd;
     TW w[4];
-    const uint64_t t0 = global_ns();
+    const long long t0 = clock64();
     for (;;) {
       ld_tagged4(a.qkv + at + 4 * lane, w);
       if (tags4(w, qtag) || *abort || timed_out(t0, a.io + 3, abort)) break;
@@ -459,6 +463,7 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
     *reinterpret_cast<float4*>((warp < grp ? qs + warp * kHd : warp == grp ? kn : vn) + 4 * lane) = v;
   }
   named_sync(1, kConsumers);
+  if (tid == 0) tr.at(cta, TB200_TRACE_WAITED);
 
   // Online softmax per warp over its positions of [lo, hi), eight at a time.
   const float scale = 1.0f / sqrtf(float(kHd));
@@ -560,7 +565,7 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
     }
   }
   if (split) {
-    // Publish this member's partial, then merge every member's in order.
+    // Publish this member's partial; then every member merges all of them.
     TW* mine = a.part_att + (size_t(g * a.nsplit + s) * grp) * kPartWords;
     if (tid < grp * 32) {
       TW* p = mine + mh * kPartWords;
@@ -575,30 +580,62 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
         st_tagged(p + 131, 0.f, ptag);
       }
     }
+    // Every member merges all members' partials: the consumer threads form
+    // kWarps / grp quarters of (head, 4 dims) threads; quarter q merges
+    // members q, q + nq, ... (two requested at once, merged in that order),
+    // then the quarters' results are merged in quarter order. The order is
+    // fixed, so every member gets the same bits whatever the timing.
+    const int nq = kWarps / grp, q = tid / (grp * 32), qh = (tid >> 5) % grp, qd = tid & 31;
+    float4 qo = make_float4(0.f, 0.f, 0.f, 0.f);
+    float qm = -INFINITY, ql = 0.f;
+    auto merge = [](float4& o, float& M, float& L, const TW (&w)[4], const TW (&ml)[2]) {
+      const float ms = tval(ml[0]), ls = tval(ml[1]);
+      if (ls > 0.f) {
+        const float Mn = fmaxf(M, ms);
+        const float cold = expf(M - Mn), cnew = expf(ms - Mn);
+        o.x = o.x * cold + tval(w[0]) * cnew;
+        o.y = o.y * cold + tval(w[1]) * cnew;
+        o.z = o.z * cold + tval(w[2]) * cnew;
+        o.w = o.w * cold + tval(w[3]) * cnew;
+        L = L * cold + ls * cnew;
+        M = Mn;
+      }
+    };
+    const long long t0 = clock64();
+    for (int sp = q; sp < ng; sp += 2 * nq) {
+      const bool two = sp + nq < ng;
+      const TW* p0 = a.part_att + (size_t(g * a.nsplit + sp) * grp + qh) * kPartWords;
+      const TW* p1 = a.part_att + (size_t(g * a.nsplit + (two ? sp + nq : sp)) * grp + qh) * kPartWords;
+      TW w0[4], w1[4], m0[2], m1[2];
+      for (;;) {
+        ld_tagged4(p0 + 4 * qd, w0);
+        ld_tagged2(p0 + 128, m0);
+        ld_tagged4(p1 + 4 * qd, w1);
+        ld_tagged2(p1 + 128, m1);
+        const bool ok = tags4(w0, ptag) && ttag(m0[0]) == ptag && ttag(m0[1]) == ptag && tags4(w1, ptag) &&
+                        ttag(m1[0]) == ptag && ttag(m1[1]) == ptag;
+        if (ok || *abort || timed_out(t0, a.io + 3, abort)) break;
+      }
+      merge(qo, qm, ql, w0, m0);
+      if (two) merge(qo, qm, ql, w1, m1);
+    }
+    named_sync(1, kConsumers);  // the warp merge above is done with wacc, wm, wl
+    *reinterpret_cast<float4*>(wacc + (q * grp + qh) * kHd + 4 * qd) = qo;
+    if (qd == 0) {
+      wm[q * kMaxGrp + qh] = qm;
+      wl[q * kMaxGrp + qh] = ql;
+    }
+    named_sync(1, kConsumers);
     o = make_float4(0.f, 0.f, 0.f, 0.f);
     M = -INFINITY;
     Ls = 0.f;
     if (tid < grp * 32) {
-      const uint64_t t0 = global_ns();
-      for (int sp = 0; sp < ng; sp++) {
-        const TW* p = a.part_att + (size_t(g * a.nsplit + sp) * grp + mh) * kPartWords;
-        TW w[4], ml[4];
-        for (;;) {
-          ld_tagged4(p + 4 * d4, w);
-          ld_tagged4(p + 128, ml);
-          if ((tags4(w, ptag) && tags4(ml, ptag)) || *abort || timed_out(t0, a.io + 3, abort)) break;
-        }
-        const float ms = tval(ml[0]), ls = tval(ml[1]);
-        if (ls > 0.f) {
-          const float Mn = fmaxf(M, ms);
-          const float cold = expf(M - Mn), cnew = expf(ms - Mn);
-          o.x = o.x * cold + tval(w[0]) * cnew;
-          o.y = o.y * cold + tval(w[1]) * cnew;
-          o.z = o.z * cold + tval(w[2]) * cnew;
-          o.w = o.w * cold + tval(w[3]) * cnew;
-          Ls = Ls * cold + ls * cnew;
-          M = Mn;
-        }
+      for (int u = 0; u < nq; u++) {
+        const float4 v = *reinterpret_cast<const float4*>(wacc + (u * grp + mh) * kHd + 4 * d4);
+        const TW w[4] = {TW(__float_as_uint(v.x)), TW(__float_as_uint(v.y)), TW(__float_as_uint(v.z)),
+                         TW(__float_as_uint(v.w))};
+        const TW ml[2] = {TW(__float_as_uint(wm[u * kMaxGrp + mh])), TW(__float_as_uint(wl[u * kMaxGrp + mh]))};
+        merge(o, M, Ls, w, ml);
       }
     }
   }
@@ -609,6 +646,39 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
 }
 
 // ---- the kernel -----------------------------------------------------------------
+
+// L2 prefetch of [p, p + bytes) (bytes a multiple of 16) in pieces.
+__device__ __forceinline__ void prefetch_range(const void* p, size_t bytes) {
+  constexpr size_t kPiece = 32 * 1024;
+  const char* b = static_cast<const char*>(p);
+  for (size_t o = 0; o < bytes; o += kPiece) bulk_prefetch_l2(b + o, uint32_t(min(kPiece, bytes - o)));
+}
+
+// Asks L2 for CTA c's rows of phase `kind` of `layer` in step `step` (the
+// lm_head: its first ring's worth) and, for ATT_O, the CTA's cached keys and
+// values (positions < pos), so that HBM keeps streaming while the ring is
+// full and the consumers wait for a vector.
+__device__ void prefetch_phase(const Args& a, const Plan& pl, int c, int G, int pos0, int step, int layer, int kind) {
+  if (step >= a.steps) return;
+  const Layer& Ly = a.layer[layer < a.L ? layer : 0];
+  size_t bytes = size_t(pl.n) * size_t(pl.cols) * 2;
+  if (kind == K_LM) bytes = min(bytes, size_t(kSlots) * kSlotBytes);
+  prefetch_range(matrix_of(a, Ly, kind) + pl.w0 * pl.cols, bytes);
+  if (kind == K_ATTO) {
+    int g, s, ng;
+    group_of(a, c, G, g, s, ng);
+    const int pos = pos0 + step, ctx = pos + 1;
+    const bool split = ctx > kRedundantCtx;
+    const int lo = split ? int((long long)s * ctx / ng) : 0;
+    const int hi = min(pos, split ? int((long long)(s + 1) * ctx / ng) : ctx);
+    if (hi > lo) {
+      const size_t esz = a.kv_f32 ? 4 : 2;
+      const size_t at = (size_t(g) * a.max_len + lo) * kHd * esz, nb = size_t(hi - lo) * kHd * esz;
+      prefetch_range(static_cast<const char*>(Ly.kc) + at, nb);
+      prefetch_range(static_cast<const char*>(Ly.vc) + at, nb);
+    }
+  }
+}
 
 template <int GRP>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
@@ -623,6 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
   __shared__ Plan plan[kKinds];
   __shared__ volatile int abort_sm;  // a wait gave up (or the arguments are bad): wait no more
   __shared__ volatile int issued_sm;
+  __shared__ volatile int progress_sm;  // the consumers' last phase with its input complete (prefetch warp)
   __shared__ int tok_sm;
 
   const int c = blockIdx.x, G = gridDim.x;
@@ -641,6 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
                     tok0 >= 0 && tok0 < a.V;
     abort_sm = ok ? 0 : 1;
     issued_sm = 0;
+    progress_sm = -1;
     tok_sm = tok0;
     if (!ok && c == 0) set_error(a.io + 3, TB200_ERR_ARG);
     trace_at(a.trace, 0, uint32_t(TB200_TRACE_OP_P_START) << 16, c, TB200_TRACE_START);
@@ -648,7 +720,29 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
   __syncthreads();
   const bool valid = !abort_sm;  // uniform: nothing is written for invalid arguments
 
-  if (warp == kWarps) {
+  if (warp == kWarps + 1) {
+    // ---- prefetch: each phase one layer ahead, once the consumers have the
+    // phase's input (a bulk prefetch waits behind the ring's copies in the
+    // copy engine, so it is issued from a thread that has nothing else to
+    // do; and after the exchange, which it would slow) ----
+    if (lane == 0 && valid) {
+      for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, 0, 0, q);
+      for (int step = 0; step < a.steps && !abort_sm; step++)
+        for (int layer = 0; layer <= a.L && !abort_sm; layer++)
+          for (int p = 0; p < kPhases && !abort_sm; p++) {
+            if (layer == a.L && p != 0) break;
+            const int ph = step * (4 * a.L + 1) + 4 * layer + p;  // as the consumers count
+            // Bounded; a prefetch that never comes costs time, not results.
+            const long long t0 = clock64();
+            while (progress_sm < ph && !abort_sm && clock64() - t0 < kWaitCycles) __nanosleep(32);
+            if (progress_sm < ph) break;
+            if (layer + 1 < a.L) prefetch_phase(a, plan[p], c, G, pos0, step, layer + 1, p);
+            else if (layer + 1 == a.L && p == 0) prefetch_phase(a, plan[K_LM], c, G, pos0, step, a.L, K_LM);
+            else if (layer == a.L)
+              for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, step + 1, 0, q);
+          }
+    }
+  } else if (warp == kWarps) {
     // ---- producer: every matrix phase's rows of this CTA, in phase order ----
     if (lane == 0 && valid) {
       const uint64_t pol = l2_evict_first();
@@ -672,6 +766,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
               bulk_g2s(ring + size_t(slot) * kSlotBytes, w + size_t(r) * pl.cols, bytes, &full[slot], pol);
               issued_sm = k + 1;
             }
+            trace_at(a.trace, layer == a.L ? trace_base(a.L, 0, G) : trace_base(layer, p, G),
+                     (uint32_t(TB200_TRACE_OP_P_QKV + kind) << 16) | uint32_t(layer), c, TB200_TRACE_ISSUED);
           }
     }
   } else if (valid) {
@@ -687,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
       // The token: the launch's input, or the previous step's choice.
       if (step > 0) {
         if (tid == 0) {
-          const uint64_t t0 = global_ns();
+          const long long t0 = clock64();
           TW w = 0;
           for (;;) {
             w = ld_tagged(a.tokw);
@@ -723,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
           float scale = 1.0f;
           if (kind == K_ATTO) {
             attention_phase<GRP>(a, Ly, ag, as, ang, pos, phase_tag(T, layer, K_QKV), out_tag, xs, xs + 1024, tid,
-                                 &abort_sm);
+                                 &abort_sm, tr, c);
             named_sync(1, kConsumers);
           } else {
             const int n_in = kind == K_DOWN ? a.F : a.H;
@@ -746,7 +842,10 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
               scale = 1.0f / sqrtf(tot / float(n_in) + a.eps);
             }
           }
-          if (tid == 0) tr.at(c, TB200_TRACE_INPUT);
+          if (tid == 0) {
+            tr.at(c, TB200_TRACE_INPUT);
+            progress_sm = step * (4 * a.L + 1) + 4 * layer + p;
+          }
           const Plan pl = plan[kind];
           const int rb = pl.cols * 2;
           for (int b = 0; b < pl.nst; b++, k++) {
@@ -756,6 +855,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
             if (kind == K_GU) rpw = (rpw + 1) & ~1;
             const int first = warp * rpw, nr = max(0, min(rpw, nrs - first));
             wait_full(&full[slot], (k / kSlots) & 1, a.io + 3, &abort_sm);
+            if (tid == 0 && b == 0) tr.at(c, TB200_TRACE_WEIGHTS);
+            if (tid == 0 && b == pl.nst - 1) tr.at(c, TB200_TRACE_LAST_WEIGHTS);
             const unsigned char* wbase = ring + size_t(slot) * kSlotBytes + size_t(first) * rb;
             WarpRows d{0.f, 1 << 20, 32};
             switch (nr) {
@@ -804,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
             const int r = own0 + tid;
             float xv = own[tid];
             TW w[kMaxKv];
-            const uint64_t t0 = global_ns();
+            const long long t0 = clock64();
             for (;;) {
               bool ok = true;
 #pragma unroll
