@@ -59,6 +59,8 @@ constexpr int kAttnPer = 8;          // cached positions per warp held in regist
 constexpr int kRedundantCtx = 256;   // contexts up to this: every group member attends over all of it
 constexpr int kPartWords = 132;      // a member's partial per head: acc[128], max, sum, 2 pad
 constexpr int kRep = 4;              // copies of the vectors every CTA reads (x, h): CTA c reads copy c % kRep
+constexpr int kLmAheadLayers = 8;    // the lm_head's first kLmAheadNum / kLmAheadDen of rows are asked of L2
+constexpr int kLmAheadNum = 1, kLmAheadDen = 6;  //   during the last kLmAheadLayers layers (a third measured no better)
 constexpr size_t kSmemBytes = size_t(kMaxCols) * 2 * 4 + size_t(kSlots) * kSlotBytes + 2 * kSlots * 8;
 
 using TW = unsigned long long;  // a tagged word
@@ -737,7 +739,16 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
             while (progress_sm < ph && !abort_sm && clock64() - t0 < kWaitCycles) __nanosleep(32);
             if (progress_sm < ph) break;
             if (layer + 1 < a.L) prefetch_phase(a, plan[p], c, G, pos0, step, layer + 1, p);
-            else if (layer + 1 == a.L && p == 0) prefetch_phase(a, plan[K_LM], c, G, pos0, step, a.L, K_LM);
+            // The head of this CTA's lm_head rows, spread over the last
+            // layers, whose phases leave HBM idle while they exchange.
+            const int j = layer - (a.L - kLmAheadLayers);
+            if (j >= 0 && layer < a.L && p == 2) {
+              const Plan& lm = plan[K_LM];
+              const size_t total = size_t(lm.n) * size_t(lm.cols) * 2 * kLmAheadNum / kLmAheadDen / 16 * 16;
+              const size_t c0 = total * size_t(j) / kLmAheadLayers / 16 * 16;
+              const size_t c1 = total * size_t(j + 1) / kLmAheadLayers / 16 * 16;
+              prefetch_range(reinterpret_cast<const char*>(a.lm_head + lm.w0 * lm.cols) + c0, c1 - c0);
+            }
             else if (layer == a.L)
               for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, step + 1, 0, q);
           }
