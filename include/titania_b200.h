@@ -339,9 +339,10 @@ TB200_API int tb200_generate(tb200_model* model, tb200_state* state, uint32_t to
  *  - TB200_DECODE_PERSISTENT: one persistent kernel (one CTA per SM) runs all
  *    of a step's phases, the phases exchanging tagged vectors instead of
  *    ending kernels, and tb200_generate / tb200_decode_enqueue run all their
- *    steps in one launch. Needs an unsharded model with head_dim 128, hidden
- *    / FFN / query widths up to 3072, at most 4 query heads per kv head, at
- *    most 8 kv heads and 64 layers (Qwen3-0.6B fits; Qwen3-4B does not).
+ *    steps in one launch. Needs an unsharded model (or a tensor-parallel
+ *    group of one) with head_dim 128, hidden / FFN / query widths up to
+ *    10240, at most 4 query heads per kv head, at most 8 kv heads and 64
+ *    layers (Qwen3-0.6B and Qwen3-4B fit).
  * tb200_state_new picks PERSISTENT where the model allows it, else FUSED.
  * Both give the same tokens and logits within the tolerance of their
  * different summation orders. */

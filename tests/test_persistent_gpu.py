@@ -3,12 +3,15 @@ launch runs every phase of every step, the phases exchanging tagged vectors)
 against the oracle and against the fused path.
 
 Shapes are chosen so that every branch of the kernel runs: the tiny model
-(few rows per CTA: K split over the warps everywhere), two layers of
-Qwen3-0.6B (q|k|v, gate|up, o_proj partials and the lm_head on the
-rows-per-warp branch; down_proj split over K), and a model with four query
-heads per kv head and more than eight residual rows per CTA (down_proj on
-the rows-per-warp branch too). Contexts past 256 positions take the split
-attention (members of a kv group exchange partial softmax results)."""
+(few rows per CTA, inputs narrower than 256 columns), two layers of
+Qwen3-0.6B (every matrix at its real per-CTA row count; the lm_head's last
+ring stage has three rows and takes the column-split branch), two layers of
+Qwen3-4B (hidden 2560, FFN 9728: the smaller ring slots, batched polls of
+the 9728-wide input, down_proj in three-row stages split by columns over
+the warps, layers streamed without L2 prefetch), and a model with four
+query heads per kv head and more than eight residual rows per CTA. Contexts
+past 256 positions take the split attention (members of a kv group
+exchange partial softmax results)."""
 
 import os
 
@@ -57,7 +60,7 @@ def test_tiny_against_oracle_and_fused_path(b200, tiny_model_dir, kv):
     assert m.generate(st, toks[-1], P + S, 3) == ref_tokens[S + 1:S + 4]
 
 
-@pytest.mark.parametrize("name", ["qwen3-0.6b-2l", "wide-gqa4"])
+@pytest.mark.parametrize("name", ["qwen3-0.6b-2l", "qwen3-4b-2l", "wide-gqa4"])
 def test_every_branch_against_fused_path_and_oracle(b200, name):
     """Logits of every step within 1e-4 of the fused path's (f32 cache: the
     two differ only in summation order) and within the north-star bound of
@@ -127,7 +130,7 @@ def test_long_context_split_attention(b200, tiny_model_dir, kv):
 
 
 def test_modes_and_rejection(b200, tiny_model_dir):
-    """A model the persistent kernel cannot run (FFN wider than 3072) keeps
+    """A model the persistent kernel cannot run (FFN wider than 10240) keeps
     the fused path by default and refuses the persistent one with a reason;
     unknown modes are refused."""
     import titania_b200 as tb
@@ -141,7 +144,7 @@ def test_modes_and_rejection(b200, tiny_model_dir):
         _lib.call("tb200_state_set_decode", st._h, 7)
     assert e.value.code == _lib.TB200_ERR_ARG
 
-    wide = dict(synth.TINY, intermediate_size=3328, num_hidden_layers=1)
+    wide = dict(synth.TINY, intermediate_size=10496, num_hidden_layers=1)
     d = os.path.join(ROOT, "_build", "wide-ffn")
     synth.write_model(d, wide, seed=2)
     mw = tb.Model.load(d, b200)
@@ -149,7 +152,7 @@ def test_modes_and_rejection(b200, tiny_model_dir):
     assert sw.decode == "fused"
     with pytest.raises(_lib.DeviceError) as e:
         sw.decode = "persistent"
-    assert e.value.code == _lib.TB200_ERR_ARG and "3072" in str(e.value)
+    assert e.value.code == _lib.TB200_ERR_ARG and "10240" in str(e.value)
     with pytest.raises(_lib.DeviceError) as e:
         mw.decode_persistent(sw, 1, 0, 2)
     assert e.value.code == _lib.TB200_ERR_ARG

@@ -180,6 +180,8 @@ int forward_tokens(tb200_state* st, size_t seq, const uint32_t* tokens, size_t n
                    uint32_t* next);
 // Sums `n` floats at `buf` over the tensor-parallel group, on stream `s`.
 int tp_allreduce(tb200_tp* tp, float* buf, size_t n, cudaStream_t s);
+// Ranks in the group (1 for a null group).
+int tp_world(const tb200_tp* tp);
 // Sets up m->p2p (every rank calls it at finalize; all ranks agree whether
 // to use it, else they keep NCCL) and releases it.
 int tp_p2p_setup(tb200_model* m);
@@ -192,6 +194,9 @@ void tp_p2p_free(tb200_model* m);
 std::string persist_unsupported(const tb200_model* m, const tb200_state* st);
 int persist_enqueue(tb200_state* st, size_t steps, bool logits);
 size_t persist_trace_slots(const tb200_state* st);
+// persist_wide.cu: the same for models wider than 3072 (up to 10240).
+std::string persist_wide_unsupported(const tb200_model* m, const tb200_state* st);
+int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits);
 
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);

@@ -73,6 +73,8 @@ int nccl_fail(Nccl* n, ncclResult_t r, const char* what) {
 
 namespace rt {
 
+int tp_world(const tb200_tp* tp) { return tp ? tp->world : 1; }
+
 int tp_allreduce(tb200_tp* tp, float* buf, size_t n, cudaStream_t s) {
   Nccl* nc = nullptr;
   if (int rc = load_nccl(&nc)) return rc;

@@ -42,6 +42,9 @@ TINY = dict(
 # the single-token kernels see the real per-CTA row counts at a fraction of
 # the oracle's time.
 QWEN3_0_6B_2L = dict(QWEN3_0_6B, num_hidden_layers=2)
+# Two layers of Qwen3-4B (its widths: hidden 2560, FFN 9728, 32 query heads
+# over 8 kv heads), for the single-token kernels' wide-input branches.
+QWEN3_4B_2L = dict(QWEN3_4B, num_hidden_layers=2)
 # Two layers with four query heads per kv head (Qwen3-4B's grouping) and a
 # hidden size that gives every CTA more than eight residual rows.
 WIDE_GQA4 = dict(
@@ -50,7 +53,7 @@ WIDE_GQA4 = dict(
     vocab_size=4096, tie_word_embeddings=True,
 )
 CONFIGS = {"qwen3-0.6b": QWEN3_0_6B, "qwen3-4b": QWEN3_4B, "tiny": TINY, "qwen3-0.6b-2l": QWEN3_0_6B_2L,
-           "wide-gqa4": WIDE_GQA4}
+           "qwen3-4b-2l": QWEN3_4B_2L, "wide-gqa4": WIDE_GQA4}
 
 
 def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
