@@ -773,9 +773,13 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
     // phase's input (a bulk prefetch waits behind the ring's copies in the
     // copy engine, so it is issued from a thread that has nothing else to
     // do; and after the exchange, which it would slow). Layers too large for
-    // L2 to hold the next one stream through the ring alone. ----
-    if (lane == 0 && valid && a.prefetch) {
-      for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, 0, 0, q);
+    // L2 to hold the next one stream their weights through the ring alone;
+    // their cached keys and values are still asked for a layer ahead. ----
+    if (lane == 0 && valid) {
+      if (a.prefetch)
+        for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, 0, 0, q);
+      else
+        prefetch_kv(a, c, G, pos0, 0, 0);
       for (int step = 0; step < a.steps && !abort_sm; step++)
         for (int layer = 0; layer <= a.L && !abort_sm; layer++)
           for (int p = 0; p < kPhases && !abort_sm; p++) {
@@ -786,7 +790,16 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
             while (progress_sm < ph && !abort_sm && clock64() - t0 < kWaitCycles) __nanosleep(32);
             if (progress_sm < ph) break;
             if (layer == a.L) {  // the next step's first layer
-              for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, step + 1, 0, q);
+              if (a.prefetch)
+                for (int q = 0; q < kPhases; q++) prefetch_phase(a, plan[q], c, G, pos0, step + 1, 0, q);
+              else
+                prefetch_kv(a, c, G, pos0, step + 1, 0);
+              continue;
+            }
+            if (!a.prefetch) {
+              // Weights two phases ahead (capped at 256 or 448 KB per CTA)
+              // measured slower here: every phase that streams got slower.
+              if (p == K_QKV) prefetch_kv(a, c, G, pos0, step, layer + 1);
               continue;
             }
             if (layer + 1 < a.L) prefetch_phase(a, plan[p], c, G, pos0, step, layer + 1, p);
