@@ -141,7 +141,7 @@ def test_tp_data_flow_gloo(tiny_model_dir):
 
 # ---- on two GPUs -------------------------------------------------------------
 
-def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0):
+def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0, decode=None):
     # No NVLink multicast (NVLS) in tests: a rank that dies bound to a
     # multicast object can fault the other ranks' GPUs.
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -158,7 +158,7 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0):
         group = TPGroup(dev, rank, world, uid[0])
         m = load_tp_model(model_dir, dev, group)
         peer = m.tp_peer_exchange
-        st = m.state(len(prompt) + steps + 2, kv=kv)
+        st = m.state(len(prompt) + steps + 2, kv=kv, decode=decode)
         logits = [m.forward(st, prompt, 0)]
         if late:
             # The last rank starts its first single-token step `late` seconds
@@ -185,13 +185,13 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0):
             toks.append(int(np.argmax(logits[-1])))
             pos += 1
         # the device-side loop and the batched path agree with the host loop
-        st2 = m.state(len(prompt) + steps + 2, kv=kv)
+        st2 = m.state(len(prompt) + steps + 2, kv=kv, decode=decode)
         first = m.forward(st2, prompt, 0, logits=False)
         gen = [first] + m.generate(st2, first, len(prompt), steps)
         bs = m.batch_state(2, len(prompt) + steps + 2, kv=kv)
         bfirst = [m.forward_seq(bs, i, prompt, 0, logits=False) for i in range(2)]
         bgen = m.generate_batch(bs, bfirst, [len(prompt)] * 2, steps)
-        q.put((rank, (np.stack(logits), toks, gen, [bfirst] + bgen.tolist(), peer)))
+        q.put((rank, (np.stack(logits), toks, gen, [bfirst] + bgen.tolist(), peer, st.decode)))
         del st, st2, bs, m
         group.close()
         dist.destroy_process_group()
@@ -200,7 +200,7 @@ def _gpu_tp_rank(rank, world, port, model_dir, prompt, steps, kv, q, late=0.0):
         q.put((rank, traceback.format_exc()))
 
 
-def _run_tp(model_dir, prompt, steps, kv, world=2, late=0.0):
+def _run_tp(model_dir, prompt, steps, kv, world=2, late=0.0, decode=None):
     import multiprocessing as mp
     import socket
     with socket.socket() as s:
@@ -208,7 +208,7 @@ def _run_tp(model_dir, prompt, steps, kv, world=2, late=0.0):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_tp_rank, args=(r, world, port, model_dir, prompt, steps, kv, q, late))
+    procs = [ctx.Process(target=_gpu_tp_rank, args=(r, world, port, model_dir, prompt, steps, kv, q, late, decode))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -261,10 +261,9 @@ def test_tp1_group_load_against_oracle(tiny_model_dir):
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
 @pytest.mark.parametrize("plen", [9, 70])
 def test_tp2_tiny_against_oracle(tiny_model_dir, kv, plen):
-    """Two ranks against the oracle. With a 9-token prompt the steps run the
-    short-context graph (attention + o_proj per kv group, NCCL for those
-    partials, peer stores for down_proj); past 64 positions every partial sum
-    goes by peer stores."""
+    """Two ranks against the oracle: single-token steps on the persistent
+    kernel (the default; o_proj and down_proj partials by peer stores),
+    prompts and the batched path with NCCL."""
     if not _two_gpus():
         pytest.skip("needs two GPUs")
     from oracle import oracle as orc
@@ -273,13 +272,36 @@ def test_tp2_tiny_against_oracle(tiny_model_dir, kv, plen):
     steps = 6
     ref_tokens, ref_logits = orc.greedy_generate(orc.Model(tiny_model_dir), prompt, steps + 1, max_len=plen + 16)
     out = _run_tp(tiny_model_dir, prompt, steps, kv)
-    for r, (logits, toks, gen, bgen, peer) in out.items():
+    for r, (logits, toks, gen, bgen, peer, decode) in out.items():
         assert peer, f"rank {r}: the partial sums should go by peer stores on distinct GPUs"
+        assert decode == "persistent", f"rank {r}: tensor-parallel single-token steps run the persistent kernel"
         for i in range(steps + 1):
             close(logits[i], ref_logits[i], REL, ABS)
         assert toks == ref_tokens, f"rank {r}"
         assert gen == ref_tokens, f"rank {r}: device loop"
         assert [row[0] for row in bgen] == ref_tokens and [row[1] for row in bgen] == ref_tokens, f"rank {r}: batch"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("plen", [9, 70])
+def test_tp2_tiny_fused_path_against_oracle(tiny_model_dir, plen):
+    """The fused single-token graphs at TP2 (what a state runs when it asks
+    for them): with a 9-token prompt the short-context graph (attention +
+    o_proj per kv group, NCCL for those partials, peer stores for
+    down_proj); past 64 positions every partial sum goes by peer stores."""
+    if not _two_gpus():
+        pytest.skip("needs two GPUs")
+    from oracle import oracle as orc
+    from titania_b200 import synth
+    prompt = synth.prompt_tokens(plen, 1024, seed=3)
+    steps = 6
+    ref_tokens, ref_logits = orc.greedy_generate(orc.Model(tiny_model_dir), prompt, steps + 1, max_len=plen + 16)
+    out = _run_tp(tiny_model_dir, prompt, steps, "f32", decode="fused")
+    for r, (logits, toks, gen, bgen, peer, decode) in out.items():
+        assert peer and decode == "fused", f"rank {r}"
+        for i in range(steps + 1):
+            close(logits[i], ref_logits[i], REL, ABS)
+        assert toks == ref_tokens and gen == ref_tokens, f"rank {r}"
 
 
 @pytest.mark.gpu
@@ -293,23 +315,47 @@ def test_tp2_qwen3_0_6b_against_oracle():
     steps = 8
     ref_tokens, ref_logits = orc.greedy_generate(orc.Model(d), prompt, steps + 1, max_len=64)
     out = _run_tp(d, prompt, steps, "f32")
-    for r, (logits, toks, gen, bgen, peer) in out.items():
+    for r, (logits, toks, gen, bgen, peer, decode) in out.items():
+        assert decode == "persistent"
         for i in range(steps + 1):
             close(logits[i], ref_logits[i], REL, ABS)
         assert toks == ref_tokens and gen == ref_tokens, f"rank {r}"
 
 
 @pytest.mark.gpu
-def test_tp2_late_rank_times_out_without_hanging(tiny_model_dir):
+def test_tp2_qwen3_4b_two_layers_against_oracle():
+    """Two layers of Qwen3-4B over two ranks (each: 4 kv heads, 4864 FFN
+    columns, the wide persistent kernel with o_proj and down_proj partials
+    exchanged by peer stores) against the oracle."""
+    if not _two_gpus():
+        pytest.skip("needs two GPUs")
+    from oracle import oracle as orc
+    from titania_b200 import synth
+    d = synth.cached_model("qwen3-4b-2l", seed=0)
+    prompt = synth.prompt_tokens(12, 151936, seed=5)
+    steps = 4
+    ref_tokens, ref_logits = orc.greedy_generate(orc.Model(d), prompt, steps + 1, max_len=32)
+    out = _run_tp(d, prompt, steps, "f32")
+    for r, (logits, toks, gen, bgen, peer, decode) in out.items():
+        assert peer and decode == "persistent", f"rank {r}"
+        for i in range(steps + 1):
+            close(logits[i], ref_logits[i], REL, ABS)
+        assert toks == ref_tokens and gen == ref_tokens, f"rank {r}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("decode", ["persistent", "fused"])
+def test_tp2_late_rank_times_out_without_hanging(tiny_model_dir, decode):
     """A rank that starts its step three seconds late: the other rank's
     kernels give up their bounded wait for its partial sums after a second
     and the call reports TB200_ERR_TIMEOUT; the late rank then finds the
-    other's flags set and finishes; both processes end normally."""
+    other's words or flags written and finishes; both processes end
+    normally."""
     if not _two_gpus():
         pytest.skip("needs two GPUs")
     from titania_b200 import _lib, synth
-    prompt = synth.prompt_tokens(70, 1024, seed=4)  # past 64 positions: no NCCL in the step
-    out = _run_tp(tiny_model_dir, prompt, 1, "f32", late=3.0)
+    prompt = synth.prompt_tokens(70, 1024, seed=4)  # past 64 positions: no NCCL in the fused step
+    out = _run_tp(tiny_model_dir, prompt, 1, "f32", late=3.0, decode=decode)
     assert out[0] == (True, _lib.TB200_ERR_TIMEOUT), out
     assert out[1][0] is True
 

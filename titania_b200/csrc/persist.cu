@@ -1016,8 +1016,8 @@ namespace rt {
 namespace P = tb::persist;
 
 // Why model m and state st cannot run the persistent step ("" when they can).
-// Models wider than kMaxCols (hidden, FFN or query width) go to the wide
-// kernel (persist_wide.cu).
+// Models wider than kMaxCols (hidden, FFN or query width), and every
+// tensor-parallel rank, go to the wide kernel (persist_wide.cu).
 static bool wide_model(const tb200_model* m) {
   return std::max({m->c.hidden_size, m->c.intermediate_size, m->q_dim}) > size_t(P::kMaxCols);
 }
@@ -1025,7 +1025,7 @@ static bool wide_model(const tb200_model* m) {
 std::string persist_unsupported(const tb200_model* m, const tb200_state* st) {
   const tb200_config& c = m->c;
   const int sms = m->dev->sms;
-  if (wide_model(m)) return persist_wide_unsupported(m, st);
+  if (wide_model(m) || tp_world(m->tp) > 1) return persist_wide_unsupported(m, st);
   if (tp_world(m->tp) > 1) return "persistent decode runs unsharded models (no tensor parallelism)";
   if (st->n_seqs != 1) return "persistent decode runs one-sequence states";
   if (c.num_hidden_layers > size_t(P::kMaxLayers)) return "persistent decode runs at most 64 layers";
@@ -1076,7 +1076,7 @@ static int persist_prepare(tb200_state* st) {
 // step's logits go to st->logits when `logits`.
 int persist_enqueue(tb200_state* st, size_t steps, bool logits) {
   if (!steps) return TB200_OK;
-  if (wide_model(st->m)) return persist_wide_enqueue(st, steps, logits);
+  if (wide_model(st->m) || tp_world(st->m->tp) > 1) return persist_wide_enqueue(st, steps, logits);
   if (int rc = persist_prepare(st)) return rc;
   const tb200_model* m = st->m;
   const tb200_config& c = m->c;

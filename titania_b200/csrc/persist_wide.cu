@@ -77,6 +77,15 @@ struct Args {
   int xs_floats;   // shared memory: the input vector (xperm) and attention scratch, then the ring
   int slot;        // bytes of a ring slot
   int prefetch;    // ask L2 for the coming layer's rows (layers small enough to fit it)
+  // Tensor parallelism (world > 1): this rank holds Hkv of the world * Hkv kv
+  // groups and F of the FFN columns. Every rank's o_proj partials
+  // [world * Hkv][H] and down_proj partials [world][H] (tagged words, each
+  // rank's own buffer mapped here over NVLink) receive this rank's rows by
+  // peer stores; the owners of a residual row sum them in group / rank
+  // order, the same on every rank. World 1: po[0] is part_o, pd unused.
+  int world, rank;
+  TW* po[8];
+  TW* pd[8];
 };
 
 // Matrix phases; K_LM is the lm_head, after the last layer.
@@ -174,6 +183,16 @@ __device__ __forceinline__ const uint16_t* matrix_of(const Args& a, const Layer&
 __device__ __forceinline__ void st_tagged(TW* p, float v, uint32_t tag) {
   const TW w = (TW(tag) << 32) | TW(__float_as_uint(v));
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// System scope: words that another GPU stores or polls.
+__device__ __forceinline__ void st_tagged_sys(TW* p, float v, uint32_t tag) {
+  const TW w = (TW(tag) << 32) | TW(__float_as_uint(v));
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ TW ld_tagged_sys(const TW* p) {
+  TW w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
 __device__ __forceinline__ TW ld_tagged(const TW* p) {
   TW w;
@@ -931,12 +950,21 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
             } else if (kind == K_QKV) {
               st_tagged(a.qkv + row, v, out_tag);
             } else if (kind == K_ATTO) {
-              st_tagged(a.part_o + size_t(ag) * a.H + row, v, out_tag);
+              if (a.world == 1) {
+                st_tagged(a.part_o + size_t(ag) * a.H + row, v, out_tag);
+              } else {  // into every rank's partials, as global kv group rank * Hkv + ag
+                const size_t at = size_t(a.rank * a.Hkv + ag) * a.H + row;
+                for (int q = 0; q < a.world; q++) st_tagged_sys(a.po[q] + at, v, out_tag);
+              }
             } else if (kind == K_DOWN) {  // the residual add on a row this CTA owns
-              const float x1 = __fadd_rn(own[row - own0], v);
-              own[row - own0] = x1;
+              if (a.world == 1) {
+                const float x1 = __fadd_rn(own[row - own0], v);
+                own[row - own0] = x1;
 #pragma unroll
-              for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + row, x1, out_tag);
+                for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + row, x1, out_tag);
+              } else {  // this rank's partial over its FFN columns, to every rank
+                for (int q = 0; q < a.world; q++) st_tagged_sys(a.pd[q] + size_t(a.rank) * a.H + row, v, out_tag);
+              }
             } else {
               if (a.logits) a.logits[row] = v;
               const unsigned long long key = argmax_key(v, uint32_t(row));
@@ -1006,11 +1034,16 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
               emit(row, v, 0.f);
             }
           }
-          if (kind == K_ATTO && tid < own1 - own0) {
+          if ((kind == K_ATTO || (kind == K_DOWN && a.world > 1)) && tid < own1 - own0) {
             // x' = x + the o_proj partials of every kv group, in group order
             // (model.rs:131-132), on this CTA's residual rows: a poll of
-            // Hkv words per row, so that the next phase reads x' alone.
+            // world * Hkv words per row, so that the next phase reads x'
+            // alone. Tensor parallel, after down_proj: x = x' + the ranks'
+            // partials in rank order.
             const int r = own0 + tid;
+            const bool att = kind == K_ATTO;
+            const int n = att ? a.Hkv * a.world : a.world;
+            const TW* src = att ? a.po[a.rank] : a.pd[a.rank];
             float xv = own[tid];
             TW w[kMaxKv];
             const long long t0 = clock64();
@@ -1018,15 +1051,15 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
               bool ok = true;
 #pragma unroll
               for (int g = 0; g < kMaxKv; g++)
-                if (g < a.Hkv) {
-                  w[g] = ld_tagged(a.part_o + size_t(g) * a.H + r);
+                if (g < n) {
+                  w[g] = a.world > 1 ? ld_tagged_sys(src + size_t(g) * a.H + r) : ld_tagged(src + size_t(g) * a.H + r);
                   ok = ok && ttag(w[g]) == out_tag;
                 }
               if (ok || abort_sm || timed_out(t0, a.io + 3, &abort_sm)) break;
             }
 #pragma unroll
             for (int g = 0; g < kMaxKv; g++)
-              if (g < a.Hkv) xv = __fadd_rn(xv, tval(w[g]));
+              if (g < n) xv = __fadd_rn(xv, tval(w[g]));
             own[tid] = xv;
 #pragma unroll
             for (int q = 0; q < kRep; q++) st_tagged(a.x + q * a.H + r, xv, out_tag);
@@ -1131,7 +1164,11 @@ namespace P = tb::persist_wide;
 std::string persist_wide_unsupported(const tb200_model* m, const tb200_state* st) {
   const tb200_config& c = m->c;
   const int sms = m->dev->sms;
-  if (tp_world(m->tp) > 1) return "persistent decode runs unsharded models (no tensor parallelism)";
+  const int world = tp_world(m->tp);
+  if (world > 1 && !m->p2p.on)
+    return "tensor-parallel persistent decode needs the ranks' peer mappings (one GPU per rank, peer access)";
+  if (world > 1 && size_t(world) * c.num_key_value_heads > size_t(P::kMaxKv))
+    return "persistent decode needs at most 8 kv heads over all ranks";
   if (st->n_seqs != 1) return "persistent decode runs one-sequence states";
   if (c.num_hidden_layers > size_t(P::kMaxLayers)) return "persistent decode runs at most 64 layers";
   if (c.head_dim != size_t(P::kHd)) return "persistent decode needs head_dim 128";
@@ -1194,7 +1231,14 @@ int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits) {
     CUDA_TRY(cudaMemsetAsync(st->ps_ctl, 0, 16, s));
     st->ps_dirty = false;
   }
-  if (uint64_t(st->ps_epoch) + uint64_t(per) * steps >= 0xFFFF0000ull) {  // tags would wrap: start over
+  const int world = tp_world(m->tp);
+  // Tensor parallel: the partials shared with the other ranks carry tags of
+  // the model's counter, which every rank advances alike (the ranks make the
+  // same calls); it is never reset, since another rank may already be
+  // writing the next launch's words (2^32 tags: ~28 M steps of Qwen3-4B).
+  uint32_t& epoch = world > 1 ? const_cast<tb200_model*>(m)->p2p.ps_epoch : st->ps_epoch;
+  if (uint64_t(epoch) + uint64_t(per) * steps >= 0xFFFF0000ull) {  // tags would wrap
+    if (world > 1) return fail(TB200_ERR_ARG, "persistent decode: the model's tag space is used up");
     CUDA_TRY(cudaMemsetAsync(st->ps_words, 0, st->ps_nwords * 8, s));
     st->ps_epoch = 1;
   }
@@ -1223,14 +1267,23 @@ int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits) {
   a.best = reinterpret_cast<unsigned long long*>(st->ps_ctl);
   a.ticket = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(st->ps_ctl) + 8);
   a.logits = logits ? st->logits : nullptr;
-  a.epoch = st->ps_epoch;
+  a.epoch = epoch;
   a.steps = int(steps);
   a.trace = st->trace;
+  a.world = world;
+  a.rank = world > 1 ? m->p2p.rank : 0;
+  a.po[0] = a.part_o;
+  if (world > 1)
+    for (int r = 0; r < world; r++) {
+      unsigned char* base = static_cast<unsigned char*>(m->p2p.peer[r]);
+      a.po[r] = reinterpret_cast<P::TW*>(base + m->p2p.off_po);
+      a.pd[r] = reinterpret_cast<P::TW*>(base + m->p2p.off_pd);
+    }
   P::smem_layout(std::max(c.hidden_size, c.intermediate_size), &a.xs_floats, &a.slot);
   const size_t layer_bytes =
       2 * c.hidden_size * (m->q_dim + 2 * m->kv_dim + 3 * c.intermediate_size) + 2 * m->q_dim * c.hidden_size;
   a.prefetch = layer_bytes <= P::kPrefetchLayerBytes ? 1 : 0;
-  st->ps_epoch += per * uint32_t(steps);
+  epoch += per * uint32_t(steps);
   st->ps_grid = grid;
   if (st->trace.rec) st->ps_traced = true;
   cudaError_t e = P::launch(a, grid, s);
