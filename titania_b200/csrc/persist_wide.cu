@@ -39,6 +39,9 @@ constexpr int kMaxKv = 8;            // kv heads (o_proj partial vectors summed 
 constexpr int kMaxOwn = 32;          // residual rows a CTA owns
 constexpr int kAttnPer = 8;          // cached positions per warp held in registers at a time
 constexpr int kRedundantCtx = 256;   // contexts up to this: every group member attends over all of it
+constexpr int kSplitMembers = 64;    // past it, at most this many members of a group split the context
+                                     // (16 measured slower for Qwen3-4B at 2K: a member's extra chunk
+                                     // costs more than the polls it saves)
 constexpr int kPartWords = 132;      // a member's partial per head: acc[128], max, sum, 2 pad
 constexpr int kRep = 4;              // copies of the vectors every CTA reads (x, h): CTA c reads copy c % kRep
 constexpr int kLmAheadLayers = 8;    // the lm_head's first kLmAheadNum / kLmAheadDen of rows are asked of L2
@@ -454,8 +457,9 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
 
   const int ctx = pos + 1;
   const bool split = ctx > kRedundantCtx;
-  const int lo = split ? int((long long)s * ctx / ng) : 0;
-  const int hi = split ? int((long long)(s + 1) * ctx / ng) : ctx;
+  const int na = min(ng, kSplitMembers);  // members that attend in split mode
+  const int lo = split ? (s < na ? int((long long)s * ctx / na) : 0) : 0;
+  const int hi = split ? (s < na ? int((long long)(s + 1) * ctx / na) : 0) : ctx;
   const size_t head0 = size_t(g) * a.max_len * kHd;
 
   // Cached positions (< pos) do not depend on this step: the first chunk is
@@ -626,7 +630,7 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
   if (split) {
     // Publish this member's partial; then every member merges all of them.
     TW* mine = a.part_att + (size_t(g * a.nsplit + s) * grp) * kPartWords;
-    if (tid < grp * 32) {
+    if (tid < grp * 32 && s < na) {
       TW* p = mine + mh * kPartWords;
       st_tagged(p + 4 * d4 + 0, o.x, ptag);
       st_tagged(p + 4 * d4 + 1, o.y, ptag);
@@ -639,9 +643,9 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
         st_tagged(p + 131, 0.f, ptag);
       }
     }
-    // Every member merges all members' partials: the consumer threads form
-    // kWarps / grp quarters of (head, 4 dims) threads; quarter q merges
-    // members q, q + nq, ... (two requested at once, merged in that order),
+    // Every member merges the attending members' partials: the consumer
+    // threads form kWarps / grp quarters of (head, 4 dims) threads; quarter q
+    // merges members q, q + nq, ... (two requested at once, merged in that order),
     // then the quarters' results are merged in quarter order. The order is
     // fixed, so every member gets the same bits whatever the timing.
     const int nq = kWarps / grp, q = tid / (grp * 32), qh = (tid >> 5) % grp, qd = tid & 31;
@@ -661,8 +665,8 @@ __device__ void attention_phase(const Args& a, const Layer& Ly, int g, int s, in
       }
     };
     const long long t0 = clock64();
-    for (int sp = q; sp < ng; sp += 2 * nq) {
-      const bool two = sp + nq < ng;
+    for (int sp = q; sp < na; sp += 2 * nq) {
+      const bool two = sp + nq < na;
       const TW* p0 = a.part_att + (size_t(g * a.nsplit + sp) * grp + qh) * kPartWords;
       const TW* p1 = a.part_att + (size_t(g * a.nsplit + (two ? sp + nq : sp)) * grp + qh) * kPartWords;
       TW w0[4], w1[4], m0[2], m1[2];
@@ -725,8 +729,9 @@ __device__ void prefetch_kv(const Args& a, int c, int G, int pos0, int step, int
   group_of(a, c, G, g, s, ng);
   const int pos = pos0 + step, ctx = pos + 1;
   const bool split = ctx > kRedundantCtx;
-  const int lo = split ? int((long long)s * ctx / ng) : 0;
-  const int hi = min(pos, split ? int((long long)(s + 1) * ctx / ng) : ctx);
+  const int na = min(ng, kSplitMembers);
+  const int lo = split ? (s < na ? int((long long)s * ctx / na) : 0) : 0;
+  const int hi = min(pos, split ? (s < na ? int((long long)(s + 1) * ctx / na) : 0) : ctx);
   if (hi > lo) {
     const size_t esz = a.kv_f32 ? 4 : 2;
     const size_t at = (size_t(g) * a.max_len + lo) * kHd * esz, nb = size_t(hi - lo) * kHd * esz;
