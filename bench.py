@@ -457,10 +457,11 @@ def run_tp(args, rank, world, torch):
     """Config 4: Qwen3-4B-shaped random-init weights, tensor-parallel over the
     `world` GPUs of this node (one rank per GPU; world 1 is the single-GPU
     baseline). bs1: a 2048-token prompt, then TP_GEN greedy steps (contexts
-    2048..2079), replayed; bs256: 256 sequences, each prefilled with 2048
-    ids, then TP_GEN steps of all at once (bf16 K/V). The all-reduces after
-    o_proj and down_proj are NCCL calls captured in the decode graphs.
-    Device time, max over ranks."""
+    2048..2079), replayed, on the state's default single-token path (the
+    persistent kernel: o_proj and down_proj partials to every rank by peer
+    stores over NVLink); bs256: 256 sequences, each prefilled with 2048 ids,
+    then TP_GEN steps of all at once (bf16 K/V; NCCL all-reduces captured in
+    the decode graphs). Device time, max over ranks."""
     import titania_b200 as tb
     from titania_b200 import synth
     from titania_b200.tp import TPGroup, load_tp_model
@@ -510,7 +511,7 @@ def run_tp(args, rank, world, torch):
         return n * TP_GEN
     steps, secs = timed(bs1, True)
     step_bytes = weights32 + kv_per_pos32 * (TP_CTX + TP_GEN / 2)
-    out["bs1"] = {"tok_s": steps / secs, "ms_per_step": secs / steps * 1e3, "kv_cache": "f32",
+    out["bs1"] = {"tok_s": steps / secs, "ms_per_step": secs / steps * 1e3, "kv_cache": "f32", "decode": st.decode,
                   "hbm_frac_of_8tbs_x_n": step_bytes * steps / secs / (NOMINAL_HBM_GBS * 1e9 * world)}
     del st
 
