@@ -100,22 +100,32 @@ def test_every_branch_against_fused_path_and_oracle(b200, name):
     assert m.generate(st2, first, P, S) == toks
 
 
-@pytest.mark.parametrize("model", ["tiny", "wide-ffn"])
+LONG_MODELS = {  # name: changes to the tiny checkpoint
+    "tiny": None,
+    "wide-ffn": dict(intermediate_size=3328),                              # the wide kernel
+    "gqa4": dict(num_attention_heads=8),                                   # four query heads per kv head
+    "gqa4-wide": dict(num_attention_heads=8, intermediate_size=3328),      # both
+}
+
+
+@pytest.mark.parametrize("model", list(LONG_MODELS))
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
 def test_long_context_split_attention(b200, tiny_model_dir, kv, model):
     """A 1100-token prompt (the tensor-core prompt path), then greedy steps
     past 1100 positions: the members of each kv group attend to their share
     of the context and merge partials. Against the oracle, on the narrow
     kernel (tiny) and the wide one (an FFN of 3328 columns, 74 members per
-    kv group; its down_proj stages of one or two rows split by columns)."""
+    kv group; its down_proj stages of one or two rows split by columns),
+    each with two and with four query heads per kv head (the merge then
+    runs in two quarters of the threads instead of four)."""
     import titania_b200 as tb
     from oracle import oracle as orc
     from titania_b200 import synth
 
     d = tiny_model_dir
-    if model == "wide-ffn":
-        d = os.path.join(ROOT, "_build", "wide-ffn-3328")
-        synth.write_model(d, dict(synth.TINY, intermediate_size=3328), seed=6)
+    if LONG_MODELS[model]:
+        d = os.path.join(ROOT, "_build", "long-" + model)
+        synth.write_model(d, dict(synth.TINY, **LONG_MODELS[model]), seed=6)
     P, S = 1100, 6
     prompt = synth.prompt_tokens(P, synth.TINY["vocab_size"], seed=8)
     ref_tokens, ref_logits = orc.greedy_generate(orc.Model(d), prompt, S + 1, max_len=P + S + 2)
