@@ -89,6 +89,12 @@ struct Args {
   int world, rank;
   TW* po[8];
   TW* pd[8];
+  // lm_split (tensor parallel, no logits wanted): rank r streams only lm_head
+  // rows [r V / world, (r + 1) V / world) and sends its best (logit, id) key
+  // as two tagged words to every rank's pk [world][2]; each rank takes the
+  // largest key (ties: the lowest id, as unsplit).
+  int lm_split;
+  TW* pk[8];
 };
 
 // Matrix phases; K_LM is the lm_head, after the last layer.
@@ -161,7 +167,12 @@ __device__ Plan plan_of(const Args& a, int kind, int c, int G) {
     if (kind == K_QKV) share(a.Q + 2 * a.KV, 4, 1, c, G, p.r0, r1), p.cols = a.H;
     else if (kind == K_GU) share(2 * a.F, 8, 2, c, G, p.r0, r1), p.cols = a.H;  // gate/up pairs: 4 h values
     else if (kind == K_DOWN) own_rows(a, c, G, p.r0, r1), p.cols = a.F;
-    else share(a.V, 1, 1, c, G, p.r0, r1), p.cols = a.H;
+    else {
+      const int v0 = a.lm_split ? int((long long)a.rank * a.V / a.world) : 0;
+      const int v1 = a.lm_split ? int((long long)(a.rank + 1) * a.V / a.world) : a.V;
+      share(v1 - v0, 1, 1, c, G, p.r0, r1), p.cols = a.H;
+      p.r0 += v0, r1 += v0;
+    }
     p.w0 = p.r0;
   }
   p.n = r1 - p.r0;
@@ -1086,8 +1097,26 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(Args a) {
         __threadfence();
         if (atomicAdd(a.ticket, 1u) == unsigned(G - 1)) {
           __threadfence();
-          const unsigned long long bb = atomicExch(a.best, 0ull);
+          unsigned long long bb = atomicExch(a.best, 0ull);
           *a.ticket = 0u;
+          if (a.lm_split) {  // this rank's best key to every rank, then the best of all ranks'
+            const uint32_t ktag = T + per_step - 1u;
+            for (int r = 0; r < a.world; r++) {
+              st_tagged_sys(a.pk[r] + 2 * a.rank, __uint_as_float(uint32_t(bb >> 32)), ktag);
+              st_tagged_sys(a.pk[r] + 2 * a.rank + 1, __uint_as_float(uint32_t(bb)), ktag);
+            }
+            const long long t0 = clock64();
+            for (int r = 0; r < a.world; r++) {
+              TW hi, lo;
+              for (;;) {
+                hi = ld_tagged_sys(a.pk[a.rank] + 2 * r);
+                lo = ld_tagged_sys(a.pk[a.rank] + 2 * r + 1);
+                if ((ttag(hi) == ktag && ttag(lo) == ktag) || abort_sm || timed_out(t0, a.io + 3, &abort_sm)) break;
+              }
+              const unsigned long long key = (static_cast<unsigned long long>(uint32_t(hi)) << 32) | uint32_t(lo);
+              bb = key > bb ? key : bb;
+            }
+          }
           const int t = int(argmax_index(bb));
           a.io[0] = t;
           a.io[1] = pos + 1;
@@ -1278,11 +1307,13 @@ int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits) {
   a.world = world;
   a.rank = world > 1 ? m->p2p.rank : 0;
   a.po[0] = a.part_o;
+  a.lm_split = world > 1 && !logits && c.vocab_size / size_t(world) >= size_t(grid) ? 1 : 0;
   if (world > 1)
     for (int r = 0; r < world; r++) {
       unsigned char* base = static_cast<unsigned char*>(m->p2p.peer[r]);
       a.po[r] = reinterpret_cast<P::TW*>(base + m->p2p.off_po);
       a.pd[r] = reinterpret_cast<P::TW*>(base + m->p2p.off_pd);
+      a.pk[r] = reinterpret_cast<P::TW*>(base + m->p2p.off_pk);
     }
   P::smem_layout(std::max(c.hidden_size, c.intermediate_size), &a.xs_floats, &a.slot);
   const size_t layer_bytes =

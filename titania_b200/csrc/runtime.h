@@ -78,11 +78,12 @@ struct TpP2p {
   bool on = false;
   int world = 1, rank = 0;
   // this rank's: recv_o [world][H], recv_d [world][H] f32, flags [2L][world]; then the persistent
-  // kernel's tagged words: o_proj partials [world * Hkv][H] and down_proj partials [world][H]
+  // kernel's tagged words: o_proj partials [world * Hkv][H], down_proj partials [world][H], argmax keys
   void* region = nullptr;
   void* peer[8] = {};                   // every rank's region as mapped here (this rank's: region)
   size_t off_d = 0, off_flags = 0;      // byte offsets of recv_d and the flags in a region
   size_t off_po = 0, off_pd = 0;        // byte offsets of the persistent kernel's partials
+  size_t off_pk = 0;                    // ... and of its vocabulary-split argmax keys [world][2]
   unsigned* tickets = nullptr;          // [2L] arrival counters of the publishing launches
   unsigned* epoch = nullptr;            // this step's flag value; advanced by the lm_head
   uint32_t ps_epoch = 1;                // tag base of the persistent kernel's next launch (every rank alike)

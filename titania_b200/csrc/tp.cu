@@ -140,7 +140,8 @@ int tp_p2p_setup(tb200_model* m) {
   p.off_flags = 2 * size_t(W) * H * 4;
   p.off_po = (p.off_flags + 2 * L * W * 4 + 255) / 256 * 256;
   p.off_pd = p.off_po + size_t(W) * m->c.num_key_value_heads * H * 8;
-  const size_t bytes = p.off_pd + size_t(W) * H * 8;
+  p.off_pk = p.off_pd + size_t(W) * H * 8;
+  const size_t bytes = p.off_pk + size_t(W) * 2 * 8;
   cudaStream_t s = m->dev->stream;
   P2pCard card{};
   bool ok = wanted;
