@@ -327,6 +327,9 @@ __device__ float poll_vector(const TW* vec, int n, uint32_t tag, const uint16_t*
       if (tags4(w, tag) || *abort) {
         float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
         if (norm) {
+          // In arrival order: the same bits whatever the order for up to two
+          // groups (n <= 2048, every normed input of the models this kernel
+          // runs but those with hidden sizes of 2049..3072).
           ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
           const uint2 g = *reinterpret_cast<const uint2*>(norm + i);
           v.x *= bf_lo(g.x), v.y *= bf_hi(g.x), v.z *= bf_lo(g.y), v.w *= bf_hi(g.y);
