@@ -328,8 +328,8 @@ __device__ float poll_vector(const TW* vec, int n, uint32_t tag, const uint16_t*
         float4 v = make_float4(tval(w[0]), tval(w[1]), tval(w[2]), tval(w[3]));
         if (norm) {
           // In arrival order: the same bits whatever the order for up to two
-          // groups (n <= 2048, every normed input of the models this kernel
-          // runs but those with hidden sizes of 2049..3072).
+          // groups, and every normed input here (the hidden vector) has at most
+          // 2048 (wider models run persist_wide.cu, which adds in group order).
           ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
           const uint2 g = *reinterpret_cast<const uint2*>(norm + i);
           v.x *= bf_lo(g.x), v.y *= bf_hi(g.x), v.z *= bf_lo(g.y), v.w *= bf_hi(g.y);
@@ -1019,10 +1019,12 @@ namespace rt {
 namespace P = tb::persist;
 
 // Why model m and state st cannot run the persistent step ("" when they can).
-// Models wider than kMaxCols (hidden, FFN or query width), and every
-// tensor-parallel rank, go to the wide kernel (persist_wide.cu).
+// Models wider than kMaxCols (hidden, FFN or query width) or with a hidden
+// size above 2048 (whose RMSNorm sums would depend on arrival order here),
+// and every tensor-parallel rank, go to the wide kernel (persist_wide.cu).
 static bool wide_model(const tb200_model* m) {
-  return std::max({m->c.hidden_size, m->c.intermediate_size, m->q_dim}) > size_t(P::kMaxCols);
+  return std::max({m->c.hidden_size, m->c.intermediate_size, m->q_dim}) > size_t(P::kMaxCols) ||
+         m->c.hidden_size > 2048;
 }
 
 std::string persist_unsupported(const tb200_model* m, const tb200_state* st) {
