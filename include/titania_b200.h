@@ -45,7 +45,10 @@ enum {
   TB200_OK = 0,
   TB200_ERR_ARG = 1,     /* an argument violates the op's contract (a reference panic) */
   TB200_ERR_CUDA = 2,    /* a CUDA runtime error */
-  TB200_ERR_TIMEOUT = 3, /* a bounded wait inside a kernel gave up */
+  TB200_ERR_TIMEOUT = 3, /* a bounded wait inside a kernel gave up: the state's cache and step
+                          * position may be partly advanced (a decode step stops where its
+                          * wait gave up); forward the sequence again from a known position
+                          * (its prompt) before decoding it further */
   TB200_ERR_IO = 4,      /* a file could not be opened or read (Weights' io::Error) */
   TB200_ERR_FORMAT = 5,  /* a file is not a valid safetensors checkpoint of bf16 tensors */
 };
