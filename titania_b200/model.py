@@ -270,8 +270,10 @@ class Model:
 
     @property
     def tp_peer_exchange(self) -> bool:
-        """Whether this tensor-parallel rank's single-token step adds the
-        o_proj / down_proj partial sums by peer stores (else NCCL)."""
+        """Whether this tensor-parallel rank's single-token steps add the
+        o_proj / down_proj partial sums by peer stores over NVLink (the
+        persistent kernel, and the fused graphs' flags); else the fused graphs
+        with NCCL."""
         return bool(_lib.lib().tb200_model_tp_peer_exchange(self._h))
 
     def state(self, max_len: int, kv: str = "f32", decode: str | None = None) -> "State":

@@ -9,8 +9,11 @@ Rank r of `world` holds, per layer (Megatron-style):
   gate_proj / up_proj        rows r*F/world .. (r+1)*F/world;
   down_proj                  the matching input columns (a partial sum);
 and all norms, the embedding and lm_head whole. The library adds the partial
-sums over the group (NCCL all-reduce) before they join the residual stream,
-so every rank computes the same logits and greedy tokens.
+sums over the group before they join the residual stream, so every rank
+computes the same logits and greedy tokens: single-token steps exchange them
+by peer stores over NVLink (the persistent kernel; when every rank has its own
+GPU), prompts and the batched path by NCCL all-reduce. Greedy steps without
+logits split the lm_head by vocabulary over the ranks.
 
 `shard_config` / `shard_tensor` are the sharding rule (pure numpy, tested on
 the CPU); `TPGroup` is the NCCL group; `load_tp_model` builds a rank's model.
