@@ -1,8 +1,11 @@
 // persist_wide.cu — the persistent batch-1 decode kernel of persist.cu for
-// models whose hidden or FFN width is above 3072 (Qwen3-4B: 2560 and 9728),
-// up to 10240: Model::forward for one token (model/model.rs:93-149) and the
-// greedy choice (model/sampler.rs:31-33), `steps` tokens per launch, with
-// the same phases, tagged-word exchanges, bounded waits and trace events.
+// models whose hidden size is above 2048 or whose FFN or query width is above
+// 3072 (Qwen3-4B: 2560 and 9728), up to 10240, and for every tensor-parallel
+// rank: Model::forward for one token (model/model.rs:93-149) and the greedy
+// choice (model/sampler.rs:31-33), `steps` tokens per launch, with the same
+// phases, tagged-word exchanges, bounded waits and trace events. Under
+// tensor parallelism (see Args) the o_proj and down_proj partials go to every
+// rank by peer stores and greedy steps split the lm_head by vocabulary.
 // What differs for wide inputs:
 //   - the input region of shared memory holds the widest input (9728 f32 for
 //     down_proj's h), so the three ring slots are smaller (62 KB for
