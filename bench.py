@@ -195,14 +195,14 @@ FUSED_NAMES = {0: "embed", 1: "q|k|v", 2: "attention", 3: "o_proj", 4: "gate|up"
                7: "attention + o_proj", 8: "gate|up (+o partials)"}
 
 
-def step_trace(m, st, first, decode):
-    """One traced single-token step at position PROMPT + 16 (the middle of
+def step_trace(m, st, first, decode, prompt=PROMPT):
+    """One traced single-token step at position prompt + 16 (the middle of
     config 0's contexts) on the given path."""
     prev = st.decode
     st.decode = decode
-    m.decode_enqueue(st, first, PROMPT, 16)
+    m.decode_enqueue(st, first, prompt, 16)
     st.trace_start(1 << 22)
-    m.decode_enqueue(st, first, PROMPT + 16, 1)
+    m.decode_enqueue(st, first, prompt + 16, 1)
     tr = st.trace_stop()
     st.decode = prev
     return timeline(tr, PERSIST_NAMES if decode == "persistent" else FUSED_NAMES)
@@ -513,6 +513,8 @@ def run_tp(args, rank, world, torch):
     step_bytes = weights32 + kv_per_pos32 * (TP_CTX + TP_GEN / 2)
     out["bs1"] = {"tok_s": steps / secs, "ms_per_step": secs / steps * 1e3, "kv_cache": "f32", "decode": st.decode,
                   "hbm_frac_of_8tbs_x_n": step_bytes * steps / secs / (NOMINAL_HBM_GBS * 1e9 * world)}
+    if st.decode == "persistent":  # where a step goes (every rank traces alike; rank 0's is reported)
+        out["bs1"]["step_timeline"] = step_trace(m, st, first, "persistent", prompt=TP_CTX)
     del st
 
     # bs256 (bf16 cache)
