@@ -193,6 +193,9 @@ PERSIST_NAMES = {32: "q|k|v", 33: "attention + o_proj partials + residual", 34: 
                  36: "lm_head + argmax", 38: "token"}
 FUSED_NAMES = {0: "embed", 1: "q|k|v", 2: "attention", 3: "o_proj", 4: "gate|up", 5: "down", 6: "lm_head",
                7: "attention + o_proj", 8: "gate|up (+o partials)"}
+BATCH_NAMES = {16: "embed", 17: "rmsnorm (tp)", 18: "q|k|v (tcgen05)", 20: "attention", 21: "o_proj (tcgen05)",
+               22: "rmsnorm 2 (tp)", 23: "gate|up (tcgen05)", 24: "down (tcgen05)", 25: "final norm (tp)",
+               26: "lm_head (tcgen05)", 27: "argmax"}
 
 
 def step_trace(m, st, first, decode, prompt=PROMPT):
@@ -417,6 +420,16 @@ def run_bs64(args, tb, m, dev, cfg, torch, world):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         secs, e2e_secs = t.tolist()
 
+    # One traced step (every kernel records its CTAs' events): per kernel, the
+    # segment from the previous kernel's last CTA to its own (they add up to
+    # the step) and the CTAs' median own work.
+    try:
+        bs.trace_start(1 << 22)
+        m.decode_batch_enqueue(bs, first, pos, 1)
+        step_timeline = timeline(bs.trace_stop(), BATCH_NAMES)
+    except Exception as e:  # secondary: report it, keep the measurement
+        step_timeline = {"error": f"{type(e).__name__}: {e}"[:300]}
+
     weights, kv_per_pos = model_bytes(cfg, kv_bytes=2)
     mean_ctx = BS64_CTX + (BS64_GEN + 1) / 2
     step_bytes = weights + BS64_SEQS * kv_per_pos * mean_ctx
@@ -437,6 +450,7 @@ def run_bs64(args, tb, m, dev, cfg, torch, world):
                 "h2d_bytes_per_step": BS64_SEQS * (4 + 8) + 3 * 4, "d2h_bytes_per_step": BS64_SEQS * 4 + 4},
         "gpu_launches": steps * (1 + 8 * L + 3),
         "clocks": clk.summary(),
+        "step_timeline": step_timeline,
     }
 
 
