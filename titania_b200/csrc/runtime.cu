@@ -1000,18 +1000,19 @@ int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_
     st->host_pos = pos + n;
     return TB200_OK;
   }
+  // One token: token, position, step counter and error word in one copy
+  // (from the slot finish() reads io back into, which this copy precedes).
   cudaStream_t s = m->dev->stream;
-  CUDA_TRY(cudaMemsetAsync(st->io + 2, 0, 2 * sizeof(int), s));  // step counter, error word
-  for (size_t i = 0; i < n; i++) {
-    int* stage = st->io_host + 2 * (pos + i);
-    stage[0] = int(tokens[i]);
-    stage[1] = int(pos + i);
-    CUDA_TRY(cudaMemcpyAsync(st->io, stage, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-    if (st->decode_mode == TB200_DECODE_PERSISTENT) {
-      if (int rc = rt::persist_enqueue(st, 1, logits != nullptr)) return rc;
-    } else {
-      CUDA_TRY(cudaGraphLaunch(step_graph(st, pos + i), s));
-    }
+  int* stage = st->io_host + 2 * st->max_len;
+  stage[0] = int(tokens[0]);
+  stage[1] = int(pos);
+  stage[2] = 0;
+  stage[3] = 0;
+  CUDA_TRY(cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s));
+  if (st->decode_mode == TB200_DECODE_PERSISTENT) {
+    if (int rc = rt::persist_enqueue(st, 1, logits != nullptr)) return rc;
+  } else {
+    CUDA_TRY(cudaGraphLaunch(step_graph(st, pos), s));
   }
   if (logits) CUDA_TRY(cudaMemcpyAsync(logits, st->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
