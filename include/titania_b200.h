@@ -479,7 +479,8 @@ enum {
   TB200_BUF_QKV = 1,    /* raw q|k|v projections, (heads + 2 kv_heads) * head_dim */
   TB200_BUF_ATT = 2,    /* attention output, heads * head_dim */
   TB200_BUF_H = 3,      /* silu(gate) * up, intermediate_size */
-  TB200_BUF_LOGITS = 4, /* vocab_size */
+  TB200_BUF_LOGITS = 4, /* vocab_size (a persistent step that wrote its logits
+                         * straight to page-locked host memory leaves it as it was) */
   TB200_BUF_X2 = 5,     /* residual stream after attention, hidden_size */
   TB200_BUF_PART = 6,   /* o_proj partials, kv_heads * hidden_size */
 };

@@ -177,3 +177,25 @@ def test_modes_and_rejection(b200, tiny_model_dir):
     prompt = synth.prompt_tokens(4, wide["vocab_size"], seed=1)
     first = mw.forward(sw, prompt, 0, logits=False)
     assert len(mw.generate(sw, first, 4, 3)) == 3
+
+
+def test_logits_into_page_locked_memory(b200, tiny_model_dir):
+    """A single-token forward whose logits buffer is page-locked host memory
+    gets them written by the persistent kernel itself (no copy after it):
+    the same bits as through a pageable buffer, step after step."""
+    torch = pytest.importorskip("torch")
+    import titania_b200 as tb
+    from titania_b200 import synth
+
+    m = tb.Model.load(tiny_model_dir, b200)
+    prompt = synth.prompt_tokens(9, synth.TINY["vocab_size"], seed=3)
+    pinned = torch.empty(synth.TINY["vocab_size"], dtype=torch.float32, pin_memory=True).numpy()
+    a, b = m.state(32), m.state(32)
+    tok_a = int(np.argmax(m.forward(a, prompt, 0)))
+    tok_b = int(np.argmax(m.forward(b, prompt, 0)))
+    for i in range(4):
+        la = m.forward(a, [tok_a], 9 + i).copy()  # pageable: copied after the kernel
+        m.forward(b, [tok_b], 9 + i, out=pinned)  # page-locked: written by the kernel
+        assert np.array_equal(la, pinned), i
+        tok_a, tok_b = int(np.argmax(la)), int(np.argmax(pinned))
+        assert tok_a == tok_b

@@ -1078,10 +1078,11 @@ static int persist_prepare(tb200_state* st) {
 
 // Enqueues `steps` greedy steps from the token and position in st->io as
 // one launch (io[2] counts generated tokens into st->tokens_out); the last
-// step's logits go to st->logits when `logits`.
-int persist_enqueue(tb200_state* st, size_t steps, bool logits) {
+// step's logits go to st->logits when `logits` (to `logits_to`, a device
+// address of page-locked host memory, when given).
+int persist_enqueue(tb200_state* st, size_t steps, bool logits, float* logits_to) {
   if (!steps) return TB200_OK;
-  if (wide_model(st->m) || tp_world(st->m->tp) > 1) return persist_wide_enqueue(st, steps, logits);
+  if (wide_model(st->m) || tp_world(st->m->tp) > 1) return persist_wide_enqueue(st, steps, logits, logits_to);
   if (int rc = persist_prepare(st)) return rc;
   const tb200_model* m = st->m;
   const tb200_config& c = m->c;
@@ -1119,7 +1120,7 @@ int persist_enqueue(tb200_state* st, size_t steps, bool logits) {
   a.io = st->io, a.tokens_out = st->tokens_out, a.tokens_cap = int(st->max_len);
   a.best = reinterpret_cast<unsigned long long*>(st->ps_ctl);
   a.ticket = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(st->ps_ctl) + 8);
-  a.logits = logits ? st->logits : nullptr;
+  a.logits = logits ? (logits_to ? logits_to : st->logits) : nullptr;
   a.epoch = st->ps_epoch;
   a.steps = int(steps);
   a.trace = st->trace;

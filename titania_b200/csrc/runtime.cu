@@ -1009,12 +1009,22 @@ int tb200_forward(tb200_model* m, tb200_state* st, const uint32_t* tokens, size_
   stage[2] = 0;
   stage[3] = 0;
   CUDA_TRY(cudaMemcpyAsync(st->io, stage, 4 * sizeof(int), cudaMemcpyHostToDevice, s));
+  // The persistent kernel writes the logits straight into page-locked host
+  // memory (as its lm_head rows finish, over PCIe) instead of a copy after it.
+  float* direct = nullptr;
+  if (logits && st->decode_mode == TB200_DECODE_PERSISTENT) {
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, logits) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer)
+      direct = static_cast<float*>(pa.devicePointer);
+    cudaGetLastError();  // a pointer CUDA does not know is an answer, not an error to keep
+  }
   if (st->decode_mode == TB200_DECODE_PERSISTENT) {
-    if (int rc = rt::persist_enqueue(st, 1, logits != nullptr)) return rc;
+    if (int rc = rt::persist_enqueue(st, 1, logits != nullptr, direct)) return rc;
   } else {
     CUDA_TRY(cudaGraphLaunch(step_graph(st, pos), s));
   }
-  if (logits) CUDA_TRY(cudaMemcpyAsync(logits, st->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
+  if (logits && !direct)
+    CUDA_TRY(cudaMemcpyAsync(logits, st->logits, m->c.vocab_size * 4, cudaMemcpyDeviceToHost, s));
   if (int rc = finish(st)) return rc;
   st->host_pos = pos + n;
   if (next_token) *next_token = uint32_t(st->io_host[2 * st->max_len + 0]);

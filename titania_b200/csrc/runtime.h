@@ -197,11 +197,11 @@ void tp_p2p_free(tb200_model* m);
 // one launch (the last step's logits to st->logits when `logits`); the trace
 // slots one step uses.
 std::string persist_unsupported(const tb200_model* m, const tb200_state* st);
-int persist_enqueue(tb200_state* st, size_t steps, bool logits);
+int persist_enqueue(tb200_state* st, size_t steps, bool logits, float* logits_to = nullptr);
 size_t persist_trace_slots(const tb200_state* st);
 // persist_wide.cu: the same for models wider than 3072 (up to 10240).
 std::string persist_wide_unsupported(const tb200_model* m, const tb200_state* st);
-int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits);
+int persist_wide_enqueue(tb200_state* st, size_t steps, bool logits, float* logits_to = nullptr);
 
 // Frees what the many-token path allocated on a state.
 void free_batch(tb200_state* st);
